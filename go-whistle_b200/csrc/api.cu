@@ -1,0 +1,539 @@
+// api.cu — the C ABI of libwhistle_b200.so (include/whistle_b200.h).
+//
+// Host-side work only: validation with the reference's messages, the
+// one-time device copy of a CQ tensor into the kernels' group-major layout,
+// views, and launches. No CPU compute path exists here: every product runs
+// on the GPU, and a missing GPU is an error status.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <atomic>
+#include <cmath>
+#include <memory>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "cq_kernels.cuh"
+#include "needle_kernels.cuh"
+
+// ------------------------------------------------------------- errors ----
+
+namespace wb {
+
+static thread_local std::string g_last_error;
+
+wc_status set_error(wc_status st, const std::string &msg) {
+    g_last_error = msg;
+    return st;
+}
+
+wc_status cuda_error(cudaError_t e, const char *what) {
+    std::string m = std::string("cuda: ") + what + ": " + cudaGetErrorString(e);
+    return set_error(e == cudaErrorMemoryAllocation ? WC_ERR_NOMEM : WC_ERR_CUDA, m);
+}
+
+static std::string fmt(const char *f, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, f);
+    vsnprintf(buf, sizeof buf, f, ap);
+    va_end(ap);
+    return buf;
+}
+
+}  // namespace wb
+
+using namespace wb;
+
+// --------------------------------------------------------- the matrix ----
+
+// Device storage shared by a matrix and its views.
+struct CqStorage {
+    uint8_t *idx = nullptr;
+    __half *nrm = nullptr;
+    size_t idx_bytes = 0, nrm_bytes = 0;
+    int device = 0;
+    ~CqStorage() {
+        int cur = 0;
+        cudaGetDevice(&cur);
+        if (cur != device) cudaSetDevice(device);
+        if (idx) cudaFree(idx);
+        if (nrm) cudaFree(nrm);
+        if (cur != device) cudaSetDevice(cur);
+    }
+};
+
+struct wc_cq {
+    std::shared_ptr<CqStorage> st;
+    CqShape shape;
+    int out = 0, row0 = 0, ld = 0;
+    bool exact = false;
+
+    CqView view() const { return CqView{st->idx, st->nrm, out, row0, ld}; }
+    bool lut() const { return !exact && shape.gb <= kLutMaxGroupBytes; }
+};
+
+static const char *kVersion = "whistle_b200 0.1";
+
+extern "C" size_t wc_last_error(char *buf, size_t len) {
+    const std::string &m = g_last_error;
+    if (buf && len > 0) {
+        size_t n = m.size() < len - 1 ? m.size() : len - 1;
+        memcpy(buf, m.data(), n);
+        buf[n] = 0;
+    }
+    return m.size();
+}
+
+extern "C" const char *wc_version(void) { return kVersion; }
+
+static wc_status check_device(const wc_cq *h) {
+    int cur = 0;
+    WB_CUDA(cudaGetDevice(&cur));
+    if (cur != h->st->device)
+        return set_error(WC_ERR_DEVICE, fmt("cq: matrix lives on device %d, device %d is current", h->st->device, cur));
+    return WC_OK;
+}
+
+// Shared memory the kernels need for this shape, against the device limit.
+static wc_status check_smem(const CqShape &s, bool lut) {
+    int dev = 0, limit = 0;
+    WB_CUDA(cudaGetDevice(&dev));
+    WB_CUDA(cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    size_t need = lut ? lut_smem_bytes(s) : exact_smem_bytes(s);
+    if (need > (size_t)limit)
+        return set_error(WC_ERR_UNSUPPORTED,
+                         fmt("cq: [*, %d] %d-bit group %d needs %zu bytes of shared memory, the device has %d", s.in,
+                             s.bits, s.group, need, limit));
+    return WC_OK;
+}
+
+extern "C" wc_status wc_cq_create(const uint8_t *index, size_t index_len, const uint8_t *norms, size_t norms_len,
+                                  const float *codebook, size_t codebook_len, int out, int in, int group, int bits,
+                                  int width, wc_cq **h) {
+    if (!h) return set_error(WC_ERR_INVALID, "cq: nil handle pointer");
+    *h = nullptr;
+    // internal/cq/matrix.go:61-73, in that order.
+    if ((bits != 2 && bits != 4) || width != bits)
+        return set_error(WC_ERR_UNSUPPORTED,
+                         fmt("cq: %d-bit CQ (index width %d) not supported, only 2 and 4", bits, width));
+    if (group < 8 || (group & (group - 1)) != 0)
+        return set_error(WC_ERR_UNSUPPORTED, fmt("cq: group %d is not a power of two >= 8", group));
+    if (out < 0 || in <= 0) return set_error(WC_ERR_UNSUPPORTED, fmt("cq: bad shape [%d, %d]", out, in));
+    if (codebook_len != ((size_t)1 << bits))
+        return set_error(WC_ERR_UNSUPPORTED, fmt("cq: %zu codebook levels for %d bits", codebook_len, bits));
+    const int groups = (in + group - 1) / group;
+    const int row_bytes = groups * group * width / 8;
+    const size_t want_idx = (size_t)out * row_bytes, want_nrm = (size_t)2 * out * groups;
+    if (index_len != want_idx || norms_len != want_nrm)
+        return set_error(WC_ERR_UNSUPPORTED, fmt("cq: %zu index and %zu norm bytes for [%d, %d], want %zu and %zu",
+                                                 index_len, norms_len, out, in, want_idx, want_nrm));
+    if ((out > 0 && (!index || !norms)) || !codebook) return set_error(WC_ERR_INVALID, "cq: nil tensor data");
+
+    std::unique_ptr<wc_cq> m(new (std::nothrow) wc_cq);
+    if (!m) return set_error(WC_ERR_NOMEM, "cq: out of host memory");
+    CqShape &s = m->shape;
+    memset(&s, 0, sizeof s);
+    s.in = in;
+    s.group = group;
+    s.bits = bits;
+    s.groups = groups;
+    s.gb = group * bits / 8;
+    s.row_bytes = row_bytes;
+    s.pad = groups * group;
+    s.cb_max = 0.0f;
+    for (int c = 0; c < (1 << bits); c++) {
+        s.cb[c] = codebook[c];
+        s.cb_max = std::fmax(s.cb_max, std::fabs(codebook[c]));  // matrix.go:87-89
+    }
+    s.lut_step = (float)(1.0 / ((double)kLutQ * std::sqrt((double)group)));  // lut.go:213
+    s.inv_sqrt = (float)(1.0 / std::sqrt((double)group));                   // kernel.go:375
+    m->out = out;
+    m->ld = out;
+    m->row0 = 0;
+
+    wc_status st = check_smem(s, m->lut());
+    if (st != WC_OK) return st;
+
+    auto storage = std::make_shared<CqStorage>();
+    WB_CUDA(cudaGetDevice(&storage->device));
+    // Group-major relayout (common.cuh CqView), done once on the host.
+    const int gb = s.gb;
+    std::vector<uint8_t> idx((size_t)out * row_bytes);
+    std::vector<uint16_t> nrm((size_t)out * groups);
+    for (int r = 0; r < out; r++) {
+        for (int g = 0; g < groups; g++) {
+            memcpy(&idx[((size_t)g * out + r) * gb], index + (size_t)r * row_bytes + (size_t)g * gb, gb);
+            const uint8_t *p = norms + 2 * ((size_t)r * groups + g);
+            nrm[(size_t)g * out + r] = (uint16_t)(p[0] | (p[1] << 8));  // little-endian FP16
+        }
+    }
+    storage->idx_bytes = idx.size() > 0 ? idx.size() : 16;
+    storage->nrm_bytes = nrm.size() > 0 ? 2 * nrm.size() : 16;
+    WB_CUDA(cudaMalloc(&storage->idx, storage->idx_bytes));
+    WB_CUDA(cudaMalloc(&storage->nrm, storage->nrm_bytes));
+    if (!idx.empty()) WB_CUDA(cudaMemcpy(storage->idx, idx.data(), idx.size(), cudaMemcpyHostToDevice));
+    if (!nrm.empty()) WB_CUDA(cudaMemcpy(storage->nrm, nrm.data(), 2 * nrm.size(), cudaMemcpyHostToDevice));
+    m->st = std::move(storage);
+    *h = m.release();
+    return WC_OK;
+}
+
+extern "C" wc_status wc_cq_rows(const wc_cq *h, int lo, int hi, wc_cq **view) {
+    if (!h || !view) return set_error(WC_ERR_INVALID, "cq: nil matrix");
+    *view = nullptr;
+    if (lo < 0 || hi < lo || hi > h->out)  // matrix.go:134
+        return set_error(WC_ERR_INVALID, fmt("cq: Rows(%d, %d) of %d rows", lo, hi, h->out));
+    wc_cq *v = new (std::nothrow) wc_cq(*h);
+    if (!v) return set_error(WC_ERR_NOMEM, "cq: out of host memory");
+    v->out = hi - lo;
+    v->row0 = h->row0 + lo;
+    *view = v;
+    return WC_OK;
+}
+
+extern "C" wc_status wc_cq_exact(const wc_cq *h, wc_cq **view) {
+    if (!h || !view) return set_error(WC_ERR_INVALID, "cq: nil matrix");
+    *view = nullptr;
+    wc_status st = check_smem(h->shape, false);
+    if (st != WC_OK) return st;
+    wc_cq *v = new (std::nothrow) wc_cq(*h);
+    if (!v) return set_error(WC_ERR_NOMEM, "cq: out of host memory");
+    v->exact = true;
+    *view = v;
+    return WC_OK;
+}
+
+extern "C" void wc_cq_destroy(wc_cq *h) { delete h; }
+extern "C" int wc_cq_out(const wc_cq *h) { return h ? h->out : 0; }
+extern "C" int wc_cq_in(const wc_cq *h) { return h ? h->shape.in : 0; }
+extern "C" int wc_cq_bits(const wc_cq *h) { return h ? h->shape.bits : 0; }
+extern "C" size_t wc_cq_bytes(const wc_cq *h) {
+    if (!h) return 0;
+    return (size_t)h->out * h->shape.row_bytes + (size_t)2 * h->out * h->shape.groups + 4u * (1u << h->shape.bits);
+}
+
+// lut.go:206 sharesTables.
+static bool shares_tables(const wc_cq *a, const wc_cq *b) {
+    if (a->shape.in != b->shape.in || a->shape.group != b->shape.group || a->shape.bits != b->shape.bits ||
+        a->shape.cb_max != b->shape.cb_max)
+        return false;
+    for (int c = 0; c < (1 << a->shape.bits); c++)
+        if (a->shape.cb[c] != b->shape.cb[c]) return false;
+    return true;
+}
+
+// One lut launch sequence for matrices that share their tables.
+static wc_status run_lut(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows,
+                         cudaStream_t st) {
+    for (int base = 0; base < n; base += kMaxLaunchMats) {
+        int cnt = n - base < kMaxLaunchMats ? n - base : kMaxLaunchMats;
+        auto p = std::make_unique<LutParams>();
+        p->shape = ms[base]->shape;
+        p->x = x;
+        int tiles = 0, used = 0;
+        for (int k = 0; k < cnt; k++) {
+            const wc_cq *m = ms[base + k];
+            if (m->out == 0) continue;
+            p->views[used] = m->view();
+            p->y[used] = ys[base + k];
+            p->tile_start[used] = tiles;
+            tiles += (m->out + kTileRows - 1) / kTileRows;
+            used++;
+        }
+        p->tile_start[used] = tiles;
+        p->n = used;
+        if (used == 0) continue;
+        for (int a0 = 0; a0 < rows; a0 += 65535) {
+            int acts = rows - a0 < 65535 ? rows - a0 : 65535;
+            p->act0 = a0;
+            cudaError_t e = launch_lut(*p, tiles, acts, st);
+            if (e != cudaSuccess) return cuda_error(e, "cq lut kernel");
+        }
+    }
+    return WC_OK;
+}
+
+extern "C" wc_status wc_cq_gemm(const wc_cq *h, const float *x, float *y, int rows, wc_stream stream) {
+    if (!h) return set_error(WC_ERR_INVALID, "cq: nil matrix");
+    if (rows < 0) return set_error(WC_ERR_INVALID, fmt("cq: GEMM of %d rows on [%d, %d]", rows, h->out, h->shape.in));
+    if (rows == 0 || h->out == 0) return WC_OK;  // kernel.go:110
+    wc_status st = check_device(h);
+    if (st != WC_OK) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (h->lut()) return run_lut(&h, 1, x, &y, rows, s);
+    cudaError_t e = launch_exact(h->shape, h->view(), x, y, rows, s);
+    return e == cudaSuccess ? WC_OK : cuda_error(e, "cq exact kernel");
+}
+
+extern "C" wc_status wc_cq_gemms(const wc_cq *const *hs, int n, const float *x, float *const *ys, int rows,
+                                 wc_stream stream) {
+    if (n < 0 || (n > 0 && (!hs || !ys))) return set_error(WC_ERR_INVALID, "cq: GEMMs of a nil list");
+    if (rows < 0) return set_error(WC_ERR_INVALID, fmt("cq: GEMMs of %d rows", rows));
+    for (int k = 0; k < n; k++) {
+        if (!hs[k]) return set_error(WC_ERR_INVALID, "cq: nil matrix");
+        if (hs[k]->shape.in != hs[0]->shape.in)
+            return set_error(WC_ERR_INVALID, fmt("cq: GEMMs mixes inputs of %d and %d", hs[0]->shape.in, hs[k]->shape.in));
+    }
+    if (rows == 0) return WC_OK;
+    cudaStream_t s = (cudaStream_t)stream;
+    // Matrices sharing the first lut matrix's tables go in one launch
+    // (kernel.go:328-346); each other one runs its own GEMM. Either way each
+    // output is the same bits as its own GEMM.
+    const wc_cq *first = nullptr;
+    std::vector<const wc_cq *> shared;
+    std::vector<float *> sys;
+    for (int k = 0; k < n; k++) {
+        const wc_cq *m = hs[k];
+        wc_status st = check_device(m);
+        if (st != WC_OK) return st;
+        if (m->out == 0) continue;
+        if (m->lut() && (!first || shares_tables(first, m))) {
+            if (!first) first = m;
+            shared.push_back(m);
+            sys.push_back(ys[k]);
+            continue;
+        }
+        st = wc_cq_gemm(m, x, ys[k], rows, stream);
+        if (st != WC_OK) return st;
+    }
+    if (!shared.empty()) return run_lut(shared.data(), (int)shared.size(), x, sys.data(), rows, s);
+    return WC_OK;
+}
+
+// Device buffers for the host-slice entry points: grown on demand, one set
+// per calling thread, freed at thread exit.
+namespace {
+struct HostScratch {
+    void *p[4] = {nullptr, nullptr, nullptr, nullptr};
+    size_t n[4] = {0, 0, 0, 0};
+    int device[4] = {-1, -1, -1, -1};
+    ~HostScratch() {
+        for (int i = 0; i < 4; i++)
+            if (p[i]) cudaFree(p[i]);
+    }
+    cudaError_t get(int i, size_t bytes, void **out) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (n[i] < bytes || device[i] != dev) {
+            if (p[i]) cudaFree(p[i]);
+            p[i] = nullptr;
+            n[i] = 0;
+            e = cudaMalloc(&p[i], bytes < 256 ? 256 : bytes);
+            if (e != cudaSuccess) return e;
+            n[i] = bytes;
+            device[i] = dev;
+        }
+        *out = p[i];
+        return cudaSuccess;
+    }
+};
+thread_local HostScratch t_scratch;
+}  // namespace
+
+extern "C" wc_status wc_cq_gemm_host(const wc_cq *h, const float *x, size_t x_len, float *y, size_t y_len, int rows) {
+    if (!h) return set_error(WC_ERR_INVALID, "cq: nil matrix");
+    const int out = h->out, in = h->shape.in;
+    if (rows < 0 || x_len != (size_t)rows * in || y_len != (size_t)rows * out)  // kernel.go:105-107
+        return set_error(WC_ERR_INVALID, fmt("cq: GEMM(len %zu, len %zu, %d rows) on [%d, %d]", y_len, x_len, rows, out, in));
+    if (rows == 0 || out == 0) return WC_OK;
+    void *dx = nullptr, *dy = nullptr;
+    WB_CUDA(t_scratch.get(0, x_len * sizeof(float), &dx));
+    WB_CUDA(t_scratch.get(1, y_len * sizeof(float), &dy));
+    WB_CUDA(cudaMemcpy(dx, x, x_len * sizeof(float), cudaMemcpyHostToDevice));
+    wc_status st = wc_cq_gemm(h, (const float *)dx, (float *)dy, rows, nullptr);
+    if (st != WC_OK) return st;
+    WB_CUDA(cudaMemcpy(y, dy, y_len * sizeof(float), cudaMemcpyDeviceToHost));
+    return WC_OK;
+}
+
+extern "C" wc_status wc_cq_gemms_host(const wc_cq *const *hs, int n, const float *x, size_t x_len, float *const *ys,
+                                      const size_t *y_lens, int rows) {
+    if (n < 0 || (n > 0 && (!hs || !ys || !y_lens))) return set_error(WC_ERR_INVALID, "cq: GEMMs of a nil list");
+    for (int k = 0; k < n; k++) {  // kernel.go:330-333
+        if (!hs[k]) return set_error(WC_ERR_INVALID, "cq: nil matrix");
+        int out = hs[k]->out, in = hs[k]->shape.in;
+        if (rows < 0 || x_len != (size_t)rows * in || y_lens[k] != (size_t)rows * out)
+            return set_error(WC_ERR_INVALID,
+                             fmt("cq: GEMMs(len %zu, len %zu, %d rows) on [%d, %d]", y_lens[k], x_len, rows, out, in));
+    }
+    if (rows == 0 || n == 0) return WC_OK;
+    size_t total = 0;
+    for (int k = 0; k < n; k++) total += y_lens[k];
+    void *dx = nullptr, *dy = nullptr;
+    WB_CUDA(t_scratch.get(0, x_len * sizeof(float), &dx));
+    WB_CUDA(t_scratch.get(1, (total ? total : 1) * sizeof(float), &dy));
+    WB_CUDA(cudaMemcpy(dx, x, x_len * sizeof(float), cudaMemcpyHostToDevice));
+    std::vector<float *> dys(n);
+    size_t off = 0;
+    for (int k = 0; k < n; k++) {
+        dys[k] = (float *)dy + off;
+        off += y_lens[k];
+    }
+    wc_status st = wc_cq_gemms(hs, n, (const float *)dx, dys.data(), rows, nullptr);
+    if (st != WC_OK) return st;
+    for (int k = 0; k < n; k++)
+        if (y_lens[k]) WB_CUDA(cudaMemcpy(ys[k], dys[k], y_lens[k] * sizeof(float), cudaMemcpyDeviceToHost));
+    return WC_OK;
+}
+
+extern "C" wc_status wc_cq_row(const wc_cq *h, int r, float *dst, wc_stream stream) {
+    if (!h) return set_error(WC_ERR_INVALID, "cq: nil matrix");
+    if (r < 0 || r >= h->out)
+        return set_error(WC_ERR_INVALID, fmt("cq: Row(len %d, %d) of [%d, %d]", h->shape.in, r, h->out, h->shape.in));
+    wc_status st = check_device(h);
+    if (st != WC_OK) return st;
+    cudaError_t e = launch_row(h->shape, h->view(), nullptr, r, 1, dst, nullptr, (cudaStream_t)stream);
+    return e == cudaSuccess ? WC_OK : cuda_error(e, "cq row kernel");
+}
+
+extern "C" wc_status wc_cq_row_gather(const wc_cq *h, const int32_t *rows, int n, float *dst, int32_t *bad,
+                                      wc_stream stream) {
+    if (!h) return set_error(WC_ERR_INVALID, "cq: nil matrix");
+    if (n < 0 || (n > 0 && (!rows || !dst))) return set_error(WC_ERR_INVALID, "cq: Row gather of a nil list");
+    if (n == 0) return WC_OK;
+    wc_status st = check_device(h);
+    if (st != WC_OK) return st;
+    cudaError_t e = launch_row(h->shape, h->view(), rows, 0, n, dst, bad, (cudaStream_t)stream);
+    return e == cudaSuccess ? WC_OK : cuda_error(e, "cq row kernel");
+}
+
+extern "C" wc_status wc_cq_row_host(const wc_cq *h, int r, float *dst, size_t dst_len) {
+    if (!h) return set_error(WC_ERR_INVALID, "cq: nil matrix");
+    if (r < 0 || r >= h->out || dst_len != (size_t)h->shape.in)  // matrix.go:162-164
+        return set_error(WC_ERR_INVALID, fmt("cq: Row(len %zu, %d) of [%d, %d]", dst_len, r, h->out, h->shape.in));
+    void *d = nullptr;
+    WB_CUDA(t_scratch.get(1, dst_len * sizeof(float), &d));
+    wc_status st = wc_cq_row(h, r, (float *)d, nullptr);
+    if (st != WC_OK) return st;
+    WB_CUDA(cudaMemcpy(dst, d, dst_len * sizeof(float), cudaMemcpyDeviceToHost));
+    return WC_OK;
+}
+
+// ------------------------------------------------------------- needle ----
+
+extern "C" wc_status wc_quantize_rows(const float *x, int rows, int cols, int width, int8_t *q, float *s,
+                                      wc_stream stream) {
+    if (width <= 0 || cols <= 0 || cols % width != 0)  // int8.go:108
+        return set_error(WC_ERR_INVALID, fmt("needle: int8 rows of %d in chunks of %d", cols, width));
+    if (rows < 0) return set_error(WC_ERR_INVALID, fmt("needle: %d rows", rows));
+    long chunks = (long)rows * (cols / width);
+    if (chunks == 0) return WC_OK;
+    cudaError_t e = launch_quantize_rows(x, (int)chunks, width, q, s, (cudaStream_t)stream);
+    return e == cudaSuccess ? WC_OK : cuda_error(e, "quantize kernel");
+}
+
+extern "C" wc_status wc_quantize_rows_host(const float *x, size_t x_len, int cols, int width, int8_t *q, float *s) {
+    if (width <= 0 || cols <= 0 || cols % width != 0)
+        return set_error(WC_ERR_INVALID, fmt("needle: int8 rows of %d in chunks of %d", cols, width));
+    if (x_len % (size_t)cols != 0)  // int8.go:126-128
+        return set_error(WC_ERR_INVALID, fmt("needle: %zu values are not rows of %d", x_len, cols));
+    if (x_len == 0) return WC_OK;
+    void *dx = nullptr, *dq = nullptr, *ds = nullptr;
+    size_t chunks = x_len / width;
+    WB_CUDA(t_scratch.get(0, x_len * sizeof(float), &dx));
+    WB_CUDA(t_scratch.get(1, x_len, &dq));
+    WB_CUDA(t_scratch.get(2, chunks * sizeof(float), &ds));
+    WB_CUDA(cudaMemcpy(dx, x, x_len * sizeof(float), cudaMemcpyHostToDevice));
+    wc_status st = wc_quantize_rows((const float *)dx, (int)(x_len / cols), cols, width, (int8_t *)dq, (float *)ds, nullptr);
+    if (st != WC_OK) return st;
+    WB_CUDA(cudaMemcpy(q, dq, x_len, cudaMemcpyDeviceToHost));
+    WB_CUDA(cudaMemcpy(s, ds, chunks * sizeof(float), cudaMemcpyDeviceToHost));
+    return WC_OK;
+}
+
+static wc_status check_attend(int heads, int kv_heads, int qk, int vd, int nkeys) {
+    if (heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0)
+        return set_error(WC_ERR_INVALID, fmt("needle: %d query heads over %d KV heads", heads, kv_heads));
+    if (qk <= 0 || vd <= 0) return set_error(WC_ERR_INVALID, fmt("needle: head widths %d and %d", qk, vd));
+    if (nkeys < 0) return set_error(WC_ERR_INVALID, fmt("needle: %d keys", nkeys));
+    return WC_OK;
+}
+
+static wc_status attend_smem_ok(const AttendParams &p) {
+    int dev = 0, limit = 0;
+    WB_CUDA(cudaGetDevice(&dev));
+    WB_CUDA(cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    if (attend_smem_bytes(p) > (size_t)limit)
+        return set_error(WC_ERR_UNSUPPORTED, fmt("needle: %d keys per query row exceed shared memory", p.max_keys));
+    return WC_OK;
+}
+
+static bool aligned4(const void *p) { return ((uintptr_t)p & 3u) == 0; }
+
+extern "C" wc_status wc_attend_int8(const float *q, int t, int heads, const int8_t *k8, const float *ks,
+                                    const int8_t *v8, const float *vs, int nkeys, int kv_heads, int qk, int vd,
+                                    const int32_t *spans, float scale, int quant_q, float *probs, float *out,
+                                    wc_stream stream) {
+    wc_status st = check_attend(heads, kv_heads, qk, vd, nkeys);
+    if (st != WC_OK) return st;
+    if (t < 0) return set_error(WC_ERR_INVALID, fmt("needle: %d query rows", t));
+    if (t == 0) return WC_OK;
+    if (t > 65535) return set_error(WC_ERR_UNSUPPORTED, fmt("needle: %d query rows in one call", t));
+    AttendParams p{};
+    p.q = q;
+    p.k8 = k8;
+    p.ks = ks;
+    p.v8 = v8;
+    p.vs = vs;
+    p.spans = spans;
+    p.nkeys_dev = nullptr;
+    p.probs = probs;
+    p.out = out;
+    p.t = t;
+    p.heads = heads;
+    p.kv_heads = kv_heads;
+    p.qk = qk;
+    p.vd = vd;
+    p.nkeys = nkeys;
+    p.cap = nkeys;
+    p.max_keys = nkeys;
+    p.scale = scale;
+    p.quant_q = quant_q ? 1 : 0;
+    p.k_aligned4 = (qk % 4 == 0) && ((kv_heads * qk) % 4 == 0) && aligned4(k8);
+    st = attend_smem_ok(p);
+    if (st != WC_OK) return st;
+    cudaError_t e = launch_attend(p, 1, (cudaStream_t)stream);
+    return e == cudaSuccess ? WC_OK : cuda_error(e, "attend kernel");
+}
+
+extern "C" wc_status wc_attend_int8_streams(int streams, const float *q, int heads, const int8_t *k8, const float *ks,
+                                            const int8_t *v8, const float *vs, int cap, const int32_t *nkeys,
+                                            int kv_heads, int qk, int vd, float scale, int quant_q, float *out,
+                                            wc_stream stream) {
+    wc_status st = check_attend(heads, kv_heads, qk, vd, cap);
+    if (st != WC_OK) return st;
+    if (streams < 0) return set_error(WC_ERR_INVALID, fmt("needle: %d streams", streams));
+    if (streams == 0) return WC_OK;
+    if (streams > 65535) return set_error(WC_ERR_UNSUPPORTED, fmt("needle: %d streams in one call", streams));
+    AttendParams p{};
+    p.q = q;
+    p.k8 = k8;
+    p.ks = ks;
+    p.v8 = v8;
+    p.vs = vs;
+    p.spans = nullptr;
+    p.nkeys_dev = nkeys;
+    p.probs = nullptr;
+    p.out = out;
+    p.t = 1;
+    p.heads = heads;
+    p.kv_heads = kv_heads;
+    p.qk = qk;
+    p.vd = vd;
+    p.nkeys = cap;
+    p.cap = cap;
+    p.max_keys = cap;
+    p.scale = scale;
+    p.quant_q = quant_q ? 1 : 0;
+    p.k_aligned4 = (qk % 4 == 0) && ((kv_heads * qk) % 4 == 0) && aligned4(k8);
+    st = attend_smem_ok(p);
+    if (st != WC_OK) return st;
+    cudaError_t e = launch_attend(p, streams, (cudaStream_t)stream);
+    return e == cudaSuccess ? WC_OK : cuda_error(e, "attend kernel");
+}

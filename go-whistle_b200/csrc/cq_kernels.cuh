@@ -1,0 +1,37 @@
+// cq_kernels.cuh — launch interfaces of the CQ kernels (cq_lut.cu,
+// cq_exact.cu) used by the C-ABI layer (api.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace wb {
+
+// Rows per CTA tile of the lut kernel.
+constexpr int kTileRows = 64;
+// Matrices per GEMMs launch (their views and outputs travel as kernel
+// parameters).
+constexpr int kMaxLaunchMats = 128;
+
+struct LutParams {
+    CqShape shape;
+    const float *x;  // [rows][in] activations
+    int act0;        // first activation of this launch (grid.y is relative)
+    int n;           // matrices in this launch
+    CqView views[kMaxLaunchMats];
+    float *y[kMaxLaunchMats];               // [rows][views[k].out] each
+    int tile_start[kMaxLaunchMats + 1];     // prefix sum of row tiles
+};
+
+size_t lut_smem_bytes(const CqShape &s);
+cudaError_t launch_lut(const LutParams &p, int tiles, int acts, cudaStream_t st);
+
+// The Exact path (kernel.go:162-373): one matrix, float32 nibble tables.
+size_t exact_smem_bytes(const CqShape &s);
+cudaError_t launch_exact(const CqShape &s, const CqView &v, const float *x, float *y, int rows, cudaStream_t st);
+
+// matrix.go:161 Row for n rows (rows: device array, or NULL with n = 1 and
+// row r0).
+cudaError_t launch_row(const CqShape &s, const CqView &v, const int32_t *rows, int r0, int n, float *dst,
+                       int32_t *bad, cudaStream_t st);
+
+}  // namespace wb

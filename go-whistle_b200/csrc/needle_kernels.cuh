@@ -1,0 +1,32 @@
+// needle_kernels.cuh — launch interfaces of the int8 kernels (int8_attend.cu)
+// used by the C-ABI layer (api.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace wb {
+
+struct AttendParams {
+    const float *q;    // [streams][t][heads][qk]
+    const int8_t *k8;  // stream b at b*cap rows: [cap][kv_heads*qk]
+    const float *ks;   // [cap][kv_heads]
+    const int8_t *v8;  // [cap][kv_heads*vd]
+    const float *vs;   // [cap][kv_heads]
+    const int32_t *spans;     // [t][4] or NULL (all keys)
+    const int32_t *nkeys_dev; // [streams] or NULL (nkeys for every stream)
+    float *probs;             // [streams][t][heads][nkeys] or NULL
+    float *out;               // [streams][t][heads][vd]
+    int t, heads, kv_heads, qk, vd;
+    int nkeys;     // keys of the single-stream call (probs row length)
+    int cap;       // rows between consecutive streams' caches
+    int max_keys;  // upper bound of keys any query row sees (shared memory)
+    float scale;
+    int quant_q;
+    int k_aligned4;  // k8 rows and q8 readable as int32 words
+};
+
+cudaError_t launch_quantize_rows(const float *x, int chunks, int width, int8_t *q, float *s, cudaStream_t st);
+size_t attend_smem_bytes(const AttendParams &p);
+cudaError_t launch_attend(const AttendParams &p, int streams, cudaStream_t st);
+
+}  // namespace wb

@@ -1,0 +1,183 @@
+/*
+ * whistle_b200.h — the C ABI of libwhistle_b200.so, the B200 (sm_100a) build of
+ * go-whistle's quantized hot path: the packed 2/4-bit CQ LUT GEMV/GEMM of
+ * internal/cq and the int8 KV-cache attention of internal/needle.
+ *
+ * Plain C: pointers, sizes and status codes; no CUDA, Go or torch types. A
+ * cgo shim binds these one for one. Each entry point names
+ * the reference routine it stands in for (file:line in the go-whistle
+ * module).
+ *
+ * Conventions
+ *  - Every call returns a wc_status. WC_OK is 0. On failure the message of
+ *    the calling thread's last error (wc_last_error) carries the text the
+ *    reference would have put in its error or panic, e.g. "cq: group 24 is
+ *    not a power of two >= 8".
+ *  - "device" pointers are CUDA global memory of the current device; "host"
+ *    pointers are ordinary process memory. The *_host entry points copy in
+ *    and out, synchronise, and so behave like the reference's Go calls.
+ *  - wc_stream is a cudaStream_t (NULL: the legacy default stream). Device
+ *    entry points only enqueue work; the caller orders and synchronises.
+ *  - A wc_cq handle belongs to the device that was current at its creation;
+ *    calls on it with another device current fail with WC_ERR_DEVICE.
+ *  - Handles are safe for concurrent use from several threads (each thread
+ *    on its own stream), as cq.Matrix is (internal/cq/matrix.go:22-24).
+ *  - Nothing in this library aborts the process, traps, or falls back to a
+ *    CPU path: a missing or unusable GPU is an error status.
+ */
+#ifndef WHISTLE_B200_H
+#define WHISTLE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum wc_status {
+    WC_OK = 0,
+    WC_ERR_INVALID = 1,     /* misuse the reference panics on: shapes, lengths, ranges */
+    WC_ERR_UNSUPPORTED = 2, /* a tensor the reference's constructor rejects with an error */
+    WC_ERR_CUDA = 3,        /* a CUDA runtime error (message has cudaGetErrorString) */
+    WC_ERR_NOMEM = 4,       /* device or host allocation failed */
+    WC_ERR_DEVICE = 5,      /* handle used with another device current */
+} wc_status;
+
+typedef struct wc_cq wc_cq; /* a device-resident CQ matrix, or a view of one */
+typedef void *wc_stream;    /* cudaStream_t */
+
+/* The calling thread's last error message (NUL-terminated, truncated to
+ * len). Returns the full message length. No reference counterpart: Go
+ * returns the error value itself. */
+size_t wc_last_error(char *buf, size_t len);
+
+/* Library version string ("whistle_b200 <major>.<minor>"). */
+const char *wc_version(void);
+
+/* ---------------------------------------------------------------- cq ---- */
+
+/*
+ * Creates a device copy of a packed CQ tensor and prepares it for products.
+ * Replaces internal/cq/matrix.go:46 New (and :60 NewGather, :111 Prepare):
+ * the same validation in the same order with the same messages
+ * (matrix.go:61-73). The fields are cact.Packed's
+ * (internal/cact/packed.go:18-29): index = out rows of RowBytes() bytes of
+ * LSB-first indices (index_len bytes), norms = out*groups little-endian FP16
+ * values (norms_len BYTES, as Packed.Norms), codebook = codebook_len float32
+ * levels, bits = Record.Bits, width = bits per stored index. Host pointers;
+ * nothing is retained after the call.
+ */
+wc_status wc_cq_create(const uint8_t *index, size_t index_len, const uint8_t *norms, size_t norms_len,
+                       const float *codebook, size_t codebook_len, int out, int in, int group, int bits, int width,
+                       wc_cq **h);
+
+/* Rows [lo, hi) as a view sharing h's device storage: matrix.go:133 Rows.
+ * The view keeps the storage alive after wc_cq_destroy(h). */
+wc_status wc_cq_rows(const wc_cq *h, int lo, int hi, wc_cq **view);
+
+/* A view whose products run the reference's Exact (nibble/nibble4, float32
+ * sums) kernels instead of the lut kernel: matrix.go:152 Exact. */
+wc_status wc_cq_exact(const wc_cq *h, wc_cq **view);
+
+/* Releases a matrix or view (device storage goes with the last of them). */
+void wc_cq_destroy(wc_cq *h);
+
+/* matrix.go:99 Out, :102 In, :105 Bits. */
+int wc_cq_out(const wc_cq *h);
+int wc_cq_in(const wc_cq *h);
+int wc_cq_bits(const wc_cq *h);
+
+/* Device bytes the matrix holds: packed index, FP16 norms and codebook
+ * (matrix.go:121 Bytes counts the reference's host copies instead). */
+size_t wc_cq_bytes(const wc_cq *h);
+
+/*
+ * y = x · Wᵀ for `rows` activations: x [rows][In], y [rows][Out], both
+ * row-major fp32 DEVICE memory. internal/cq/kernel.go:85 GEMM (and :78 GEMV
+ * for rows = 1). The lut kernel's result is bit-identical to the
+ * reference's lut kernel; an Exact view's to its nibble4/nibble kernels.
+ * rows = 0 or Out = 0 is a no-op (kernel.go:110).
+ */
+wc_status wc_cq_gemm(const wc_cq *h, const float *x, float *y, int rows, wc_stream stream);
+
+/* GEMM on HOST slices with the reference's length check and panic text
+ * (kernel.go:105-107): x_len = len(x), y_len = len(dst). Synchronous. */
+wc_status wc_cq_gemm_host(const wc_cq *h, const float *x, size_t x_len, float *y, size_t y_len, int rows);
+
+/*
+ * internal/cq/kernel.go:134 GEMMs: ys[k] = x · hs[k]ᵀ for n matrices that
+ * read the same x [rows][In] (DEVICE). Matrices that share the input width,
+ * group, index width and codebook (lut.go:206 sharesTables) run as ONE
+ * launch that rotates and tabulates each activation once for all of them;
+ * the others run one GEMM each. Every ys[k] equals wc_cq_gemm's bit for
+ * bit. hs and ys are host arrays of n device pointers.
+ */
+wc_status wc_cq_gemms(const wc_cq *const *hs, int n, const float *x, float *const *ys, int rows, wc_stream stream);
+
+/* GEMMs on HOST slices: y_lens[k] = len(dsts[k]). Synchronous. */
+wc_status wc_cq_gemms_host(const wc_cq *const *hs, int n, const float *x, size_t x_len, float *const *ys,
+                           const size_t *y_lens, int rows);
+
+/* internal/cq/matrix.go:161 Row: row r dequantised exactly as cact.CQ does
+ * (bit for bit) into dst [In] (DEVICE). */
+wc_status wc_cq_row(const wc_cq *h, int r, float *dst, wc_stream stream);
+
+/* Row for n rows at once (an embedding gather for n streams): rows is a
+ * DEVICE array of n row numbers, dst is [n][In] DEVICE. Rows out of range
+ * produce zeros and set *bad (DEVICE int, may be NULL) to 1. */
+wc_status wc_cq_row_gather(const wc_cq *h, const int32_t *rows, int n, float *dst, int32_t *bad,
+                           wc_stream stream);
+
+/* Row on a HOST dst of dst_len floats, with matrix.go:162's panic text. */
+wc_status wc_cq_row_host(const wc_cq *h, int r, float *dst, size_t dst_len);
+
+/* ------------------------------------------------------------ needle ---- */
+
+/*
+ * internal/needle/int8.go:115 QuantizeRows (and :125 Int8Rows.Append when q
+ * and s point at a cache's tail): x [rows][cols] fp32 in chunks of width,
+ * q [rows][cols] int8, s [rows*cols/width] fp32; all DEVICE. Each chunk is
+ * int8.go:36 QuantizeRow bit for bit.
+ */
+wc_status wc_quantize_rows(const float *x, int rows, int cols, int width, int8_t *q, float *s, wc_stream stream);
+
+/* QuantizeRows on HOST memory (x_len values), with int8.go:108's checks. */
+wc_status wc_quantize_rows_host(const float *x, size_t x_len, int cols, int width, int8_t *q, float *s);
+
+/*
+ * internal/needle/int8.go:208 AttendInt8Spans (int8.go:194 AttendInt8 is the
+ * span pair {0,0},{0,keys(i)}). DEVICE memory:
+ *   q      [t][heads][qk] fp32
+ *   k8, ks the keys: [nkeys][kv_heads*qk] int8 and [nkeys][kv_heads] fp32
+ *   v8, vs the values: [nkeys][kv_heads*vd] int8 and [nkeys][kv_heads] fp32
+ *   spans  [t][4] int32: lo0, hi0, lo1, hi1, two ascending disjoint key
+ *          ranges per query row
+ *   probs  [t][heads][nkeys] fp32 or NULL; written at span keys only
+ *   out    [t][heads][vd] fp32
+ * Query head h reads KV head h / (heads / kv_heads). quant_q != 0 quantises
+ * each query head to int8 first (Int8.Act), making the logits exact int32
+ * dot products. The result equals the reference's generic (purego) path bit
+ * for bit up to the last-bit rounding of exp noted in DESIGN.md.
+ */
+wc_status wc_attend_int8(const float *q, int t, int heads, const int8_t *k8, const float *ks, const int8_t *v8,
+                         const float *vs, int nkeys, int kv_heads, int qk, int vd, const int32_t *spans, float scale,
+                         int quant_q, float *probs, float *out, wc_stream stream);
+
+/*
+ * The decode step of `streams` independent streams, one query row each,
+ * against each stream's own int8 KV cache: AttendInt8 (int8.go:194) per
+ * stream with keys(0) = nkeys[b], as Attention.extendInt8 (cache.go:120)
+ * and cross.attend (decoder/cross.go:273) call it. Stream b's cache starts
+ * at b*cap rows of k8/ks/v8/vs (layouts as in wc_attend_int8); q is
+ * [streams][heads][qk], out [streams][heads][vd], nkeys [streams] int32;
+ * all DEVICE. nkeys[b] > cap is clamped to cap.
+ */
+wc_status wc_attend_int8_streams(int streams, const float *q, int heads, const int8_t *k8, const float *ks,
+                                 const int8_t *v8, const float *vs, int cap, const int32_t *nkeys, int kv_heads,
+                                 int qk, int vd, float scale, int quant_q, float *out, wc_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

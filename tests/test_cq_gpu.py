@@ -1,0 +1,225 @@
+"""CQ products on the GPU through the C ABI, bit for bit against the oracle's
+restatement of the reference's lut and Exact kernels."""
+
+from __future__ import annotations
+
+import threading
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+# internal/cq/cq_test.go:183 testShapes, Whistle's shapes (parallel_test.go:29)
+# and the benchmark configurations' shapes: (out, in, group).
+SHAPES = [(1, 8, 8), (3, 16, 8), (4, 13, 8), (5, 40, 32), (7, 200, 128), (6, 384, 128), (9, 129, 128),
+          (33, 256, 128), (384, 512, 128), (96, 512, 128), (4133, 300, 64), (1031, 200, 32),
+          (2048, 512, 32), (512, 512, 32), (512, 2048, 32), (128, 2048, 128)]
+
+
+def bits_eq(a, b) -> bool:
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    return a.shape == b.shape and np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def make(wb, orc, seed, out, in_, group, bits, codebook="reference"):
+    rng = np.random.default_rng(seed)
+    p = wb.synth.random_packed(rng, out, in_, group, bits, codebook)
+    return rng, p, wb.cq.New(p), orc.OracleMatrix.of(p)
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=[f"{o}x{i}g{g}" for o, i, g in SHAPES])
+@pytest.mark.parametrize("bits", [2, 4])
+def test_gemm_lut_bit_exact(wb, orc, cuda, shape, bits):
+    out, in_, group = shape
+    rng, p, m, om = make(wb, orc, 100 + out + in_ + bits, out, in_, group, bits)
+    for rows in (1, 3, 6):
+        x = rng.normal(size=rows * in_).astype(np.float32)
+        want = orc.gemm_lut(om, x, rows).reshape(-1)
+        got = np.zeros(rows * out, np.float32)
+        m.GEMM(got, x, rows)
+        assert bits_eq(got, want), rows
+        xd = cuda.from_numpy(x).cuda()
+        yd = cuda.empty(rows * out, dtype=cuda.float32, device="cuda")
+        m.GEMM(yd, xd, rows)
+        assert bits_eq(yd.cpu().numpy(), want), rows
+
+
+@pytest.mark.parametrize("bits", [2, 4])
+def test_gemm_many_activations(wb, orc, cuda, bits):
+    """A prefill-sized batch (375 frames) and a batch past one grid's 65535
+    activations."""
+    rng, p, m, om = make(wb, orc, 7, 384, 512, 128, bits, "lloyd")
+    x = rng.normal(size=375 * 512).astype(np.float32)
+    got = np.zeros(375 * 384, np.float32)
+    m.GEMM(got, x, 375)
+    assert bits_eq(got, orc.gemm_lut(om, x, 375, threads=8).reshape(-1))
+    rng, p, m, om = make(wb, orc, 8, 5, 32, 32, bits)
+    rows = 70000
+    x = rng.normal(size=rows * 32).astype(np.float32)
+    got = np.zeros(rows * 5, np.float32)
+    m.GEMM(got, x, rows)
+    assert bits_eq(got, orc.gemm_lut(om, x, rows, threads=8).reshape(-1))
+
+
+@pytest.mark.parametrize("bits", [2, 4])
+def test_rows_views(wb, orc, cuda, bits):
+    """cq_test.go:335 TestRow (views part) and asm_test.go:171: views that
+    start and end inside a block equal the full product's rows."""
+    for out, in_, group in ((70, 384, 128), (45, 2048, 128), (33, 40, 8)):
+        rng, p, m, om = make(wb, orc, out, out, in_, group, bits)
+        x = rng.normal(size=3 * in_).astype(np.float32)
+        full = orc.gemm_lut(om, x, 3)
+        for lo, hi in ((0, out), (5, out - 7), (out // 3, out - out // 5), (out - 1, out)):
+            v = m.Rows(lo, hi)
+            assert v.Out() == hi - lo and v.In() == in_ and v.Bits() == bits
+            got = np.zeros(3 * (hi - lo), np.float32)
+            v.GEMM(got, x, 3)
+            assert bits_eq(got.reshape(3, -1), full[:, lo:hi]), (lo, hi)
+            vv = v.Rows(1, hi - lo) if hi - lo > 1 else v
+            got2 = np.zeros(3 * vv.Out(), np.float32)
+            vv.GEMM(got2, x, 3)
+            off = 1 if hi - lo > 1 else 0
+            assert bits_eq(got2.reshape(3, -1), full[:, lo + off:hi])
+
+
+def test_gemms_shared_and_mixed(wb, orc, cuda):
+    """parallel_test.go:101 TestGEMMsMatchesGEMM: q/k/v/gate sharing tables,
+    a matrix with another codebook, an Exact view and an empty view."""
+    rng = np.random.default_rng(382)
+    ps = [wb.synth.random_packed(rng, o, 512, 128, 2, "lloyd") for o in (384, 96, 128, 512)]
+    other = wb.synth.random_packed(rng, 64, 512, 128, 2, "reference")
+    ms = [wb.cq.New(p) for p in ps] + [wb.cq.New(other)]
+    ms.append(ms[0].Exact().Rows(3, 40))
+    ms.append(ms[1].Rows(5, 5))
+    oms = [orc.OracleMatrix.of(p) for p in ps] + [orc.OracleMatrix.of(other)]
+    for rows in (1, 3, 8):
+        x = rng.normal(size=rows * 512).astype(np.float32)
+        dsts = [np.zeros(rows * m.Out(), np.float32) for m in ms]
+        wb.cq.GEMMs(ms, dsts, x, rows)
+        for k, om in enumerate(oms):
+            assert bits_eq(dsts[k], orc.gemm_lut(om, x, rows).reshape(-1)), k
+        assert bits_eq(dsts[5].reshape(rows, -1), orc.gemm_exact(oms[0], x, rows)[:, 3:40])
+        assert dsts[6].size == 0
+        # device form: one launch for the shared set
+        xd = cuda.from_numpy(x).cuda()
+        yds = [cuda.empty(rows * m.Out(), dtype=cuda.float32, device="cuda") for m in ms]
+        wb.cq.GEMMs(ms, yds, xd, rows)
+        for k in range(len(ms)):
+            assert bits_eq(yds[k].cpu().numpy(), dsts[k]), k
+
+
+@pytest.mark.parametrize("bits", [2, 4])
+def test_exact_bit_exact(wb, orc, cuda, bits):
+    """cq_test.go:516 TestExact: an Exact view runs the nibble4/nibble float
+    kernels, the reference's purego bits."""
+    for out, in_, group in ((70, 384, 128), (5, 40, 32), (4, 13, 8), (31, 512, 32)):
+        rng, p, m, om = make(wb, orc, 19 + out, out, in_, group, bits)
+        e = m.Exact()
+        for rows in (1, 3, 4, 5, 6, 9):
+            x = rng.normal(size=rows * in_).astype(np.float32)
+            got = np.zeros(rows * out, np.float32)
+            e.GEMM(got, x, rows)
+            assert bits_eq(got, orc.gemm_exact(om, x, rows).reshape(-1)), (out, rows)
+        v = e.Rows(1, out)
+        x = rng.normal(size=5 * in_).astype(np.float32)
+        got = np.zeros(5 * (out - 1), np.float32)
+        v.GEMM(got, x, 5)
+        assert bits_eq(got.reshape(5, -1), orc.gemm_exact(om, x, 5)[:, 1:])
+
+
+@pytest.mark.parametrize("bits", [2, 4])
+def test_row_bit_exact(wb, orc, cuda, bits):
+    """matrix.go:161 Row equals cact.CQ's dequantisation bit for bit."""
+    for out, in_, group in ((7, 200, 128), (9, 129, 128), (4, 13, 8), (64, 512, 32)):
+        rng, p, m, om = make(wb, orc, 5 + out, out, in_, group, bits)
+        for r in range(out):
+            got = np.zeros(in_, np.float32)
+            m.Row(got, r)
+            assert bits_eq(got, orc.row(om, r)), r
+        v = m.Rows(1, out)
+        got = np.zeros(in_, np.float32)
+        v.Row(got, 0)
+        assert bits_eq(got, orc.row(om, 1))
+        # batched gather with an out-of-range row
+        import ctypes
+
+        rows = np.array([0, out - 1, out, 2 % out], np.int32)
+        rd = cuda.from_numpy(rows).cuda()
+        dst = cuda.full((4, in_), 7.0, dtype=cuda.float32, device="cuda")
+        bad = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+        wb._lib.check(wb._lib.lib().wc_cq_row_gather(m.handle, ctypes.c_void_p(rd.data_ptr()), 4,
+                                                     ctypes.c_void_p(dst.data_ptr()),
+                                                     ctypes.c_void_p(bad.data_ptr()), None))
+        d = dst.cpu().numpy()
+        assert bits_eq(d[0], orc.row(om, 0)) and bits_eq(d[1], orc.row(om, out - 1))
+        assert np.all(d[2] == 0) and bits_eq(d[3], orc.row(om, 2 % out)) and int(bad.item()) == 1
+
+
+def test_no_rows(wb, orc, cuda):
+    """cq_test.go:304 TestGEMMNoRows: Out 0 and empty views are no-ops."""
+    rng = np.random.default_rng(5)
+    empty = wb.cq.New(wb.synth.random_packed(rng, 0, 256, 128, 2))
+    m = wb.cq.New(wb.synth.random_packed(rng, 64, 256, 128, 4))
+    x = rng.normal(size=2 * 256).astype(np.float32)
+    for v in (empty, m.Rows(32, 32), m.Rows(5, 5)):
+        v.GEMM(np.zeros(0, np.float32), x, 2)
+        v.GEMV(np.zeros(0, np.float32), x[:256])
+        v.Exact().GEMM(np.zeros(0, np.float32), x, 2)
+    m.GEMM(np.zeros(0, np.float32), np.zeros(0, np.float32), 0)
+
+
+def test_gemm_panics(wb, cuda):
+    """cq_test.go:587 TestGEMMPanics, with the reference's panic texts."""
+    m = wb.cq.New(wb.synth.random_packed(np.random.default_rng(9), 4, 128, 128, 4))
+    cases = {
+        "short x": lambda: m.GEMV(np.zeros(4, np.float32), np.zeros(127, np.float32)),
+        "short dst": lambda: m.GEMV(np.zeros(3, np.float32), np.zeros(128, np.float32)),
+        "rows": lambda: m.GEMM(np.zeros(8, np.float32), np.zeros(128, np.float32), 2),
+        "row": lambda: m.Row(np.zeros(128, np.float32), 4),
+        "view": lambda: m.Rows(3, 5),
+    }
+    for name, f in cases.items():
+        with pytest.raises(wb.Panic):
+            f()
+    with pytest.raises(wb.Panic, match=r"^cq: GEMM\(len 4, len 127, 1 rows\) on \[4, 128\]$"):
+        m.GEMV(np.zeros(4, np.float32), np.zeros(127, np.float32))
+    with pytest.raises(wb.Panic, match=r"^cq: Rows\(3, 5\) of 4 rows$"):
+        m.Rows(3, 5)
+
+
+def test_concurrent(wb, orc, cuda):
+    """cq_test.go:393 TestGEMMConcurrent: threads on their own streams, views
+    of one matrix, every result the serial one's bits."""
+    rng, p, m, om = make(wb, orc, 15, 70, 384, 128, 4)
+    x = rng.normal(size=3 * 384).astype(np.float32)
+    views = [(0, 70), (5, 40), (33, 70), (64, 66)]
+    full = orc.gemm_lut(om, x, 3)
+    errors = []
+
+    def work(g):
+        s = cuda.cuda.Stream()
+        with cuda.cuda.stream(s):
+            xd = cuda.from_numpy(x).cuda()
+            for n in range(20):
+                lo, hi = views[(g + n) % len(views)]
+                yd = cuda.empty(3 * (hi - lo), dtype=cuda.float32, device="cuda")
+                m.Rows(lo, hi).GEMM(yd, xd, 3)
+                s.synchronize()
+                if not bits_eq(yd.cpu().numpy().reshape(3, -1), full[:, lo:hi]):
+                    errors.append((g, n))
+
+    ts = [threading.Thread(target=work, args=(g,)) for g in range(8)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    assert not errors
+
+
+def test_bytes(wb, cuda):
+    rng = np.random.default_rng(1)
+    p = wb.synth.random_packed(rng, 70, 384, 128, 2)
+    m = wb.cq.New(p)
+    assert m.Bytes() == p.Index.size + p.Norms.size + 4 * 4
