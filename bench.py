@@ -1,0 +1,421 @@
+#!/usr/bin/env python
+"""bench.py — CQ LUT GEMV HBM GB/s on B200 (BASELINE.json's metric).
+
+Workload (configs[1], the mixed 2/4-bit sweep): batch-1 GEMVs on packed CQ
+matrices, group 32, {512x512, 512 out x 2048 in, 2048x512, 16384x512} x
+{2-bit, 4-bit}, 1000 calls each. One step runs all 8 x 1000 calls. Each
+call reads its own weights: the calls cycle through distinct copies that
+total >= 4x the L2 size per shape, so the weights stream from HBM (inputs
+larger than L2; no flush needed). The 1000 calls of a shape share their
+input x and run as cq.GEMMs (internal/cq/kernel.go:134) through the C ABI,
+captured once in a CUDA graph and replayed per step.
+
+value = algorithmic bytes of all calls (SURVEY's B = Out*RowBytes +
+2*Out*Groups + 4*In + 4*Out + 4*2^bits per GEMV) / device time, summed over
+ranks (weak scaling: every rank runs the full sweep on its own GPU).
+
+`--impl reference` times the reference's algorithm on the host cores (the
+oracle's C restatement of the lut kernel with the reference's work split;
+the reference is Go and cannot be built in this image).
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+GROUP = 32
+# (out, in, bits)
+SWEEP = [(512, 512, 2), (512, 512, 4), (512, 2048, 2), (512, 2048, 4), (2048, 512, 2), (2048, 512, 4),
+         (16384, 512, 2), (16384, 512, 4)]
+METRIC = "CQ LUT GEMV HBM GB/s"
+UNIT = "GB/s"
+WORKLOAD = "configs[1]: CQ LUT GEMV sweep, batch 1, G32, {512x512, 512x2048(in), 2048x512, 16384x512} x {2,4}-bit"
+
+
+def gemv_bytes(out, in_, bits, group=GROUP):
+    groups = (in_ + group - 1) // group
+    return out * groups * group * bits // 8 + 2 * out * groups + 4 * in_ + 4 * out + 4 * (1 << bits)
+
+
+def weight_bytes(out, in_, bits, group=GROUP):
+    groups = (in_ + group - 1) // group
+    return out * groups * group * bits // 8 + 2 * out * groups
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ----------------------------------------------------------------- clocks ----
+
+class ClockSampler:
+    """nvidia-smi samples of this GPU's clocks during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 7]
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[0]))
+                smax = float(r[1])
+            except ValueError:
+                continue
+            for name, v in zip(names, r[4:8]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------- reference ----
+
+def run_reference(args, world, rank):
+    """The reference's lut path on the host cores (oracle port), same metric."""
+    if rank != 0:
+        return
+    import oracle
+
+    pkg = __import__("importlib").import_module("go-whistle_b200")
+    oracle.build()
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(1001)
+    preps = []
+    for out, in_, bits in SWEEP:
+        p = pkg.synth.random_packed(rng, out, in_, GROUP, bits)
+        om = oracle.OracleMatrix.of(p)
+        preps.append((oracle.PreparedLUT(om), om, rng.normal(size=in_).astype(np.float32),
+                      np.zeros(out, np.float32), gemv_bytes(out, in_, bits)))
+    # calls per shape so that one step is about 1.5 s of CPU work
+    reps = []
+    for prep, om, x, y, b in preps:
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < 0.05:
+            prep.gemm(x, 1, y, threads)
+            n += 1
+        per = (time.perf_counter() - t0) / n
+        reps.append(max(1, int(0.19 / per)))
+
+    def step():
+        for (prep, om, x, y, b), r in zip(preps, reps):
+            for _ in range(r):
+                prep.gemm(x, 1, y, threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    total = sum(b * r for (_, _, _, _, b), r in zip(preps, reps)) * args.steps
+    value = total / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8 index, int32 sums, f32",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "calls_per_shape_per_step": reps},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{sum(reps)} GEMV calls per step over the 8 sweep shapes, one matrix each, "
+                                   f"lut kernel restated in C (oracle/cq_oracle.c) with the reference's work split"},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(seconds_per_shape=1.2):
+    """Bounded CPU sample: the oracle's lut path (reference split), all cores."""
+    import oracle
+
+    pkg = __import__("importlib").import_module("go-whistle_b200")
+    oracle.build()
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(1002)
+    total_b, total_t, calls = 0, 0.0, 0
+    for out, in_, bits in SWEEP:
+        p = pkg.synth.random_packed(rng, out, in_, GROUP, bits)
+        prep = oracle.PreparedLUT(oracle.OracleMatrix.of(p))
+        x = rng.normal(size=in_).astype(np.float32)
+        y = np.zeros(out, np.float32)
+        prep.gemm(x, 1, y, threads)
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            prep.gemm(x, 1, y, threads)
+            n += 1
+            dt = time.perf_counter() - t0
+            if dt >= seconds_per_shape and n >= 3:
+                break
+        total_b += n * gemv_bytes(out, in_, bits)
+        total_t += dt
+        calls += n
+    return {"value": round(total_b / total_t / 1e9, 3), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{calls} GEMV calls over the 8 sweep shapes (~{seconds_per_shape}s each), one matrix per "
+                      f"shape, lut kernel restated in C with the reference's work split"}
+
+
+# ------------------------------------------------------------------ b200 ----
+
+class Shape:
+    """One sweep shape: distinct weight copies as Rows views of one matrix."""
+
+    def __init__(self, pkg, torch, out, in_, bits, calls, l2_bytes, rng):
+        self.out, self.in_, self.bits, self.calls = out, in_, bits, calls
+        wb = weight_bytes(out, in_, bits)
+        self.copies = min(calls, max(1, math.ceil(4 * l2_bytes / wb)))
+        groups = (in_ + GROUP - 1) // GROUP
+        row_bytes = groups * GROUP * bits // 8
+        rows = self.copies * out
+        base = rng.integers(0, 256, size=min(rows * row_bytes, 1 << 26), dtype=np.uint8)
+        index = np.resize(base, rows * row_bytes)
+        norms = np.resize(pkg.synth.random_norms16(rng, min(rows * groups, 1 << 22)).astype("<u2").view(np.uint8),
+                          2 * rows * groups)
+        cb = np.sort(rng.normal(0.0, 0.02, size=1 << bits)).astype(np.float32)
+        p = pkg.cq.Packed(Out=rows, In=in_, Group=GROUP, Bits=bits, Width=bits, Codebook=cb, Index=index,
+                          Norms=norms)
+        self.big = pkg.cq.New(p)
+        del index, norms, base
+        self.views = [self.big.Rows(k * out, (k + 1) * out) for k in range(self.copies)]
+        self.handles = (ctypes.c_void_p * calls)(*[self.views[c % self.copies].handle.value for c in range(calls)])
+        self.hot = (ctypes.c_void_p * calls)(*[self.views[0].handle.value] * calls)
+        self.x = torch.randn(in_, device="cuda", dtype=torch.float32)
+        self.y = torch.empty(calls, out, device="cuda", dtype=torch.float32)
+        self.ys = (ctypes.c_void_p * calls)(*[self.y.data_ptr() + 4 * out * c for c in range(calls)])
+        self.bytes = calls * gemv_bytes(out, in_, bits)
+        self.x_host = torch.empty(in_, dtype=torch.float32).pin_memory()
+        self.x_host.copy_(self.x.cpu())
+        self.y_host = torch.empty(calls, out, dtype=torch.float32).pin_memory()
+
+    def run(self, lib, stream, hot=False):
+        st = lib.wc_cq_gemms(self.hot if hot else self.handles, self.calls, ctypes.c_void_p(self.x.data_ptr()),
+                             self.ys, 1, stream)
+        if st != 0:
+            raise RuntimeError(self._err())
+
+    def _err(self):
+        pkg = __import__("importlib").import_module("go-whistle_b200")
+        return pkg._lib.last_error()
+
+
+def run_b200(args, world, rank, local):
+    import torch
+
+    pkg = __import__("importlib").import_module("go-whistle_b200")
+    lib = pkg._lib.lib()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    props = torch.cuda.get_device_properties(dev)
+    l2 = getattr(props, "L2_cache_size", 126 * 1024 * 1024) or 126 * 1024 * 1024
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        pg = dist
+
+    rng = np.random.default_rng(1000 + rank)
+    sweep = SWEEP
+    if args.only:
+        o, i, b = (int(v) for v in args.only.split("x"))
+        sweep = [(o, i, b)]
+    shapes = [Shape(pkg, torch, o, i, b, args.calls, l2, rng) for o, i, b in sweep]
+    stream = torch.cuda.Stream()
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    bytes_per_step = sum(s.bytes for s in shapes)
+
+    def step():
+        for s in shapes:
+            s.run(lib, sptr)
+
+    # Per-shape device GB/s (eager, for the breakdown) and the hot-L2 figure.
+    per_shape = {}
+    with torch.cuda.stream(stream):
+        for s in shapes:
+            s.run(lib, sptr)
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 5
+            ev0.record(stream)
+            for _ in range(reps):
+                s.run(lib, sptr)
+            ev1.record(stream)
+            ev1.synchronize()
+            cold = s.bytes * reps / (ev0.elapsed_time(ev1) / 1e3) / 1e9
+            ev0.record(stream)
+            for _ in range(reps):
+                s.run(lib, sptr, hot=True)
+            ev1.record(stream)
+            ev1.synchronize()
+            hot = s.bytes * reps / (ev0.elapsed_time(ev1) / 1e3) / 1e9
+            per_shape[f"{s.out}x{s.in_}/{s.bits}b"] = {"cold_hbm_gbs": round(cold, 1), "hot_l2_gbs": round(hot, 1),
+                                                        "weight_copies": s.copies}
+
+    # Capture one step in a CUDA graph.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        step()  # warm the launch path before capture
+        stream.synchronize()
+        n0 = lib.wc_launch_count()
+        with torch.cuda.graph(graph, stream=stream, capture_error_mode="relaxed"):
+            step()
+        launches_per_step = lib.wc_launch_count() - n0
+    torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    gpu_id = f"GPU-{props.uuid}" if getattr(props, "uuid", None) else str(local)
+    sampler = ClockSampler(gpu_id)
+    sampler.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    if pg:
+        pg.barrier()
+    ms = ev0.elapsed_time(ev1)
+    if pg:
+        t = torch.tensor([ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = world * bytes_per_step * args.steps / (ms / 1e3) / 1e9
+
+    # End to end through the C ABI: x from pinned host memory in, every
+    # output back to pinned host memory, each step.
+    h2d = sum(4 * s.in_ for s in shapes)
+    d2h = sum(4 * s.calls * s.out for s in shapes)
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        for s in shapes:
+            s.x.copy_(s.x_host, non_blocking=True)
+            s.run(lib, sptr)
+            s.y_host.copy_(s.y, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        e2e_step()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if pg:
+        t = torch.tensor([e2e_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * bytes_per_step * e2e_steps / (e2e_ms / 1e3) / 1e9
+
+    peak, peak_kind = peaks()
+    avg_launch_ms = ms_per_step / max(launches_per_step, 1)
+    bytes_per_launch = bytes_per_step / max(launches_per_step, 1)
+    achieved = bytes_per_launch / (avg_launch_ms / 1e3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "cq_lut_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8 index, int32 table sums, f32 epilogue", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "calls_per_shape": args.calls, "group": GROUP,
+                   "cache": "inputs larger than L2: weights cycle through >= 4x L2 of distinct copies per shape",
+                   "launch": "cq.GEMMs over the calls of a shape (shared x), CUDA graph of one step",
+                   "bytes_per_step": bytes_per_step, "parallelism": f"replicas x{world} (no collectives)",
+                   "per_shape": per_shape},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
+                     "kernel": "cq_lut_kernel", "bytes_per_launch": int(bytes_per_launch)},
+        "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": int(launches_per_step * args.steps),
+        "clocks": clocks,
+    }
+    if args.only:
+        line["config"]["workload"] = f"one shape {args.only} (profiling run, not the headline workload)"
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.only:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--calls", type=int, default=1000)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", default="", help="one shape OUTxINxBITS (profiling runs)")
+    args = ap.parse_args()
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    run_b200(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -44,6 +44,7 @@ _c_float = ctypes.c_float
 _SIGS = {
     "wc_last_error": (_c_size, [ctypes.c_char_p, _c_size]),
     "wc_version": (ctypes.c_char_p, []),
+    "wc_launch_count": (ctypes.c_uint64, []),
     "wc_cq_create": (_c_int, [_c_void_p, _c_size, _c_void_p, _c_size, _c_void_p, _c_size, _c_int, _c_int, _c_int,
                               _c_int, _c_int, ctypes.POINTER(_c_void_p)]),
     "wc_cq_rows": (_c_int, [_c_void_p, _c_int, _c_int, ctypes.POINTER(_c_void_p)]),

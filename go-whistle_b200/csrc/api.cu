@@ -53,9 +53,11 @@ using namespace wb;
 
 // Device storage shared by a matrix and its views.
 struct CqStorage {
-    uint8_t *idx = nullptr;
+    uint8_t *idx = nullptr;   // group-major layout (common.cuh CqView)
     __half *nrm = nullptr;
-    size_t idx_bytes = 0, nrm_bytes = 0;
+    uint8_t *sidx = nullptr;  // stream layout (cq_lut_stream.cu), or null
+    __half *snrm = nullptr;
+    size_t idx_bytes = 0, nrm_bytes = 0, sidx_bytes = 0, snrm_bytes = 0;
     int device = 0;
     ~CqStorage() {
         int cur = 0;
@@ -63,6 +65,8 @@ struct CqStorage {
         if (cur != device) cudaSetDevice(device);
         if (idx) cudaFree(idx);
         if (nrm) cudaFree(nrm);
+        if (sidx) cudaFree(sidx);
+        if (snrm) cudaFree(snrm);
         if (cur != device) cudaSetDevice(cur);
     }
 };
@@ -74,10 +78,46 @@ struct wc_cq {
     bool exact = false;
 
     CqView view() const { return CqView{st->idx, st->nrm, out, row0, ld}; }
+    CqView stream_view() const { return CqView{st->sidx, st->snrm, out, row0, ld}; }
     bool lut() const { return !exact && shape.gb <= kLutMaxGroupBytes; }
+    bool streamable() const { return lut() && st->sidx != nullptr; }
 };
 
+// The stream layout of cq_lut_stream.cu: superchunks of 64 index bytes, each
+// row's byte pairs permuted by its lane (row mod 32), norms in phase order.
+static void stream_layout(const uint8_t *index, const uint8_t *norms, int out, int groups, int gb, int row_bytes,
+                          std::vector<uint8_t> &sidx, std::vector<uint16_t> &snrm) {
+    const int P = gb / 2, NG = 32 / P, nsc = row_bytes / 64;
+    sidx.assign((size_t)out * row_bytes, 0);
+    snrm.assign((size_t)nsc * out * NG, 0);
+    for (int r = 0; r < out; r++) {
+        const int lam = r & 31, a = lam / P, c = lam % P;
+        const uint8_t *src = index + (size_t)r * row_bytes;
+        for (int sc = 0; sc < nsc; sc++) {
+            uint8_t chunk[64];
+            for (int slot = 0; slot < 32; slot++) {
+                int q = slot / P, t = slot % P;
+                int o = P * ((q + a) % NG) + (t + c) % P;
+                chunk[2 * slot] = src[64 * sc + 2 * o];
+                chunk[2 * slot + 1] = src[64 * sc + 2 * o + 1];
+            }
+            for (int i = 0; i < 4; i++)
+                memcpy(&sidx[(((size_t)sc * 4 + i) * out + r) * 16], chunk + 16 * i, 16);
+            for (int q = 0; q < NG; q++) {
+                int g = sc * NG + (q + a) % NG;
+                const uint8_t *pn = norms + 2 * ((size_t)r * groups + g);
+                snrm[((size_t)sc * out + r) * NG + q] = (uint16_t)(pn[0] | (pn[1] << 8));
+            }
+        }
+    }
+}
+
 static const char *kVersion = "whistle_b200 0.1";
+static std::atomic<uint64_t> g_launches{0};
+
+void wb::count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+extern "C" uint64_t wc_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 extern "C" size_t wc_last_error(char *buf, size_t len) {
     const std::string &m = g_last_error;
@@ -178,6 +218,22 @@ extern "C" wc_status wc_cq_create(const uint8_t *index, size_t index_len, const 
     WB_CUDA(cudaMalloc(&storage->nrm, storage->nrm_bytes));
     if (!idx.empty()) WB_CUDA(cudaMemcpy(storage->idx, idx.data(), idx.size(), cudaMemcpyHostToDevice));
     if (!nrm.empty()) WB_CUDA(cudaMemcpy(storage->nrm, nrm.data(), 2 * nrm.size(), cudaMemcpyHostToDevice));
+    if (out > 0 && m->lut() && stream_eligible(s)) {
+        int dev = 0, limit = 0;
+        WB_CUDA(cudaGetDevice(&dev));
+        WB_CUDA(cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+        if (stream_smem_bytes(s) <= (size_t)limit) {
+            std::vector<uint8_t> sidx;
+            std::vector<uint16_t> snrm;
+            stream_layout(index, norms, out, groups, gb, row_bytes, sidx, snrm);
+            storage->sidx_bytes = sidx.size();
+            storage->snrm_bytes = 2 * snrm.size();
+            WB_CUDA(cudaMalloc(&storage->sidx, storage->sidx_bytes));
+            WB_CUDA(cudaMalloc(&storage->snrm, storage->snrm_bytes));
+            WB_CUDA(cudaMemcpy(storage->sidx, sidx.data(), sidx.size(), cudaMemcpyHostToDevice));
+            WB_CUDA(cudaMemcpy(storage->snrm, snrm.data(), 2 * snrm.size(), cudaMemcpyHostToDevice));
+        }
+    }
     m->st = std::move(storage);
     *h = m.release();
     return WC_OK;
@@ -214,7 +270,8 @@ extern "C" int wc_cq_in(const wc_cq *h) { return h ? h->shape.in : 0; }
 extern "C" int wc_cq_bits(const wc_cq *h) { return h ? h->shape.bits : 0; }
 extern "C" size_t wc_cq_bytes(const wc_cq *h) {
     if (!h) return 0;
-    return (size_t)h->out * h->shape.row_bytes + (size_t)2 * h->out * h->shape.groups + 4u * (1u << h->shape.bits);
+    size_t one = (size_t)h->out * h->shape.row_bytes + (size_t)2 * h->out * h->shape.groups;
+    return (h->st->sidx ? 2 * one : one) + 4u * (1u << h->shape.bits);
 }
 
 // lut.go:206 sharesTables.
@@ -227,9 +284,64 @@ static bool shares_tables(const wc_cq *a, const wc_cq *b) {
     return true;
 }
 
+// Streaming kernel threshold: index bytes of one activation's products
+// below which the per-tile kernel (no per-SM table build) answers faster.
+static const size_t kStreamMinBytes = 2u << 20;
+
+static int sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+    return n;
+}
+
+// The streaming kernel for one activation, if every matrix has the stream
+// layout and the products are large enough; returns false otherwise.
+static bool try_stream(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows, cudaStream_t st,
+                       wc_status *status) {
+    if (rows != 1 || n == 0) return false;
+    size_t total = 0;
+    for (int k = 0; k < n; k++) {
+        if (!ms[k]->streamable()) return false;
+        total += (size_t)ms[k]->out * ms[k]->shape.row_bytes;
+    }
+    if (total < kStreamMinBytes) return false;
+    const int sms = sm_count();
+    *status = WC_OK;
+    for (int base = 0; base < n; base += kMaxStreamMats) {
+        int cnt = n - base < kMaxStreamMats ? n - base : kMaxStreamMats;
+        auto p = std::make_unique<StreamParams>();
+        p->shape = ms[base]->shape;
+        p->x = x;
+        int tiles = 0, used = 0;
+        for (int k = 0; k < cnt; k++) {
+            const wc_cq *m = ms[base + k];
+            if (m->out == 0) continue;
+            p->views[used] = m->stream_view();
+            p->y[used] = ys[base + k];
+            p->tile_start[used] = tiles;
+            tiles += (m->out + 31) / 32;
+            used++;
+        }
+        p->tile_start[used] = tiles;
+        p->n = used;
+        p->total_tiles = tiles;
+        if (used == 0) continue;
+        int ctas = tiles < sms ? tiles : sms;
+        cudaError_t e = launch_stream(*p, ctas, st);
+        if (e != cudaSuccess) {
+            *status = cuda_error(e, "cq stream kernel");
+            return true;
+        }
+    }
+    return true;
+}
+
 // One lut launch sequence for matrices that share their tables.
 static wc_status run_lut(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows,
                          cudaStream_t st) {
+    wc_status sst;
+    if (try_stream(ms, n, x, ys, rows, st, &sst)) return sst;
     for (int base = 0; base < n; base += kMaxLaunchMats) {
         int cnt = n - base < kMaxLaunchMats ? n - base : kMaxLaunchMats;
         auto p = std::make_unique<LutParams>();

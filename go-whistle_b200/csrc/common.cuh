@@ -55,6 +55,8 @@ struct CqShape {
 namespace wb {
 wc_status set_error(wc_status st, const std::string &msg);
 wc_status cuda_error(cudaError_t e, const char *what);
+// Counts one kernel launch (wc_launch_count).
+void count_launch();
 }  // namespace wb
 
 #define WB_CUDA(call)                                            \

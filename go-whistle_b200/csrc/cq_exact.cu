@@ -169,6 +169,7 @@ cudaError_t launch_exact(const CqShape &s, const CqView &v, const float *x, floa
     for (int a0 = 0; a0 < rows; a0 += 65535) {
         int n = rows - a0 < 65535 ? rows - a0 : 65535;
         cq_exact_kernel<<<dim3(tiles, n), kExactThreads, smem, st>>>(s, v, x, y, rows, four, a0);
+        count_launch();
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
@@ -180,6 +181,7 @@ cudaError_t launch_row(const CqShape &s, const CqView &v, const int32_t *rows, i
     if (n <= 0) return cudaSuccess;
     int threads = s.group < 128 ? (s.group < 32 ? 32 : s.group) : 128;
     cq_row_kernel<<<n, threads, sizeof(float) * s.group, st>>>(s, v, rows, r0, dst, bad);
+    count_launch();
     return cudaGetLastError();
 }
 

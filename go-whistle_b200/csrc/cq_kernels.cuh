@@ -25,6 +25,22 @@ struct LutParams {
 size_t lut_smem_bytes(const CqShape &s);
 cudaError_t launch_lut(const LutParams &p, int tiles, int acts, cudaStream_t st);
 
+// The streaming batch-1 kernel (cq_lut_stream.cu): views point at the
+// "stream layout" (sidx/snrm) and tiles are 32 rows.
+constexpr int kMaxStreamMats = 512;
+struct StreamParams {
+    CqShape shape;
+    const float *x;   // one activation [in]
+    int n;            // matrices
+    int total_tiles;  // Σ ceil(out/32)
+    CqView views[kMaxStreamMats];
+    float *y[kMaxStreamMats];
+    int tile_start[kMaxStreamMats + 1];
+};
+bool stream_eligible(const CqShape &s);
+size_t stream_smem_bytes(const CqShape &s);
+cudaError_t launch_stream(const StreamParams &p, int ctas, cudaStream_t st);
+
 // The Exact path (kernel.go:162-373): one matrix, float32 nibble tables.
 size_t exact_smem_bytes(const CqShape &s);
 cudaError_t launch_exact(const CqShape &s, const CqView &v, const float *x, float *y, int rows, cudaStream_t st);

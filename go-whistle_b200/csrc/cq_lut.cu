@@ -228,6 +228,7 @@ cudaError_t launch_lut(const LutParams &p, int tiles, int acts, cudaStream_t st)
     if (e != cudaSuccess) return e;
     dim3 grid(tiles, acts);
     fn<<<grid, kThreads, smem, st>>>(p);
+    count_launch();
     return cudaGetLastError();
 }
 

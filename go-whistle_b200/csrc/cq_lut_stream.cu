@@ -1,0 +1,317 @@
+// cq_lut_stream.cu — the streaming CQ LUT GEMV for large batch-1 products
+// (many GEMMs matrices, or one large matrix), on sm_100a.
+//
+// Same arithmetic as cq_lut.cu (and so the reference's lut kernel, bit for
+// bit); a different shape of work, built to run at HBM speed:
+//
+// * Persistent CTAs, one per SM. Each rotates and tabulates the activation
+//   once, then streams its share of 32-row warp tiles of every matrix.
+// * Byte tables. For each index byte position j the CTA holds all 256
+//   values T_j[b] = v_{2j}[b & 15] + v_{2j+1}[b >> 4] (the lo and hi nibble
+//   tables of lut.go:239-282 added, stored with a +16384 bias as uint16), so
+//   one shared-memory load serves one index byte (the reference's VPSHUFB
+//   kernel needs two). Up to 256 byte positions (128 KB) are resident; wider
+//   rows are processed in passes of 256 positions, the partial row sums
+//   carried in the output between passes (the group order is kept).
+// * Conflict-free lookups. Tables are laid out T[b][j] (j fastest), so the
+//   bank of a lookup depends only on j. The HBM layout permutes each row's
+//   64-byte superchunks by the row's lane (root row mod 32) such that, at
+//   every step, the 32 lanes of a warp touch 32 distinct byte pairs of the
+//   superchunk while each lane still reads its registers in a fixed order
+//   and finishes one whole group per phase. The address of a lookup is one
+//   PRMT: (b << 8) | colbyte, colbyte from a per-lane packed table.
+// * Exactness: the integer group sums are exact; each group's term
+//   float32(Σv) · (norm · step) goes through shared memory so the row's terms
+//   are added in group order, as lut.go:309 does.
+//
+// Layouts (built by api.cu at matrix creation, "stream layout"):
+//   sidx[((sc*4 + i)*ld + R)*16 + k]  byte k of quarter i of superchunk sc of
+//                                     root row R, slot order (below)
+//   snrm[(sc*ld + R)*NG + q]          FP16 norm of the group in phase q
+// with P = gb/2 byte pairs per group, NG = 32/P groups per superchunk, lane
+// id λ = R mod 32 = P·a + c, and slot s = P·q + t holding the superchunk's
+// byte pair o(s) = P·((q + a) mod NG) + ((t + c) mod P).
+#include "common.cuh"
+#include "cq_kernels.cuh"
+
+namespace wb {
+
+namespace {
+
+constexpr int kStreamThreads = 512;
+constexpr int kStreamWarps = kStreamThreads / 32;
+constexpr int kPassPositions = 256;               // byte positions per table pass
+constexpr int kTabBytes = 2 * 256 * 128 * 2;      // two blocks of [256 b][128 j] uint16
+constexpr int kNibBytes = 2 * 16 * kPassPositions * 2;  // lo/hi nibble tables [16][256] uint16
+constexpr uint32_t kEntryBias = 8192;             // per nibble entry, so a byte entry carries 16384
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ int find_tile_matrix(const StreamParams &p, int t) {
+    int lo = 0, hi = p.n - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (p.tile_start[mid] <= t)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    return lo;
+}
+
+// Rotation, group bounds, 8191/M and steps for one activation (lut.go:160-178).
+__device__ void rotate_and_bound(const CqShape &s, const float *x, float *xs, float *steps, float *invs) {
+    const int tid = threadIdx.x, pad = s.pad, G = s.group, half = G >> 1;
+    for (int k = tid; k < pad; k += kStreamThreads) xs[k] = k < s.in ? x[k] : 0.0f;
+    __syncthreads();
+    for (int h = 1; h < G; h <<= 1) {
+        for (int b = tid; b < pad / 2; b += kStreamThreads) {
+            int g = b / half, t = b % half;
+            int j = g * G + (t / h) * 2 * h + (t % h);
+            float a = xs[j], c = xs[j + h];
+            xs[j] = __fadd_rn(a, c);
+            xs[j + h] = __fsub_rn(a, c);
+        }
+        __syncthreads();
+    }
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int g = warp; g < s.groups; g += kStreamWarps) {
+        const float *xg = xs + g * G;
+        float mx = 0.0f;
+        if (s.bits == 2) {
+            for (int q = lane; q < half; q += 32) mx = fmaxf(mx, __fadd_rn(fabsf(xg[2 * q]), fabsf(xg[2 * q + 1])));
+        } else {
+            for (int q = lane; q < G; q += 32) mx = fmaxf(mx, fabsf(xg[q]));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) {
+            float m = __fmul_rn(s.cb_max, mx);
+            invs[g] = m > 0.0f ? __fdiv_rn((float)kLutQ, m) : 0.0f;
+            steps[g] = __fmul_rn(m, s.lut_step);
+        }
+    }
+    __syncthreads();
+}
+
+// Byte tables for byte positions [j0, j0 + npos) of the row.
+__device__ void build_pass_tables(const CqShape &s, const float *xs, const float *invs, int j0, int npos,
+                                  uint16_t *nib, uint16_t *tab) {
+    const int tid = threadIdx.x;
+    const int G = s.group;
+    // Nibble tables, biased: nib[e][c][j] for the lo (e = 0) and hi (e = 1)
+    // nibble of byte position j0 + j (lut.go:248-255, 272-279).
+    for (int u = tid; u < 2 * kPassPositions; u += kStreamThreads) {
+        int e = u / kPassPositions, j = u % kPassPositions;
+        uint16_t *dst = nib + e * 16 * kPassPositions + j;
+        if (j >= npos) {
+#pragma unroll
+            for (int c = 0; c < 16; c++) dst[c * kPassPositions] = (uint16_t)kEntryBias;
+            continue;
+        }
+        int np = 2 * (j0 + j) + e;  // nibble position in the row
+        if (s.bits == 4) {
+            int g = np / G;
+            float a = __fmul_rn(xs[np], invs[g]);
+#pragma unroll
+            for (int c = 0; c < 16; c++)
+                dst[c * kPassPositions] = (uint16_t)(__float2int_rn(__fmul_rn(s.cb[c], a)) + (int)kEntryBias);
+        } else {
+            int g = (2 * np) / G;
+            float inv = invs[g];
+            float a = __fmul_rn(xs[2 * np], inv), b = __fmul_rn(xs[2 * np + 1], inv);
+#pragma unroll
+            for (int c = 0; c < 16; c++) {
+                float v = __fadd_rn(__fmul_rn(s.cb[c & 3], a), __fmul_rn(s.cb[c >> 2], b));
+                dst[c * kPassPositions] = (uint16_t)(__float2int_rn(v) + (int)kEntryBias);
+            }
+        }
+    }
+    __syncthreads();
+    // Byte tables: tab[blk][b][jj] = nib[0][b & 15][j] + nib[1][b >> 4][j],
+    // j = 128·blk + jj; 8 positions (16 bytes) per store, packed adds (no
+    // carry: each half stays below 2^15).
+    const int units = 2 * 256 * 16;
+    for (int u = tid; u < units; u += kStreamThreads) {
+        int blk = u / (256 * 16), b = (u / 16) % 256, ch = u % 16;
+        int j = 128 * blk + 8 * ch;
+        const uint4 lo = *reinterpret_cast<const uint4 *>(nib + (b & 15) * kPassPositions + j);
+        const uint4 hi = *reinterpret_cast<const uint4 *>(nib + 16 * kPassPositions + (b >> 4) * kPassPositions + j);
+        uint4 r;
+        r.x = lo.x + hi.x;
+        r.y = lo.y + hi.y;
+        r.z = lo.z + hi.z;
+        r.w = lo.w + hi.w;
+        *reinterpret_cast<uint4 *>(tab + ((size_t)blk * 256 + b) * 128 + 8 * ch) = r;
+    }
+    __syncthreads();
+}
+
+template <int GB>
+__global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const __grid_constant__ StreamParams p) {
+    constexpr int P = GB / 2;    // byte pairs per group
+    constexpr int NG = 32 / P;   // groups per 64-byte superchunk
+    extern __shared__ __align__(16) unsigned char smem[];
+    const CqShape &s = p.shape;
+    uint16_t *tab = reinterpret_cast<uint16_t *>(smem);                    // kTabBytes
+    uint16_t *nib = reinterpret_cast<uint16_t *>(smem + kTabBytes);        // kNibBytes
+    float *terms = reinterpret_cast<float *>(smem + kTabBytes + kNibBytes);  // [warps][NG][32]
+    float *steps = terms + kStreamWarps * NG * 32;                         // [groups]
+    float *invs = steps + s.groups;                                        // [groups]
+    float *xs = invs + s.groups;                                           // [pad]
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t tab_s = (uint32_t)__cvta_generic_to_shared(tab);
+    float *wterms = terms + warp * NG * 32;
+    const int nsc = s.row_bytes / 64;
+    const int npass = (s.row_bytes + kPassPositions - 1) / kPassPositions;
+
+    // This CTA's tiles: a contiguous share of all matrices' 32-row tiles.
+    const int t_begin = (int)(((long long)p.total_tiles * blockIdx.x) / gridDim.x);
+    const int t_end = (int)(((long long)p.total_tiles * (blockIdx.x + 1)) / gridDim.x);
+
+    rotate_and_bound(s, p.x, xs, steps, invs);
+
+    for (int pass = 0; pass < npass; pass++) {
+        const int j0 = pass * kPassPositions;
+        const int npos = min(kPassPositions, s.row_bytes - j0);
+        __syncthreads();
+        build_pass_tables(s, xs, invs, j0, npos, nib, tab);
+        const int sc0 = j0 / 64, nsc_pass = npos / 64;
+
+        int cached_off = -1;
+        uint32_t cbw[16];  // colbyte(slot s, half e) at byte 2s+e: 4·o(s) + 2e
+#pragma unroll
+        for (int w = 0; w < 16; w++) cbw[w] = 0;
+        int a_rot = 0;
+
+        for (int t = t_begin + warp; t < t_end; t += kStreamWarps) {
+            const int k = find_tile_matrix(p, t);
+            const CqView v = p.views[k];
+            const int r = (t - p.tile_start[k]) * 32 + lane;
+            const bool valid = r < v.out;
+            const int R = v.row0 + r;
+            const int off = v.row0 & 31;
+            if (off != cached_off) {
+                cached_off = off;
+                const int lam = (off + lane) & 31;
+                const int a = lam / P, c = lam % P;
+                a_rot = a;
+#pragma unroll
+                for (int w = 0; w < 16; w++) {
+                    uint32_t word = 0;
+#pragma unroll
+                    for (int bb = 0; bb < 4; bb++) {
+                        int slot = (4 * w + bb) >> 1, e = bb & 1;
+                        int q = slot / P, tt = slot % P;
+                        int o = P * ((q + a) % NG) + (tt + c) % P;
+                        word |= (uint32_t)(4 * o + 2 * e) << (8 * bb);
+                    }
+                    cbw[w] = word;
+                }
+            }
+            float *yk = p.y[k];
+            float y = 0.0f;
+            if (pass > 0 && valid) y = yk[r];
+
+            for (int scl = 0; scl < nsc_pass; scl++) {
+                const int sc = sc0 + scl;
+                uint4 d[4];
+                uint32_t nw[(NG + 1) / 2];
+                if (valid) {
+                    const uint8_t *base = v.idx + ((size_t)sc * 4 * v.ld + R) * 16;
+#pragma unroll
+                    for (int i = 0; i < 4; i++)
+                        d[i] = __ldg(reinterpret_cast<const uint4 *>(base + (size_t)i * v.ld * 16));
+                    const __half *nb = v.nrm + ((size_t)sc * v.ld + R) * NG;
+                    if constexpr (NG == 8) {
+                        uint4 t4 = __ldg(reinterpret_cast<const uint4 *>(nb));
+                        nw[0] = t4.x; nw[1] = t4.y; nw[2] = t4.z; nw[3] = t4.w;
+                    } else if constexpr (NG == 4) {
+                        uint2 t2 = __ldg(reinterpret_cast<const uint2 *>(nb));
+                        nw[0] = t2.x; nw[1] = t2.y;
+                    } else if constexpr (NG == 2) {
+                        nw[0] = __ldg(reinterpret_cast<const uint32_t *>(nb));
+                    } else {
+                        nw[0] = __ldg(reinterpret_cast<const uint16_t *>(nb));
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; i++) d[i] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+                    for (int i = 0; i < (NG + 1) / 2; i++) nw[i] = 0;
+                }
+                const uint32_t dw[16] = {d[0].x, d[0].y, d[0].z, d[0].w, d[1].x, d[1].y, d[1].z, d[1].w,
+                                         d[2].x, d[2].y, d[2].z, d[2].w, d[3].x, d[3].y, d[3].z, d[3].w};
+                const uint32_t tb = tab_s + (uint32_t)((scl >> 1) * (256 * 128 * 2) + (scl & 1) * 128);
+#pragma unroll
+                for (int q = 0; q < NG; q++) {
+                    int32_t acc = 0;
+#pragma unroll
+                    for (int tt = 0; tt < P; tt++) {
+                        const int slot = P * q + tt;
+                        const uint32_t word = dw[slot >> 1];
+#pragma unroll
+                        for (int e = 0; e < 2; e++) {
+                            const int m = ((2 * slot) & 3) + e;      // byte of the data word
+                            const int kc = (2 * slot + e) & 3;       // byte of the colbyte word
+                            const uint32_t sel = (uint32_t)(4 + kc) | ((uint32_t)m << 4) |
+                                                 ((uint32_t)(12 + kc) << 8) | ((uint32_t)(12 + kc) << 12);
+                            const uint32_t addr = prmt(word, cbw[(2 * slot + e) >> 2], sel);
+                            acc += (int32_t)lds_u16(tb + addr);
+                        }
+                    }
+                    const int32_t sum = acc - (int32_t)(2 * kEntryBias) * GB;
+                    const int gl = (q + a_rot) % NG;        // group within the superchunk
+                    const int g = sc * NG + gl;              // group in the row
+                    const uint32_t nbits = (nw[q >> 1] >> (16 * (q & 1))) & 0xffffu;
+                    const float nrm = __half2float(__ushort_as_half((unsigned short)nbits));
+                    const float coef = __fmul_rn(nrm, steps[g]);
+                    wterms[gl * 32 + lane] = __fmul_rn(__int2float_rn(sum), coef);
+                }
+#pragma unroll
+                for (int gl = 0; gl < NG; gl++) y = __fadd_rn(y, wterms[gl * 32 + lane]);
+            }
+            if (valid) yk[r] = y;
+        }
+    }
+}
+
+}  // namespace
+
+bool stream_eligible(const CqShape &s) {
+    return (s.gb == 8 || s.gb == 16 || s.gb == 32 || s.gb == 64) && s.row_bytes % 64 == 0 && s.row_bytes >= 64;
+}
+
+size_t stream_smem_bytes(const CqShape &s) {
+    int ng = 64 / s.gb;
+    return (size_t)kTabBytes + kNibBytes + sizeof(float) * ((size_t)kStreamWarps * ng * 32 + 2 * s.groups + s.pad);
+}
+
+cudaError_t launch_stream(const StreamParams &p, int ctas, cudaStream_t st) {
+    size_t smem = stream_smem_bytes(p.shape);
+    void (*fn)(StreamParams);
+    switch (p.shape.gb) {
+        case 8: fn = cq_lut_stream_kernel<8>; break;
+        case 16: fn = cq_lut_stream_kernel<16>; break;
+        case 32: fn = cq_lut_stream_kernel<32>; break;
+        default: fn = cq_lut_stream_kernel<64>; break;
+    }
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    fn<<<ctas, kStreamThreads, smem, st>>>(p);
+    count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace wb

@@ -170,6 +170,7 @@ cudaError_t launch_quantize_rows(const float *x, int chunks, int width, int8_t *
     if (chunks <= 0) return cudaSuccess;
     const int warps = 8;
     quantize_rows_kernel<<<(chunks + warps - 1) / warps, warps * 32, 0, st>>>(x, chunks, width, q, s);
+    count_launch();
     return cudaGetLastError();
 }
 
@@ -182,6 +183,7 @@ cudaError_t launch_attend(const AttendParams &p, int streams, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(attend_int8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     attend_int8_kernel<<<dim3(p.heads, p.t, streams), kAttThreads, smem, st>>>(p);
+    count_launch();
     return cudaGetLastError();
 }
 

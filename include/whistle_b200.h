@@ -55,6 +55,11 @@ size_t wc_last_error(char *buf, size_t len);
 /* Library version string ("whistle_b200 <major>.<minor>"). */
 const char *wc_version(void);
 
+/* Kernels this library has launched in this process so far (all devices,
+ * all threads). A diagnostic with no reference counterpart: benchmarks read
+ * it before and after a timed region to count their launches. */
+uint64_t wc_launch_count(void);
+
 /* ---------------------------------------------------------------- cq ---- */
 
 /*

@@ -223,3 +223,46 @@ def test_bytes(wb, cuda):
     p = wb.synth.random_packed(rng, 70, 384, 128, 2)
     m = wb.cq.New(p)
     assert m.Bytes() == p.Index.size + p.Norms.size + 4 * 4
+
+
+# Products large enough (>= 2 MB of index bytes per activation) for the
+# streaming kernel: every group width it takes (gb 8, 16, 32, 64), one and
+# several table passes (rows of 256 and 1024 index bytes), and GEMMs over
+# views that start inside a 32-row tile.
+STREAM_CASES = [(16384, 512, 32, 4), (8199, 512, 128, 4), (16384, 512, 32, 2), (8192, 2048, 32, 4),
+                (8192, 2048, 32, 2), (20000, 512, 128, 2), (4096, 2048, 128, 4)]
+
+
+@pytest.mark.parametrize("case", STREAM_CASES, ids=[f"{o}x{i}g{g}b{b}" for o, i, g, b in STREAM_CASES])
+def test_stream_kernel_bit_exact(wb, orc, cuda, case):
+    out, in_, group, bits = case
+    rng, p, m, om = make(wb, orc, out + in_ + group + bits, out, in_, group, bits, "lloyd")
+    x = rng.normal(size=in_).astype(np.float32)
+    want = orc.gemm_lut(om, x, 1, threads=8).reshape(-1)
+    xd = cuda.from_numpy(x).cuda()
+    yd = cuda.full((out,), float("nan"), dtype=cuda.float32, device="cuda")
+    m.GEMV(yd, xd)
+    assert bits_eq(yd.cpu().numpy(), want)
+    # GEMMs over views of the same matrix, unaligned starts, > 1 launch of views
+    bounds = [(0, 1000), (5, 1200), (33, 2500), (1000, 1001), (out - 700, out)]
+    views = [m.Rows(lo, hi) for lo, hi in bounds] * 3
+    yds = [cuda.full((v.Out(),), float("nan"), dtype=cuda.float32, device="cuda") for v in views]
+    wb.cq.GEMMs(views, yds, xd, 1)
+    for (lo, hi), y in zip(bounds * 3, yds):
+        assert bits_eq(y.cpu().numpy(), want[lo:hi]), (lo, hi)
+
+
+def test_stream_many_matrices(wb, orc, cuda):
+    """More matrices than one launch carries, each its own weights."""
+    rng = np.random.default_rng(77)
+    ps = [wb.synth.random_packed(rng, 96, 512, 32, 4, "lloyd") for _ in range(600)]
+    for p in ps[1:]:
+        p.Codebook = ps[0].Codebook
+    ms = [wb.cq.New(p) for p in ps]
+    x = rng.normal(size=512).astype(np.float32)
+    xd = cuda.from_numpy(x).cuda()
+    yds = [cuda.empty(96, dtype=cuda.float32, device="cuda") for _ in ms]
+    wb.cq.GEMMs(ms, yds, xd, 1)
+    for p, y in zip(ps[::37], yds[::37]):
+        want = orc.gemm_lut(orc.OracleMatrix.of(p), x, 1).reshape(-1)
+        assert bits_eq(y.cpu().numpy(), want)
