@@ -57,6 +57,11 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
     return v;
 }
 
+// Hint: fetch [addr, addr + bytes) into L2 (bytes a multiple of 16, > 0).
+__device__ __forceinline__ void prefetch_l2(const void *addr, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(addr), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ int find_tile_matrix(const StreamParams &p, int t) {
     int lo = 0, hi = p.n - 1;
     while (lo < hi) {
@@ -140,10 +145,12 @@ __device__ void build_pass_tables(const CqShape &s, const float *xs, const float
     __syncthreads();
     // Byte tables: tab[blk][b][jj] = nib[0][b & 15][j] + nib[1][b >> 4][j],
     // j = 128·blk + jj; 8 positions (16 bytes) per store, packed adds (no
-    // carry: each half stays below 2^15).
-    const int units = 2 * 256 * 16;
+    // carry: each half stays below 2^15). Only the npos positions in use.
+    const int chunks = (npos + 7) / 8;
+    const int units = 256 * chunks;
     for (int u = tid; u < units; u += kStreamThreads) {
-        int blk = u / (256 * 16), b = (u / 16) % 256, ch = u % 16;
+        int b = u / chunks, cg = u % chunks;
+        int blk = cg / 16, ch = cg % 16;
         int j = 128 * blk + 8 * ch;
         const uint4 lo = *reinterpret_cast<const uint4 *>(nib + (b & 15) * kPassPositions + j);
         const uint4 hi = *reinterpret_cast<const uint4 *>(nib + 16 * kPassPositions + (b >> 4) * kPassPositions + j);
@@ -155,6 +162,104 @@ __device__ void build_pass_tables(const CqShape &s, const float *xs, const float
         *reinterpret_cast<uint4 *>(tab + ((size_t)blk * 256 + b) * 128 + 8 * ch) = r;
     }
     __syncthreads();
+}
+
+// Lane 0 of a warp asks L2 for tile t's index bytes and norms of
+// superchunks [sc0, sc0 + nsc_pass): 4 runs of 32 rows x 16 bytes and one
+// run of 32 rows x NG norms per superchunk, all inside the matrix.
+template <int NG>
+__device__ __forceinline__ void prefetch_tile(const StreamParams &p, int t, int sc0, int nsc_pass) {
+    const int k = find_tile_matrix(p, t);
+    const CqView &v = p.views[k];
+    const int r0 = (t - p.tile_start[k]) * 32;
+    const int rows = min(32, v.out - r0);
+    const int R0 = v.row0 + r0;
+    for (int scl = 0; scl < nsc_pass; scl++) {
+        const int sc = sc0 + scl;
+#pragma unroll
+        for (int i = 0; i < 4; i++) prefetch_l2(v.idx + (((size_t)sc * 4 + i) * v.ld + R0) * 16, (uint32_t)rows * 16);
+        // The norm run may start off a 16-byte boundary: prefetch its aligned
+        // interior only, which stays inside the run.
+        const uintptr_t a0 = (uintptr_t)(v.nrm + ((size_t)sc * v.ld + R0) * NG);
+        const uintptr_t a1 = a0 + (uintptr_t)rows * NG * 2;
+        const uintptr_t s0 = (a0 + 15) & ~(uintptr_t)15, s1 = a1 & ~(uintptr_t)15;
+        if (s1 > s0) prefetch_l2(reinterpret_cast<const void *>(s0), (uint32_t)(s1 - s0));
+    }
+}
+
+// One superchunk of a 32-row tile: 32 slots of two table lookups each, one
+// group per phase; the group terms go through shared memory so the row adds
+// them in group order. SCL (the superchunk within the pass) fixes the table
+// block and half, so every lookup is one PRMT, one LDS and one IADD.
+template <int GB, int SCL>
+__device__ __forceinline__ float superchunk(const uint4 (&d)[4], const uint32_t (&nw)[4], const uint32_t (&cbw)[16],
+                                            const uint16_t *tab, const float *steps, float *wterms, int lane,
+                                            int a_rot, int sc, float y) {
+    constexpr int P = GB / 2, NG = 32 / P;
+    const unsigned char *tb = reinterpret_cast<const unsigned char *>(tab) + (SCL >> 1) * (256 * 128 * 2) +
+                              (SCL & 1) * 128;
+    const uint32_t dw[16] = {d[0].x, d[0].y, d[0].z, d[0].w, d[1].x, d[1].y, d[1].z, d[1].w,
+                             d[2].x, d[2].y, d[2].z, d[2].w, d[3].x, d[3].y, d[3].z, d[3].w};
+#pragma unroll
+    for (int q = 0; q < NG; q++) {
+        int32_t acc0 = 0, acc1 = 0;
+#pragma unroll
+        for (int tt = 0; tt < P; tt++) {
+            const int slot = P * q + tt;
+            const uint32_t word = dw[slot >> 1];
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int m = ((2 * slot) & 3) + e;  // byte of the data word
+                const int kc = (2 * slot + e) & 3;   // byte of the colbyte word
+                const uint32_t sel = (uint32_t)(4 + kc) | ((uint32_t)m << 4) | ((uint32_t)(12 + kc) << 8) |
+                                     ((uint32_t)(12 + kc) << 12);
+                const uint32_t addr = prmt(word, cbw[(2 * slot + e) >> 2], sel);
+                const int32_t v = *reinterpret_cast<const uint16_t *>(tb + addr);
+                if (e == 0)
+                    acc0 += v;
+                else
+                    acc1 += v;
+            }
+        }
+        const int32_t sum = acc0 + acc1 - (int32_t)(2 * kEntryBias) * GB;
+        const int gl = (q + a_rot) & (NG - 1);  // group within the superchunk
+        const int g = sc * NG + gl;             // group in the row
+        const uint32_t nbits = (nw[q >> 1] >> (16 * (q & 1))) & 0xffffu;
+        const float nrm = __half2float(__ushort_as_half((unsigned short)nbits));
+        const float coef = __fmul_rn(nrm, steps[g]);
+        wterms[gl * 32 + lane] = __fmul_rn(__int2float_rn(sum), coef);
+    }
+#pragma unroll
+    for (int gl = 0; gl < NG; gl++) y = __fadd_rn(y, wterms[gl * 32 + lane]);
+    return y;
+}
+
+template <int NG>
+__device__ __forceinline__ void load_superchunk(const CqView &v, int sc, int R, bool valid, uint4 (&d)[4],
+                                                uint32_t (&nw)[4]) {
+    if (valid) {
+        const uint8_t *base = v.idx + ((size_t)sc * 4 * v.ld + R) * 16;
+#pragma unroll
+        for (int i = 0; i < 4; i++) d[i] = __ldg(reinterpret_cast<const uint4 *>(base + (size_t)i * v.ld * 16));
+        const __half *nb = v.nrm + ((size_t)sc * v.ld + R) * NG;
+        if constexpr (NG == 8) {
+            uint4 t4 = __ldg(reinterpret_cast<const uint4 *>(nb));
+            nw[0] = t4.x; nw[1] = t4.y; nw[2] = t4.z; nw[3] = t4.w;
+        } else if constexpr (NG == 4) {
+            uint2 t2 = __ldg(reinterpret_cast<const uint2 *>(nb));
+            nw[0] = t2.x; nw[1] = t2.y; nw[2] = 0; nw[3] = 0;
+        } else if constexpr (NG == 2) {
+            nw[0] = __ldg(reinterpret_cast<const uint32_t *>(nb)); nw[1] = 0; nw[2] = 0; nw[3] = 0;
+        } else {
+            nw[0] = __ldg(reinterpret_cast<const uint16_t *>(nb)); nw[1] = 0; nw[2] = 0; nw[3] = 0;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            d[i] = make_uint4(0, 0, 0, 0);
+            nw[i] = 0;
+        }
+    }
 }
 
 template <int GB>
@@ -171,7 +276,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const 
     float *xs = invs + s.groups;                                           // [pad]
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t tab_s = (uint32_t)__cvta_generic_to_shared(tab);
     float *wterms = terms + warp * NG * 32;
     const int nsc = s.row_bytes / 64;
     const int npass = (s.row_bytes + kPassPositions - 1) / kPassPositions;
@@ -180,14 +284,18 @@ __global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const 
     const int t_begin = (int)(((long long)p.total_tiles * blockIdx.x) / gridDim.x);
     const int t_end = (int)(((long long)p.total_tiles * (blockIdx.x + 1)) / gridDim.x);
 
+    // The first tile's data streams into L2 while the tables are built.
+    if (lane == 0 && t_begin + warp < t_end) prefetch_tile<NG>(p, t_begin + warp, 0, min(nsc, kPassPositions / 64));
+
     rotate_and_bound(s, p.x, xs, steps, invs);
 
     for (int pass = 0; pass < npass; pass++) {
         const int j0 = pass * kPassPositions;
         const int npos = min(kPassPositions, s.row_bytes - j0);
+        const int sc0 = j0 / 64, nsc_pass = npos / 64;
+        if (pass > 0 && lane == 0 && t_begin + warp < t_end) prefetch_tile<NG>(p, t_begin + warp, sc0, nsc_pass);
         __syncthreads();
         build_pass_tables(s, xs, invs, j0, npos, nib, tab);
-        const int sc0 = j0 / 64, nsc_pass = npos / 64;
 
         int cached_off = -1;
         uint32_t cbw[16];  // colbyte(slot s, half e) at byte 2s+e: 4·o(s) + 2e
@@ -202,6 +310,15 @@ __global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const 
             const bool valid = r < v.out;
             const int R = v.row0 + r;
             const int off = v.row0 & 31;
+
+            // All of the tile's superchunk loads go out before any lookup.
+            uint4 d0[4], d1[4], d2[4], d3[4];
+            uint32_t n0[4], n1[4], n2[4], n3[4];
+            load_superchunk<NG>(v, sc0, R, valid, d0, n0);
+            if (nsc_pass > 1) load_superchunk<NG>(v, sc0 + 1, R, valid, d1, n1);
+            if (nsc_pass > 2) load_superchunk<NG>(v, sc0 + 2, R, valid, d2, n2);
+            if (nsc_pass > 3) load_superchunk<NG>(v, sc0 + 3, R, valid, d3, n3);
+
             if (off != cached_off) {
                 cached_off = off;
                 const int lam = (off + lane) & 31;
@@ -224,64 +341,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const 
             float y = 0.0f;
             if (pass > 0 && valid) y = yk[r];
 
-            for (int scl = 0; scl < nsc_pass; scl++) {
-                const int sc = sc0 + scl;
-                uint4 d[4];
-                uint32_t nw[(NG + 1) / 2];
-                if (valid) {
-                    const uint8_t *base = v.idx + ((size_t)sc * 4 * v.ld + R) * 16;
-#pragma unroll
-                    for (int i = 0; i < 4; i++)
-                        d[i] = __ldg(reinterpret_cast<const uint4 *>(base + (size_t)i * v.ld * 16));
-                    const __half *nb = v.nrm + ((size_t)sc * v.ld + R) * NG;
-                    if constexpr (NG == 8) {
-                        uint4 t4 = __ldg(reinterpret_cast<const uint4 *>(nb));
-                        nw[0] = t4.x; nw[1] = t4.y; nw[2] = t4.z; nw[3] = t4.w;
-                    } else if constexpr (NG == 4) {
-                        uint2 t2 = __ldg(reinterpret_cast<const uint2 *>(nb));
-                        nw[0] = t2.x; nw[1] = t2.y;
-                    } else if constexpr (NG == 2) {
-                        nw[0] = __ldg(reinterpret_cast<const uint32_t *>(nb));
-                    } else {
-                        nw[0] = __ldg(reinterpret_cast<const uint16_t *>(nb));
-                    }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 4; i++) d[i] = make_uint4(0, 0, 0, 0);
-#pragma unroll
-                    for (int i = 0; i < (NG + 1) / 2; i++) nw[i] = 0;
-                }
-                const uint32_t dw[16] = {d[0].x, d[0].y, d[0].z, d[0].w, d[1].x, d[1].y, d[1].z, d[1].w,
-                                         d[2].x, d[2].y, d[2].z, d[2].w, d[3].x, d[3].y, d[3].z, d[3].w};
-                const uint32_t tb = tab_s + (uint32_t)((scl >> 1) * (256 * 128 * 2) + (scl & 1) * 128);
-#pragma unroll
-                for (int q = 0; q < NG; q++) {
-                    int32_t acc = 0;
-#pragma unroll
-                    for (int tt = 0; tt < P; tt++) {
-                        const int slot = P * q + tt;
-                        const uint32_t word = dw[slot >> 1];
-#pragma unroll
-                        for (int e = 0; e < 2; e++) {
-                            const int m = ((2 * slot) & 3) + e;      // byte of the data word
-                            const int kc = (2 * slot + e) & 3;       // byte of the colbyte word
-                            const uint32_t sel = (uint32_t)(4 + kc) | ((uint32_t)m << 4) |
-                                                 ((uint32_t)(12 + kc) << 8) | ((uint32_t)(12 + kc) << 12);
-                            const uint32_t addr = prmt(word, cbw[(2 * slot + e) >> 2], sel);
-                            acc += (int32_t)lds_u16(tb + addr);
-                        }
-                    }
-                    const int32_t sum = acc - (int32_t)(2 * kEntryBias) * GB;
-                    const int gl = (q + a_rot) % NG;        // group within the superchunk
-                    const int g = sc * NG + gl;              // group in the row
-                    const uint32_t nbits = (nw[q >> 1] >> (16 * (q & 1))) & 0xffffu;
-                    const float nrm = __half2float(__ushort_as_half((unsigned short)nbits));
-                    const float coef = __fmul_rn(nrm, steps[g]);
-                    wterms[gl * 32 + lane] = __fmul_rn(__int2float_rn(sum), coef);
-                }
-#pragma unroll
-                for (int gl = 0; gl < NG; gl++) y = __fadd_rn(y, wterms[gl * 32 + lane]);
-            }
+            y = superchunk<GB, 0>(d0, n0, cbw, tab, steps, wterms, lane, a_rot, sc0, y);
+            if (nsc_pass > 1) y = superchunk<GB, 1>(d1, n1, cbw, tab, steps, wterms, lane, a_rot, sc0 + 1, y);
+            if (nsc_pass > 2) y = superchunk<GB, 2>(d2, n2, cbw, tab, steps, wterms, lane, a_rot, sc0 + 2, y);
+            if (nsc_pass > 3) y = superchunk<GB, 3>(d3, n3, cbw, tab, steps, wterms, lane, a_rot, sc0 + 3, y);
             if (valid) yk[r] = y;
         }
     }
