@@ -326,6 +326,7 @@ static bool try_stream(const wc_cq *const *ms, int n, const float *x, float *con
         p->tile_start[used] = tiles;
         p->n = used;
         p->total_tiles = tiles;
+        p->smem_base = stream_smem_base();
         if (used == 0) continue;
         int ctas = tiles < sms ? tiles : sms;
         cudaError_t e = launch_stream(*p, ctas, st);

@@ -33,10 +33,12 @@ struct StreamParams {
     const float *x;   // one activation [in]
     int n;            // matrices
     int total_tiles;  // Σ ceil(out/32)
+    int smem_base;    // stream_smem_base() the launch was sized for
     CqView views[kMaxStreamMats];
     float *y[kMaxStreamMats];
     int tile_start[kMaxStreamMats + 1];
 };
+int stream_smem_base();
 bool stream_eligible(const CqShape &s);
 size_t stream_smem_bytes(const CqShape &s);
 cudaError_t launch_stream(const StreamParams &p, int ctas, cudaStream_t st);

@@ -31,6 +31,8 @@
 // with P = gb/2 byte pairs per group, NG = 32/P groups per superchunk, lane
 // id λ = R mod 32 = P·a + c, and slot s = P·q + t holding the superchunk's
 // byte pair o(s) = P·((q + a) mod NG) + ((t + c) mod P).
+#include <mutex>
+
 #include "common.cuh"
 #include "cq_kernels.cuh"
 
@@ -42,19 +44,25 @@ constexpr int kStreamThreads = 512;
 constexpr int kStreamWarps = kStreamThreads / 32;
 constexpr int kPassPositions = 256;               // byte positions per table pass
 constexpr int kTabBytes = 2 * 256 * 128 * 2;      // two blocks of [256 b][128 j] uint16
+constexpr uint32_t kTabAbs = 65536;               // shared-window address of the byte tables
 constexpr int kNibBytes = 2 * 16 * kPassPositions * 2;  // lo/hi nibble tables [16][256] uint16
 constexpr uint32_t kEntryBias = 8192;             // per nibble entry, so a byte entry carries 16384
 
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+// d = byte permute of {b, a} by an immediate selector.
+template <uint32_t SEL>
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b) {
     uint32_t d;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "n"(SEL));
     return d;
 }
 
-__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
+// A byte-table entry at shared-window address addr + IMM: one LDS, the
+// table's absolute base folded into the immediate.
+template <uint32_t IMM>
+__device__ __forceinline__ int32_t lds_tab(uint32_t addr) {
     uint16_t v;
-    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
-    return v;
+    asm("ld.shared.u16 %0, [%1+%2];" : "=h"(v) : "r"(addr), "n"(IMM));
+    return (int32_t)v;
 }
 
 // Hint: fetch [addr, addr + bytes) into L2 (bytes a multiple of 16, > 0).
@@ -193,11 +201,10 @@ __device__ __forceinline__ void prefetch_tile(const StreamParams &p, int t, int 
 // block and half, so every lookup is one PRMT, one LDS and one IADD.
 template <int GB, int SCL>
 __device__ __forceinline__ float superchunk(const uint4 (&d)[4], const uint32_t (&nw)[4], const uint32_t (&cbw)[16],
-                                            const uint16_t *tab, const float *steps, float *wterms, int lane,
-                                            int a_rot, int sc, float y) {
+                                            const float *steps, float *wterms, int lane, int a_rot, int sc,
+                                            float y) {
     constexpr int P = GB / 2, NG = 32 / P;
-    const unsigned char *tb = reinterpret_cast<const unsigned char *>(tab) + (SCL >> 1) * (256 * 128 * 2) +
-                              (SCL & 1) * 128;
+    constexpr uint32_t TB = kTabAbs + (SCL >> 1) * (256 * 128 * 2) + (SCL & 1) * 128;
     const uint32_t dw[16] = {d[0].x, d[0].y, d[0].z, d[0].w, d[1].x, d[1].y, d[1].z, d[1].w,
                              d[2].x, d[2].y, d[2].z, d[2].w, d[3].x, d[3].y, d[3].z, d[3].w};
 #pragma unroll
@@ -207,19 +214,28 @@ __device__ __forceinline__ float superchunk(const uint4 (&d)[4], const uint32_t 
         for (int tt = 0; tt < P; tt++) {
             const int slot = P * q + tt;
             const uint32_t word = dw[slot >> 1];
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const int m = ((2 * slot) & 3) + e;  // byte of the data word
-                const int kc = (2 * slot + e) & 3;   // byte of the colbyte word
-                const uint32_t sel = (uint32_t)(4 + kc) | ((uint32_t)m << 4) | ((uint32_t)(12 + kc) << 8) |
-                                     ((uint32_t)(12 + kc) << 12);
-                const uint32_t addr = prmt(word, cbw[(2 * slot + e) >> 2], sel);
-                const int32_t v = *reinterpret_cast<const uint16_t *>(tb + addr);
-                if (e == 0)
-                    acc0 += v;
-                else
-                    acc1 += v;
+            // Byte e of the pair is byte m = (2·slot & 3) + e of the data word
+            // and its colbyte is byte kc = (2·slot + e) & 3 of cbw; the
+            // selector puts the colbyte in byte 0, the data byte in byte 1 and
+            // zeros (the colbyte's sign, colbytes < 128) above.
+            // An even slot uses bytes 0 and 1 of both words, an odd one 2 and 3.
+            constexpr uint32_t E0 = 0x4 | (0 << 4) | (0xc << 8) | (0xc << 12);
+            constexpr uint32_t E1 = 0x5 | (1 << 4) | (0xd << 8) | (0xd << 12);
+            constexpr uint32_t O0 = 0x6 | (2 << 4) | (0xe << 8) | (0xe << 12);
+            constexpr uint32_t O1 = 0x7 | (3 << 4) | (0xf << 8) | (0xf << 12);
+            const uint32_t cw = cbw[slot >> 1];
+            int32_t v[2];
+            if (slot & 1) {
+                v[0] = lds_tab<TB>(prmt<O0>(word, cw));
+                v[1] = lds_tab<TB>(prmt<O1>(word, cw));
+            } else {
+                v[0] = lds_tab<TB>(prmt<E0>(word, cw));
+                v[1] = lds_tab<TB>(prmt<E1>(word, cw));
             }
+            if (tt & 1)
+                acc1 += v[0] + v[1];
+            else
+                acc0 += v[0] + v[1];
         }
         const int32_t sum = acc0 + acc1 - (int32_t)(2 * kEntryBias) * GB;
         const int gl = (q + a_rot) & (NG - 1);  // group within the superchunk
@@ -262,20 +278,41 @@ __device__ __forceinline__ void load_superchunk(const CqView &v, int sc, int R, 
     }
 }
 
+// Tile t's matrix, trying k (the previous tile's) first.
+__device__ __forceinline__ int tile_matrix_from(const StreamParams &p, int t, int k) {
+    if (k >= 0 && p.tile_start[k] <= t && t < p.tile_start[k + 1]) return k;
+    return find_tile_matrix(p, t);
+}
+
 template <int GB>
 __global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const __grid_constant__ StreamParams p) {
     constexpr int P = GB / 2;    // byte pairs per group
     constexpr int NG = 32 / P;   // groups per 64-byte superchunk
     extern __shared__ __align__(16) unsigned char smem[];
     const CqShape &s = p.shape;
-    uint16_t *tab = reinterpret_cast<uint16_t *>(smem);                    // kTabBytes
-    uint16_t *nib = reinterpret_cast<uint16_t *>(smem + kTabBytes);        // kNibBytes
-    float *terms = reinterpret_cast<float *>(smem + kTabBytes + kNibBytes);  // [warps][NG][32]
+    // Small buffers from the start of dynamic shared memory, the byte tables
+    // at shared-window address kTabAbs (the host sized the allocation for
+    // the window offset the probe kernel measured).
+    const uint32_t base = (uint32_t)__cvta_generic_to_shared(smem);
+    uint16_t *nib = reinterpret_cast<uint16_t *>(smem);                    // kNibBytes
+    float *terms = reinterpret_cast<float *>(smem + kNibBytes);            // [warps][NG][32]
     float *steps = terms + kStreamWarps * NG * 32;                         // [groups]
     float *invs = steps + s.groups;                                        // [groups]
     float *xs = invs + s.groups;                                           // [pad]
+    uint16_t *tab = reinterpret_cast<uint16_t *>(smem + (kTabAbs - base));  // kTabBytes
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (base != p.smem_base) {
+        // Not the layout the host sized: leave NaN, never a wrong number.
+        const int t_b = (int)(((long long)p.total_tiles * blockIdx.x) / gridDim.x);
+        const int t_e = (int)(((long long)p.total_tiles * (blockIdx.x + 1)) / gridDim.x);
+        for (int t = t_b + warp; t < t_e; t += kStreamWarps) {
+            const int k = find_tile_matrix(p, t);
+            const int r = (t - p.tile_start[k]) * 32 + lane;
+            if (r < p.views[k].out) p.y[k][r] = __int_as_float(0x7fc00000);
+        }
+        return;
+    }
     float *wterms = terms + warp * NG * 32;
     const int nsc = s.row_bytes / 64;
     const int npass = (s.row_bytes + kPassPositions - 1) / kPassPositions;
@@ -303,8 +340,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const 
         for (int w = 0; w < 16; w++) cbw[w] = 0;
         int a_rot = 0;
 
+        int k = -1;
         for (int t = t_begin + warp; t < t_end; t += kStreamWarps) {
-            const int k = find_tile_matrix(p, t);
+            k = tile_matrix_from(p, t, k);
             const CqView v = p.views[k];
             const int r = (t - p.tile_start[k]) * 32 + lane;
             const bool valid = r < v.out;
@@ -341,24 +379,59 @@ __global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const 
             float y = 0.0f;
             if (pass > 0 && valid) y = yk[r];
 
-            y = superchunk<GB, 0>(d0, n0, cbw, tab, steps, wterms, lane, a_rot, sc0, y);
-            if (nsc_pass > 1) y = superchunk<GB, 1>(d1, n1, cbw, tab, steps, wterms, lane, a_rot, sc0 + 1, y);
-            if (nsc_pass > 2) y = superchunk<GB, 2>(d2, n2, cbw, tab, steps, wterms, lane, a_rot, sc0 + 2, y);
-            if (nsc_pass > 3) y = superchunk<GB, 3>(d3, n3, cbw, tab, steps, wterms, lane, a_rot, sc0 + 3, y);
+            y = superchunk<GB, 0>(d0, n0, cbw, steps, wterms, lane, a_rot, sc0, y);
+            if (nsc_pass > 1) y = superchunk<GB, 1>(d1, n1, cbw, steps, wterms, lane, a_rot, sc0 + 1, y);
+            if (nsc_pass > 2) y = superchunk<GB, 2>(d2, n2, cbw, steps, wterms, lane, a_rot, sc0 + 2, y);
+            if (nsc_pass > 3) y = superchunk<GB, 3>(d3, n3, cbw, steps, wterms, lane, a_rot, sc0 + 3, y);
             if (valid) yk[r] = y;
         }
     }
 }
 
+__global__ void smem_base_probe_kernel(int *out) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    *out = (int)__cvta_generic_to_shared(smem);
+}
+
 }  // namespace
+
+// Where dynamic shared memory starts in a CTA's shared window (the stream
+// kernel, like the probe, declares no static shared memory). Measured once
+// per device.
+int stream_smem_base() {
+    static int cached[64];
+    static bool init[64];
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    std::lock_guard<std::mutex> lock(mu);
+    if (init[dev]) return cached[dev];
+    int *d = nullptr, h = -1;
+    if (cudaMalloc(&d, sizeof(int)) != cudaSuccess) return -1;
+    smem_base_probe_kernel<<<1, 1, 16>>>(d);
+    count_launch();
+    if (cudaMemcpy(&h, d, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) h = -1;
+    cudaFree(d);
+    cached[dev] = h;
+    init[dev] = true;
+    return h;
+}
+
+static size_t stream_small_bytes(const CqShape &s) {
+    int ng = 64 / s.gb;
+    return (size_t)kNibBytes + sizeof(float) * ((size_t)kStreamWarps * ng * 32 + 2 * s.groups + s.pad);
+}
 
 bool stream_eligible(const CqShape &s) {
     return (s.gb == 8 || s.gb == 16 || s.gb == 32 || s.gb == 64) && s.row_bytes % 64 == 0 && s.row_bytes >= 64;
 }
 
+// Dynamic shared memory of a launch: the small buffers must end below the
+// tables' absolute address, and the tables end kTabBytes above it.
 size_t stream_smem_bytes(const CqShape &s) {
-    int ng = 64 / s.gb;
-    return (size_t)kTabBytes + kNibBytes + sizeof(float) * ((size_t)kStreamWarps * ng * 32 + 2 * s.groups + s.pad);
+    int b = stream_smem_base();
+    if (b < 0 || (size_t)b + stream_small_bytes(s) > kTabAbs) return (size_t)1 << 30;  // never fits
+    return (size_t)kTabAbs + kTabBytes - (size_t)b;
 }
 
 cudaError_t launch_stream(const StreamParams &p, int ctas, cudaStream_t st) {
