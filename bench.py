@@ -242,6 +242,61 @@ class Shape:
         return pkg._lib.last_error()
 
 
+def attention_component(pkg, torch, lib, stream, streams=256, layers=8, reps=5, flags=3):
+    """one decode step's int8 attention for `streams` streams over
+    `layers` layers, each layer with its own caches (self: 8 query heads over
+    2 KV heads, qk 48, v 64, 224 positions; cross: 8 heads over 375 frames),
+    as two wc_attend_int8_streams launches per layer, in a CUDA graph."""
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(3000)
+    geo = {"self": (8, 2, 48, 64, 224), "cross": (8, 8, 48, 64, 375)}
+    bufs, algo = [], 0
+    for _layer in range(layers):
+        for name, (heads, kvh, qk, vd, cap) in geo.items():
+            k8 = torch.randint(-127, 128, (streams * cap * kvh * qk,), dtype=torch.int8, device=dev)
+            v8 = torch.randint(-127, 128, (streams * cap * kvh * vd,), dtype=torch.int8, device=dev)
+            ks = torch.empty(streams * cap * kvh, device=dev).uniform_(0.01, 0.05)
+            vs = torch.empty(streams * cap * kvh, device=dev).uniform_(0.01, 0.05)
+            q = torch.randn(streams * heads * qk, device=dev)
+            nk = torch.full((streams,), cap, dtype=torch.int32, device=dev)
+            out = torch.empty(streams * heads * vd, device=dev)
+            bufs.append((name, heads, kvh, qk, vd, cap, q, k8, ks, v8, vs, nk, out))
+            algo += streams * (cap * kvh * (qk + vd) + cap * kvh * 8 + heads * qk * 4 + heads * vd * 4)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+
+    def step():
+        for (name, heads, kvh, qk, vd, cap, q, k8, ks, v8, vs, nk, out) in bufs:
+            st = lib.wc_attend_int8_streams(streams, P(q), heads, P(k8), P(ks), P(v8), P(vs), cap, P(nk), kvh, qk,
+                                            vd, float(np.sqrt(qk)), flags, P(out), stream)
+            if st != 0:
+                raise RuntimeError(pkg._lib.last_error())
+
+    s = torch.cuda.Stream()
+    sptr = ctypes.c_void_p(s.cuda_stream)
+    stream = sptr
+    with torch.cuda.stream(s):
+        step()
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s, capture_error_mode="relaxed"):
+            step()
+        g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(reps):
+            g.replay()
+        e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    del g
+    mode = "any-order float sums (1e-5 rel)" if flags & 2 else "exact reference order"
+    return {"workload": f"configs[3]: {streams} streams x {layers} layers, self 8/2 heads qk48 v64 x224 + "
+                        f"cross 8 heads x375 frames, int8 KV, quant_q, {mode}",
+            "gbs": round(algo / (ms / 1e3) / 1e9, 1), "us_per_decode_step": round(ms * 1e3, 2),
+            "attention_tokens_per_s": round(streams / (ms / 1e3), 1), "algorithmic_bytes": algo,
+            "launches": 2 * layers}
+
+
 def run_b200(args, world, rank, local):
     import torch
 
@@ -399,6 +454,9 @@ def run_b200(args, world, rank, local):
     }
     if args.only:
         line["config"]["workload"] = f"one shape {args.only} (profiling run, not the headline workload)"
+    elif not args.no_components:
+        line["components"] = {"int8_attention": attention_component(pkg, torch, lib, None, flags=3),
+                              "int8_attention_exact_order": attention_component(pkg, torch, lib, None, flags=1)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.only:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -418,10 +476,20 @@ def main():
     ap.add_argument("--calls", type=int, default=1000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default="", help="one shape OUTxINxBITS (profiling runs)")
+    ap.add_argument("--no-components", action="store_true", help="skip the attention component")
+    ap.add_argument("--attention-only", action="store_true", help="only the attention component (profiling)")
     args = ap.parse_args()
     world, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, world, rank)
+        return
+    if args.attention_only:
+        import torch
+
+        pkg = __import__("importlib").import_module("go-whistle_b200")
+        torch.cuda.set_device(local)
+        for flags in (3, 1):
+            print(json.dumps(attention_component(pkg, torch, pkg._lib.lib(), None, flags=flags)), flush=True)
         return
     run_b200(args, world, rank, local)
 

@@ -578,10 +578,52 @@ static wc_status attend_smem_ok(const AttendParams &p) {
 }
 
 static bool aligned4(const void *p) { return ((uintptr_t)p & 3u) == 0; }
+static bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+// The any-order kernel when asked for and its shape is supported; else the
+// exact-order v2 kernel when its layout conditions hold and its shared
+// memory fits; else the per-head kernel.
+static wc_status run_attend(AttendParams &p, int streams, cudaStream_t st, bool any_order) {
+    const int gs = p.heads / p.kv_heads;
+    if (any_order && aligned4(p.v8) && aligned16(p.k8) && (p.kv_heads * p.qk) % 16 == 0 &&
+        (p.kv_heads * p.vd) % 4 == 0) {
+        int kvpc = 1;
+        while (kvpc * 2 <= p.kv_heads && p.kv_heads % (kvpc * 2) == 0 && kvpc * 2 * p.vd <= 128 &&
+               kvpc * 2 * gs <= 8)
+            kvpc *= 2;
+        p.kv_per_cta = kvpc;
+        p.v_prefetch = aligned16(p.v8) && (p.kv_heads * p.vd) % 16 == 0 && (kvpc * p.vd) % 16 == 0 && p.vd % 16 == 0;
+        int dev = 0, limit = 0;
+        WB_CUDA(cudaGetDevice(&dev));
+        WB_CUDA(cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+        if (attend_any_supported(p) && attend_any_smem_bytes(p) <= (size_t)limit) {
+            cudaError_t e = launch_attend_any(p, streams, st);
+            return e == cudaSuccess ? WC_OK : cuda_error(e, "attend kernel");
+        }
+    }
+    const bool v2 = p.qk % 16 == 0 && p.vd % 16 == 0 && p.qk <= 128 && aligned16(p.k8) && aligned16(p.v8) &&
+                    (p.kv_heads * p.qk) % 16 == 0 && (p.kv_heads * p.vd) % 16 == 0;
+    if (v2) {
+        int kvpc = 1;
+        while (kvpc * 2 <= p.kv_heads && p.kv_heads % (kvpc * 2) == 0 && kvpc * gs * p.vd < 128) kvpc *= 2;
+        p.kv_per_cta = kvpc;
+        int dev = 0, limit = 0;
+        WB_CUDA(cudaGetDevice(&dev));
+        WB_CUDA(cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+        if (attend_v2_smem_bytes(p) <= (size_t)limit) {
+            cudaError_t e = launch_attend_v2(p, streams, st);
+            return e == cudaSuccess ? WC_OK : cuda_error(e, "attend kernel");
+        }
+    }
+    wc_status ok = attend_smem_ok(p);
+    if (ok != WC_OK) return ok;
+    cudaError_t e = launch_attend(p, streams, st);
+    return e == cudaSuccess ? WC_OK : cuda_error(e, "attend kernel");
+}
 
 extern "C" wc_status wc_attend_int8(const float *q, int t, int heads, const int8_t *k8, const float *ks,
                                     const int8_t *v8, const float *vs, int nkeys, int kv_heads, int qk, int vd,
-                                    const int32_t *spans, float scale, int quant_q, float *probs, float *out,
+                                    const int32_t *spans, float scale, int flags, float *probs, float *out,
                                     wc_stream stream) {
     wc_status st = check_attend(heads, kv_heads, qk, vd, nkeys);
     if (st != WC_OK) return st;
@@ -607,17 +649,14 @@ extern "C" wc_status wc_attend_int8(const float *q, int t, int heads, const int8
     p.cap = nkeys;
     p.max_keys = nkeys;
     p.scale = scale;
-    p.quant_q = quant_q ? 1 : 0;
+    p.quant_q = (flags & WC_ATTEND_QUANT_Q) ? 1 : 0;
     p.k_aligned4 = (qk % 4 == 0) && ((kv_heads * qk) % 4 == 0) && aligned4(k8);
-    st = attend_smem_ok(p);
-    if (st != WC_OK) return st;
-    cudaError_t e = launch_attend(p, 1, (cudaStream_t)stream);
-    return e == cudaSuccess ? WC_OK : cuda_error(e, "attend kernel");
+    return run_attend(p, 1, (cudaStream_t)stream, (flags & WC_ATTEND_ANY_ORDER) != 0);
 }
 
 extern "C" wc_status wc_attend_int8_streams(int streams, const float *q, int heads, const int8_t *k8, const float *ks,
                                             const int8_t *v8, const float *vs, int cap, const int32_t *nkeys,
-                                            int kv_heads, int qk, int vd, float scale, int quant_q, float *out,
+                                            int kv_heads, int qk, int vd, float scale, int flags, float *out,
                                             wc_stream stream) {
     wc_status st = check_attend(heads, kv_heads, qk, vd, cap);
     if (st != WC_OK) return st;
@@ -643,10 +682,7 @@ extern "C" wc_status wc_attend_int8_streams(int streams, const float *q, int hea
     p.cap = cap;
     p.max_keys = cap;
     p.scale = scale;
-    p.quant_q = quant_q ? 1 : 0;
+    p.quant_q = (flags & WC_ATTEND_QUANT_Q) ? 1 : 0;
     p.k_aligned4 = (qk % 4 == 0) && ((kv_heads * qk) % 4 == 0) && aligned4(k8);
-    st = attend_smem_ok(p);
-    if (st != WC_OK) return st;
-    cudaError_t e = launch_attend(p, streams, (cudaStream_t)stream);
-    return e == cudaSuccess ? WC_OK : cuda_error(e, "attend kernel");
+    return run_attend(p, streams, (cudaStream_t)stream, (flags & WC_ATTEND_ANY_ORDER) != 0);
 }

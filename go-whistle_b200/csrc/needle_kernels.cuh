@@ -23,10 +23,17 @@ struct AttendParams {
     float scale;
     int quant_q;
     int k_aligned4;  // k8 rows and q8 readable as int32 words
+    int kv_per_cta;  // v2 and any-order: KV heads per CTA
+    int v_prefetch;  // any-order: V row slices are 16-byte aligned (L2 prefetch)
 };
 
 cudaError_t launch_quantize_rows(const float *x, int chunks, int width, int8_t *q, float *s, cudaStream_t st);
 size_t attend_smem_bytes(const AttendParams &p);
 cudaError_t launch_attend(const AttendParams &p, int streams, cudaStream_t st);
+size_t attend_any_smem_bytes(const AttendParams &p);
+bool attend_any_supported(const AttendParams &p);
+cudaError_t launch_attend_any(const AttendParams &p, int streams, cudaStream_t st);
+size_t attend_v2_smem_bytes(const AttendParams &p);
+cudaError_t launch_attend_v2(const AttendParams &p, int streams, cudaStream_t st);
 
 }  // namespace wb

@@ -139,6 +139,17 @@ wc_status wc_cq_row_host(const wc_cq *h, int r, float *dst, size_t dst_len);
 
 /* ------------------------------------------------------------ needle ---- */
 
+/* Flags of the attention entry points. */
+enum {
+    /* Quantise each query head to int8 first (Int8.Act): exact int32 logits. */
+    WC_ATTEND_QUANT_Q = 1,
+    /* Let the float sums (softmax sum, the weighted sum of the values) run in
+     * any order, with FMAs and expf: several times the throughput, results
+     * within 1e-5 relative of the exact order. Without it the reference's
+     * generic order is followed operation by operation. */
+    WC_ATTEND_ANY_ORDER = 2,
+};
+
 /*
  * internal/needle/int8.go:115 QuantizeRows (and :125 Int8Rows.Append when q
  * and s point at a cache's tail): x [rows][cols] fp32 in chunks of width,
@@ -160,14 +171,15 @@ wc_status wc_quantize_rows_host(const float *x, size_t x_len, int cols, int widt
  *          ranges per query row
  *   probs  [t][heads][nkeys] fp32 or NULL; written at span keys only
  *   out    [t][heads][vd] fp32
- * Query head h reads KV head h / (heads / kv_heads). quant_q != 0 quantises
- * each query head to int8 first (Int8.Act), making the logits exact int32
- * dot products. The result equals the reference's generic (purego) path bit
- * for bit up to the last-bit rounding of exp noted in DESIGN.md.
+ * Query head h reads KV head h / (heads / kv_heads). flags: WC_ATTEND_QUANT_Q
+ * quantises each query head to int8 first (Int8.Act), making the logits
+ * exact int32 dot products; without WC_ATTEND_ANY_ORDER the result equals
+ * the reference's generic (purego) path bit for bit, up to the last-bit
+ * rounding of exp noted in DESIGN.md.
  */
 wc_status wc_attend_int8(const float *q, int t, int heads, const int8_t *k8, const float *ks, const int8_t *v8,
                          const float *vs, int nkeys, int kv_heads, int qk, int vd, const int32_t *spans, float scale,
-                         int quant_q, float *probs, float *out, wc_stream stream);
+                         int flags, float *probs, float *out, wc_stream stream);
 
 /*
  * The decode step of `streams` independent streams, one query row each,
@@ -180,7 +192,7 @@ wc_status wc_attend_int8(const float *q, int t, int heads, const int8_t *k8, con
  */
 wc_status wc_attend_int8_streams(int streams, const float *q, int heads, const int8_t *k8, const float *ks,
                                  const int8_t *v8, const float *vs, int cap, const int32_t *nkeys, int kv_heads,
-                                 int qk, int vd, float scale, int quant_q, float *out, wc_stream stream);
+                                 int qk, int vd, float scale, int flags, float *out, wc_stream stream);
 
 #ifdef __cplusplus
 }

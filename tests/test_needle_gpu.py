@@ -137,3 +137,64 @@ def test_attend_streams(wb, orc, cuda, geom):
     wb._lib.check(wb._lib.lib().wc_attend_int8_streams(streams, dp(qd), heads, dp(k8d), dp(ksd), dp(v8d), dp(vsd),
                                                        cap, dp(nkd), kvh, qk, vd, float(scale), 1, dp(out), None))
     assert bits_eq(out.cpu().numpy(), want)
+
+
+WC_ATTEND_QUANT_Q, WC_ATTEND_ANY_ORDER = 1, 2
+# The north star's tolerance for the float results of the attention: the
+# any-order kernel (float sums reordered, FMA, expf) must stay within 1e-5
+# relative of the reference's order; the integer work (query codes, int32
+# logits) is exact either way.
+ANY_ORDER_RTOL = 1e-5
+
+
+@pytest.mark.parametrize("geom", GEOMS, ids=[f"h{g[0]}kv{g[1]}qk{g[2]}v{g[3]}n{g[4]}" for g in GEOMS])
+@pytest.mark.parametrize("quant_q", [True, False])
+def test_attend_any_order_within_tolerance(wb, orc, cuda, geom, quant_q):
+    heads, kvh, qk, vd, n = geom
+    rng = np.random.default_rng(7 * sum(geom) + quant_q)
+    rows = 3 if n >= 3 else 1
+    q = rng.normal(size=rows * heads * qk).astype(np.float32)
+    k8, ks = kv(wb, orc, rng, n, kvh, qk)
+    v8, vs = kv(wb, orc, rng, n, kvh, vd, False)
+    scale = np.float32(np.sqrt(qk))
+    spans = np.array([[0, min(2, n), max(min(2, n), n - 5 - i), n - rows + i + 1] for i in range(rows)], np.int32)
+    spans[:, 2] = np.minimum(spans[:, 2], spans[:, 3])
+    want, wprobs = orc.attend_int8_spans(q, rows, heads, k8, ks, v8, vs, n, kvh, qk, vd, spans, scale, quant_q,
+                                         want_probs=True)
+    D = lambda a: cuda.from_numpy(np.ascontiguousarray(a)).cuda()
+    qd, k8d, ksd, v8d, vsd, spd = D(q), D(k8), D(ks), D(v8), D(vs), D(spans.reshape(-1))
+    out = cuda.zeros(rows * heads * vd, dtype=cuda.float32, device="cuda")
+    probs = cuda.zeros(rows * heads * n, dtype=cuda.float32, device="cuda")
+    flags = WC_ATTEND_ANY_ORDER | (WC_ATTEND_QUANT_Q if quant_q else 0)
+    wb._lib.check(wb._lib.lib().wc_attend_int8(dp(qd), rows, heads, dp(k8d), dp(ksd), dp(v8d), dp(vsd), n, kvh, qk,
+                                               vd, dp(spd), float(scale), flags, dp(probs), dp(out), None))
+    got = out.cpu().numpy().reshape(rows * heads, vd)
+    want = want.reshape(rows * heads, vd)
+    scale_row = np.maximum(np.abs(want).max(axis=1, keepdims=True), 1e-30)
+    assert np.all(np.abs(got - want) <= ANY_ORDER_RTOL * scale_row)
+    gp = probs.cpu().numpy()
+    assert np.all(np.abs(gp - wprobs) <= ANY_ORDER_RTOL * np.maximum(np.abs(wprobs), 1e-3))
+
+
+@pytest.mark.parametrize("geom", [(8, 2, 48, 64, 224), (8, 8, 48, 64, 375), (8, 8, 64, 64, 224)])
+def test_attend_streams_any_order(wb, orc, cuda, geom):
+    heads, kvh, qk, vd, cap = geom
+    streams = 64
+    rng = np.random.default_rng(cap + 1)
+    nk = rng.integers(1, cap + 1, streams).astype(np.int32)
+    nk[0], nk[1] = cap, 1
+    q = rng.normal(size=streams * heads * qk).astype(np.float32)
+    k8, ks = wb.synth.random_kv(rng, streams * cap, kvh, qk)
+    v8, vs = wb.synth.random_kv(rng, streams * cap, kvh, vd)
+    scale = np.float32(np.sqrt(qk))
+    want = orc.attend_streams(q, heads, k8, ks, v8, vs, cap, nk, kvh, qk, vd, scale, threads=8)
+    D = lambda a: cuda.from_numpy(np.ascontiguousarray(a)).cuda()
+    qd, k8d, ksd, v8d, vsd, nkd = D(q), D(k8), D(ks), D(v8), D(vs), D(nk)
+    out = cuda.zeros(streams * heads * vd, dtype=cuda.float32, device="cuda")
+    wb._lib.check(wb._lib.lib().wc_attend_int8_streams(streams, dp(qd), heads, dp(k8d), dp(ksd), dp(v8d), dp(vsd),
+                                                       cap, dp(nkd), kvh, qk, vd, float(scale),
+                                                       WC_ATTEND_QUANT_Q | WC_ATTEND_ANY_ORDER, dp(out), None))
+    got = out.cpu().numpy().reshape(-1, vd)
+    want = want.reshape(-1, vd)
+    scale_row = np.maximum(np.abs(want).max(axis=1, keepdims=True), 1e-30)
+    assert np.all(np.abs(got - want) <= ANY_ORDER_RTOL * scale_row)
