@@ -11,6 +11,7 @@
 
 #include <atomic>
 #include <cmath>
+#include <mutex>
 #include <memory>
 #include <new>
 #include <string>
@@ -71,11 +72,28 @@ struct CqStorage {
     }
 };
 
+// A view's bf16 weight image for the tensor-core GEMM, built on first use.
+struct TcImage {
+    std::mutex mu;
+    unsigned char *b = nullptr;
+    size_t bytes = 0;
+    int device = 0;
+    ~TcImage() {
+        if (!b) return;
+        int cur = 0;
+        cudaGetDevice(&cur);
+        if (cur != device) cudaSetDevice(device);
+        cudaFree(b);
+        if (cur != device) cudaSetDevice(cur);
+    }
+};
+
 struct wc_cq {
     std::shared_ptr<CqStorage> st;
     CqShape shape;
     int out = 0, row0 = 0, ld = 0;
     bool exact = false;
+    std::shared_ptr<TcImage> tc = std::make_shared<TcImage>();  // per view, not shared with copies
 
     CqView view() const { return CqView{st->idx, st->nrm, out, row0, ld}; }
     CqView stream_view() const { return CqView{st->sidx, st->snrm, out, row0, ld}; }
@@ -248,6 +266,7 @@ extern "C" wc_status wc_cq_rows(const wc_cq *h, int lo, int hi, wc_cq **view) {
     if (!v) return set_error(WC_ERR_NOMEM, "cq: out of host memory");
     v->out = hi - lo;
     v->row0 = h->row0 + lo;
+    v->tc = std::make_shared<TcImage>();
     *view = v;
     return WC_OK;
 }
@@ -260,6 +279,7 @@ extern "C" wc_status wc_cq_exact(const wc_cq *h, wc_cq **view) {
     wc_cq *v = new (std::nothrow) wc_cq(*h);
     if (!v) return set_error(WC_ERR_NOMEM, "cq: out of host memory");
     v->exact = true;
+    v->tc = std::make_shared<TcImage>();
     *view = v;
     return WC_OK;
 }
@@ -526,6 +546,94 @@ extern "C" wc_status wc_cq_row_host(const wc_cq *h, int r, float *dst, size_t ds
     if (st != WC_OK) return st;
     WB_CUDA(cudaMemcpy(dst, d, dst_len * sizeof(float), cudaMemcpyDeviceToHost));
     return WC_OK;
+}
+
+// ------------------------------------------------------- tensor cores ----
+
+// The per-device error word of the kernels' bounded waits.
+static int *device_err_word() {
+    static int *words[64];
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!words[dev]) {
+        if (cudaMalloc(&words[dev], sizeof(int)) != cudaSuccess) return nullptr;
+        if (cudaMemset(words[dev], 0, sizeof(int)) != cudaSuccess) return nullptr;
+    }
+    return words[dev];
+}
+
+extern "C" wc_status wc_device_status(int *code) {
+    if (!code) return set_error(WC_ERR_INVALID, "nil code pointer");
+    *code = 0;
+    WB_CUDA(cudaDeviceSynchronize());
+    int *w = device_err_word();
+    if (!w) return set_error(WC_ERR_NOMEM, "cuda: error word");
+    WB_CUDA(cudaMemcpy(code, w, sizeof(int), cudaMemcpyDeviceToHost));
+    WB_CUDA(cudaMemset(w, 0, sizeof(int)));
+    return WC_OK;
+}
+
+static wc_status tc_supported(const wc_cq *h) {
+    if (h->shape.group > 256)
+        return set_error(WC_ERR_UNSUPPORTED, fmt("cq: tensor-core GEMM of group %d (at most 256)", h->shape.group));
+    int dev = 0, limit = 0;
+    WB_CUDA(cudaGetDevice(&dev));
+    WB_CUDA(cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    if (tc_smem_bytes() > (size_t)limit) return set_error(WC_ERR_UNSUPPORTED, "cq: tensor-core GEMM shared memory");
+    return WC_OK;
+}
+
+extern "C" wc_status wc_cq_prepare_tc(const wc_cq *h) {
+    if (!h) return set_error(WC_ERR_INVALID, "cq: nil matrix");
+    wc_status st = check_device(h);
+    if (st != WC_OK) return st;
+    if ((st = tc_supported(h)) != WC_OK) return st;
+    std::lock_guard<std::mutex> lock(h->tc->mu);
+    if (h->tc->b || h->out == 0) return WC_OK;
+    const int kchunks = tc_kchunks(h->shape);
+    const size_t bytes = tc_b_bytes(h->out, kchunks);
+    unsigned char *b = nullptr;
+    WB_CUDA(cudaMalloc(&b, bytes));
+    cudaError_t e = launch_dequant_bf16(h->shape, h->view(), b, nullptr);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaFree(b);
+        return cuda_error(e, "cq dequant kernel");
+    }
+    h->tc->b = b;
+    h->tc->bytes = bytes;
+    WB_CUDA(cudaGetDevice(&h->tc->device));
+    return WC_OK;
+}
+
+extern "C" wc_status wc_cq_gemm_ex(const wc_cq *h, const float *x, float *y, int rows, int flags, wc_stream stream) {
+    if (!(flags & WC_GEMM_TENSOR_CORES)) return wc_cq_gemm(h, x, y, rows, stream);
+    if (!h) return set_error(WC_ERR_INVALID, "cq: nil matrix");
+    if (rows < 0) return set_error(WC_ERR_INVALID, fmt("cq: GEMM of %d rows on [%d, %d]", rows, h->out, h->shape.in));
+    if (rows == 0 || h->out == 0) return WC_OK;
+    wc_status st = wc_cq_prepare_tc(h);
+    if (st != WC_OK) return st;
+    const int kchunks = tc_kchunks(h->shape);
+    void *a = nullptr;
+    WB_CUDA(t_scratch.get(3, tc_a_bytes(rows, kchunks), &a));
+    int *err = device_err_word();
+    if (!err) return set_error(WC_ERR_NOMEM, "cuda: error word");
+    cudaStream_t s = (cudaStream_t)stream;
+    cudaError_t e = launch_rotate_bf16(h->shape, x, rows, (unsigned char *)a, s);
+    if (e != cudaSuccess) return cuda_error(e, "cq rotate kernel");
+    TcParams p{};
+    p.a = (const unsigned char *)a;
+    p.b = h->tc->b;
+    p.y = y;
+    p.m = rows;
+    p.n = h->out;
+    p.ldy = h->out;
+    p.kchunks = kchunks;
+    p.err = err;
+    e = launch_gemm_tc(p, s);
+    return e == cudaSuccess ? WC_OK : cuda_error(e, "cq tensor-core kernel");
 }
 
 // ------------------------------------------------------------- needle ----

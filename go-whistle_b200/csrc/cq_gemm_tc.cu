@@ -1,0 +1,357 @@
+// cq_gemm_tc.cu — the batched CQ GEMM on the 5th-generation tensor cores
+// (tcgen05, TMEM accumulators), for encoder prefill and many-row decode.
+//
+// The product is taken in the rotated domain, where a CQ matrix needs no
+// Hadamard transform (internal/cq/matrix.go:1-13):
+//   y[m, r] = Σ_k x̂[m, k] · ŵ[r, k],   x̂_g = H·x_g,   ŵ[r, k] = cb[idx[r,k]]·n[r,g]/√G
+// Both operands go to bf16 (x̂ per activation by `rotate_bf16_kernel`, ŵ once
+// per matrix by `dequant_bf16_kernel`) and the tensor cores accumulate in
+// fp32. This is not the reference's lut arithmetic, so it is not bit-exact:
+// every element is within the bf16 bound stated in tests/test_gemm_tc_gpu.py
+// of the float64 product. It is only used when asked for
+// (wc_cq_gemm_ex with WC_GEMM_TENSOR_CORES).
+//
+// Operand images in global memory are pre-swizzled 128 x 64 bf16 tiles
+// (K-major, 128-byte swizzle: 16-byte chunk c of row r at chunk c ^ (r & 7)),
+// so a stage of the main loop is two 1-D bulk copies (cp.async.bulk, no
+// tensor map, no multicast). One CTA computes a 128 x 128 tile of y:
+//   warp 0 lane 0   producer: bulk copies of the A and B chunks per stage
+//   warp 1          TMEM allocation; lane 0 issues the MMAs (K = 16 each)
+//   warps 2-5       epilogue: TMEM -> registers -> y (fp32)
+// Every wait on an mbarrier is bounded; on timeout the CTA records an error
+// code, skips its remaining work, frees its TMEM and returns.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "cq_kernels.cuh"
+
+namespace wb {
+
+namespace {
+
+constexpr int kTcM = 128;         // UMMA M (cta_group::1)
+constexpr int kTcN = 128;         // UMMA N, TMEM columns
+constexpr int kTcK = 64;          // bf16 elements per 128-byte row of a chunk
+constexpr int kStages = 4;
+constexpr int kChunkBytes = kTcM * 128;  // one 128 x 64 bf16 tile, A and B alike
+constexpr int kTcThreads = 192;
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// Bounded wait for the phase with the given parity; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    for (uint32_t it = 0; it < kSpinLimit; it++) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms
+// 1024 bytes apart (SBO), version 1 (sm_100).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor: D f32, A and B bf16, both K-major, N = kTcN, M = kTcM.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcN >> 3) << 17) |
+                            ((uint32_t)(kTcM >> 4) << 24);
+
+__device__ __forceinline__ void umma_bf16(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(dtmem),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Byte offset of element (row, k) of a 128 x 64 bf16 swizzled chunk.
+__device__ __forceinline__ uint32_t swz(int row, int k) {
+    return (uint32_t)row * 128u + ((uint32_t)(((k >> 3) ^ (row & 7)) & 7) << 4) + (uint32_t)(k & 7) * 2u;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) cq_gemm_tc_kernel(const __grid_constant__ TcParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // 1024-byte alignment for the swizzle atoms.
+    unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    unsigned char *sa = smem;                                  // [kStages][kChunkBytes]
+    unsigned char *sb = smem + kStages * kChunkBytes;          // [kStages][kChunkBytes]
+    uint64_t *full = reinterpret_cast<uint64_t *>(sb + kStages * kChunkBytes);
+    uint64_t *empty = full + kStages;
+    uint64_t *done = empty + kStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    int *bail = reinterpret_cast<int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nt = blockIdx.x, mt = blockIdx.y;
+    const int kchunks = p.kchunks;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        *bail = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"((uint32_t)kTcN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    const unsigned char *ga = p.a + (size_t)mt * kchunks * kChunkBytes;
+    const unsigned char *gb = p.b + (size_t)nt * kchunks * kChunkBytes;
+
+    if (warp == 0 && lane == 0) {
+        // Producer.
+        for (int kc = 0; kc < kchunks; kc++) {
+            const int s = kc % kStages, round = kc / kStages;
+            if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
+                atomicExch(p.err, 1);
+                atomicExch(bail, 1);
+                break;
+            }
+            mbar_expect_tx(&full[s], 2 * kChunkBytes);
+            bulk_g2s(sa + s * kChunkBytes, ga + (size_t)kc * kChunkBytes, kChunkBytes, &full[s]);
+            bulk_g2s(sb + s * kChunkBytes, gb + (size_t)kc * kChunkBytes, kChunkBytes, &full[s]);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer.
+        bool ok = true;
+        for (int kc = 0; kc < kchunks && ok; kc++) {
+            const int s = kc % kStages, round = kc / kStages;
+            if (!mbar_wait(&full[s], round & 1)) {
+                atomicExch(p.err, 2);
+                atomicExch(bail, 1);
+                ok = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a0 = smem_u32(sa + s * kChunkBytes), b0 = smem_u32(sb + s * kChunkBytes);
+#pragma unroll
+            for (int k = 0; k < kTcK / 16; k++)
+                umma_bf16(tmem, umma_desc(a0 + 32 * k), umma_desc(b0 + 32 * k), (kc > 0 || k > 0) ? 1u : 0u);
+            umma_commit(&empty[s]);
+        }
+        umma_commit(done);
+    } else if (warp >= 2) {
+        // Epilogue: warp w reads TMEM lanes 32·(w mod 4) .. +31.
+        const int part = warp & 3;
+        bool ok = mbar_wait(done, 0);
+        if (!ok) {
+            atomicExch(p.err, 3);
+            atomicExch(bail, 1);
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        ok = __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int *>(bail) == 0);
+        if (ok) {
+            const int row = mt * kTcM + part * 32 + lane;
+#pragma unroll 1
+            for (int c = 0; c < kTcN; c += 32) {
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t)(part * 32) << 16) + (uint32_t)c, r);
+                const int col = nt * kTcN + c;
+                if (row < p.m && col < p.n) {
+                    float *y = p.y + (size_t)row * p.ldy + col;
+                    if (col + 32 <= p.n && (p.ldy & 3) == 0 && (((uintptr_t)y) & 15) == 0) {
+#pragma unroll
+                        for (int q = 0; q < 8; q++)
+                            reinterpret_cast<float4 *>(y)[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                                                          __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < 32; q++)
+                            if (col + q < p.n) y[q] = __uint_as_float(r[q]);
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kTcN)
+                     : "memory");
+    }
+}
+
+// x̂ = H·x per group of G (no 1/√G: it is in ŵ), bf16, into the swizzled
+// image [m_tile][kc][128 rows][128 B]; rows past m and columns past In are
+// zero. One warp per (row, group): lanes hold E = G/32 elements (G >= 32)
+// or 32/G groups share a warp (G < 32); the butterflies are fwht's.
+__global__ void rotate_bf16_kernel(const float *__restrict__ x, int m, int in, int G, int groups, int kchunks,
+                                   int mtiles, unsigned char *__restrict__ a) {
+    const int lane = threadIdx.x & 31;
+    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // global warp
+    const int E = G >= 32 ? G / 32 : 1;
+    const int L = G >= 32 ? 32 : G;        // lanes per group
+    const int gpw = 32 / L;                // groups per warp
+    const int units = mtiles * kTcM * ((groups + gpw - 1) / gpw);
+    if (gw >= units) return;
+    const int gpr = (groups + gpw - 1) / gpw;
+    const int row = gw / gpr, g = (gw % gpr) * gpw + lane / L;
+    const int lig = lane % L;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        v[e] = 0.0f;
+        if (e < E && g < groups && row < m) {
+            const int k = g * G + lig * E + e;
+            if (k < in) v[e] = x[(size_t)row * in + k];
+        }
+    }
+    for (int h = 1; h < G; h <<= 1) {
+        if (h < E) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                if (e < E && (e & h) == 0) {
+                    const float a0 = v[e], b0 = v[e + h];
+                    v[e] = a0 + b0;
+                    v[e + h] = a0 - b0;
+                }
+            }
+        } else {
+            const int pl = h / E;
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const float o = __shfl_xor_sync(0xffffffffu, v[e], pl);
+                v[e] = (lig & pl) ? o - v[e] : v[e] + o;
+            }
+        }
+    }
+    if (g >= groups) return;
+    const int mtile = row / kTcM, r = row % kTcM;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        if (e < E) {
+            const int k = g * G + lig * E + e;
+            const int kc = k / kTcK;
+            unsigned char *base = a + ((size_t)mtile * kchunks + kc) * kChunkBytes;
+            *reinterpret_cast<__nv_bfloat16 *>(base + swz(r, k % kTcK)) = __float2bfloat16_rn(v[e]);
+        }
+    }
+}
+
+// ŵ[r, k] = cb[idx]·n[r, g]·(1/√G) in bf16, swizzled [n_tile][kc][128][128 B];
+// rows past Out are zero. One thread per (row, 8 columns).
+__global__ void dequant_bf16_kernel(const __grid_constant__ CqShape s, const CqView v, int ntiles, int kchunks,
+                                    unsigned char *__restrict__ b) {
+    const int units = ntiles * kTcN * (kchunks * kTcK / 8);
+    const int u = blockIdx.x * blockDim.x + threadIdx.x;
+    if (u >= units) return;
+    const int per_row = kchunks * kTcK / 8;
+    const int row = u / per_row, k0 = (u % per_row) * 8;
+    const int ntile = row / kTcN, r = row % kTcN, kc = k0 / kTcK;
+    __align__(16) __nv_bfloat16 out[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        const int k = k0 + e;
+        float w = 0.0f;
+        if (row < v.out && k < s.pad) {
+            const int g = k / s.group, kin = k % s.group;
+            const size_t lrow = (size_t)g * v.ld + (size_t)(v.row0 + row);
+            const int bit = kin * s.bits;
+            const uint32_t code = (v.idx[lrow * s.gb + (bit >> 3)] >> (bit & 7)) & ((1u << s.bits) - 1u);
+            w = s.cb[code] * __half2float(v.nrm[lrow]) * s.inv_sqrt;
+        }
+        out[e] = __float2bfloat16_rn(w);
+    }
+    unsigned char *base = b + ((size_t)ntile * kchunks + kc) * kChunkBytes;
+    *reinterpret_cast<uint4 *>(base + swz(r, k0 % kTcK)) = *reinterpret_cast<const uint4 *>(out);
+}
+
+}  // namespace
+
+size_t tc_a_bytes(int m, int kchunks) { return (size_t)((m + kTcM - 1) / kTcM) * kchunks * kChunkBytes; }
+size_t tc_b_bytes(int n, int kchunks) { return (size_t)((n + kTcN - 1) / kTcN) * kchunks * kChunkBytes; }
+int tc_kchunks(const CqShape &s) { return (s.pad + kTcK - 1) / kTcK; }
+
+cudaError_t launch_dequant_bf16(const CqShape &s, const CqView &v, unsigned char *b, cudaStream_t st) {
+    const int kchunks = tc_kchunks(s), ntiles = (v.out + kTcN - 1) / kTcN;
+    const long units = (long)ntiles * kTcN * (kchunks * kTcK / 8);
+    if (units == 0) return cudaSuccess;
+    dequant_bf16_kernel<<<(int)((units + 255) / 256), 256, 0, st>>>(s, v, ntiles, kchunks, b);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rotate_bf16(const CqShape &s, const float *x, int m, unsigned char *a, cudaStream_t st) {
+    const int kchunks = tc_kchunks(s), mtiles = (m + kTcM - 1) / kTcM;
+    const int L = s.group >= 32 ? 32 : s.group, gpw = 32 / L;
+    const long warps = (long)mtiles * kTcM * ((s.groups + gpw - 1) / gpw);
+    if (warps == 0) return cudaSuccess;
+    // Padding columns past groups·G within the last chunk stay zero.
+    if (s.pad % kTcK != 0) {
+        cudaError_t e = cudaMemsetAsync(a, 0, tc_a_bytes(m, kchunks), st);
+        if (e != cudaSuccess) return e;
+    }
+    rotate_bf16_kernel<<<(int)((warps + 7) / 8), 256, 0, st>>>(x, m, s.in, s.group, s.groups, kchunks, mtiles, a);
+    count_launch();
+    return cudaGetLastError();
+}
+
+size_t tc_smem_bytes() { return 1024 + 2 * kStages * kChunkBytes + 8 * (2 * kStages + 1) + 16; }
+
+cudaError_t launch_gemm_tc(const TcParams &p, cudaStream_t st) {
+    const size_t smem = tc_smem_bytes();
+    cudaError_t e = cudaFuncSetAttribute(cq_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((p.n + kTcN - 1) / kTcN, (p.m + kTcM - 1) / kTcM);
+    cq_gemm_tc_kernel<<<grid, kTcThreads, smem, st>>>(p);
+    count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace wb

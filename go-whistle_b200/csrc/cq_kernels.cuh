@@ -38,6 +38,23 @@ struct StreamParams {
     float *y[kMaxStreamMats];
     int tile_start[kMaxStreamMats + 1];
 };
+// The tensor-core GEMM (cq_gemm_tc.cu): operand images are pre-swizzled
+// 128 x 64 bf16 tiles.
+struct TcParams {
+    const unsigned char *a;  // x̂ image [m_tiles][kchunks][128][128 B]
+    const unsigned char *b;  // ŵ image [n_tiles][kchunks][128][128 B]
+    float *y;                // [m][ldy] fp32
+    int m, n, ldy, kchunks;
+    int *err;                // device error word (bounded waits)
+};
+int tc_kchunks(const CqShape &s);
+size_t tc_a_bytes(int m, int kchunks);
+size_t tc_b_bytes(int n, int kchunks);
+size_t tc_smem_bytes();
+cudaError_t launch_dequant_bf16(const CqShape &s, const CqView &v, unsigned char *b, cudaStream_t st);
+cudaError_t launch_rotate_bf16(const CqShape &s, const float *x, int m, unsigned char *a, cudaStream_t st);
+cudaError_t launch_gemm_tc(const TcParams &p, cudaStream_t st);
+
 int stream_smem_base();
 bool stream_eligible(const CqShape &s);
 size_t stream_smem_bytes(const CqShape &s);

@@ -106,6 +106,32 @@ size_t wc_cq_bytes(const wc_cq *h);
  */
 wc_status wc_cq_gemm(const wc_cq *h, const float *x, float *y, int rows, wc_stream stream);
 
+/* Flags of wc_cq_gemm_ex. */
+enum {
+    /* Run the product on the tensor cores (tcgen05, bf16 operands in the
+     * rotated domain, fp32 accumulation) instead of the bit-exact lut
+     * kernel: for many rows (encoder prefill, batched decode). Each output
+     * is within the bf16 bound DESIGN.md states; not bit-exact. */
+    WC_GEMM_TENSOR_CORES = 1,
+};
+
+/*
+ * wc_cq_gemm with options (flags above). With WC_GEMM_TENSOR_CORES the first
+ * call on a matrix builds its bf16 weight image on the device (or call
+ * wc_cq_prepare_tc first, outside any stream capture), and each call uses a
+ * per-thread device buffer for the rotated activations, grown on demand.
+ * No reference counterpart: the reference has only the exact kernels.
+ */
+wc_status wc_cq_gemm_ex(const wc_cq *h, const float *x, float *y, int rows, int flags, wc_stream stream);
+
+/* Builds the tensor-core weight image of h now (synchronous). */
+wc_status wc_cq_prepare_tc(const wc_cq *h);
+
+/* Synchronises the current device and reports (and clears) the error word
+ * of the kernels' bounded waits: *code = 0 if none expired. A diagnostic
+ * with no reference counterpart. */
+wc_status wc_device_status(int *code);
+
 /* GEMM on HOST slices with the reference's length check and panic text
  * (kernel.go:105-107): x_len = len(x), y_len = len(dst). Synchronous. */
 wc_status wc_cq_gemm_host(const wc_cq *h, const float *x, size_t x_len, float *y, size_t y_len, int rows);

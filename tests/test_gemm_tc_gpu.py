@@ -1,0 +1,91 @@
+"""The tensor-core CQ GEMM (wc_cq_gemm_ex with WC_GEMM_TENSOR_CORES).
+
+It multiplies in the rotated domain with bf16 operands and fp32
+accumulation, so it is checked against the float64 product of the
+reference's dequantisation (internal/cq/cq_test.go:70 dequant64) under the
+bf16 bound this repository states for it: per element
+
+    |y - y64| <= (2^-7 + (K + log2 G + 4) · 2^-24) · Σ_k |x̂_k| · |ŵ_k|
+
+(x̂ = H·x per group, ŵ = cb[idx]·n/√G; 2^-7 covers the bf16 rounding of both
+operands, the second term the fp32 rotation, scaling and accumulation), and
+by cosine >= 0.9999 per row.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+import refmath
+
+pytestmark = pytest.mark.gpu
+
+WC_GEMM_TENSOR_CORES = 1
+
+
+def rotated_operands(p, x):
+    """x̂ (float64, per group, unscaled) and ŵ (float64) of the rotated product."""
+    G = p.group
+    groups = (p.in_ + G - 1) // G
+    rows = x.shape[0]
+    xp = np.zeros((rows, groups * G))
+    xp[:, : p.in_] = x
+    h = refmath.sylvester(G)
+    xh = np.einsum("jk,rgk->rgj", h, xp.reshape(rows, groups, G)).reshape(rows, groups * G)
+    cb = np.asarray(p.codebook, np.float64)
+    w = cb[refmath.unpack(p)].reshape(p.out, groups, G) * refmath.norms(p)[:, :, None] / np.sqrt(G)
+    return xh, w.reshape(p.out, groups * G)
+
+
+def tc_gemm(wb, cuda, m, x):
+    rows = x.shape[0]
+    xd = cuda.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    yd = cuda.full((rows, m.Out()), float("nan"), dtype=cuda.float32, device="cuda")
+    wb._lib.check(wb._lib.lib().wc_cq_gemm_ex(m.handle, ctypes.c_void_p(xd.data_ptr()),
+                                              ctypes.c_void_p(yd.data_ptr()), rows, WC_GEMM_TENSOR_CORES, None))
+    code = ctypes.c_int(-1)
+    wb._lib.check(wb._lib.lib().wc_device_status(ctypes.byref(code)))
+    assert code.value == 0, f"a bounded wait expired (code {code.value})"
+    return yd.cpu().numpy()
+
+
+CASES = [(128, 128, 64, 32, 4), (300, 200, 512, 32, 4), (257, 96, 512, 128, 2), (129, 384, 512, 128, 2),
+         (64, 1024, 512, 128, 2), (200, 512, 2048, 32, 4), (1000, 2048, 512, 32, 4), (130, 70, 200, 32, 2)]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"m{c[0]}_{c[1]}x{c[2]}g{c[3]}b{c[4]}" for c in CASES])
+def test_tc_gemm_within_bf16_bound(wb, cuda, case):
+    rows, out, in_, group, bits = case
+    rng = np.random.default_rng(sum(case))
+    p = wb.synth.random_packed(rng, out, in_, group, bits, "lloyd")
+    m = wb.cq.New(p)
+    x = rng.normal(size=(rows, in_)).astype(np.float32)
+    got = tc_gemm(wb, cuda, m, x)
+    assert np.all(np.isfinite(got))
+    xh, w = rotated_operands(p, x.astype(np.float64))
+    want = xh @ w.T
+    K = w.shape[1]
+    gamma = 2.0 ** -7 + (K + np.log2(group) + 4) * 2.0 ** -24
+    bound = gamma * (np.abs(xh) @ np.abs(w).T)
+    assert np.all(np.abs(got - want) <= bound)
+    # the rotated product is the reference's product: dequant64 · x
+    assert np.allclose(want, x.astype(np.float64) @ refmath.dequant64(p).T, rtol=1e-9, atol=1e-9)
+    for i in range(0, rows, max(1, rows // 7)):
+        assert refmath.cosine(got[i], want[i]) >= 0.9999
+
+
+def test_tc_gemm_views_and_reuse(wb, cuda):
+    """Rows views build their own weight image; repeated calls agree."""
+    rng = np.random.default_rng(11)
+    p = wb.synth.random_packed(rng, 700, 512, 32, 4, "lloyd")
+    m = wb.cq.New(p)
+    x = rng.normal(size=(256, 512)).astype(np.float32)
+    full = tc_gemm(wb, cuda, m, x)
+    again = tc_gemm(wb, cuda, m, x)
+    assert np.array_equal(full, again)
+    for lo, hi in ((0, 128), (5, 300), (640, 700)):
+        part = tc_gemm(wb, cuda, m.Rows(lo, hi), x)
+        assert np.array_equal(part, full[:, lo:hi])
