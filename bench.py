@@ -297,6 +297,56 @@ def attention_component(pkg, torch, lib, stream, streams=256, layers=8, reps=5, 
             "launches": 2 * layers}
 
 
+def prefill_component(pkg, torch, lib, frames=24000, reps=5):
+    """encoder prefill GEMMs, X = 64 streams x 375 frames = 24,000
+    rows x 512 fp32 ~N(0,1) times 4-bit G32 CQ weights 512->2048 (up),
+    2048->512 (down), 512->1536 (QKV), and Whistle's qkvg set (384+96+128+512
+    rows x 512, 2-bit G128) as one more point, on the tensor cores
+    (wc_cq_gemm_ex, WC_GEMM_TENSOR_CORES), each in a CUDA graph."""
+    rng = np.random.default_rng(2000)
+    peaks_gbs, _ = peaks()
+    pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    tflops_peak = float(pk.get("bf16_tflops", 1590.0))
+    shapes = [("up 512->2048 CQ4 G32", 2048, 512, 32, 4), ("down 2048->512 CQ4 G32", 512, 2048, 32, 4),
+              ("qkv 512->1536 CQ4 G32", 1536, 512, 32, 4), ("whistle qkvg 1120x512 CQ2 G128", 1120, 512, 128, 2)]
+    res = {}
+    st = torch.cuda.Stream()
+    sptr = ctypes.c_void_p(st.cuda_stream)
+    for name, out, in_, group, bits in shapes:
+        p = pkg.synth.random_packed(rng, out, in_, group, bits)
+        m = pkg.cq.New(p)
+        pkg._lib.check(lib.wc_cq_prepare_tc(m.handle))
+        x = torch.randn(frames, in_, device="cuda", dtype=torch.float32)
+        y = torch.empty(frames, out, device="cuda", dtype=torch.float32)
+        args = (m.handle, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(y.data_ptr()), frames, 1, sptr)
+        with torch.cuda.stream(st):
+            pkg._lib.check(lib.wc_cq_gemm_ex(*args))
+            st.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st, capture_error_mode="relaxed"):
+                pkg._lib.check(lib.wc_cq_gemm_ex(*args))
+            g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(reps):
+                g.replay()
+            e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        del g
+        groups = (in_ + group - 1) // group
+        wbytes = out * groups * group * bits // 8 + 2 * out * groups
+        algo = wbytes + 4 * frames * in_ + 4 * frames * out
+        flops = 2.0 * frames * out * in_
+        t_roof = max(algo / (peaks_gbs * 1e9), flops / (tflops_peak * 1e12))
+        res[name] = {"us": round(ms * 1e3, 2), "gbs": round(algo / (ms / 1e3) / 1e9, 1),
+                     "tflops": round(flops / (ms / 1e3) / 1e12, 1), "roofline_frac": round(t_roof / (ms / 1e3), 3),
+                     "algorithmic_bytes": algo}
+    return {"workload": f"configs[2]: {frames} x in fp32 ~N(0,1) prefill rows, tensor cores (bf16 operands in the "
+                        f"rotated domain, fp32 accumulate)", "per_matrix": res,
+            "roofline": "max(algorithmic bytes / measured HBM, flops / measured bf16 peak)"}
+
+
 def run_b200(args, world, rank, local):
     import torch
 
@@ -456,7 +506,8 @@ def run_b200(args, world, rank, local):
         line["config"]["workload"] = f"one shape {args.only} (profiling run, not the headline workload)"
     elif not args.no_components:
         line["components"] = {"int8_attention": attention_component(pkg, torch, lib, None, flags=3),
-                              "int8_attention_exact_order": attention_component(pkg, torch, lib, None, flags=1)}
+                              "int8_attention_exact_order": attention_component(pkg, torch, lib, None, flags=1),
+                              "cq_gemm_prefill": prefill_component(pkg, torch, lib)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.only:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -478,10 +529,18 @@ def main():
     ap.add_argument("--only", default="", help="one shape OUTxINxBITS (profiling runs)")
     ap.add_argument("--no-components", action="store_true", help="skip the attention component")
     ap.add_argument("--attention-only", action="store_true", help="only the attention component (profiling)")
+    ap.add_argument("--prefill-only", action="store_true", help="only the prefill GEMM component (profiling)")
     args = ap.parse_args()
     world, rank, local = dist_env()
     if args.impl == "reference":
         run_reference(args, world, rank)
+        return
+    if args.prefill_only:
+        import torch
+
+        pkg = __import__("importlib").import_module("go-whistle_b200")
+        torch.cuda.set_device(local)
+        print(json.dumps(prefill_component(pkg, torch, pkg._lib.lib())), flush=True)
         return
     if args.attention_only:
         import torch

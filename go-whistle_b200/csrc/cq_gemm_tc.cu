@@ -32,7 +32,7 @@ namespace {
 constexpr int kTcM = 128;         // UMMA M (cta_group::1)
 constexpr int kTcN = 128;         // UMMA N, TMEM columns
 constexpr int kTcK = 64;          // bf16 elements per 128-byte row of a chunk
-constexpr int kStages = 4;
+constexpr int kStages = 2;
 constexpr int kChunkBytes = kTcM * 128;  // one 128 x 64 bf16 tile, A and B alike
 constexpr int kTcThreads = 192;
 constexpr uint32_t kSpinLimit = 1u << 22;
@@ -114,7 +114,7 @@ __device__ __forceinline__ uint32_t swz(int row, int k) {
     return (uint32_t)row * 128u + ((uint32_t)(((k >> 3) ^ (row & 7)) & 7) << 4) + (uint32_t)(k & 7) * 2u;
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1) cq_gemm_tc_kernel(const __grid_constant__ TcParams p) {
+__global__ void __launch_bounds__(kTcThreads, 3) cq_gemm_tc_kernel(const __grid_constant__ TcParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte alignment for the swizzle atoms.
     unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -195,27 +195,44 @@ __global__ void __launch_bounds__(kTcThreads, 1) cq_gemm_tc_kernel(const __grid_
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         ok = __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int *>(bail) == 0);
-        if (ok) {
-            const int row = mt * kTcM + part * 32 + lane;
-#pragma unroll 1
-            for (int c = 0; c < kTcN; c += 32) {
-                uint32_t r[32];
-                tmem_ld32(tmem + ((uint32_t)(part * 32) << 16) + (uint32_t)c, r);
-                const int col = nt * kTcN + c;
-                if (row < p.m && col < p.n) {
-                    float *y = p.y + (size_t)row * p.ldy + col;
-                    if (col + 32 <= p.n && (p.ldy & 3) == 0 && (((uintptr_t)y) & 15) == 0) {
+        // Stage 64 columns at a time through the (now idle) pipeline
+        // buffers, rows padded to 68 floats, then store whole row segments:
+        // each warp writes rows part, part+4, ... as 256 contiguous bytes.
+        float *stage = reinterpret_cast<float *>(sa);
+        constexpr int kHalf = 64, kPad = kHalf + 4;
+        const int erow = part * 32 + lane;  // this thread's TMEM lane / tile row
+        for (int h = 0; h < kTcN; h += kHalf) {
+            if (ok) {
 #pragma unroll
-                        for (int q = 0; q < 8; q++)
-                            reinterpret_cast<float4 *>(y)[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                                                          __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
-                    } else {
+                for (int c = 0; c < kHalf; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(tmem + ((uint32_t)(part * 32) << 16) + (uint32_t)(h + c), r);
 #pragma unroll
-                        for (int q = 0; q < 32; q++)
-                            if (col + q < p.n) y[q] = __uint_as_float(r[q]);
+                    for (int q = 0; q < 8; q++)
+                        *reinterpret_cast<uint4 *>(stage + erow * kPad + c + 4 * q) =
+                            make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+                }
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (ok) {
+                const int col0 = nt * kTcN + h;
+                // 16 lanes per row (16 bytes each): two rows per instruction.
+                const int sub = lane >> 4, c4 = (lane & 15) * 4;
+                for (int rr = (warp - 2) * 2 + sub; rr < kTcM; rr += 8) {
+                    const int row = mt * kTcM + rr, col = col0 + c4;
+                    if (row < p.m && col < p.n) {
+                        const float4 v = *reinterpret_cast<const float4 *>(stage + rr * kPad + c4);
+                        float *y = p.y + (size_t)row * p.ldy + col;
+                        if (col + 4 <= p.n && (p.ldy & 3) == 0 && (((uintptr_t)y) & 15) == 0) {
+                            *reinterpret_cast<float4 *>(y) = v;
+                        } else {
+                            const float vv[4] = {v.x, v.y, v.z, v.w};
+                            for (int q = 0; q < 4 && col + q < p.n; q++) y[q] = vv[q];
+                        }
                     }
                 }
             }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -229,58 +246,73 @@ __global__ void __launch_bounds__(kTcThreads, 1) cq_gemm_tc_kernel(const __grid_
 
 // x̂ = H·x per group of G (no 1/√G: it is in ŵ), bf16, into the swizzled
 // image [m_tile][kc][128 rows][128 B]; rows past m and columns past In are
-// zero. One warp per (row, group): lanes hold E = G/32 elements (G >= 32)
-// or 32/G groups share a warp (G < 32); the butterflies are fwht's.
-__global__ void rotate_bf16_kernel(const float *__restrict__ x, int m, int in, int G, int groups, int kchunks,
-                                   int mtiles, unsigned char *__restrict__ a) {
+// zero. Each lane owns a 32-column segment of one row (four 16-byte chunks
+// of the image): the butterflies with h < 32 run in registers, those with
+// h >= 32 (G > 32) between the lanes of a group by shuffles; for G < 32 a
+// segment holds 32/G whole groups. Same butterflies as fwht.
+__global__ void __launch_bounds__(256) rotate_bf16_kernel(const float *__restrict__ x, int m, int in, int G,
+                                                          int kpad, int kchunks, int mtiles,
+                                                          unsigned char *__restrict__ a) {
     const int lane = threadIdx.x & 31;
-    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // global warp
-    const int E = G >= 32 ? G / 32 : 1;
-    const int L = G >= 32 ? 32 : G;        // lanes per group
-    const int gpw = 32 / L;                // groups per warp
-    const int units = mtiles * kTcM * ((groups + gpw - 1) / gpw);
-    if (gw >= units) return;
-    const int gpr = (groups + gpw - 1) / gpw;
-    const int row = gw / gpr, g = (gw % gpr) * gpw + lane / L;
-    const int lig = lane % L;
-    float v[8];
+    const int segs = kpad / 32;                       // segments per row (kpad: multiple of 32)
+    const long seg = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long total = (long)mtiles * kTcM * segs;
+    // Whole warps stay in the loop so the shuffles see every lane.
+    const bool live = seg < total;
+    const int row = live ? (int)(seg / segs) : 0, sg = live ? (int)(seg % segs) : 0;
+    const int k0 = sg * 32;
+    float v[32];
+    if (live && row < m && k0 + 32 <= in && (in & 3) == 0 && (((uintptr_t)x) & 15) == 0) {
+        const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)row * in + k0);
 #pragma unroll
-    for (int e = 0; e < 8; e++) {
-        v[e] = 0.0f;
-        if (e < E && g < groups && row < m) {
-            const int k = g * G + lig * E + e;
-            if (k < in) v[e] = x[(size_t)row * in + k];
+        for (int q = 0; q < 8; q++) {
+            const float4 f = __ldg(src + q);
+            v[4 * q] = f.x;
+            v[4 * q + 1] = f.y;
+            v[4 * q + 2] = f.z;
+            v[4 * q + 3] = f.w;
         }
-    }
-    for (int h = 1; h < G; h <<= 1) {
-        if (h < E) {
+    } else {
 #pragma unroll
-            for (int e = 0; e < 8; e++) {
-                if (e < E && (e & h) == 0) {
+        for (int e = 0; e < 32; e++) v[e] = (live && row < m && k0 + e < in) ? x[(size_t)row * in + k0 + e] : 0.0f;
+    }
+    const int gin = G < 32 ? G : 32;  // butterflies inside the segment
+#pragma unroll
+    for (int h = 1; h < 32; h <<= 1) {
+        if (h < gin) {
+#pragma unroll
+            for (int e = 0; e < 32; e++) {
+                if ((e & h) == 0) {
                     const float a0 = v[e], b0 = v[e + h];
                     v[e] = a0 + b0;
                     v[e + h] = a0 - b0;
                 }
             }
-        } else {
-            const int pl = h / E;
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-                const float o = __shfl_xor_sync(0xffffffffu, v[e], pl);
-                v[e] = (lig & pl) ? o - v[e] : v[e] + o;
-            }
         }
     }
-    if (g >= groups) return;
-    const int mtile = row / kTcM, r = row % kTcM;
+    for (int h = 32; h < G; h <<= 1) {  // across the lanes of a group
+        const int pl = h / 32;
 #pragma unroll
-    for (int e = 0; e < 8; e++) {
-        if (e < E) {
-            const int k = g * G + lig * E + e;
-            const int kc = k / kTcK;
-            unsigned char *base = a + ((size_t)mtile * kchunks + kc) * kChunkBytes;
-            *reinterpret_cast<__nv_bfloat16 *>(base + swz(r, k % kTcK)) = __float2bfloat16_rn(v[e]);
+        for (int e = 0; e < 32; e++) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[e], pl);
+            v[e] = (sg & pl) ? o - v[e] : v[e] + o;
         }
+    }
+    if (!live) return;
+    const int mtile = row / kTcM, r = row % kTcM, kc = k0 / kTcK;
+    unsigned char *base = a + ((size_t)mtile * kchunks + kc) * kChunkBytes;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        uint4 w;
+        __nv_bfloat162 t0 = __floats2bfloat162_rn(v[8 * c], v[8 * c + 1]);
+        __nv_bfloat162 t1 = __floats2bfloat162_rn(v[8 * c + 2], v[8 * c + 3]);
+        __nv_bfloat162 t2 = __floats2bfloat162_rn(v[8 * c + 4], v[8 * c + 5]);
+        __nv_bfloat162 t3 = __floats2bfloat162_rn(v[8 * c + 6], v[8 * c + 7]);
+        w.x = *reinterpret_cast<uint32_t *>(&t0);
+        w.y = *reinterpret_cast<uint32_t *>(&t1);
+        w.z = *reinterpret_cast<uint32_t *>(&t2);
+        w.w = *reinterpret_cast<uint32_t *>(&t3);
+        *reinterpret_cast<uint4 *>(base + swz(r, (k0 % kTcK) + 8 * c)) = w;
     }
 }
 
@@ -329,15 +361,13 @@ cudaError_t launch_dequant_bf16(const CqShape &s, const CqView &v, unsigned char
 
 cudaError_t launch_rotate_bf16(const CqShape &s, const float *x, int m, unsigned char *a, cudaStream_t st) {
     const int kchunks = tc_kchunks(s), mtiles = (m + kTcM - 1) / kTcM;
-    const int L = s.group >= 32 ? 32 : s.group, gpw = 32 / L;
-    const long warps = (long)mtiles * kTcM * ((s.groups + gpw - 1) / gpw);
-    if (warps == 0) return cudaSuccess;
-    // Padding columns past groups·G within the last chunk stay zero.
-    if (s.pad % kTcK != 0) {
-        cudaError_t e = cudaMemsetAsync(a, 0, tc_a_bytes(m, kchunks), st);
-        if (e != cudaSuccess) return e;
-    }
-    rotate_bf16_kernel<<<(int)((warps + 7) / 8), 256, 0, st>>>(x, m, s.in, s.group, s.groups, kchunks, mtiles, a);
+    // Segments cover kchunks·64 columns: the padding past groups·G is zero
+    // (x is zero there, and H of zeros is zero within a group of G <= 32;
+    // for larger G the padding is whole groups of zeros).
+    const int kpad = kchunks * kTcK;
+    const long threads = (long)mtiles * kTcM * (kpad / 32);
+    if (threads == 0) return cudaSuccess;
+    rotate_bf16_kernel<<<(int)((threads + 255) / 256), 256, 0, st>>>(x, m, s.in, s.group, kpad, kchunks, mtiles, a);
     count_launch();
     return cudaGetLastError();
 }
