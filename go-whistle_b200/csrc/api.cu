@@ -636,6 +636,34 @@ extern "C" wc_status wc_cq_gemm_ex(const wc_cq *h, const float *x, float *y, int
     return e == cudaSuccess ? WC_OK : cuda_error(e, "cq tensor-core kernel");
 }
 
+// Tensor-core GEMM without any allocation: see whistle_b200.h.
+extern "C" wc_status wc_cq_gemm_tc_noalloc(const wc_cq *h, const float *x, float *y, int rows, int *err,
+                                           wc_stream stream) {
+    if (!h) return set_error(WC_ERR_INVALID, "cq: nil matrix");
+    if (rows < 0) return set_error(WC_ERR_INVALID, fmt("cq: GEMM of %d rows on [%d, %d]", rows, h->out, h->shape.in));
+    if (rows == 0 || h->out == 0) return WC_OK;
+    wc_status st = check_device(h);
+    if (st != WC_OK) return st;
+    if ((st = tc_supported(h)) != WC_OK) return st;
+    const int kchunks = tc_kchunks(h->shape);
+    const size_t need = tc_a_bytes(rows, kchunks), have = noalloc_scratch_bytes();
+    if (need > have)
+        return set_error(WC_ERR_INVALID,
+                         fmt("cq: %d rows of %d columns need %zu bytes of scratch; the no-allocation GEMM has %zu "
+                             "(at most %zu rows at this width)",
+                             rows, kchunks * 64, need, have, (have / (size_t)(kchunks * 64 * 2)) / 128 * 128));
+    const unsigned char *wimg = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(h->tc->mu);
+        wimg = h->tc->b;
+    }
+    if (!wimg)
+        return set_error(WC_ERR_INVALID,
+                         "cq: matrix has no tensor-core weight image: call wc_cq_prepare_tc at load time first");
+    cudaError_t e = gemm_tc_noalloc(h->shape, wimg, x, y, rows, h->out, err, (cudaStream_t)stream);
+    return e == cudaSuccess ? WC_OK : cuda_error(e, "cq tensor-core kernel (no allocation)");
+}
+
 // ------------------------------------------------------------- needle ----
 
 extern "C" wc_status wc_quantize_rows(const float *x, int rows, int cols, int width, int8_t *q, float *s,

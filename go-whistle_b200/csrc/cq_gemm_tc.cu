@@ -22,6 +22,8 @@
 // code, skips its remaining work, frees its TMEM and returns.
 #include <cuda_bf16.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "cq_kernels.cuh"
 
@@ -373,6 +375,68 @@ cudaError_t launch_rotate_bf16(const CqShape &s, const float *x, int m, unsigned
 }
 
 size_t tc_smem_bytes() { return 1024 + 2 * kStages * kChunkBytes + 8 * (2 * kStages + 1) + 16; }
+
+// ---- the no-allocation entry point's scratch --------------------------------
+//
+// One file-scope device array holds the rotated-activation image of
+// wc_cq_gemm_tc_noalloc (kNoAllocScratchBytes) followed by its error word.
+// Every GPU that loads the library carries it until the process exits.
+// Host code cannot use the array's name as a device address (it names a
+// host-side shadow), so each device's address is looked up once with
+// cudaGetSymbolAddress, with that device current, and handed to the kernels.
+constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes + 256];
+
+size_t noalloc_scratch_bytes() { return kNoAllocScratchBytes; }
+
+// The array's device address on the current device (set-up on first use).
+static cudaError_t noalloc_scratch(unsigned char **out) {
+    static unsigned char *addr[64];
+    static std::mutex mu;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        addr[dev] = static_cast<unsigned char *>(p);
+    }
+    *out = addr[dev];
+    return cudaSuccess;
+}
+
+// Rotation into the static image, then the tensor-core GEMM, with no
+// allocation. The caller has checked that the image fits
+// (tc_a_bytes(rows, kchunks) <= kNoAllocScratchBytes) and that the weight
+// image wimg exists. err: a device int for the bounded waits' error code,
+// or null for the array's own word (cleared here on every call).
+cudaError_t gemm_tc_noalloc(const CqShape &s, const unsigned char *wimg, const float *x, float *y, int rows, int n,
+                            int *err, cudaStream_t st) {
+    unsigned char *base = nullptr;
+    cudaError_t e = noalloc_scratch(&base);
+    if (e != cudaSuccess) return e;
+    int *word = reinterpret_cast<int *>(base + kNoAllocScratchBytes);
+    if (!err) {
+        e = cudaMemsetAsync(word, 0, sizeof(int), st);
+        if (e != cudaSuccess) return e;
+        err = word;
+    }
+    e = launch_rotate_bf16(s, x, rows, base, st);
+    if (e != cudaSuccess) return e;
+    TcParams p{};
+    p.a = base;
+    p.b = wimg;
+    p.y = y;
+    p.m = rows;
+    p.n = n;
+    p.ldy = n;
+    p.kchunks = tc_kchunks(s);
+    p.err = err;
+    return launch_gemm_tc(p, st);
+}
 
 cudaError_t launch_gemm_tc(const TcParams &p, cudaStream_t st) {
     const size_t smem = tc_smem_bytes();

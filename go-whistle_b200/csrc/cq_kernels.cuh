@@ -54,6 +54,10 @@ size_t tc_smem_bytes();
 cudaError_t launch_dequant_bf16(const CqShape &s, const CqView &v, unsigned char *b, cudaStream_t st);
 cudaError_t launch_rotate_bf16(const CqShape &s, const float *x, int m, unsigned char *a, cudaStream_t st);
 cudaError_t launch_gemm_tc(const TcParams &p, cudaStream_t st);
+// wc_cq_gemm_tc_noalloc's core: the same kernels on a static scratch array.
+size_t noalloc_scratch_bytes();
+cudaError_t gemm_tc_noalloc(const CqShape &s, const unsigned char *wimg, const float *x, float *y, int rows, int n,
+                            int *err, cudaStream_t st);
 
 int stream_smem_base();
 bool stream_eligible(const CqShape &s);

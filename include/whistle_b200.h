@@ -127,6 +127,36 @@ wc_status wc_cq_gemm_ex(const wc_cq *h, const float *x, float *y, int rows, int 
 /* Builds the tensor-core weight image of h now (synchronous). */
 wc_status wc_cq_prepare_tc(const wc_cq *h);
 
+/*
+ * The tensor-core GEMM (wc_cq_gemm_ex with WC_GEMM_TENSOR_CORES) for callers
+ * that must not allocate GPU memory while they run. Examples: a real-time
+ * transcription loop, where a cudaMalloc can synchronise the device and
+ * stall a decode step for milliseconds; or a serving process that reserves
+ * its GPU memory once at start-up, next to other models, and cannot let a
+ * call grow it. This entry point calls no cudaMalloc, cudaFree or other
+ * allocating routine: the rotated activations go to a fixed 16 MiB array
+ * that the library keeps on every GPU it is loaded on, until the process
+ * exits. It has no counterpart in the reference.
+ *
+ *  - rows · K · 2 bytes must fit in 16 MiB, K = In rounded up to the group
+ *    and to 64 (16,384 rows at In = 512, 4,096 at In = 2048); larger calls
+ *    fail with WC_ERR_INVALID and leave y alone.
+ *  - h must already have its weight image: call wc_cq_prepare_tc when the
+ *    matrix is loaded (that call allocates; this one does not).
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture.
+ *  - All calls share the one array, which keeps the last call's contents:
+ *    calls whose work overlaps on the GPU (on different streams, or from
+ *    different threads without ordering) race and corrupt each other.
+ *  - err: a device int that receives the error code of the kernels' bounded
+ *    waits (0 = none; the caller clears it), or NULL to use a word inside
+ *    the array, cleared by each call.
+ * x [rows][In] and y [rows][Out] are fp32 DEVICE memory; y as
+ * wc_cq_gemm_ex with WC_GEMM_TENSOR_CORES computes it.
+ */
+wc_status wc_cq_gemm_tc_noalloc(const wc_cq *h, const float *x, float *y, int rows, int *err, wc_stream stream);
+
 /* Synchronises the current device and reports (and clears) the error word
  * of the kernels' bounded waits: *code = 0 if none expired. A diagnostic
  * with no reference counterpart. */

@@ -1,0 +1,91 @@
+"""wc_cq_gemm_tc_noalloc: the tensor-core GEMM for callers that must not
+allocate GPU memory while they run (a real-time transcription loop that
+cannot afford a cudaMalloc stall in a decode step, or a serving process whose
+GPU memory is reserved once at start-up). It runs the same kernels as
+wc_cq_gemm_ex with WC_GEMM_TENSOR_CORES, on a fixed scratch array inside the
+library instead of an allocated buffer.
+
+This file is collected last (its name sorts last) so that a run that stops
+at the first failure has already run every other test; it also passes on
+its own in a fresh process.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+import refmath
+
+pytestmark = pytest.mark.gpu
+
+WC_GEMM_TENSOR_CORES = 1
+WC_ERR_INVALID = 1
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _bf16_bound(p, x, want_rows):
+    """The tensor-core tests' per-element bound (test_gemm_tc_gpu.py)."""
+    G = p.group
+    groups = (p.in_ + G - 1) // G
+    xp = np.zeros((x.shape[0], groups * G))
+    xp[:, : p.in_] = x
+    xh = np.einsum("jk,rgk->rgj", refmath.sylvester(G), xp.reshape(x.shape[0], groups, G)).reshape(x.shape[0], -1)
+    cb = np.asarray(p.codebook, np.float64)
+    w = (cb[refmath.unpack(p)].reshape(p.out, groups, G) * refmath.norms(p)[:, :, None] / np.sqrt(G)).reshape(p.out, -1)
+    gamma = 2.0 ** -7 + (w.shape[1] + np.log2(G) + 4) * 2.0 ** -24
+    return xh @ w.T, gamma * (np.abs(xh) @ np.abs(w).T)
+
+
+@pytest.mark.parametrize("shape", [(512, 512, 32, 4), (1120, 512, 128, 2), (300, 2048, 32, 4)])
+def test_no_alloc_matches_allocating_entry_point(wb, cuda, shape):
+    out, in_, group, bits = shape
+    lib = wb._lib.lib()
+    rng = np.random.default_rng(out + in_)
+    p = wb.synth.random_packed(rng, out, in_, group, bits, "lloyd")
+    m = wb.cq.New(p)
+    # Load time: the weight image is built here (this call may allocate).
+    wb._lib.check(lib.wc_cq_prepare_tc(m.handle))
+    err = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    # Two calls in a row with different inputs: the second must not see the
+    # first's scratch contents.
+    for rows in (200, 1000):
+        x = cuda.randn(rows, in_, device="cuda", dtype=cuda.float32)
+        want = cuda.empty(rows, out, device="cuda", dtype=cuda.float32)
+        got = cuda.full((rows, out), float("nan"), device="cuda", dtype=cuda.float32)
+        wb._lib.check(lib.wc_cq_gemm_ex(m.handle, _ptr(x), _ptr(want), rows, WC_GEMM_TENSOR_CORES, None))
+        wb._lib.check(lib.wc_cq_gemm_tc_noalloc(m.handle, _ptr(x), _ptr(got), rows, _ptr(err), None))
+        cuda.cuda.synchronize()
+        assert int(err.item()) == 0
+        g, w = got.cpu().numpy(), want.cpu().numpy()
+        # Same kernels on the same inputs: the same bits, and so within the
+        # tensor-core bound of the float64 product.
+        assert np.array_equal(g.view(np.uint32), w.view(np.uint32))
+        ref, bound = _bf16_bound(p, x.cpu().numpy().astype(np.float64), rows)
+        assert np.all(np.abs(g - ref) <= bound)
+
+
+def test_no_alloc_limits(wb, cuda):
+    lib = wb._lib.lib()
+    rng = np.random.default_rng(5)
+    p = wb.synth.random_packed(rng, 128, 2048, 32, 4, "lloyd")
+    m = wb.cq.New(p)
+    x = cuda.zeros(5000, 2048, device="cuda", dtype=cuda.float32)
+    y = cuda.full((5000, 128), 7.0, device="cuda", dtype=cuda.float32)
+    # Not prepared: refused, nothing allocated on its behalf.
+    assert lib.wc_cq_gemm_tc_noalloc(m.handle, _ptr(x), _ptr(y), 16, None, None) == WC_ERR_INVALID
+    assert "wc_cq_prepare_tc" in wb._lib.last_error()
+    wb._lib.check(lib.wc_cq_prepare_tc(m.handle))
+    # 5000 rows of 2048 columns exceed the 16 MiB array (4096 rows at most).
+    assert lib.wc_cq_gemm_tc_noalloc(m.handle, _ptr(x), _ptr(y), 5000, None, None) == WC_ERR_INVALID
+    assert "4096 rows" in wb._lib.last_error()
+    assert bool((y == 7.0).all())
+    # At the limit it runs.
+    wb._lib.check(lib.wc_cq_gemm_tc_noalloc(m.handle, _ptr(x), _ptr(y), 4096, None, None))
+    cuda.cuda.synchronize()
+    assert bool((y[:4096] == 0.0).all()) and bool((y[4096:] == 7.0).all())
