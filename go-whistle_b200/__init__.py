@@ -8,12 +8,14 @@ mirroring the reference's Go API for the path:
   ``GEMMs`` — internal/cq;
 - ``needle``: ``QuantizeRow``, ``QuantizeRows``, ``Int8Rows``, ``AttendInt8``,
   ``AttendInt8Spans`` — internal/needle's int8 numerics;
-- ``synth``: seeded synthetic tensors in the reference's formats.
+- ``synth``: seeded synthetic tensors in the reference's formats;
+- ``dp``: data parallelism over independent streams (shards, gathering,
+  missing-shard detection).
 
 Import it by its directory name: ``importlib.import_module("go-whistle_b200")``.
 """
 
-from . import _lib, cq, needle, synth  # noqa: F401
+from . import _lib, cq, dp, needle, synth  # noqa: F401
 from ._lib import CQError, CudaError, Panic, WhistleError  # noqa: F401
 
 LIB_PATH = _lib.LIB_PATH
