@@ -485,6 +485,46 @@ extern "C" wc_status wc_cq_gemm_host(const wc_cq *h, const float *x, size_t x_le
     return WC_OK;
 }
 
+// Streams and events of the host-slice entry points, one set per calling
+// thread: kernels run on `comp`, device-to-host copies on `copy`, so the copy
+// of one chunk of outputs overlaps the kernels of the next chunk.
+namespace {
+struct HostPipe {
+    static const int kChunks = 8;
+    cudaStream_t comp = nullptr, copy = nullptr;
+    cudaEvent_t ev[kChunks] = {};
+    int device = -1;
+    void release() {
+        for (int i = 0; i < kChunks; i++)
+            if (ev[i]) cudaEventDestroy(ev[i]);
+        if (comp) cudaStreamDestroy(comp);
+        if (copy) cudaStreamDestroy(copy);
+        comp = copy = nullptr;
+        for (int i = 0; i < kChunks; i++) ev[i] = nullptr;
+        device = -1;
+    }
+    ~HostPipe() { release(); }
+    cudaError_t get() {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (device == dev) return cudaSuccess;
+        release();
+        if ((e = cudaStreamCreateWithFlags(&comp, cudaStreamNonBlocking)) != cudaSuccess) return e;
+        if ((e = cudaStreamCreateWithFlags(&copy, cudaStreamNonBlocking)) != cudaSuccess) return e;
+        for (int i = 0; i < kChunks; i++)
+            if ((e = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming)) != cudaSuccess) return e;
+        device = dev;
+        return cudaSuccess;
+    }
+};
+thread_local HostPipe t_pipe;
+}  // namespace
+
+// Output bytes per chunk below which a host GEMMs call is not split: one
+// chunk's copy then costs about as much as a launch.
+static const size_t kHostChunkMinBytes = 1u << 20;
+
 extern "C" wc_status wc_cq_gemms_host(const wc_cq *const *hs, int n, const float *x, size_t x_len, float *const *ys,
                                       const size_t *y_lens, int rows) {
     if (n < 0 || (n > 0 && (!hs || !ys || !y_lens))) return set_error(WC_ERR_INVALID, "cq: GEMMs of a nil list");
@@ -499,19 +539,71 @@ extern "C" wc_status wc_cq_gemms_host(const wc_cq *const *hs, int n, const float
     size_t total = 0;
     for (int k = 0; k < n; k++) total += y_lens[k];
     void *dx = nullptr, *dy = nullptr;
+    WB_CUDA(t_pipe.get());
     WB_CUDA(t_scratch.get(0, x_len * sizeof(float), &dx));
     WB_CUDA(t_scratch.get(1, (total ? total : 1) * sizeof(float), &dy));
-    WB_CUDA(cudaMemcpy(dx, x, x_len * sizeof(float), cudaMemcpyHostToDevice));
     std::vector<float *> dys(n);
     size_t off = 0;
     for (int k = 0; k < n; k++) {
         dys[k] = (float *)dy + off;
         off += y_lens[k];
     }
-    wc_status st = wc_cq_gemms(hs, n, (const float *)dx, dys.data(), rows, nullptr);
+    // Chunks of whole matrices with about equal output bytes. Every
+    // chunk's kernels are queued before any copy, so a copy into pageable
+    // memory (which returns only once it is done) never holds back the
+    // next chunk's kernels.
+    const size_t out_bytes = total * sizeof(float);
+    int chunks = (int)(out_bytes / kHostChunkMinBytes);
+    chunks = chunks < 1 ? 1 : chunks > HostPipe::kChunks ? HostPipe::kChunks : chunks;
+    const size_t per_chunk = (total + chunks - 1) / chunks;
+    int bounds[HostPipe::kChunks + 1];
+    int nb = 0;
+    bounds[0] = 0;
+    size_t acc = 0;
+    for (int k = 0; k < n; k++) {
+        acc += y_lens[k];
+        if ((acc >= per_chunk && nb + 1 < chunks) || k == n - 1) {
+            bounds[++nb] = k + 1;
+            acc = 0;
+        }
+    }
+    wc_status st = WC_OK;
+    cudaError_t e = cudaMemcpyAsync(dx, x, x_len * sizeof(float), cudaMemcpyHostToDevice, t_pipe.comp);
+    int issued = 0;
+    if (e != cudaSuccess) st = cuda_error(e, "cq GEMMs host copy");
+    for (int c = 0; c < nb && st == WC_OK; c++) {
+        st = wc_cq_gemms(hs + bounds[c], bounds[c + 1] - bounds[c], (const float *)dx, dys.data() + bounds[c], rows,
+                         (wc_stream)t_pipe.comp);
+        if (st != WC_OK) break;
+        if ((e = cudaEventRecord(t_pipe.ev[c], t_pipe.comp)) != cudaSuccess) {
+            st = cuda_error(e, "cq GEMMs host pipeline");
+            break;
+        }
+        issued = c + 1;
+    }
+    // Copies of the chunks whose kernels were queued; contiguous outputs
+    // (host and device) go in one copy.
+    for (int c = 0; c < issued && st == WC_OK; c++) {
+        if ((e = cudaStreamWaitEvent(t_pipe.copy, t_pipe.ev[c], 0)) != cudaSuccess) {
+            st = cuda_error(e, "cq GEMMs host pipeline");
+            break;
+        }
+        for (int k = bounds[c]; k < bounds[c + 1] && st == WC_OK;) {
+            size_t len = y_lens[k];
+            int j = k + 1;
+            while (j < bounds[c + 1] && ys[j - 1] + y_lens[j - 1] == ys[j]) len += y_lens[j++];
+            if (len && (e = cudaMemcpyAsync(ys[k], dys[k], len * sizeof(float), cudaMemcpyDeviceToHost,
+                                            t_pipe.copy)) != cudaSuccess)
+                st = cuda_error(e, "cq GEMMs host copy");
+            k = j;
+        }
+    }
+    // Nothing stays in flight into the caller's memory after return.
+    cudaError_t e1 = cudaStreamSynchronize(t_pipe.copy);
+    cudaError_t e2 = cudaStreamSynchronize(t_pipe.comp);
     if (st != WC_OK) return st;
-    for (int k = 0; k < n; k++)
-        if (y_lens[k]) WB_CUDA(cudaMemcpy(ys[k], dys[k], y_lens[k] * sizeof(float), cudaMemcpyDeviceToHost));
+    if (e1 != cudaSuccess) return cuda_error(e1, "cq GEMMs host copy");
+    if (e2 != cudaSuccess) return cuda_error(e2, "cq GEMMs host kernels");
     return WC_OK;
 }
 

@@ -266,3 +266,30 @@ def test_stream_many_matrices(wb, orc, cuda):
     for p, y in zip(ps[::37], yds[::37]):
         want = orc.gemm_lut(orc.OracleMatrix.of(p), x, 1).reshape(-1)
         assert bits_eq(y.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("rows,view_rows", [(1, 16384), (3, 4096)])
+def test_gemms_host_chunked(wb, orc, cuda, rows, view_rows):
+    """GEMMs on host slices with outputs large enough to split into chunks
+    (3 and 4 MiB: the kernels of one chunk overlap the copy of the previous
+    one), outputs in one contiguous host array and in separate arrays: bit
+    for bit the device call's and the oracle's."""
+    rng = np.random.default_rng(90 + rows)
+    n = 64
+    base = wb.synth.random_packed(rng, n * view_rows, 512, 32, 2, "lloyd")
+    big = wb.cq.New(base)
+    views = [big.Rows(k * view_rows, (k + 1) * view_rows) for k in range(n)]
+    x = rng.normal(size=rows * 512).astype(np.float32)
+    flat = np.full((n, rows * view_rows), np.nan, np.float32)
+    wb.cq.GEMMs(views, [flat[k] for k in range(n)], x, rows)
+    sep = [np.full(rows * view_rows, np.nan, np.float32) for _ in range(n)]
+    wb.cq.GEMMs(views, sep, x, rows)
+    xd = cuda.from_numpy(x).cuda()
+    yds = [cuda.empty(rows * view_rows, dtype=cuda.float32, device="cuda") for _ in views]
+    wb.cq.GEMMs(views, yds, xd, rows)
+    for k in range(n):
+        dev = yds[k].cpu().numpy()
+        assert bits_eq(flat[k], dev) and bits_eq(sep[k], dev), k
+    want = orc.gemm_lut(orc.OracleMatrix.of(base), x, rows, threads=8).reshape(rows, n, view_rows)
+    for k in (0, 17, n - 1):
+        assert bits_eq(flat[k].reshape(rows, view_rows), want[:, k])
