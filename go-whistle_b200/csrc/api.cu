@@ -808,11 +808,60 @@ static wc_status attend_smem_ok(const AttendParams &p) {
 static bool aligned4(const void *p) { return ((uintptr_t)p & 3u) == 0; }
 static bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
-// The any-order kernel when asked for and its shape is supported; else the
-// exact-order v2 kernel when its layout conditions hold and its shared
-// memory fits; else the per-head kernel.
+// The bulk-copy kernel (int8_attend_bulk.cu) for one query row per stream
+// over all keys, when the cache rows can be bulk-copied (16-byte aligned
+// rows and head slices). A CTA takes every KV head of its stream (whole
+// rows: one bulk copy per chunk) when that fits and there are at least half
+// as many streams as SMs; otherwise the KV-head group per CTA (kvpc) is the
+// smallest whose query heads have at least 512 output columns (four per
+// consumer thread), or the largest that fits, made smaller while the CTAs
+// would not cover every SM. Returns false when the kernel does not apply.
+static bool try_attend_bulk(AttendParams &p, int streams, cudaStream_t st, bool any_order, wc_status *status) {
+    if (p.t != 1 || p.spans || p.probs || p.qk % 16 != 0 || p.vd % 16 != 0) return false;
+    if (!aligned16(p.k8) || !aligned16(p.v8) || !aligned4(p.ks) || !aligned4(p.vs)) return false;
+    int dev = 0, limit = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+        return false;
+    const int gs = p.heads / p.kv_heads, sms = sm_count();
+    std::vector<int> ok;  // usable group sizes, ascending
+    for (int kvpc = 1; kvpc <= p.kv_heads; kvpc++) {
+        if (p.kv_heads % kvpc != 0 || !attend_bulk_shape_ok(p, kvpc)) continue;
+        AttendParams q = p;
+        q.kv_per_cta = kvpc;
+        if (attend_bulk_layout(q).total > (size_t)limit) continue;
+        int blocks = 0;
+        if (attend_bulk_occupancy(q, !any_order, &blocks) != cudaSuccess || blocks < 1) continue;
+        ok.push_back(kvpc);
+    }
+    if (ok.empty()) return false;
+    size_t pick = ok.size() - 1;
+    if (ok.back() != p.kv_heads || 2LL * streams < sms) {
+        for (size_t i = 0; i < ok.size(); i++)
+            if (ok[i] * gs * p.vd >= 512) {
+                pick = i;
+                break;
+            }
+        while (pick > 0 && (long long)streams * (p.kv_heads / ok[pick]) < sms) pick--;
+    }
+    p.err = device_err_word();
+    if (!p.err) return false;
+    p.kv_per_cta = ok[pick];
+    p.bulk_whole = ok[pick] == p.kv_heads;
+    p.bulk_scales = aligned16(p.ks) && aligned16(p.vs) && ((size_t)p.cap * p.kv_heads) % 4 == 0;
+    cudaError_t e = launch_attend_bulk(p, streams, !any_order, st);
+    *status = e == cudaSuccess ? WC_OK : cuda_error(e, "attend bulk kernel");
+    return true;
+}
+
+// The bulk-copy kernel when it applies; else the any-order kernel when asked
+// for and its shape is supported; else the exact-order v2 kernel when its
+// layout conditions hold and its shared memory fits; else the per-head
+// kernel.
 static wc_status run_attend(AttendParams &p, int streams, cudaStream_t st, bool any_order) {
     const int gs = p.heads / p.kv_heads;
+    wc_status bst;
+    if (try_attend_bulk(p, streams, st, any_order, &bst)) return bst;
     if (any_order && aligned4(p.v8) && aligned16(p.k8) && (p.kv_heads * p.qk) % 16 == 0 &&
         (p.kv_heads * p.vd) % 4 == 0) {
         int kvpc = 1;

@@ -25,6 +25,16 @@ struct AttendParams {
     int k_aligned4;  // k8 rows and q8 readable as int32 words
     int kv_per_cta;  // v2 and any-order: KV heads per CTA
     int v_prefetch;  // any-order: V row slices are 16-byte aligned (L2 prefetch)
+    int *err;        // bulk kernel: device error word of its bounded waits
+    int bulk_whole;  // bulk kernel: the CTA holds every KV head (contiguous chunks)
+    int bulk_scales; // bulk kernel: scale chunks start 16-byte aligned (cap·kv_heads % 4 == 0)
+};
+
+// Shared-memory layout of the bulk kernel (int8_attend_bulk.cu), in bytes.
+struct BulkLayout {
+    size_t stage, scale_off;  // one ring stage; its scale block
+    size_t lg, q8, qf, red, bars, total;
+    int lstride;              // floats per head row of logits
 };
 
 cudaError_t launch_quantize_rows(const float *x, int chunks, int width, int8_t *q, float *s, cudaStream_t st);
@@ -35,5 +45,9 @@ bool attend_any_supported(const AttendParams &p);
 cudaError_t launch_attend_any(const AttendParams &p, int streams, cudaStream_t st);
 size_t attend_v2_smem_bytes(const AttendParams &p);
 cudaError_t launch_attend_v2(const AttendParams &p, int streams, cudaStream_t st);
+BulkLayout attend_bulk_layout(const AttendParams &p);
+bool attend_bulk_shape_ok(const AttendParams &p, int kvpc);
+cudaError_t attend_bulk_occupancy(const AttendParams &p, bool exact, int *blocks_per_sm);
+cudaError_t launch_attend_bulk(const AttendParams &p, int streams, bool exact, cudaStream_t st);
 
 }  // namespace wb
