@@ -819,20 +819,24 @@ static bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 static bool try_attend_bulk(AttendParams &p, int streams, cudaStream_t st, bool any_order, wc_status *status) {
     if (p.t != 1 || p.spans || p.probs || p.qk % 16 != 0 || p.vd % 16 != 0) return false;
     if (!aligned16(p.k8) || !aligned16(p.v8) || !aligned4(p.ks) || !aligned4(p.vs)) return false;
-    int dev = 0, limit = 0;
+    int dev = 0, limit = 0, per_sm = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+        cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess)
         return false;
     const int gs = p.heads / p.kv_heads, sms = sm_count();
     std::vector<int> ok;  // usable group sizes, ascending
+    std::vector<BulkLayout> lay;
     for (int kvpc = 1; kvpc <= p.kv_heads; kvpc++) {
         if (p.kv_heads % kvpc != 0 || !attend_bulk_shape_ok(p, kvpc)) continue;
         AttendParams q = p;
         q.kv_per_cta = kvpc;
-        if (attend_bulk_layout(q).total > (size_t)limit) continue;
+        const BulkLayout L = attend_bulk_pick_layout(q, (size_t)per_sm, (size_t)limit);
+        if (L.total > (size_t)limit) continue;
         int blocks = 0;
-        if (attend_bulk_occupancy(q, !any_order, &blocks) != cudaSuccess || blocks < 1) continue;
+        if (attend_bulk_occupancy(q, L, !any_order, &blocks) != cudaSuccess || blocks < 1) continue;
         ok.push_back(kvpc);
+        lay.push_back(L);
     }
     if (ok.empty()) return false;
     size_t pick = ok.size() - 1;
@@ -849,7 +853,7 @@ static bool try_attend_bulk(AttendParams &p, int streams, cudaStream_t st, bool 
     p.kv_per_cta = ok[pick];
     p.bulk_whole = ok[pick] == p.kv_heads;
     p.bulk_scales = aligned16(p.ks) && aligned16(p.vs) && ((size_t)p.cap * p.kv_heads) % 4 == 0;
-    cudaError_t e = launch_attend_bulk(p, streams, !any_order, st);
+    cudaError_t e = launch_attend_bulk(p, lay[pick], streams, !any_order, st);
     *status = e == cudaSuccess ? WC_OK : cuda_error(e, "attend bulk kernel");
     return true;
 }

@@ -14,7 +14,8 @@
 // One CTA per (stream, group of kvpc KV heads) and 160 threads:
 //   warp 0      producer: streams the CTA's K rows (kvpc·qk bytes per key)
 //               chunk after chunk, then its V rows (kvpc·vd bytes per key),
-//               32 keys per chunk, through a ring of 4 stages. With every
+//               32 keys per chunk, through a ring of 2-8 stages (the
+//               deepest that leaves room for two CTAs per SM). With every
 //               KV head in the CTA a chunk is one contiguous range: one
 //               cp.async.bulk for the rows and one for their scales. With
 //               part of the heads, one bulk copy per row, and the row's
@@ -27,7 +28,7 @@
 //               accumulated into registers (each thread 1, 2 or 4 adjacent
 //               output columns, or several groups of 4, so that all 128
 //               threads work), eight keys' loads ahead of their adds.
-// The producer runs ahead by up to 4 chunks, so V chunks arrive while the
+// The producer runs ahead by the ring's depth, so V chunks arrive while the
 // consumers do the softmax. No tensor map, no multicast. Every mbarrier
 // wait is bounded; on timeout the CTA records an error code and returns
 // after its copies in flight have landed (also a bounded wait).
@@ -39,7 +40,7 @@ namespace wb {
 namespace {
 
 constexpr int kBulkKeys = 32;        // keys per chunk: one row per producer lane
-constexpr int kBulkStages = 4;
+constexpr int kBulkMaxStages = 8;
 constexpr int kBulkConsumers = 128;  // 4 warps
 constexpr int kBulkThreads = 32 + kBulkConsumers;
 constexpr uint32_t kBulkSpinLimit = 1u << 22;
@@ -131,19 +132,21 @@ __device__ __forceinline__ void accumulate(float *acc, float w, uint32_t v) {
 
 }  // namespace
 
-BulkLayout attend_bulk_layout(const AttendParams &p) {
+// The layout for `stages` ring stages (2 .. 8).
+BulkLayout attend_bulk_layout(const AttendParams &p, int stages) {
     BulkLayout L{};
+    L.stages = stages < 2 ? 2 : stages > kBulkMaxStages ? kBulkMaxStages : stages;
     const int kvpc = p.kv_per_cta, hb = kvpc * (p.heads / p.kv_heads);
     const int seg = kvpc * (p.qk > p.vd ? p.qk : p.vd);
     L.scale_off = ((size_t)kBulkKeys * seg + 15) & ~(size_t)15;
     L.stage = (L.scale_off + (size_t)kBulkKeys * kvpc * 4 + 127) & ~(size_t)127;
     L.lstride = (p.max_keys + 3) & ~3;
-    L.lg = L.stage * kBulkStages;
+    L.lg = L.stage * L.stages;
     L.q8 = L.lg + sizeof(float) * (size_t)hb * L.lstride;
     L.qf = (L.q8 + (size_t)hb * p.qk + 15) & ~(size_t)15;
     L.red = L.qf + sizeof(float) * (size_t)hb * p.qk;  // [hb] sq, [hb] max, [hb] sum
     L.bars = (L.red + sizeof(float) * 3 * (size_t)hb + 7) & ~(size_t)7;
-    L.total = L.bars + sizeof(uint64_t) * 2 * kBulkStages + 16;
+    L.total = L.bars + sizeof(uint64_t) * 2 * L.stages + 16;
     return L;
 }
 
@@ -166,8 +169,9 @@ __global__ void __launch_bounds__(kBulkThreads, 6) attend_int8_bulk_kernel(const
     float *sq = reinterpret_cast<float *>(smem + L.red);
     float *hmax = sq + hb, *hsum = hmax + hb;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars);
-    uint64_t *empty = full + kBulkStages;
-    int *bail = reinterpret_cast<int *>(empty + kBulkStages);
+    const int NS = L.stages;
+    uint64_t *empty = full + NS;
+    int *bail = reinterpret_cast<int *>(empty + NS);
 
     int nkeys = p.nkeys;
     if (p.nkeys_dev) nkeys = min(max(p.nkeys_dev[b], 0), p.cap);
@@ -176,7 +180,7 @@ __global__ void __launch_bounds__(kBulkThreads, 6) attend_int8_bulk_kernel(const
     const uint32_t kseg = (uint32_t)(kvpc * qk), vseg = (uint32_t)(kvpc * vd);
 
     if (tid == 0) {
-        for (int s = 0; s < kBulkStages; s++) {
+        for (int s = 0; s < NS; s++) {
             bar_init(&full[s], 33);  // lane 0's expect-tx arrival + 32 copy arrivals
             bar_init(&empty[s], kBulkConsumers / 32);
         }
@@ -193,7 +197,7 @@ __global__ void __launch_bounds__(kBulkThreads, 6) attend_int8_bulk_kernel(const
         const float *vs = p.vs + (size_t)b * p.cap * kvh + kv0;
         int issued = 0;
         for (int s = 0; s < 2 * nch; s++) {
-            const int st = s % kBulkStages, round = s / kBulkStages;
+            const int st = s % NS, round = s / NS;
             bool ok = round == 0 || bar_wait(&empty[st], (round - 1) & 1);
             ok = __all_sync(0xffffffffu, ok && *reinterpret_cast<volatile int *>(bail) == 0);
             if (!ok) {
@@ -240,8 +244,8 @@ __global__ void __launch_bounds__(kBulkThreads, 6) attend_int8_bulk_kernel(const
         // Nothing may land in shared memory after the CTA exits: wait
         // (bounded) for the last stages issued. On the normal path the
         // consumers already saw them complete.
-        for (int s = max(0, issued - kBulkStages); s < issued; s++)
-            if (!bar_wait(&full[s % kBulkStages], (s / kBulkStages) & 1) && lane == 0) atomicExch(p.err, 5);
+        for (int s = max(0, issued - NS); s < issued; s++)
+            if (!bar_wait(&full[s % NS], (s / NS) & 1) && lane == 0) atomicExch(p.err, 5);
         return;
     }
 
@@ -284,7 +288,7 @@ __global__ void __launch_bounds__(kBulkThreads, 6) attend_int8_bulk_kernel(const
     }
     bool ok = true;
     for (int c = 0; c < nch && ok; c++) {
-        const int st = c % kBulkStages, round = c / kBulkStages;
+        const int st = c % NS, round = c / NS;
         ok = __all_sync(0xffffffffu, bar_wait(&full[st], round & 1));
         if (!ok) break;
         const unsigned char *stage = smem + (size_t)st * L.stage;
@@ -399,7 +403,7 @@ __global__ void __launch_bounds__(kBulkThreads, 6) attend_int8_bulk_kernel(const
         for (int i = 0; i < CPT; i++) acc[CPT * j + i] = 0.0f;
     }
     for (int c = 0; c < nch && ok; c++) {
-        const int s = nch + c, st = s % kBulkStages, round = s / kBulkStages;
+        const int s = nch + c, st = s % NS, round = s / NS;
         ok = __all_sync(0xffffffffu, bar_wait(&full[st], round & 1));
         if (!ok) break;
         const unsigned char *stage = smem + (size_t)st * L.stage;
@@ -493,16 +497,29 @@ bool attend_bulk_shape_ok(const AttendParams &p, int kvpc) {
            p.kv_heads % kvpc == 0 && kBulkConsumers % hb == 0 && hb * p.vd <= 16 * kBulkConsumers;
 }
 
-cudaError_t attend_bulk_occupancy(const AttendParams &p, bool exact, int *blocks_per_sm) {
-    const BulkLayout L = attend_bulk_layout(p);
+// The deepest ring (up to 8 stages) that still lets two CTAs share an SM,
+// or, when even two stages do not, the deepest that fits one CTA.
+BulkLayout attend_bulk_pick_layout(const AttendParams &p, size_t smem_per_sm, size_t smem_per_block) {
+    const size_t two = smem_per_sm / 2 > 1024 ? smem_per_sm / 2 - 1024 : 0;  // 1 KB reserved per CTA
+    for (int st = kBulkMaxStages; st >= 2; st--) {
+        BulkLayout L = attend_bulk_layout(p, st);
+        if (L.total <= two) return L;
+    }
+    for (int st = kBulkMaxStages; st >= 2; st--) {
+        BulkLayout L = attend_bulk_layout(p, st);
+        if (L.total <= smem_per_block) return L;
+    }
+    return attend_bulk_layout(p, 2);
+}
+
+cudaError_t attend_bulk_occupancy(const AttendParams &p, const BulkLayout &L, bool exact, int *blocks_per_sm) {
     void (*fn)(AttendParams, BulkLayout) = exact ? bulk_fn<true>(p.qk / 16, bulk_cols(p)) : bulk_fn<false>(p.qk / 16, bulk_cols(p));
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
     if (e != cudaSuccess) return e;
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, fn, kBulkThreads, L.total);
 }
 
-cudaError_t launch_attend_bulk(const AttendParams &p, int streams, bool exact, cudaStream_t st) {
-    const BulkLayout L = attend_bulk_layout(p);
+cudaError_t launch_attend_bulk(const AttendParams &p, const BulkLayout &L, int streams, bool exact, cudaStream_t st) {
     void (*fn)(AttendParams, BulkLayout) = exact ? bulk_fn<true>(p.qk / 16, bulk_cols(p)) : bulk_fn<false>(p.qk / 16, bulk_cols(p));
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
     if (e != cudaSuccess) return e;

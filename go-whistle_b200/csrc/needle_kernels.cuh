@@ -35,6 +35,7 @@ struct BulkLayout {
     size_t stage, scale_off;  // one ring stage; its scale block
     size_t lg, q8, qf, red, bars, total;
     int lstride;              // floats per head row of logits
+    int stages;               // ring stages
 };
 
 cudaError_t launch_quantize_rows(const float *x, int chunks, int width, int8_t *q, float *s, cudaStream_t st);
@@ -45,9 +46,10 @@ bool attend_any_supported(const AttendParams &p);
 cudaError_t launch_attend_any(const AttendParams &p, int streams, cudaStream_t st);
 size_t attend_v2_smem_bytes(const AttendParams &p);
 cudaError_t launch_attend_v2(const AttendParams &p, int streams, cudaStream_t st);
-BulkLayout attend_bulk_layout(const AttendParams &p);
+BulkLayout attend_bulk_layout(const AttendParams &p, int stages);
+BulkLayout attend_bulk_pick_layout(const AttendParams &p, size_t smem_per_sm, size_t smem_per_block);
 bool attend_bulk_shape_ok(const AttendParams &p, int kvpc);
-cudaError_t attend_bulk_occupancy(const AttendParams &p, bool exact, int *blocks_per_sm);
-cudaError_t launch_attend_bulk(const AttendParams &p, int streams, bool exact, cudaStream_t st);
+cudaError_t attend_bulk_occupancy(const AttendParams &p, const BulkLayout &L, bool exact, int *blocks_per_sm);
+cudaError_t launch_attend_bulk(const AttendParams &p, const BulkLayout &L, int streams, bool exact, cudaStream_t st);
 
 }  // namespace wb
