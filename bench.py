@@ -355,6 +355,69 @@ def prefill_component(pkg, torch, lib, frames=24000, reps=5):
             "roofline": "max(algorithmic bytes / measured HBM, flops / measured bf16 peak)"}
 
 
+def decode_gemm_component(pkg, torch, lib, streams=256, reps=20):
+    """Multi-stream decode GEMMs: `streams` activation rows (one per stream)
+    through Whistle's self-attention projections (q 384, k 96, v 128, gate
+    512 from x 512; CQ2 G128, one GEMMs call) and the 16384 x 512 CQ4 G32
+    vocabulary head, with WC_GEMM_AUTO (tensor cores at this batch), each
+    call captured in a CUDA graph."""
+    rng = np.random.default_rng(4000)
+    peaks_gbs, _ = peaks()
+    pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    tflops_peak = float(pk.get("bf16_tflops", 1590.0))
+    sets = [("qkvg 384+96+128+512 x512 CQ2 G128", [384, 96, 128, 512], 512, 128, 2),
+            ("head 16384x512 CQ4 G32", [16384], 512, 32, 4)]
+    st = torch.cuda.Stream()
+    sptr = ctypes.c_void_p(st.cuda_stream)
+    res = {}
+    for name, outs, in_, group, bits in sets:
+        ps, ms = [], []
+        for o in outs:
+            p = pkg.synth.random_packed(rng, o, in_, group, bits)
+            if ps:
+                p.Codebook = ps[0].Codebook
+            ps.append(p)
+            ms.append(pkg.cq.New(p))
+            pkg._lib.check(lib.wc_cq_prepare_tc(ms[-1].handle))
+        x = torch.randn(streams, in_, device="cuda", dtype=torch.float32)
+        ys = [torch.empty(streams, o, device="cuda", dtype=torch.float32) for o in outs]
+        hs = (ctypes.c_void_p * len(ms))(*[m.handle.value for m in ms])
+        yp = (ctypes.c_void_p * len(ms))(*[y.data_ptr() for y in ys])
+        n0 = lib.wc_launch_count()
+
+        def call():
+            pkg._lib.check(lib.wc_cq_gemms_ex(hs, len(ms), ctypes.c_void_p(x.data_ptr()), yp, streams, 2, sptr))
+
+        with torch.cuda.stream(st):
+            call()
+            st.synchronize()
+            launches = lib.wc_launch_count() - n0
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st, capture_error_mode="relaxed"):
+                call()
+            g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(reps):
+                g.replay()
+            e1.record(st)
+        torch.cuda.synchronize()
+        ms_call = e0.elapsed_time(e1) / reps
+        del g
+        algo = sum(pkg.synth.algorithmic_bytes_gemv(o, in_, group, bits) - 4 * in_ - 4 * o for o in outs)
+        algo += 4 * streams * in_ + 4 * streams * sum(outs)
+        flops = 2.0 * streams * in_ * sum(outs)
+        t_roof = max(algo / (peaks_gbs * 1e9), flops / (tflops_peak * 1e12))
+        res[name] = {"us": round(ms_call * 1e3, 2), "gbs": round(algo / (ms_call / 1e3) / 1e9, 1),
+                     "tflops": round(flops / (ms_call / 1e3) / 1e12, 1),
+                     "roofline_frac": round(t_roof / (ms_call / 1e3), 3), "algorithmic_bytes": algo,
+                     "launches": launches}
+    return {"workload": f"{streams} decode streams: one activation row each, WC_GEMM_AUTO (tensor cores, bf16 "
+                        f"operands, fp32 accumulate)", "per_set": res,
+            "roofline": "max(algorithmic bytes / measured HBM, flops / measured bf16 peak); launch-bound at "
+                        "this size"}
+
+
 def run_b200(args, world, rank, local):
     import torch
 
@@ -514,7 +577,8 @@ def run_b200(args, world, rank, local):
     elif not args.no_components:
         line["components"] = {"int8_attention": attention_component(pkg, torch, lib, None, flags=3),
                               "int8_attention_exact_order": attention_component(pkg, torch, lib, None, flags=1),
-                              "cq_gemm_prefill": prefill_component(pkg, torch, lib)}
+                              "cq_gemm_prefill": prefill_component(pkg, torch, lib),
+                              "cq_gemm_decode_streams": decode_gemm_component(pkg, torch, lib)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.only:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -537,6 +601,7 @@ def main():
     ap.add_argument("--no-components", action="store_true", help="skip the attention component")
     ap.add_argument("--attention-only", action="store_true", help="only the attention component (profiling)")
     ap.add_argument("--prefill-only", action="store_true", help="only the prefill GEMM component (profiling)")
+    ap.add_argument("--decode-gemm-only", action="store_true", help="only the multi-stream decode GEMM component")
     args = ap.parse_args()
     world, rank, local = dist_env()
     if args.impl == "reference":
@@ -548,6 +613,13 @@ def main():
         pkg = __import__("importlib").import_module("go-whistle_b200")
         torch.cuda.set_device(local)
         print(json.dumps(prefill_component(pkg, torch, pkg._lib.lib())), flush=True)
+        return
+    if args.decode_gemm_only:
+        import torch
+
+        pkg = __import__("importlib").import_module("go-whistle_b200")
+        torch.cuda.set_device(local)
+        print(json.dumps(decode_gemm_component(pkg, torch, pkg._lib.lib())), flush=True)
         return
     if args.attention_only:
         import torch

@@ -57,6 +57,7 @@ _SIGS = {
     "wc_cq_gemm": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p]),
     "wc_cq_gemm_host": (_c_int, [_c_void_p, _c_void_p, _c_size, _c_void_p, _c_size, _c_int]),
     "wc_cq_gemm_ex": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p]),
+    "wc_cq_gemms_ex": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p]),
     "wc_cq_prepare_tc": (_c_int, [_c_void_p]),
     "wc_cq_gemm_tc_noalloc": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p]),
     "wc_device_status": (_c_int, [ctypes.POINTER(_c_int)]),

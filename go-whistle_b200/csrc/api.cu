@@ -306,7 +306,10 @@ static bool shares_tables(const wc_cq *a, const wc_cq *b) {
 
 // Streaming kernel threshold: index bytes of one activation's products
 // below which the per-tile kernel (no per-SM table build) answers faster.
-static const size_t kStreamMinBytes = 2u << 20;
+#ifndef WB_STREAM_MIN_BYTES
+#define WB_STREAM_MIN_BYTES (2u << 20)
+#endif
+static const size_t kStreamMinBytes = WB_STREAM_MIN_BYTES;
 
 static int sm_count() {
     int dev = 0, n = 0;
@@ -700,32 +703,97 @@ extern "C" wc_status wc_cq_prepare_tc(const wc_cq *h) {
     return WC_OK;
 }
 
+// Batch size from which WC_GEMM_AUTO takes the tensor cores: below it the
+// exact lut kernel's table work per activation is cheaper than the
+// rotation, operand images and tiles of the tensor-core path.
+static const int kTcAutoRows = 32;
+
+// Tensor-core products of matrices that read the same x (same In): one
+// rotation into the x̂ image per group size G, then one grouped launch per
+// kMaxTcMats matrices of that G. The image lives in the calling thread's
+// scratch, so one thread's calls must not overlap on the GPU (one stream
+// per thread, as the header states).
+static wc_status run_tc(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows, cudaStream_t s) {
+    for (int k = 0; k < n; k++) {
+        wc_status st = wc_cq_prepare_tc(ms[k]);
+        if (st != WC_OK) return st;
+    }
+    int *err = device_err_word();
+    if (!err) return set_error(WC_ERR_NOMEM, "cuda: error word");
+    std::vector<char> done(n, 0);
+    for (int i = 0; i < n; i++) {
+        if (done[i] || ms[i]->out == 0) continue;
+        const CqShape &sh = ms[i]->shape;
+        const int kchunks = tc_kchunks(sh);
+        void *a = nullptr;
+        WB_CUDA(t_scratch.get(3, tc_a_bytes(rows, kchunks), &a));
+        cudaError_t e = launch_rotate_bf16(sh, x, rows, (unsigned char *)a, s);
+        if (e != cudaSuccess) return cuda_error(e, "cq rotate kernel");
+        TcParams p{};
+        p.a = (const unsigned char *)a;
+        p.m = rows;
+        p.kchunks = kchunks;
+        p.err = err;
+        int tiles = 0;
+        for (int j = i; j < n; j++) {
+            const wc_cq *m = ms[j];
+            if (done[j] || m->out == 0 || m->shape.group != sh.group || m->shape.pad != sh.pad) continue;
+            done[j] = 1;
+            TcMat &t = p.mats[p.nmats++];
+            {
+                std::lock_guard<std::mutex> lock(m->tc->mu);
+                t.b = m->tc->b;
+            }
+            t.y = ys[j];
+            t.n = m->out;
+            t.ldy = m->out;
+            t.tile0 = tiles;
+            tiles += (m->out + 127) / 128;
+            if (p.nmats == kMaxTcMats) {
+                // Full: launch, and start the next group of matrices on the
+                // same image (a later launch only reads it).
+                e = launch_gemm_tc(p, s);
+                if (e != cudaSuccess) return cuda_error(e, "cq tensor-core kernel");
+                p.nmats = 0;
+                tiles = 0;
+            }
+        }
+        if (p.nmats > 0) {
+            e = launch_gemm_tc(p, s);
+            if (e != cudaSuccess) return cuda_error(e, "cq tensor-core kernel");
+        }
+    }
+    return WC_OK;
+}
+
+static bool use_tc(int rows, int flags) {
+    return (flags & WC_GEMM_TENSOR_CORES) || ((flags & WC_GEMM_AUTO) && rows >= kTcAutoRows);
+}
+
 extern "C" wc_status wc_cq_gemm_ex(const wc_cq *h, const float *x, float *y, int rows, int flags, wc_stream stream) {
-    if (!(flags & WC_GEMM_TENSOR_CORES)) return wc_cq_gemm(h, x, y, rows, stream);
+    if (!use_tc(rows, flags)) return wc_cq_gemm(h, x, y, rows, stream);
     if (!h) return set_error(WC_ERR_INVALID, "cq: nil matrix");
     if (rows < 0) return set_error(WC_ERR_INVALID, fmt("cq: GEMM of %d rows on [%d, %d]", rows, h->out, h->shape.in));
     if (rows == 0 || h->out == 0) return WC_OK;
-    wc_status st = wc_cq_prepare_tc(h);
+    wc_status st = check_device(h);
     if (st != WC_OK) return st;
-    const int kchunks = tc_kchunks(h->shape);
-    void *a = nullptr;
-    WB_CUDA(t_scratch.get(3, tc_a_bytes(rows, kchunks), &a));
-    int *err = device_err_word();
-    if (!err) return set_error(WC_ERR_NOMEM, "cuda: error word");
-    cudaStream_t s = (cudaStream_t)stream;
-    cudaError_t e = launch_rotate_bf16(h->shape, x, rows, (unsigned char *)a, s);
-    if (e != cudaSuccess) return cuda_error(e, "cq rotate kernel");
-    TcParams p{};
-    p.a = (const unsigned char *)a;
-    p.b = h->tc->b;
-    p.y = y;
-    p.m = rows;
-    p.n = h->out;
-    p.ldy = h->out;
-    p.kchunks = kchunks;
-    p.err = err;
-    e = launch_gemm_tc(p, s);
-    return e == cudaSuccess ? WC_OK : cuda_error(e, "cq tensor-core kernel");
+    return run_tc(&h, 1, x, &y, rows, (cudaStream_t)stream);
+}
+
+extern "C" wc_status wc_cq_gemms_ex(const wc_cq *const *hs, int n, const float *x, float *const *ys, int rows,
+                                    int flags, wc_stream stream) {
+    if (!use_tc(rows, flags)) return wc_cq_gemms(hs, n, x, ys, rows, stream);
+    if (n < 0 || (n > 0 && (!hs || !ys))) return set_error(WC_ERR_INVALID, "cq: GEMMs of a nil list");
+    if (rows < 0) return set_error(WC_ERR_INVALID, fmt("cq: GEMMs of %d rows", rows));
+    for (int k = 0; k < n; k++) {
+        if (!hs[k]) return set_error(WC_ERR_INVALID, "cq: nil matrix");
+        if (hs[k]->shape.in != hs[0]->shape.in)
+            return set_error(WC_ERR_INVALID, fmt("cq: GEMMs mixes inputs of %d and %d", hs[0]->shape.in, hs[k]->shape.in));
+        wc_status st = check_device(hs[k]);
+        if (st != WC_OK) return st;
+    }
+    if (rows == 0 || n == 0) return WC_OK;
+    return run_tc(hs, n, x, ys, rows, (cudaStream_t)stream);
 }
 
 // Tensor-core GEMM without any allocation: see whistle_b200.h.

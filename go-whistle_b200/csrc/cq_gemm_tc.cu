@@ -129,8 +129,13 @@ __global__ void __launch_bounds__(kTcThreads, 3) cq_gemm_tc_kernel(const __grid_
     int *bail = reinterpret_cast<int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nt = blockIdx.x, mt = blockIdx.y;
+    const int mt = blockIdx.y;
     const int kchunks = p.kchunks;
+    // This CTA's matrix and its n-tile within it.
+    int mi = 0;
+    while (mi + 1 < p.nmats && p.mats[mi + 1].tile0 <= (int)blockIdx.x) mi++;
+    const TcMat &mat = p.mats[mi];
+    const int nt = (int)blockIdx.x - mat.tile0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) {
@@ -153,10 +158,13 @@ __global__ void __launch_bounds__(kTcThreads, 3) cq_gemm_tc_kernel(const __grid_
     const uint32_t tmem = *tmem_slot;
 
     const unsigned char *ga = p.a + (size_t)mt * kchunks * kChunkBytes;
-    const unsigned char *gb = p.b + (size_t)nt * kchunks * kChunkBytes;
+    const unsigned char *gb = mat.b + (size_t)nt * kchunks * kChunkBytes;
 
     if (warp == 0 && lane == 0) {
-        // Producer.
+        // Producer. As a programmatic dependent of the rotation, wait for
+        // it (and its writes of the x̂ image) before the first copy; the
+        // set-up above already overlapped its tail.
+        if (p.pdl) asm volatile("griddepcontrol.wait;" ::: "memory");
         for (int kc = 0; kc < kchunks; kc++) {
             const int s = kc % kStages, round = kc / kStages;
             if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
@@ -222,14 +230,14 @@ __global__ void __launch_bounds__(kTcThreads, 3) cq_gemm_tc_kernel(const __grid_
                 const int sub = lane >> 4, c4 = (lane & 15) * 4;
                 for (int rr = (warp - 2) * 2 + sub; rr < kTcM; rr += 8) {
                     const int row = mt * kTcM + rr, col = col0 + c4;
-                    if (row < p.m && col < p.n) {
+                    if (row < p.m && col < mat.n) {
                         const float4 v = *reinterpret_cast<const float4 *>(stage + rr * kPad + c4);
-                        float *y = p.y + (size_t)row * p.ldy + col;
-                        if (col + 4 <= p.n && (p.ldy & 3) == 0 && (((uintptr_t)y) & 15) == 0) {
+                        float *y = mat.y + (size_t)row * mat.ldy + col;
+                        if (col + 4 <= mat.n && (mat.ldy & 3) == 0 && (((uintptr_t)y) & 15) == 0) {
                             *reinterpret_cast<float4 *>(y) = v;
                         } else {
                             const float vv[4] = {v.x, v.y, v.z, v.w};
-                            for (int q = 0; q < 4 && col + q < p.n; q++) y[q] = vv[q];
+                            for (int q = 0; q < 4 && col + q < mat.n; q++) y[q] = vv[q];
                         }
                     }
                 }
@@ -255,7 +263,9 @@ __global__ void __launch_bounds__(kTcThreads, 3) cq_gemm_tc_kernel(const __grid_
 __global__ void __launch_bounds__(256) rotate_bf16_kernel(const float *__restrict__ x, int m, int in, int G,
                                                           int kpad, int kchunks, int mtiles,
                                                           unsigned char *__restrict__ a) {
-    const int lane = threadIdx.x & 31;
+    // A GEMM launched as this kernel's programmatic dependent may start its
+    // set-up now; it waits for this grid's completion before reading a.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int segs = kpad / 32;                       // segments per row (kpad: multiple of 32)
     const long seg = (long)blockIdx.x * blockDim.x + threadIdx.x;
     const long total = (long)mtiles * kTcM * segs;
@@ -428,24 +438,41 @@ cudaError_t gemm_tc_noalloc(const CqShape &s, const unsigned char *wimg, const f
     if (e != cudaSuccess) return e;
     TcParams p{};
     p.a = base;
-    p.b = wimg;
-    p.y = y;
     p.m = rows;
-    p.n = n;
-    p.ldy = n;
     p.kchunks = tc_kchunks(s);
     p.err = err;
+    p.nmats = 1;
+    p.mats[0] = TcMat{wimg, y, n, n, 0};
     return launch_gemm_tc(p, st);
 }
 
+int tc_total_tiles(const TcParams &p) {
+    const TcMat &l = p.mats[p.nmats - 1];
+    return l.tile0 + (l.n + kTcN - 1) / kTcN;
+}
+
+// The GEMM as a programmatic dependent launch of the rotation just queued
+// on st: its CTAs may start while the rotation drains, and the producer
+// waits for it before reading the x̂ image (griddepcontrol.wait).
 cudaError_t launch_gemm_tc(const TcParams &p, cudaStream_t st) {
     const size_t smem = tc_smem_bytes();
     cudaError_t e = cudaFuncSetAttribute(cq_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    dim3 grid((p.n + kTcN - 1) / kTcN, (p.m + kTcM - 1) / kTcM);
-    cq_gemm_tc_kernel<<<grid, kTcThreads, smem, st>>>(p);
+    TcParams q = p;
+    q.pdl = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)tc_total_tiles(p), (unsigned)((p.m + kTcM - 1) / kTcM));
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, cq_gemm_tc_kernel, q);
     count_launch();
-    return cudaGetLastError();
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace wb

@@ -40,12 +40,20 @@ struct StreamParams {
 };
 // The tensor-core GEMM (cq_gemm_tc.cu): operand images are pre-swizzled
 // 128 x 64 bf16 tiles.
-struct TcParams {
-    const unsigned char *a;  // x̂ image [m_tiles][kchunks][128][128 B]
+constexpr int kMaxTcMats = 16;  // matrices one grouped tensor-core launch carries
+struct TcMat {
     const unsigned char *b;  // ŵ image [n_tiles][kchunks][128][128 B]
     float *y;                // [m][ldy] fp32
-    int m, n, ldy, kchunks;
+    int n, ldy;
+    int tile0;               // first n-tile of this matrix in the launch's grid
+};
+struct TcParams {
+    const unsigned char *a;  // x̂ image [m_tiles][kchunks][128][128 B], shared by the matrices
+    int m, kchunks;
     int *err;                // device error word (bounded waits)
+    int nmats;               // matrices in this launch (1 .. kMaxTcMats)
+    int pdl;                 // launched as a programmatic dependent of the rotation
+    TcMat mats[kMaxTcMats];
 };
 int tc_kchunks(const CqShape &s);
 size_t tc_a_bytes(int m, int kchunks);
@@ -53,6 +61,8 @@ size_t tc_b_bytes(int n, int kchunks);
 size_t tc_smem_bytes();
 cudaError_t launch_dequant_bf16(const CqShape &s, const CqView &v, unsigned char *b, cudaStream_t st);
 cudaError_t launch_rotate_bf16(const CqShape &s, const float *x, int m, unsigned char *a, cudaStream_t st);
+// Total n-tiles of a launch: mats[nmats - 1].tile0 + its tiles.
+int tc_total_tiles(const TcParams &p);
 cudaError_t launch_gemm_tc(const TcParams &p, cudaStream_t st);
 // wc_cq_gemm_tc_noalloc's core: the same kernels on a static scratch array.
 size_t noalloc_scratch_bytes();

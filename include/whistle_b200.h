@@ -4,7 +4,7 @@
  * internal/cq and the int8 KV-cache attention of internal/needle.
  *
  * Plain C: pointers, sizes and status codes; no CUDA, Go or torch types. A
- * cgo shim (INTEGRATION.md) binds these one for one. Each entry point names
+ * cgo shim binds these one for one. Each entry point names
  * the reference routine it stands in for (file:line in the go-whistle
  * module).
  *
@@ -106,23 +106,40 @@ size_t wc_cq_bytes(const wc_cq *h);
  */
 wc_status wc_cq_gemm(const wc_cq *h, const float *x, float *y, int rows, wc_stream stream);
 
-/* Flags of wc_cq_gemm_ex. */
+/* Flags of wc_cq_gemm_ex and wc_cq_gemms_ex. */
 enum {
     /* Run the product on the tensor cores (tcgen05, bf16 operands in the
      * rotated domain, fp32 accumulation) instead of the bit-exact lut
-     * kernel: for many rows (encoder prefill, batched decode). Each output
-     * is within the bf16 bound DESIGN.md states; not bit-exact. */
+     * kernel: for many rows (encoder prefill, batched decode). Not
+     * bit-exact: each output y is within
+     * (2^-7 + (K + log2 G + 4)·2^-24) · Σ_k |x̂_k|·|ŵ_k| of the exact
+     * product (K = In rounded up to the group, x̂ and ŵ the rotated
+     * activation and weights). */
     WC_GEMM_TENSOR_CORES = 1,
+    /* The tensor cores from 32 rows on, the bit-exact lut kernel below:
+     * the choice a batched caller (multi-stream decode, prefill) makes. */
+    WC_GEMM_AUTO = 2,
 };
 
 /*
  * wc_cq_gemm with options (flags above). With WC_GEMM_TENSOR_CORES the first
  * call on a matrix builds its bf16 weight image on the device (or call
  * wc_cq_prepare_tc first, outside any stream capture), and each call uses a
- * per-thread device buffer for the rotated activations, grown on demand.
- * No reference counterpart: the reference has only the exact kernels.
+ * per-thread device buffer for the rotated activations, grown on demand: a
+ * thread's tensor-core calls must not overlap on the GPU (use one stream
+ * per calling thread). No reference counterpart: the reference has only
+ * the exact kernels.
  */
 wc_status wc_cq_gemm_ex(const wc_cq *h, const float *x, float *y, int rows, int flags, wc_stream stream);
+
+/*
+ * internal/cq/kernel.go:134 GEMMs with the options of wc_cq_gemm_ex. On the
+ * tensor cores the matrices that share a group size share one rotation of
+ * x, and up to 16 of them run as one grouped launch; otherwise it is
+ * wc_cq_gemms. Each ys[k] equals what wc_cq_gemm_ex gives for hs[k].
+ */
+wc_status wc_cq_gemms_ex(const wc_cq *const *hs, int n, const float *x, float *const *ys, int rows, int flags,
+                         wc_stream stream);
 
 /* Builds the tensor-core weight image of h now (synchronous). */
 wc_status wc_cq_prepare_tc(const wc_cq *h);
@@ -231,7 +248,10 @@ wc_status wc_quantize_rows_host(const float *x, size_t x_len, int cols, int widt
  * quantises each query head to int8 first (Int8.Act), making the logits
  * exact int32 dot products; without WC_ATTEND_ANY_ORDER the result equals
  * the reference's generic (purego) path bit for bit, up to the last-bit
- * rounding of exp noted in DESIGN.md.
+ * rounding of exp: the reference rounds Go's float64 math.Exp, this library
+ * CUDA's double exp; both are within one float64 ulp, so their float32
+ * roundings can differ only when e^x lies within about 2^-29 (relative) of
+ * a float32 rounding boundary.
  */
 wc_status wc_attend_int8(const float *q, int t, int heads, const int8_t *k8, const float *ks, const int8_t *v8,
                          const float *vs, int nkeys, int kv_heads, int qk, int vd, const int32_t *spans, float scale,

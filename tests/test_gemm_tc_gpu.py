@@ -89,3 +89,62 @@ def test_tc_gemm_views_and_reuse(wb, cuda):
     for lo, hi in ((0, 128), (5, 300), (640, 700)):
         part = tc_gemm(wb, cuda, m.Rows(lo, hi), x)
         assert np.array_equal(part, full[:, lo:hi])
+
+
+WC_GEMM_AUTO = 2
+
+
+def tc_gemms(wb, cuda, ms, x, flags):
+    rows = x.shape[0]
+    lib = wb._lib.lib()
+    xd = cuda.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    yds = [cuda.full((rows, m.Out()), float("nan"), dtype=cuda.float32, device="cuda") for m in ms]
+    hs = (ctypes.c_void_p * len(ms))(*[m.handle.value for m in ms])
+    ys = (ctypes.c_void_p * len(ms))(*[y.data_ptr() for y in yds])
+    wb._lib.check(lib.wc_cq_gemms_ex(hs, len(ms), ctypes.c_void_p(xd.data_ptr()), ys, rows, flags, None))
+    code = ctypes.c_int(-1)
+    wb._lib.check(lib.wc_device_status(ctypes.byref(code)))
+    assert code.value == 0, f"a bounded wait expired (code {code.value})"
+    return [y.cpu().numpy() for y in yds]
+
+
+@pytest.mark.parametrize("rows", [1, 96, 256])
+def test_tc_gemms_grouped(wb, cuda, rows):
+    """GEMMs on the tensor cores: Whistle's q/k/v/gate set (one rotation,
+    one grouped launch), a second group size in the same call, and more
+    matrices than one launch carries. Every output has the bits of its own
+    wc_cq_gemm_ex call and stays within the bf16 bound."""
+    rng = np.random.default_rng(40 + rows)
+    in_ = 512
+    ps = [wb.synth.random_packed(rng, o, in_, 128, 2, "lloyd") for o in (384, 96, 128, 512)]
+    ps += [wb.synth.random_packed(rng, o, in_, 32, 4, "lloyd") for o in (200, 64)]
+    ps += [wb.synth.random_packed(rng, 40 + 8 * k, in_, 128, 2, "lloyd") for k in range(14)]
+    ms = [wb.cq.New(p) for p in ps]
+    x = rng.normal(size=(rows, in_)).astype(np.float32)
+    got = tc_gemms(wb, cuda, ms, x, WC_GEMM_TENSOR_CORES)
+    for k, (p, m) in enumerate(zip(ps, ms)):
+        single = tc_gemm(wb, cuda, m, x)
+        assert np.array_equal(got[k].view(np.uint32), single.view(np.uint32)), k
+        xh, w = rotated_operands(p, x.astype(np.float64))
+        gamma = 2.0 ** -7 + (w.shape[1] + np.log2(p.group) + 4) * 2.0 ** -24
+        assert np.all(np.abs(got[k] - xh @ w.T) <= gamma * (np.abs(xh) @ np.abs(w).T)), k
+
+
+def test_auto_dispatch(wb, orc, cuda):
+    """WC_GEMM_AUTO: below 32 rows the bit-exact lut kernel (the oracle's
+    bits), from 32 rows the tensor cores (WC_GEMM_TENSOR_CORES's bits)."""
+    rng = np.random.default_rng(77)
+    ps = [wb.synth.random_packed(rng, o, 512, 128, 2, "lloyd") for o in (384, 96)]
+    ps[1].Codebook = ps[0].Codebook
+    ms = [wb.cq.New(p) for p in ps]
+    for rows in (8, 31, 32, 64):
+        x = rng.normal(size=(rows, 512)).astype(np.float32)
+        got = tc_gemms(wb, cuda, ms, x, WC_GEMM_AUTO)
+        if rows < 32:
+            for p, g in zip(ps, got):
+                want = orc.gemm_lut(orc.OracleMatrix.of(p), x, rows)
+                assert np.array_equal(g.view(np.uint32), want.view(np.uint32))
+        else:
+            tc = tc_gemms(wb, cuda, ms, x, WC_GEMM_TENSOR_CORES)
+            for g, t in zip(got, tc):
+                assert np.array_equal(g.view(np.uint32), t.view(np.uint32))

@@ -1,4 +1,4 @@
-"""Data parallelism across processes (SURVEY.md §8e), on the CPU: world-size
+"""Data parallelism across processes, on the CPU: world-size
 2 gloo ranks and a TCP store, launched as child processes. No GPU: the path
 has no data-path collective; these check the host logic (shard map,
 max-over-ranks timing, result gathering) and failure detection (a rank that
