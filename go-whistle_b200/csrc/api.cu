@@ -331,33 +331,70 @@ static bool try_stream(const wc_cq *const *ms, int n, const float *x, float *con
     if (total < kStreamMinBytes) return false;
     const int sms = sm_count();
     *status = WC_OK;
-    for (int base = 0; base < n; base += kMaxStreamMats) {
-        int cnt = n - base < kMaxStreamMats ? n - base : kMaxStreamMats;
-        auto p = std::make_unique<StreamParams>();
-        p->shape = ms[base]->shape;
+    // Consecutive matrices that are views of one storage with equal Out, a
+    // constant row step and evenly spaced outputs form one run (a stack of
+    // calls on one weight tensor is a single run), so one launch carries
+    // up to kMaxStreamRuns runs of any length.
+    auto p = std::make_unique<StreamParams>();
+    auto flush = [&]() -> bool {
+        if (p->nruns == 0) return true;
+        const StreamRun &l = p->runs[p->nruns - 1];
+        p->total_tiles = l.tile0 + l.count * l.tpm;
+        p->shape = ms[0]->shape;
         p->x = x;
-        int tiles = 0, used = 0;
-        for (int k = 0; k < cnt; k++) {
-            const wc_cq *m = ms[base + k];
-            if (m->out == 0) continue;
-            p->views[used] = m->stream_view();
-            p->y[used] = ys[base + k];
-            p->tile_start[used] = tiles;
-            tiles += (m->out + 31) / 32;
-            used++;
-        }
-        p->tile_start[used] = tiles;
-        p->n = used;
-        p->total_tiles = tiles;
         p->smem_base = stream_smem_base();
-        if (used == 0) continue;
-        int ctas = tiles < sms ? tiles : sms;
+        const int ctas = p->total_tiles < sms ? p->total_tiles : sms;
         cudaError_t e = launch_stream(*p, ctas, st);
+        p->nruns = 0;
         if (e != cudaSuccess) {
             *status = cuda_error(e, "cq stream kernel");
-            return true;
+            return false;
         }
+        return true;
+    };
+    p->nruns = 0;
+    long long tiles = 0;
+    for (int k = 0; k < n; k++) {
+        const wc_cq *m = ms[k];
+        if (m->out == 0) continue;
+        const CqView sv = m->stream_view();
+        const int tpm = (m->out + 31) / 32;
+        if (p->nruns > 0) {
+            StreamRun &r = p->runs[p->nruns - 1];
+            const bool same = sv.idx == r.v.idx && sv.nrm == r.v.nrm && sv.ld == r.v.ld && sv.out == r.v.out;
+            const int last_row0 = r.v.row0 + (r.count - 1) * r.row_step;
+            const intptr_t last_y = (intptr_t)(r.y + (long long)(r.count - 1) * r.y_step);
+            const intptr_t dy = (intptr_t)ys[k] - last_y;  // bytes; a whole number of floats
+            const bool fits = tiles + tpm < (1LL << 30) && dy % (intptr_t)sizeof(float) == 0;
+            const long long ystep = (long long)(dy / (intptr_t)sizeof(float));
+            if (same && fits && r.count == 1) {
+                r.row_step = sv.row0 - last_row0;
+                r.y_step = ystep;
+                r.count = 2;
+                tiles += tpm;
+                continue;
+            }
+            if (same && fits && sv.row0 - last_row0 == r.row_step && ystep == r.y_step) {
+                r.count++;
+                tiles += tpm;
+                continue;
+            }
+        }
+        if (p->nruns == kMaxStreamRuns || tiles + tpm >= (1LL << 30)) {
+            if (!flush()) return true;
+            tiles = 0;
+        }
+        StreamRun &r = p->runs[p->nruns++];
+        r.v = sv;
+        r.y = ys[k];
+        r.y_step = 0;
+        r.row_step = 0;
+        r.count = 1;
+        r.tpm = tpm;
+        r.tile0 = (int)tiles;
+        tiles += tpm;
     }
+    flush();
     return true;
 }
 

@@ -26,17 +26,27 @@ size_t lut_smem_bytes(const CqShape &s);
 cudaError_t launch_lut(const LutParams &p, int tiles, int acts, cudaStream_t st);
 
 // The streaming batch-1 kernel (cq_lut_stream.cu): views point at the
-// "stream layout" (sidx/snrm) and tiles are 32 rows.
-constexpr int kMaxStreamMats = 512;
+// "stream layout" (sidx/snrm) and tiles are 32 rows. Matrices come as
+// strided runs: matrix i of a run is the view v with row0 + i·row_step,
+// writing y + i·y_step (one matrix per run in general; many for a stack of
+// views of one storage with evenly spaced outputs).
+constexpr int kMaxStreamRuns = 256;
+struct StreamRun {
+    CqView v;          // the run's first matrix
+    float *y;          // its output [v.out]
+    long long y_step;  // floats between consecutive matrices' outputs
+    int row_step;      // layout rows between consecutive matrices' row0
+    int count;         // matrices in the run
+    int tpm;           // 32-row tiles per matrix
+    int tile0;         // the run's first tile in the launch
+};
 struct StreamParams {
     CqShape shape;
     const float *x;   // one activation [in]
-    int n;            // matrices
-    int total_tiles;  // Σ ceil(out/32)
+    int nruns;
+    int total_tiles;  // Σ count·tpm
     int smem_base;    // stream_smem_base() the launch was sized for
-    CqView views[kMaxStreamMats];
-    float *y[kMaxStreamMats];
-    int tile_start[kMaxStreamMats + 1];
+    StreamRun runs[kMaxStreamRuns];
 };
 // The tensor-core GEMM (cq_gemm_tc.cu): operand images are pre-swizzled
 // 128 x 64 bf16 tiles.

@@ -70,16 +70,40 @@ __device__ __forceinline__ void prefetch_l2(const void *addr, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(addr), "r"(bytes) : "memory");
 }
 
-__device__ __forceinline__ int find_tile_matrix(const StreamParams &p, int t) {
-    int lo = 0, hi = p.n - 1;
+// The run holding tile t.
+__device__ __forceinline__ int find_run(const StreamParams &p, int t) {
+    int lo = 0, hi = p.nruns - 1;
     while (lo < hi) {
         int mid = (lo + hi + 1) >> 1;
-        if (p.tile_start[mid] <= t)
+        if (p.runs[mid].tile0 <= t)
             lo = mid;
         else
             hi = mid - 1;
     }
     return lo;
+}
+
+// Tile t's run, trying k (the previous tile's) first.
+__device__ __forceinline__ int run_from(const StreamParams &p, int t, int k) {
+    if (k >= 0 && p.runs[k].tile0 <= t && t < p.runs[k].tile0 + p.runs[k].count * p.runs[k].tpm) return k;
+    return find_run(p, t);
+}
+
+// Tile t of run k: its matrix's view and output, and the tile's first row.
+struct TileLoc {
+    CqView v;
+    float *y;
+    int r0;
+};
+__device__ __forceinline__ TileLoc tile_loc(const StreamParams &p, int t, int k) {
+    const StreamRun &R = p.runs[k];
+    const int u = t - R.tile0, i = u / R.tpm;
+    TileLoc L;
+    L.v = R.v;
+    L.v.row0 += i * R.row_step;
+    L.y = R.y + (long long)i * R.y_step;
+    L.r0 = (u - i * R.tpm) * 32;
+    return L;
 }
 
 // Rotation, group bounds, 8191/M and steps for one activation (lut.go:160-178).
@@ -177,9 +201,9 @@ __device__ void build_pass_tables(const CqShape &s, const float *xs, const float
 // run of 32 rows x NG norms per superchunk, all inside the matrix.
 template <int NG>
 __device__ __forceinline__ void prefetch_tile(const StreamParams &p, int t, int sc0, int nsc_pass) {
-    const int k = find_tile_matrix(p, t);
-    const CqView &v = p.views[k];
-    const int r0 = (t - p.tile_start[k]) * 32;
+    const TileLoc L = tile_loc(p, t, find_run(p, t));
+    const CqView &v = L.v;
+    const int r0 = L.r0;
     const int rows = min(32, v.out - r0);
     const int R0 = v.row0 + r0;
     for (int scl = 0; scl < nsc_pass; scl++) {
@@ -278,12 +302,6 @@ __device__ __forceinline__ void load_superchunk(const CqView &v, int sc, int R, 
     }
 }
 
-// Tile t's matrix, trying k (the previous tile's) first.
-__device__ __forceinline__ int tile_matrix_from(const StreamParams &p, int t, int k) {
-    if (k >= 0 && p.tile_start[k] <= t && t < p.tile_start[k + 1]) return k;
-    return find_tile_matrix(p, t);
-}
-
 template <int GB>
 __global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const __grid_constant__ StreamParams p) {
     constexpr int P = GB / 2;    // byte pairs per group
@@ -307,9 +325,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const 
         const int t_b = (int)(((long long)p.total_tiles * blockIdx.x) / gridDim.x);
         const int t_e = (int)(((long long)p.total_tiles * (blockIdx.x + 1)) / gridDim.x);
         for (int t = t_b + warp; t < t_e; t += kStreamWarps) {
-            const int k = find_tile_matrix(p, t);
-            const int r = (t - p.tile_start[k]) * 32 + lane;
-            if (r < p.views[k].out) p.y[k][r] = __int_as_float(0x7fc00000);
+            const TileLoc L = tile_loc(p, t, find_run(p, t));
+            const int r = L.r0 + lane;
+            if (r < L.v.out) L.y[r] = __int_as_float(0x7fc00000);
         }
         return;
     }
@@ -342,9 +360,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const 
 
         int k = -1;
         for (int t = t_begin + warp; t < t_end; t += kStreamWarps) {
-            k = tile_matrix_from(p, t, k);
-            const CqView v = p.views[k];
-            const int r = (t - p.tile_start[k]) * 32 + lane;
+            k = run_from(p, t, k);
+            const TileLoc loc = tile_loc(p, t, k);
+            const CqView &v = loc.v;
+            const int r = loc.r0 + lane;
             const bool valid = r < v.out;
             const int R = v.row0 + r;
             const int off = v.row0 & 31;
@@ -375,7 +394,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const 
                     cbw[w] = word;
                 }
             }
-            float *yk = p.y[k];
+            float *yk = loc.y;
             float y = 0.0f;
             if (pass > 0 && valid) y = yk[r];
 

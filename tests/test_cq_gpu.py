@@ -3,6 +3,7 @@ restatement of the reference's lut and Exact kernels."""
 
 from __future__ import annotations
 
+import ctypes
 import threading
 
 import numpy as np
@@ -293,3 +294,54 @@ def test_gemms_host_chunked(wb, orc, cuda, rows, view_rows):
     want = orc.gemm_lut(orc.OracleMatrix.of(base), x, rows, threads=8).reshape(rows, n, view_rows)
     for k in (0, 17, n - 1):
         assert bits_eq(flat[k].reshape(rows, view_rows), want[:, k])
+
+
+def test_stream_runs(wb, orc, cuda):
+    """GEMMs calls the streaming kernel carries as strided runs: a stack of
+    views with a constant row step and contiguous outputs, one matrix
+    repeated into evenly spaced outputs with gaps, steps that change (new
+    runs), and more distinct runs than one launch holds. Bit for bit the
+    oracle's products."""
+    rng = np.random.default_rng(123)
+    base = wb.synth.random_packed(rng, 64 * 160, 512, 32, 4, "lloyd")
+    big = wb.cq.New(base)
+    want = orc.gemm_lut(orc.OracleMatrix.of(base), (x := rng.normal(size=512).astype(np.float32)), 1, threads=8)
+    want = want.reshape(-1)
+    xd = cuda.from_numpy(x).cuda()
+    lib = wb._lib.lib()
+
+    def gemms(views, out_ptrs):
+        hs = (ctypes.c_void_p * len(views))(*[v.handle.value for v in views])
+        ys = (ctypes.c_void_p * len(views))(*out_ptrs)
+        wb._lib.check(lib.wc_cq_gemms(hs, len(views), ctypes.c_void_p(xd.data_ptr()), ys, 1, None))
+        cuda.cuda.synchronize()
+
+    # a stack: 64 views of 160 rows, outputs back to back (one run)
+    views = [big.Rows(160 * k, 160 * (k + 1)) for k in range(64)]
+    y = cuda.full((64 * 160,), float("nan"), dtype=cuda.float32, device="cuda")
+    gemms(views, [y.data_ptr() + 4 * 160 * k for k in range(64)])
+    assert bits_eq(y.cpu().numpy(), want)
+    # one view repeated 60 times into outputs 200 floats apart (row step 0)
+    y2 = cuda.full((60 * 200,), float("nan"), dtype=cuda.float32, device="cuda")
+    v = views[5]
+    gemms([v] * 60, [y2.data_ptr() + 4 * 200 * k for k in range(60)])
+    got = y2.cpu().numpy().reshape(60, 200)
+    for k in range(60):
+        assert bits_eq(got[k, :160], want[800:960]) and np.all(np.isnan(got[k, 160:]))
+    # steps that change: rows 0, 160, 320 then 960, 1280, ...; outputs packed
+    # (each call streams at least 2 MB of index, so the streaming kernel runs)
+    idx = [0, 1, 2, 6, 8, 10, 12, 13, 63, 62, 61] * 6
+    y3 = cuda.full((len(idx) * 160,), float("nan"), dtype=cuda.float32, device="cuda")
+    gemms([views[i] for i in idx], [y3.data_ptr() + 4 * 160 * j for j in range(len(idx))])
+    got = y3.cpu().numpy().reshape(len(idx), 160)
+    for j, i in enumerate(idx):
+        assert bits_eq(got[j], want[160 * i:160 * (i + 1)])
+    # 300 matrices in random order into randomly placed outputs: about one
+    # run each, more than one launch holds
+    order = rng.integers(0, 64, 300)
+    place = rng.permutation(300)
+    y4 = cuda.full((300 * 160,), float("nan"), dtype=cuda.float32, device="cuda")
+    gemms([views[i] for i in order], [y4.data_ptr() + 4 * 160 * int(place[j]) for j in range(300)])
+    got = y4.cpu().numpy().reshape(300, 160)
+    for j, i in enumerate(order):
+        assert bits_eq(got[place[j]], want[160 * i:160 * (i + 1)])
