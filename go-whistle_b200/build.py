@@ -1,4 +1,5 @@
-"""Builds libwhistle_b200.so in-tree with nvcc for sm_100a (no GPU needed).
+"""Builds libwhistle_b200.so in-tree with nvcc for sm_100a (no GPU needed),
+and the C++ host mirror libwhistle_b200_host.so (g++) beside it.
 
     python go-whistle_b200/build.py [--verbose]
 
@@ -19,6 +20,8 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 LIB = HERE / "libwhistle_b200.so"
+HOST = HERE / "host"
+HOST_LIB = HERE / "libwhistle_b200_host.so"
 OBJ = HERE / "_build"
 INCLUDE = HERE.parent / "include"
 
@@ -46,8 +49,36 @@ def _stale() -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
+def _host_stale() -> bool:
+    if not HOST_LIB.exists():
+        return True
+    t = HOST_LIB.stat().st_mtime
+    deps = list(HOST.glob("*.cpp")) + list(HOST.glob("*.hpp")) + [LIB, INCLUDE / "whistle_b200.h"]
+    return any(d.stat().st_mtime > t for d in deps)
+
+
+def build_host(force: bool = False, verbose: bool = False) -> Path:
+    """The C++ host mirror (host/whistle.hpp) as libwhistle_b200_host.so,
+    linked against libwhistle_b200.so beside it."""
+    if not force and not _host_stale():
+        return HOST_LIB
+    cxx = os.environ.get("CXX") or shutil.which("g++") or "g++"
+    tmp = HOST_LIB.with_suffix(".so.tmp")
+    cmd = [cxx, "-O2", "-std=c++17", "-Wall", "-Wextra", "-fPIC", "-shared", "-I", str(INCLUDE),
+           *map(str, sorted(HOST.glob("*.cpp"))), "-o", str(tmp), "-L", str(HERE), "-lwhistle_b200",
+           "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if verbose or r.returncode != 0:
+        sys.stderr.write(r.stdout + r.stderr)
+    if r.returncode != 0:
+        raise RuntimeError("g++ failed on the C++ host mirror")
+    os.replace(tmp, HOST_LIB)
+    return HOST_LIB
+
+
 def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and not _stale():
+        build_host(force=False, verbose=verbose)
         return LIB
     OBJ.mkdir(exist_ok=True)
     cc = nvcc()
@@ -71,6 +102,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         sys.stderr.write(r.stdout + r.stderr)
         raise RuntimeError("nvcc link failed")
     os.replace(tmp, LIB)
+    build_host(force=True, verbose=verbose)
     return LIB
 
 

@@ -482,11 +482,11 @@ extern "C" wc_status wc_cq_gemms(const wc_cq *const *hs, int n, const float *x, 
 // per calling thread, freed at thread exit.
 namespace {
 struct HostScratch {
-    void *p[4] = {nullptr, nullptr, nullptr, nullptr};
-    size_t n[4] = {0, 0, 0, 0};
-    int device[4] = {-1, -1, -1, -1};
+    void *p[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+    size_t n[5] = {0, 0, 0, 0, 0};
+    int device[5] = {-1, -1, -1, -1, -1};
     ~HostScratch() {
-        for (int i = 0; i < 4; i++)
+        for (int i = 0; i < 5; i++)
             if (p[i]) cudaFree(p[i]);
     }
     cudaError_t get(int i, size_t bytes, void **out) {
@@ -1038,6 +1038,65 @@ extern "C" wc_status wc_attend_int8(const float *q, int t, int heads, const int8
     p.quant_q = (flags & WC_ATTEND_QUANT_Q) ? 1 : 0;
     p.k_aligned4 = (qk % 4 == 0) && ((kv_heads * qk) % 4 == 0) && aligned4(k8);
     return run_attend(p, 1, (cudaStream_t)stream, (flags & WC_ATTEND_ANY_ORDER) != 0);
+}
+
+// AttendInt8Spans on host slices: every array is copied to one device
+// buffer (the caller's probs too, so entries outside the spans keep their
+// values), the kernels run, and out and probs are copied back.
+extern "C" wc_status wc_attend_int8_host(const float *q, size_t q_len, int t, int heads, const int8_t *k8,
+                                         size_t k8_len, const float *ks, size_t ks_len, const int8_t *v8,
+                                         size_t v8_len, const float *vs, size_t vs_len, int kv_heads, int qk, int vd,
+                                         const int32_t *spans, float scale, int flags, float *probs, size_t probs_len,
+                                         float *out, size_t out_len) {
+    if (t < 0) return set_error(WC_ERR_INVALID, fmt("needle: %d query rows", t));
+    wc_status st = check_attend(heads, kv_heads, qk, vd, 0);
+    if (st != WC_OK) return st;
+    const size_t kcols = (size_t)kv_heads * qk, vcols = (size_t)kv_heads * vd;
+    if (k8_len % kcols != 0)
+        return set_error(WC_ERR_INVALID, fmt("needle: %zu key codes are not rows of %zu", k8_len, kcols));
+    const size_t n = k8_len / kcols;
+    if (ks_len != n * kv_heads || v8_len != n * vcols || vs_len != n * kv_heads)
+        return set_error(WC_ERR_INVALID, fmt("needle: %zu keys with %zu key scales, %zu value codes and %zu value "
+                                             "scales",
+                                             n, ks_len, v8_len, vs_len));
+    if (q_len != (size_t)t * heads * qk || out_len != (size_t)t * heads * vd ||
+        (probs && probs_len < (size_t)t * heads * n))
+        return set_error(WC_ERR_INVALID, fmt("needle: AttendInt8(len %zu, %d rows, %d heads of %d) into %zu outputs "
+                                             "and %zu probabilities",
+                                             q_len, t, heads, qk, out_len, probs ? probs_len : 0));
+    if (n > (size_t)INT32_MAX) return set_error(WC_ERR_UNSUPPORTED, "needle: too many keys");
+    if (t == 0) return WC_OK;
+    auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    const size_t b_q = up(q_len * 4), b_k = up(k8_len ? k8_len : 1), b_ks = up(ks_len * 4 + 4),
+                 b_v = up(v8_len ? v8_len : 1), b_vs = up(vs_len * 4 + 4), b_sp = up((size_t)t * 16),
+                 b_p = probs ? up((size_t)t * heads * n * 4 + 4) : 0, b_o = up(out_len * 4);
+    void *base = nullptr;
+    WB_CUDA(t_scratch.get(4, b_q + b_k + b_ks + b_v + b_vs + b_sp + b_p + b_o, &base));
+    // One buffer: q, k codes, k scales, v codes, v scales, spans, probs, out.
+    char *c = (char *)base;
+    const size_t o_k = b_q, o_ks = o_k + b_k, o_v = o_ks + b_ks, o_vs = o_v + b_v, o_sp = o_vs + b_vs,
+                 o_p = o_sp + b_sp, o_o = o_p + b_p;
+    float *dq = (float *)c;
+    int8_t *dk = (int8_t *)(c + o_k);
+    float *dks = (float *)(c + o_ks);
+    int8_t *dv = (int8_t *)(c + o_v);
+    float *dvs = (float *)(c + o_vs);
+    int32_t *dsp = (int32_t *)(c + o_sp);
+    float *dp = probs ? (float *)(c + o_p) : nullptr;
+    float *dout = (float *)(c + o_o);
+    WB_CUDA(cudaMemcpy(dq, q, q_len * 4, cudaMemcpyHostToDevice));
+    if (k8_len) WB_CUDA(cudaMemcpy(dk, k8, k8_len, cudaMemcpyHostToDevice));
+    if (ks_len) WB_CUDA(cudaMemcpy(dks, ks, ks_len * 4, cudaMemcpyHostToDevice));
+    if (v8_len) WB_CUDA(cudaMemcpy(dv, v8, v8_len, cudaMemcpyHostToDevice));
+    if (vs_len) WB_CUDA(cudaMemcpy(dvs, vs, vs_len * 4, cudaMemcpyHostToDevice));
+    if (spans) WB_CUDA(cudaMemcpy(dsp, spans, (size_t)t * 16, cudaMemcpyHostToDevice));
+    if (probs && n) WB_CUDA(cudaMemcpy(dp, probs, (size_t)t * heads * n * 4, cudaMemcpyHostToDevice));
+    st = wc_attend_int8(dq, t, heads, dk, dks, dv, dvs, (int)n, kv_heads, qk, vd, spans ? dsp : nullptr, scale, flags,
+                        dp, dout, nullptr);
+    if (st != WC_OK) return st;
+    WB_CUDA(cudaMemcpy(out, dout, out_len * 4, cudaMemcpyDeviceToHost));
+    if (probs && n) WB_CUDA(cudaMemcpy(probs, dp, (size_t)t * heads * n * 4, cudaMemcpyDeviceToHost));
+    return WC_OK;
 }
 
 extern "C" wc_status wc_attend_int8_streams(int streams, const float *q, int heads, const int8_t *k8, const float *ks,

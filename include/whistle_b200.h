@@ -258,6 +258,19 @@ wc_status wc_attend_int8(const float *q, int t, int heads, const int8_t *k8, con
                          int flags, float *probs, float *out, wc_stream stream);
 
 /*
+ * AttendInt8Spans (internal/needle/int8.go:208) on host slices, as the Go
+ * shim calls it: q [t][heads][qk]; k8/ks and v8/vs the int8 rows and
+ * scales of Int8Rows (nkeys = k8_len / (kv_heads·qk)); spans [t][4] or
+ * NULL for every key; probs NULL or at least t·heads·nkeys values, written
+ * at the spans' keys only; out [t][heads][vd]. Lengths are checked (a
+ * mismatch is WC_ERR_INVALID); synchronous.
+ */
+wc_status wc_attend_int8_host(const float *q, size_t q_len, int t, int heads, const int8_t *k8, size_t k8_len,
+                              const float *ks, size_t ks_len, const int8_t *v8, size_t v8_len, const float *vs,
+                              size_t vs_len, int kv_heads, int qk, int vd, const int32_t *spans, float scale,
+                              int flags, float *probs, size_t probs_len, float *out, size_t out_len);
+
+/*
  * The decode step of `streams` independent streams, one query row each,
  * against each stream's own int8 KV cache: AttendInt8 (int8.go:194) per
  * stream with keys(0) = nkeys[b], as Attention.extendInt8 (cache.go:120)
