@@ -399,15 +399,26 @@ static bool try_stream(const wc_cq *const *ms, int n, const float *x, float *con
 }
 
 // One lut launch sequence for matrices that share their tables.
-static wc_status run_lut(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows,
-                         cudaStream_t st) {
-    wc_status sst;
-    if (try_stream(ms, n, x, ys, rows, st, &sst)) return sst;
+// Activations up to which a product below the streaming threshold runs on
+// the cluster kernel (groups split over the CTAs of a cluster) instead of
+// the per-tile kernel (every CTA tabulates the whole activation).
+static const int kSplitMaxRows = 4;
+
+static bool try_split(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows, cudaStream_t st,
+                      wc_status *status) {
+    if (rows > kSplitMaxRows || n == 0 || !split_eligible(ms[0]->shape)) return false;
+    int dev = 0, limit = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+        return false;
+    if (split_smem_bytes(ms[0]->shape) > (size_t)limit) return false;
+    *status = WC_OK;
     for (int base = 0; base < n; base += kMaxLaunchMats) {
         int cnt = n - base < kMaxLaunchMats ? n - base : kMaxLaunchMats;
         auto p = std::make_unique<LutParams>();
         p->shape = ms[base]->shape;
         p->x = x;
+        p->tile_rows = 32;
         int tiles = 0, used = 0;
         for (int k = 0; k < cnt; k++) {
             const wc_cq *m = ms[base + k];
@@ -415,7 +426,42 @@ static wc_status run_lut(const wc_cq *const *ms, int n, const float *x, float *c
             p->views[used] = m->view();
             p->y[used] = ys[base + k];
             p->tile_start[used] = tiles;
-            tiles += (m->out + kTileRows - 1) / kTileRows;
+            tiles += split_tiles(m->out);
+            used++;
+        }
+        p->tile_start[used] = tiles;
+        p->n = used;
+        if (used == 0) continue;
+        p->act0 = 0;
+        cudaError_t e = launch_split(*p, tiles, rows, st);
+        if (e != cudaSuccess) {
+            *status = cuda_error(e, "cq split kernel");
+            return true;
+        }
+    }
+    return true;
+}
+
+static wc_status run_lut(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows,
+                         cudaStream_t st) {
+    wc_status sst;
+    if (try_stream(ms, n, x, ys, rows, st, &sst)) return sst;
+    if (try_split(ms, n, x, ys, rows, st, &sst)) return sst;
+    for (int base = 0; base < n; base += kMaxLaunchMats) {
+        int cnt = n - base < kMaxLaunchMats ? n - base : kMaxLaunchMats;
+        auto p = std::make_unique<LutParams>();
+        p->shape = ms[base]->shape;
+        p->x = x;
+        // One activation: smaller tiles, so more CTAs share the latency.
+        p->tile_rows = rows == 1 ? kTileRowsOne : kTileRows;
+        int tiles = 0, used = 0;
+        for (int k = 0; k < cnt; k++) {
+            const wc_cq *m = ms[base + k];
+            if (m->out == 0) continue;
+            p->views[used] = m->view();
+            p->y[used] = ys[base + k];
+            p->tile_start[used] = tiles;
+            tiles += (m->out + p->tile_rows - 1) / p->tile_rows;
             used++;
         }
         p->tile_start[used] = tiles;

@@ -6,8 +6,10 @@
 
 namespace wb {
 
-// Rows per CTA tile of the lut kernel.
+// Rows per CTA tile of the lut kernel: kTileRows for several activations,
+// kTileRowsOne for one (four times the CTAs, for latency).
 constexpr int kTileRows = 64;
+constexpr int kTileRowsOne = 16;
 // Matrices per GEMMs launch (their views and outputs travel as kernel
 // parameters).
 constexpr int kMaxLaunchMats = 128;
@@ -17,6 +19,7 @@ struct LutParams {
     const float *x;  // [rows][in] activations
     int act0;        // first activation of this launch (grid.y is relative)
     int n;           // matrices in this launch
+    int tile_rows;   // kTileRows or kTileRowsOne
     CqView views[kMaxLaunchMats];
     float *y[kMaxLaunchMats];               // [rows][views[k].out] each
     int tile_start[kMaxLaunchMats + 1];     // prefix sum of row tiles
@@ -24,6 +27,13 @@ struct LutParams {
 
 size_t lut_smem_bytes(const CqShape &s);
 cudaError_t launch_lut(const LutParams &p, int tiles, int acts, cudaStream_t st);
+
+// The cluster kernel for one (or a few) activations at low latency
+// (cq_lut_split.cu): LutParams with tiles of 32 rows (split_tiles).
+bool split_eligible(const CqShape &s);
+size_t split_smem_bytes(const CqShape &s);
+int split_tiles(int out);
+cudaError_t launch_split(const LutParams &p, int tiles, int acts, cudaStream_t st);
 
 // The streaming batch-1 kernel (cq_lut_stream.cu): views point at the
 // "stream layout" (sidx/snrm) and tiles are 32 rows. Matrices come as

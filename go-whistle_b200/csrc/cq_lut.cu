@@ -105,6 +105,49 @@ __device__ __forceinline__ int32_t lookup_dispatch(const uint8_t *src, const int
     }
 }
 
+// A (row, group) item's index bytes, loaded ahead of the table build so the
+// load's latency overlaps it.
+template <int GB>
+struct ItemWords {
+    uint32_t w[GB >= 4 ? GB / 4 : 1];
+};
+
+template <int GB>
+__device__ __forceinline__ void load_item(ItemWords<GB> &W, const uint8_t *__restrict__ src) {
+    if constexpr (GB >= 16) {
+#pragma unroll
+        for (int c = 0; c < GB / 16; c++) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(src) + c);
+            W.w[4 * c] = v.x;
+            W.w[4 * c + 1] = v.y;
+            W.w[4 * c + 2] = v.z;
+            W.w[4 * c + 3] = v.w;
+        }
+    } else if constexpr (GB == 8) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2 *>(src));
+        W.w[0] = v.x;
+        W.w[1] = v.y;
+    } else if constexpr (GB == 4) {
+        W.w[0] = __ldg(reinterpret_cast<const uint32_t *>(src));
+    } else {
+        W.w[0] = __ldg(reinterpret_cast<const uint16_t *>(src));
+    }
+}
+
+// The same sum as lookup_group<GB> on preloaded bytes.
+template <int GB>
+__device__ __forceinline__ int32_t lookup_item(const ItemWords<GB> &W, const int16_t *__restrict__ tab, int pos0) {
+    int32_t sum = 0;
+#pragma unroll
+    for (int b = 0; b < GB; b++) {
+        const uint32_t byte = (W.w[b >> 2] >> (8 * (b & 3))) & 0xffu;
+        const int pos = pos0 + b;
+        sum += tab[(2 * pos) * 16 + (byte & 15u)];
+        sum += tab[(2 * pos + 1) * 16 + (byte >> 4)];
+    }
+    return sum;
+}
+
 template <int GB>
 __global__ void __launch_bounds__(kThreads) cq_lut_kernel(const __grid_constant__ LutParams p) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -116,12 +159,32 @@ __global__ void __launch_bounds__(kThreads) cq_lut_kernel(const __grid_constant_
     float *xs = reinterpret_cast<float *>(smem);                              // [pad]
     float *steps = xs + pad;                                                  // [groups]
     float *invs = steps + groups;                                             // [groups]
-    float *terms = invs + groups;                                             // [kTileRows][groups+1]
+    float *terms = invs + groups;                                             // [tile rows][groups+1]
     size_t tab_off = (sizeof(float) * ((size_t)pad + 2 * groups + (size_t)kTileRows * (groups + 1)) + 15) & ~(size_t)15;
     int16_t *tab = reinterpret_cast<int16_t *>(smem + tab_off);               // [npos][16]
 
     const int act = blockIdx.y + p.act0;
     const float *x = p.x + (size_t)act * s.in;
+
+    // This CTA's matrix and row tile, and this thread's first (row, group)
+    // item, whose index bytes and norm are loaded now.
+    const int TR = p.tile_rows;
+    const int k = find_matrix(p, blockIdx.x);
+    const CqView v = p.views[k];
+    const int r0 = (blockIdx.x - p.tile_start[k]) * TR;
+    const int nrows = min(TR, v.out - r0);
+    ItemWords<(GB > 0 ? GB : 4)> first;
+    __half first_n = __ushort_as_half((unsigned short)0);
+    bool have_first = false;
+    if constexpr (GB > 0) {
+        const int rl = tid % TR, g = tid / TR;
+        if (tid < TR * groups && rl < nrows) {
+            const size_t lrow = (size_t)g * v.ld + (size_t)(v.row0 + r0 + rl);
+            load_item<GB>(first, v.idx + lrow * gb);
+            first_n = v.nrm[lrow];
+            have_first = true;
+        }
+    }
 
     // Rotate: x zero-padded to pad (lut.go:163-165), then fwht per group.
     for (int k = tid; k < pad; k += kThreads) xs[k] = k < s.in ? x[k] : 0.0f;
@@ -176,15 +239,17 @@ __global__ void __launch_bounds__(kThreads) cq_lut_kernel(const __grid_constant_
     }
     __syncthreads();
 
-    // This CTA's matrix and row tile.
-    const int k = find_matrix(p, blockIdx.x);
-    const CqView v = p.views[k];
-    const int r0 = (blockIdx.x - p.tile_start[k]) * kTileRows;
-    const int nrows = min(kTileRows, v.out - r0);
-
     // (row, group) items: exact integer sums, one float term each.
-    for (int e = tid; e < kTileRows * groups; e += kThreads) {
-        int rl = e % kTileRows, g = e / kTileRows;
+    if constexpr (GB > 0) {
+        if (have_first) {
+            const int rl = tid % TR, g = tid / TR;
+            const int32_t sum = lookup_item<GB>(first, tab, g * gb);
+            const float coef = __fmul_rn(__half2float(first_n), steps[g]);
+            terms[rl * (groups + 1) + g] = __fmul_rn(__int2float_rn(sum), coef);
+        }
+    }
+    for (int e = tid + (GB > 0 ? kThreads : 0); e < TR * groups; e += kThreads) {
+        int rl = e % TR, g = e / TR;
         if (rl >= nrows) continue;
         size_t lrow = (size_t)g * v.ld + (size_t)(v.row0 + r0 + rl);
         int32_t sum = lookup_dispatch<GB>(v.idx + lrow * gb, tab, g * gb, gb);
