@@ -355,6 +355,49 @@ def prefill_component(pkg, torch, lib, frames=24000, reps=5):
             "roofline": "max(algorithmic bytes / measured HBM, flops / measured bf16 peak)"}
 
 
+def single_call_component(pkg, torch, lib, calls=20, reps=10):
+    """Batch-1 latency: one GEMV call at a time (configs[0]'s 2048 x 512
+    CQ4 G32, and the 16384 x 512 CQ4 vocabulary head), `calls` calls in a row
+    captured in a CUDA graph; hot = the same weights each call (L2-resident,
+    as a decode loop's weights are), cold = a distinct copy per call."""
+    rng = np.random.default_rng(5000)
+    st = torch.cuda.Stream()
+    sptr = ctypes.c_void_p(st.cuda_stream)
+    res = {}
+    for name, out, in_, group, bits in (("configs[0] 2048x512 CQ4 G32", 2048, 512, 32, 4),
+                                        ("head 16384x512 CQ4 G32", 16384, 512, 32, 4)):
+        mats = [pkg.cq.New(pkg.synth.random_packed(rng, out, in_, group, bits)) for _ in range(calls)]
+        x = torch.randn(in_, device="cuda", dtype=torch.float32)
+        y = torch.empty(out, device="cuda", dtype=torch.float32)
+        row = {}
+        for mode in ("hot", "cold"):
+            def run():
+                for i in range(calls):
+                    m = mats[0] if mode == "hot" else mats[i]
+                    pkg._lib.check(lib.wc_cq_gemm(m.handle, ctypes.c_void_p(x.data_ptr()),
+                                                  ctypes.c_void_p(y.data_ptr()), 1, sptr))
+
+            with torch.cuda.stream(st):
+                run()
+                st.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=st, capture_error_mode="relaxed"):
+                    run()
+                g.replay()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                for _ in range(reps):
+                    g.replay()
+                e1.record(st)
+            torch.cuda.synchronize()
+            row[f"us_per_call_{mode}"] = round(e0.elapsed_time(e1) * 1e3 / (reps * calls), 2)
+            del g
+        row["algorithmic_bytes"] = pkg.synth.algorithmic_bytes_gemv(out, in_, group, bits)
+        res[name] = row
+    return {"workload": "batch-1 GEMV latency, calls back to back in a CUDA graph (launch gaps included)",
+            "per_shape": res}
+
+
 def decode_gemm_component(pkg, torch, lib, streams=256, reps=20):
     """Multi-stream decode GEMMs: `streams` activation rows (one per stream)
     through Whistle's self-attention projections (q 384, k 96, v 128, gate
@@ -578,7 +621,8 @@ def run_b200(args, world, rank, local):
         line["components"] = {"int8_attention": attention_component(pkg, torch, lib, None, flags=3),
                               "int8_attention_exact_order": attention_component(pkg, torch, lib, None, flags=1),
                               "cq_gemm_prefill": prefill_component(pkg, torch, lib),
-                              "cq_gemm_decode_streams": decode_gemm_component(pkg, torch, lib)}
+                              "cq_gemm_decode_streams": decode_gemm_component(pkg, torch, lib),
+                              "cq_gemv_single_call": single_call_component(pkg, torch, lib)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.only:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
