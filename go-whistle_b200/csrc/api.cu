@@ -790,6 +790,8 @@ extern "C" wc_status wc_cq_prepare_tc(const wc_cq *h) {
 // exact lut kernel's table work per activation is cheaper than the
 // rotation, operand images and tiles of the tensor-core path.
 static const int kTcAutoRows = 32;
+// Rows from which the tensor-core path uses the persistent kernel.
+static const int kTcPersistRows = 1024;
 
 // Tensor-core products of matrices that read the same x (same In): one
 // rotation into the x̂ image per group size G, then one grouped launch per
@@ -817,6 +819,11 @@ static wc_status run_tc(const wc_cq *const *ms, int n, const float *x, float *co
         p.m = rows;
         p.kchunks = kchunks;
         p.err = err;
+        // Many rows: the persistent kernel (256-row weight tiles, two TMEM
+        // accumulators); few: one 128 x 128 tile per CTA.
+        const bool persistent = rows >= kTcPersistRows;
+        const int tile_n = persistent ? 256 : 128;
+        auto launch = [&]() { return persistent ? launch_gemm_tc_persistent(p, s) : launch_gemm_tc(p, s); };
         int tiles = 0;
         for (int j = i; j < n; j++) {
             const wc_cq *m = ms[j];
@@ -831,18 +838,18 @@ static wc_status run_tc(const wc_cq *const *ms, int n, const float *x, float *co
             t.n = m->out;
             t.ldy = m->out;
             t.tile0 = tiles;
-            tiles += (m->out + 127) / 128;
+            tiles += (m->out + tile_n - 1) / tile_n;
             if (p.nmats == kMaxTcMats) {
                 // Full: launch, and start the next group of matrices on the
                 // same image (a later launch only reads it).
-                e = launch_gemm_tc(p, s);
+                e = launch();
                 if (e != cudaSuccess) return cuda_error(e, "cq tensor-core kernel");
                 p.nmats = 0;
                 tiles = 0;
             }
         }
         if (p.nmats > 0) {
-            e = launch_gemm_tc(p, s);
+            e = launch();
             if (e != cudaSuccess) return cuda_error(e, "cq tensor-core kernel");
         }
     }

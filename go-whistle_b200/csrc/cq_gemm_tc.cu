@@ -254,6 +254,205 @@ __global__ void __launch_bounds__(kTcThreads, 3) cq_gemm_tc_kernel(const __grid_
     }
 }
 
+// ---- persistent kernel for many rows (encoder prefill) --------------------
+//
+// One CTA per SM loops over 128 x 256 tiles of y (t -> n-tile t mod NT,
+// m-tile t / NT, so the CTAs running together share m-tiles of x̂ in L2).
+// TMEM holds two 128 x 256 fp32 accumulators (all 512 columns): while the
+// epilogue warps drain one tile's accumulator, the MMA warp fills the other.
+//   warp 0 lane 0   producer: per 64-wide K chunk, one bulk copy of the x̂
+//                   chunk and two of the ŵ chunk (its two 128-row halves)
+//                   into a 3-stage ring
+//   warp 1 lane 0   MMA issuer: tcgen05.mma M = 128, N = 256, K = 16
+//   warps 2-5       epilogue: TMEM -> registers -> a per-warp staging tile
+//                   -> 256-byte row segments of y
+// Bounded waits as in the kernel above.
+constexpr int kPN = 256;
+constexpr int kPStages = 3;
+constexpr int kPStageBytes = 3 * kChunkBytes;  // x̂ 16 KB + ŵ 32 KB
+constexpr int kPThreads = 320;  // producer, MMA, eight epilogue warps
+constexpr int kPStgStride = 36;  // floats per staged row (32 + 4)
+constexpr uint32_t kPIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kPN >> 3) << 17) |
+                             ((uint32_t)(kTcM >> 4) << 24);
+
+__device__ __forceinline__ void umma_bf16_n256(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(dtmem),
+        "l"(adesc), "l"(bdesc), "r"(kPIdesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_p(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// The matrix and 256-row tile of global n-tile nt (mats[].tile0 in
+// 256-row units).
+__device__ __forceinline__ int p_matrix(const TcParams &p, int nt) {
+    int mi = 0;
+    while (mi + 1 < p.nmats && p.mats[mi + 1].tile0 <= nt) mi++;
+    return mi;
+}
+
+__global__ void __launch_bounds__(kPThreads, 1) cq_gemm_tc_persistent_kernel(const __grid_constant__ TcParams p,
+                                                                             int ntg, int total) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    unsigned char *ring = smem;                                              // [stages][x̂ 16K | ŵ 32K]
+    float *stg = reinterpret_cast<float *>(ring + kPStages * kPStageBytes);  // [8 warps][32][36]
+    uint64_t *full = reinterpret_cast<uint64_t *>(stg + 8 * 32 * kPStgStride);
+    uint64_t *empty = full + kPStages;
+    uint64_t *accf = empty + kPStages;  // [2] accumulator b is ready
+    uint64_t *acce = accf + 2;          // [2] accumulator b is drained
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acce + 2);
+    int *bail = reinterpret_cast<int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kchunks = p.kchunks;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&accf[b], 1);
+            mbar_init(&acce[b], 8);
+        }
+        *bail = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(2u * kPN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+    volatile int *vbail = bail;
+
+    if (warp == 0 && lane == 0) {
+        if (p.pdl) asm volatile("griddepcontrol.wait;" ::: "memory");
+        int c = 0;
+        for (int t = blockIdx.x; t < total && !*vbail; t += gridDim.x) {
+            const int nt = t % ntg, mt = t / ntg;
+            const TcMat &mat = p.mats[p_matrix(p, nt)];
+            const unsigned char *ga = p.a + (size_t)mt * kchunks * kChunkBytes;
+            const unsigned char *gb = mat.b + (size_t)(2 * (nt - mat.tile0)) * kchunks * kChunkBytes;
+            for (int kc = 0; kc < kchunks; kc++, c++) {
+                const int s = c % kPStages, round = c / kPStages;
+                if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
+                    atomicExch(p.err, 11);
+                    atomicExch(bail, 1);
+                    break;
+                }
+                unsigned char *st = ring + (size_t)s * kPStageBytes;
+                mbar_expect_tx(&full[s], kPStageBytes);
+                bulk_g2s(st, ga + (size_t)kc * kChunkBytes, kChunkBytes, &full[s]);
+                bulk_g2s(st + kChunkBytes, gb + (size_t)kc * kChunkBytes, kChunkBytes, &full[s]);
+                bulk_g2s(st + 2 * kChunkBytes, gb + (size_t)(kchunks + kc) * kChunkBytes, kChunkBytes, &full[s]);
+            }
+        }
+        // Nothing may land in shared memory after exit.
+        for (int q = c - kPStages < 0 ? 0 : c - kPStages; q < c; q++)
+            if (!mbar_wait(&full[q % kPStages], (q / kPStages) & 1)) atomicExch(p.err, 12);
+    } else if (warp == 1 && lane == 0) {
+        int c = 0, i = 0;
+        for (int t = blockIdx.x; t < total && !*vbail; t += gridDim.x, i++) {
+            const int b = i & 1, u = i >> 1;
+            if (u > 0 && !mbar_wait(&acce[b], (u - 1) & 1)) {
+                atomicExch(p.err, 13);
+                atomicExch(bail, 1);
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t d = tmem + (uint32_t)(b * kPN);
+            bool ok = true;
+            for (int kc = 0; kc < kchunks; kc++, c++) {
+                const int s = c % kPStages, round = c / kPStages;
+                if (!mbar_wait(&full[s], round & 1)) {
+                    atomicExch(p.err, 14);
+                    atomicExch(bail, 1);
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t a0 = smem_u32(ring + (size_t)s * kPStageBytes);
+                const uint32_t b0 = a0 + kChunkBytes;
+#pragma unroll
+                for (int k = 0; k < kTcK / 16; k++)
+                    umma_bf16_n256(d, umma_desc(a0 + 32 * k), umma_desc(b0 + 32 * k), (kc > 0 || k > 0) ? 1u : 0u);
+                umma_commit(&empty[s]);
+            }
+            if (!ok) break;
+            umma_commit(&accf[b]);
+        }
+    } else if (warp >= 2) {
+        const int part = warp & 3;          // TMEM lanes 32·part .. +31
+        const int half = (warp - 2) >> 2;   // columns 128·half .. +127
+        float *mystg = stg + (size_t)(warp - 2) * 32 * kPStgStride;
+        int i = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x, i++) {
+            const int b = i & 1, u = i >> 1;
+            bool ok = mbar_wait(&accf[b], u & 1);
+            ok = __all_sync(0xffffffffu, ok && *vbail == 0);
+            if (!ok) {
+                if (lane == 0) {
+                    atomicExch(p.err, 15);
+                    atomicExch(bail, 1);
+                }
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int nt = t % ntg, mt = t / ntg;
+            const TcMat &mat = p.mats[p_matrix(p, nt)];
+            const int col_base = (nt - mat.tile0) * kPN;
+            for (int cc = half * (kPN / 2); cc < (half + 1) * (kPN / 2); cc += 32) {
+                {
+                    uint32_t r[32];
+                    tmem_ld32(tmem + ((uint32_t)(part * 32) << 16) + (uint32_t)(b * kPN + cc), r);
+#pragma unroll
+                    for (int q = 0; q < 8; q++)
+                        *reinterpret_cast<uint4 *>(mystg + lane * kPStgStride + 4 * q) =
+                            make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+                }
+                __syncwarp();
+                // The warp's 32 rows x 32 columns: 8 lanes per row, four rows
+                // per instruction.
+                const int sub = lane >> 3, c4 = (lane & 7) * 4;
+                for (int rr = sub; rr < 32; rr += 4) {
+                    const int row = mt * kTcM + part * 32 + rr, col = col_base + cc + c4;
+                    if (row < p.m && col < mat.n) {
+                        const float4 v = *reinterpret_cast<const float4 *>(mystg + rr * kPStgStride + c4);
+                        float *y = mat.y + (size_t)row * mat.ldy + col;
+                        if (col + 4 <= mat.n && (mat.ldy & 3) == 0 && (((uintptr_t)y) & 15) == 0) {
+                            *reinterpret_cast<float4 *>(y) = v;
+                        } else {
+                            const float vv[4] = {v.x, v.y, v.z, v.w};
+                            for (int q = 0; q < 4 && col + q < mat.n; q++) y[q] = vv[q];
+                        }
+                    }
+                }
+                __syncwarp();
+            }
+            // This warp's quarter of accumulator b is read: release it.
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive_p(&acce[b]);
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2u * kPN) : "memory");
+    }
+}
+
 // x̂ = H·x per group of G (no 1/√G: it is in ŵ), bf16, into the swizzled
 // image [m_tile][kc][128 rows][128 B]; rows past m and columns past In are
 // zero. Each lane owns a 32-column segment of one row (four 16-byte chunks
@@ -328,6 +527,68 @@ __global__ void __launch_bounds__(256) rotate_bf16_kernel(const float *__restric
     }
 }
 
+// The same image with four columns per lane: a warp's loads are 512
+// contiguous bytes of one row, the butterflies with h < 4 run in registers
+// and those with h >= 4 between lanes (xor h/4), and each lane stores its
+// four bf16 values as 8 bytes of the swizzled chunk. Rows are padded to a
+// whole number of warps (lanes past kpad hold zeros and store nothing), so
+// a group (G <= 128: at most 32 lanes) never straddles two warps.
+__global__ void __launch_bounds__(256) rotate_bf16_v2_kernel(const float *__restrict__ x, int m, int in, int G,
+                                                             int kpad, int kchunks, int mtiles,
+                                                             unsigned char *__restrict__ a) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int lanes_row = ((kpad / 4) + 31) & ~31;
+    const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long total = (long)mtiles * kTcM * lanes_row;
+    const bool live = t < total;
+    const int row = live ? (int)(t / lanes_row) : 0;
+    const int c0 = live ? (int)(t % lanes_row) * 4 : kpad;
+    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (live && row < m && c0 < in) {
+        const float *src = x + (size_t)row * in + c0;
+        if (c0 + 4 <= in && (((uintptr_t)src) & 15) == 0) {
+            const float4 f = __ldg(reinterpret_cast<const float4 *>(src));
+            v[0] = f.x;
+            v[1] = f.y;
+            v[2] = f.z;
+            v[3] = f.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; e++) v[e] = c0 + e < in ? src[e] : 0.0f;
+        }
+    }
+#pragma unroll
+    for (int h = 1; h < 4; h <<= 1) {
+        if (h < G) {
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                if ((e & h) == 0) {
+                    const float a0 = v[e], b0 = v[e + h];
+                    v[e] = a0 + b0;
+                    v[e + h] = a0 - b0;
+                }
+            }
+        }
+    }
+    for (int h = 4; h < G; h <<= 1) {
+        const int pl = h / 4;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[e], pl);
+            v[e] = (c0 & h) ? o - v[e] : v[e] + o;
+        }
+    }
+    if (!live || c0 >= kpad) return;
+    const int mtile = row / kTcM, r = row % kTcM, kc = c0 / kTcK;
+    unsigned char *base = a + ((size_t)mtile * kchunks + kc) * kChunkBytes;
+    __nv_bfloat162 p0 = __floats2bfloat162_rn(v[0], v[1]);
+    __nv_bfloat162 p1 = __floats2bfloat162_rn(v[2], v[3]);
+    uint2 w;
+    w.x = *reinterpret_cast<uint32_t *>(&p0);
+    w.y = *reinterpret_cast<uint32_t *>(&p1);
+    *reinterpret_cast<uint2 *>(base + swz(r, c0 % kTcK)) = w;
+}
+
 // ŵ[r, k] = cb[idx]·n[r, g]·(1/√G) in bf16, swizzled [n_tile][kc][128][128 B];
 // rows past Out are zero. One thread per (row, 8 columns).
 __global__ void dequant_bf16_kernel(const __grid_constant__ CqShape s, const CqView v, int ntiles, int kchunks,
@@ -359,11 +620,14 @@ __global__ void dequant_bf16_kernel(const __grid_constant__ CqShape s, const CqV
 }  // namespace
 
 size_t tc_a_bytes(int m, int kchunks) { return (size_t)((m + kTcM - 1) / kTcM) * kchunks * kChunkBytes; }
-size_t tc_b_bytes(int n, int kchunks) { return (size_t)((n + kTcN - 1) / kTcN) * kchunks * kChunkBytes; }
+// Weight images hold an even number of 128-row tiles (rows past Out are
+// zero), so the persistent kernel's 256-row tiles never read past them.
+static int tc_b_tiles(int n) { return ((n + 2 * kTcN - 1) / (2 * kTcN)) * 2; }
+size_t tc_b_bytes(int n, int kchunks) { return (size_t)tc_b_tiles(n) * kchunks * kChunkBytes; }
 int tc_kchunks(const CqShape &s) { return (s.pad + kTcK - 1) / kTcK; }
 
 cudaError_t launch_dequant_bf16(const CqShape &s, const CqView &v, unsigned char *b, cudaStream_t st) {
-    const int kchunks = tc_kchunks(s), ntiles = (v.out + kTcN - 1) / kTcN;
+    const int kchunks = tc_kchunks(s), ntiles = tc_b_tiles(v.out);
     const long units = (long)ntiles * kTcN * (kchunks * kTcK / 8);
     if (units == 0) return cudaSuccess;
     dequant_bf16_kernel<<<(int)((units + 255) / 256), 256, 0, st>>>(s, v, ntiles, kchunks, b);
@@ -377,6 +641,14 @@ cudaError_t launch_rotate_bf16(const CqShape &s, const float *x, int m, unsigned
     // (x is zero there, and H of zeros is zero within a group of G <= 32;
     // for larger G the padding is whole groups of zeros).
     const int kpad = kchunks * kTcK;
+    if (s.group <= 128 && m < 1024) {  // few rows: four columns per lane, more lanes in flight
+        const long threads = (long)mtiles * kTcM * (((kpad / 4) + 31) & ~31);
+        if (threads == 0) return cudaSuccess;
+        rotate_bf16_v2_kernel<<<(int)((threads + 255) / 256), 256, 0, st>>>(x, m, s.in, s.group, kpad, kchunks,
+                                                                             mtiles, a);
+        count_launch();
+        return cudaGetLastError();
+    }
     const long threads = (long)mtiles * kTcM * (kpad / 32);
     if (threads == 0) return cudaSuccess;
     rotate_bf16_kernel<<<(int)((threads + 255) / 256), 256, 0, st>>>(x, m, s.in, s.group, kpad, kchunks, mtiles, a);
@@ -444,6 +716,41 @@ cudaError_t gemm_tc_noalloc(const CqShape &s, const unsigned char *wimg, const f
     p.nmats = 1;
     p.mats[0] = TcMat{wimg, y, n, n, 0};
     return launch_gemm_tc(p, st);
+}
+
+size_t tc_persistent_smem_bytes() {
+    return 1024 + (size_t)kPStages * kPStageBytes + sizeof(float) * 8 * 32 * kPStgStride + 8 * (2 * kPStages + 4) + 16;
+}
+
+// The persistent kernel over mats[].tile0 in 256-row units; one CTA per SM
+// (up to the tiles), as a programmatic dependent of the rotation.
+cudaError_t launch_gemm_tc_persistent(const TcParams &p, cudaStream_t st) {
+    const size_t smem = tc_persistent_smem_bytes();
+    cudaError_t e =
+        cudaFuncSetAttribute(cq_gemm_tc_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const TcMat &l = p.mats[p.nmats - 1];
+    const int ntg = l.tile0 + (l.n + kPN - 1) / kPN;
+    const int mtiles = (p.m + kTcM - 1) / kTcM;
+    const int total = ntg * mtiles;
+    if (total == 0) return cudaSuccess;
+    TcParams q = p;
+    q.pdl = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)(total < sms ? total : sms));
+    cfg.blockDim = dim3(kPThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, cq_gemm_tc_persistent_kernel, q, ntg, total);
+    count_launch();
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 int tc_total_tiles(const TcParams &p) {

@@ -84,6 +84,10 @@ cudaError_t launch_rotate_bf16(const CqShape &s, const float *x, int m, unsigned
 // Total n-tiles of a launch: mats[nmats - 1].tile0 + its tiles.
 int tc_total_tiles(const TcParams &p);
 cudaError_t launch_gemm_tc(const TcParams &p, cudaStream_t st);
+// The persistent kernel for many rows: 128 x 256 tiles, mats[].tile0 in
+// 256-row units.
+size_t tc_persistent_smem_bytes();
+cudaError_t launch_gemm_tc_persistent(const TcParams &p, cudaStream_t st);
 // wc_cq_gemm_tc_noalloc's core: the same kernels on a static scratch array.
 size_t noalloc_scratch_bytes();
 cudaError_t gemm_tc_noalloc(const CqShape &s, const unsigned char *wimg, const float *x, float *y, int rows, int n,

@@ -52,8 +52,13 @@ def tc_gemm(wb, cuda, m, x):
     return yd.cpu().numpy()
 
 
+# (rows, out, in, group, bits); from 1024 rows the persistent kernel runs
+# (128 x 256 tiles, two TMEM accumulators): outputs narrower than one tile,
+# not a multiple of 256, K not a multiple of 64, several tiles per CTA.
 CASES = [(128, 128, 64, 32, 4), (300, 200, 512, 32, 4), (257, 96, 512, 128, 2), (129, 384, 512, 128, 2),
-         (64, 1024, 512, 128, 2), (200, 512, 2048, 32, 4), (1000, 2048, 512, 32, 4), (130, 70, 200, 32, 2)]
+         (64, 1024, 512, 128, 2), (200, 512, 2048, 32, 4), (1000, 2048, 512, 32, 4), (130, 70, 200, 32, 2),
+         (1024, 96, 512, 128, 2), (1500, 700, 200, 32, 2), (2500, 2048, 512, 32, 4), (1100, 512, 2048, 32, 4),
+         (24000, 384, 512, 128, 2)]
 
 
 @pytest.mark.parametrize("case", CASES, ids=[f"m{c[0]}_{c[1]}x{c[2]}g{c[3]}b{c[4]}" for c in CASES])
@@ -108,7 +113,7 @@ def tc_gemms(wb, cuda, ms, x, flags):
     return [y.cpu().numpy() for y in yds]
 
 
-@pytest.mark.parametrize("rows", [1, 96, 256])
+@pytest.mark.parametrize("rows", [1, 96, 256, 1200])
 def test_tc_gemms_grouped(wb, cuda, rows):
     """GEMMs on the tensor cores: Whistle's q/k/v/gate set (one rotation,
     one grouped launch), a second group size in the same call, and more
