@@ -153,7 +153,7 @@ BulkLayout attend_bulk_layout(const AttendParams &p, int stages) {
 namespace {
 
 template <int QKV, bool EXACT, int COLS>  // qk / 16; exact order; output columns per consumer thread
-__global__ void __launch_bounds__(kBulkThreads, 6) attend_int8_bulk_kernel(const __grid_constant__ AttendParams p,
+__global__ void __launch_bounds__(kBulkThreads, (COLS >= 8 || QKV >= 6) ? 4 : 6) attend_int8_bulk_kernel(const __grid_constant__ AttendParams p,
                                                                        const __grid_constant__ BulkLayout L) {
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int qk = 16 * QKV;
