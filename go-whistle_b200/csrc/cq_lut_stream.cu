@@ -358,23 +358,40 @@ __global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const 
         for (int w = 0; w < 16; w++) cbw[w] = 0;
         int a_rot = 0;
 
+        // Rolling prefetch: a warp's first tile is loaded here; afterwards,
+        // as soon as a superchunk's registers are consumed, the same
+        // superchunk of the warp's next tile is loaded into them, so a
+        // tile's worth of loads is in flight while the warp computes. With
+        // 8-byte groups the extra live state would spill, so that variant
+        // loads each tile at the top of its iteration.
+        constexpr bool kRoll = GB > 8;
         int k = -1;
+        uint4 d0[4], d1[4], d2[4], d3[4];
+        uint32_t n0[4], n1[4], n2[4], n3[4];
+        if (kRoll && t_begin + warp < t_end) {
+            k = run_from(p, t_begin + warp, k);
+            const TileLoc l0 = tile_loc(p, t_begin + warp, k);
+            const bool v0 = l0.r0 + lane < l0.v.out;
+            const int R0 = l0.v.row0 + l0.r0 + lane;
+            load_superchunk<NG>(l0.v, sc0, R0, v0, d0, n0);
+            if (nsc_pass > 1) load_superchunk<NG>(l0.v, sc0 + 1, R0, v0, d1, n1);
+            if (nsc_pass > 2) load_superchunk<NG>(l0.v, sc0 + 2, R0, v0, d2, n2);
+            if (nsc_pass > 3) load_superchunk<NG>(l0.v, sc0 + 3, R0, v0, d3, n3);
+        }
         for (int t = t_begin + warp; t < t_end; t += kStreamWarps) {
             k = run_from(p, t, k);
             const TileLoc loc = tile_loc(p, t, k);
             const CqView &v = loc.v;
             const int r = loc.r0 + lane;
             const bool valid = r < v.out;
-            const int R = v.row0 + r;
             const int off = v.row0 & 31;
-
-            // All of the tile's superchunk loads go out before any lookup.
-            uint4 d0[4], d1[4], d2[4], d3[4];
-            uint32_t n0[4], n1[4], n2[4], n3[4];
-            load_superchunk<NG>(v, sc0, R, valid, d0, n0);
-            if (nsc_pass > 1) load_superchunk<NG>(v, sc0 + 1, R, valid, d1, n1);
-            if (nsc_pass > 2) load_superchunk<NG>(v, sc0 + 2, R, valid, d2, n2);
-            if (nsc_pass > 3) load_superchunk<NG>(v, sc0 + 3, R, valid, d3, n3);
+            if (!kRoll) {
+                const int R = v.row0 + r;
+                load_superchunk<NG>(v, sc0, R, valid, d0, n0);
+                if (nsc_pass > 1) load_superchunk<NG>(v, sc0 + 1, R, valid, d1, n1);
+                if (nsc_pass > 2) load_superchunk<NG>(v, sc0 + 2, R, valid, d2, n2);
+                if (nsc_pass > 3) load_superchunk<NG>(v, sc0 + 3, R, valid, d3, n3);
+            }
 
             if (off != cached_off) {
                 cached_off = off;
@@ -398,11 +415,35 @@ __global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const 
             float y = 0.0f;
             if (pass > 0 && valid) y = yk[r];
 
+            // The warp's next tile.
+            const int tn = t + kStreamWarps;
+            const bool nxt = kRoll && tn < t_end;
+            int kn = k;
+            TileLoc ln = loc;
+            int Rn = 0;
+            bool vn = false;
+            if (nxt) {
+                kn = run_from(p, tn, k);
+                ln = tile_loc(p, tn, kn);
+                Rn = ln.v.row0 + ln.r0 + lane;
+                vn = ln.r0 + lane < ln.v.out;
+            }
             y = superchunk<GB, 0>(d0, n0, cbw, steps, wterms, lane, a_rot, sc0, y);
-            if (nsc_pass > 1) y = superchunk<GB, 1>(d1, n1, cbw, steps, wterms, lane, a_rot, sc0 + 1, y);
-            if (nsc_pass > 2) y = superchunk<GB, 2>(d2, n2, cbw, steps, wterms, lane, a_rot, sc0 + 2, y);
-            if (nsc_pass > 3) y = superchunk<GB, 3>(d3, n3, cbw, steps, wterms, lane, a_rot, sc0 + 3, y);
+            if (nxt) load_superchunk<NG>(ln.v, sc0, Rn, vn, d0, n0);
+            if (nsc_pass > 1) {
+                y = superchunk<GB, 1>(d1, n1, cbw, steps, wterms, lane, a_rot, sc0 + 1, y);
+                if (nxt) load_superchunk<NG>(ln.v, sc0 + 1, Rn, vn, d1, n1);
+            }
+            if (nsc_pass > 2) {
+                y = superchunk<GB, 2>(d2, n2, cbw, steps, wterms, lane, a_rot, sc0 + 2, y);
+                if (nxt) load_superchunk<NG>(ln.v, sc0 + 2, Rn, vn, d2, n2);
+            }
+            if (nsc_pass > 3) {
+                y = superchunk<GB, 3>(d3, n3, cbw, steps, wterms, lane, a_rot, sc0 + 3, y);
+                if (nxt) load_superchunk<NG>(ln.v, sc0 + 3, Rn, vn, d3, n3);
+            }
             if (valid) yk[r] = y;
+            k = kn;
         }
     }
 }
