@@ -611,7 +611,8 @@ def run_b200(args, world, rank, local):
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
                      "kernel": "cq_lut_stream_kernel", "bytes_per_launch": int(bytes_per_launch)},
         "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "call": "wc_cq_gemms_host per shape (pinned host x and outputs), wall clock", "steps": e2e_steps},
+                "call": "wc_cq_gemms_host per shape (pinned host x and outputs), wall clock", "steps": e2e_steps,
+                "d2h": "the kernels store the results into the page-locked host outputs over PCIe"},
         "gpu_launches": int(launches_per_step * args.steps), "gpu_launches_scope": "per rank",
         "clocks": clocks,
     }

@@ -296,6 +296,7 @@ extern "C" size_t wc_cq_bytes(const wc_cq *h) {
 
 // lut.go:206 sharesTables.
 static bool shares_tables(const wc_cq *a, const wc_cq *b) {
+    if (a->st == b->st) return true;  // views of one storage: one shape and codebook
     if (a->shape.in != b->shape.in || a->shape.group != b->shape.group || a->shape.bits != b->shape.bits ||
         a->shape.cb_max != b->shape.cb_max)
         return false;
@@ -317,6 +318,38 @@ static int sm_count() {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
     return n;
 }
+
+// Set while a host-slice call runs its kernels straight into the caller's
+// page-locked outputs: a stream launch of several table passes then keeps
+// its partial sums in `part` (grown on demand, one per calling thread), so
+// each output is written once, by the last pass.
+namespace {
+struct HostDirect {
+    bool on = false;
+    float *part = nullptr;
+    size_t n = 0;
+    int device = -1;
+    ~HostDirect() {
+        if (part) cudaFree(part);
+    }
+    cudaError_t get(size_t floats, float **out) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (n < floats || device != dev) {
+            if (part) cudaFree(part);
+            part = nullptr;
+            n = 0;
+            if ((e = cudaMalloc(&part, floats * sizeof(float))) != cudaSuccess) return e;
+            n = floats;
+            device = dev;
+        }
+        *out = part;
+        return cudaSuccess;
+    }
+};
+thread_local HostDirect t_direct;
+}  // namespace
 
 // The streaming kernel for one activation, if every matrix has the stream
 // layout and the products are large enough; returns false otherwise.
@@ -343,8 +376,11 @@ static bool try_stream(const wc_cq *const *ms, int n, const float *x, float *con
         p->shape = ms[0]->shape;
         p->x = x;
         p->smem_base = stream_smem_base();
+        p->part = nullptr;
+        cudaError_t e = cudaSuccess;
+        if (t_direct.on && stream_passes(p->shape) > 1) e = t_direct.get((size_t)p->total_tiles * 32, &p->part);
         const int ctas = p->total_tiles < sms ? p->total_tiles : sms;
-        cudaError_t e = launch_stream(*p, ctas, st);
+        if (e == cudaSuccess) e = launch_stream(*p, ctas, st);
         p->nruns = 0;
         if (e != cudaSuccess) {
             *status = cuda_error(e, "cq stream kernel");
@@ -506,10 +542,15 @@ extern "C" wc_status wc_cq_gemms(const wc_cq *const *hs, int n, const float *x, 
     const wc_cq *first = nullptr;
     std::vector<const wc_cq *> shared;
     std::vector<float *> sys;
+    shared.reserve(n);
+    sys.reserve(n);
+    int cur = 0;
+    WB_CUDA(cudaGetDevice(&cur));
     for (int k = 0; k < n; k++) {
         const wc_cq *m = hs[k];
-        wc_status st = check_device(m);
-        if (st != WC_OK) return st;
+        if (m->st->device != cur)
+            return set_error(WC_ERR_DEVICE,
+                             fmt("cq: matrix lives on device %d, device %d is current", m->st->device, cur));
         if (m->out == 0) continue;
         if (m->lut() && (!first || shares_tables(first, m))) {
             if (!first) first = m;
@@ -517,7 +558,7 @@ extern "C" wc_status wc_cq_gemms(const wc_cq *const *hs, int n, const float *x, 
             sys.push_back(ys[k]);
             continue;
         }
-        st = wc_cq_gemm(m, x, ys[k], rows, stream);
+        wc_status st = wc_cq_gemm(m, x, ys[k], rows, stream);
         if (st != WC_OK) return st;
     }
     if (!shared.empty()) return run_lut(shared.data(), (int)shared.size(), x, sys.data(), rows, s);
@@ -561,14 +602,7 @@ extern "C" wc_status wc_cq_gemm_host(const wc_cq *h, const float *x, size_t x_le
     if (rows < 0 || x_len != (size_t)rows * in || y_len != (size_t)rows * out)  // kernel.go:105-107
         return set_error(WC_ERR_INVALID, fmt("cq: GEMM(len %zu, len %zu, %d rows) on [%d, %d]", y_len, x_len, rows, out, in));
     if (rows == 0 || out == 0) return WC_OK;
-    void *dx = nullptr, *dy = nullptr;
-    WB_CUDA(t_scratch.get(0, x_len * sizeof(float), &dx));
-    WB_CUDA(t_scratch.get(1, y_len * sizeof(float), &dy));
-    WB_CUDA(cudaMemcpy(dx, x, x_len * sizeof(float), cudaMemcpyHostToDevice));
-    wc_status st = wc_cq_gemm(h, (const float *)dx, (float *)dy, rows, nullptr);
-    if (st != WC_OK) return st;
-    WB_CUDA(cudaMemcpy(y, dy, y_len * sizeof(float), cudaMemcpyDeviceToHost));
-    return WC_OK;
+    return wc_cq_gemms_host(&h, 1, x, x_len, &y, &y_len, rows);
 }
 
 // Streams and events of the host-slice entry points, one set per calling
@@ -611,6 +645,71 @@ thread_local HostPipe t_pipe;
 // chunk's copy then costs about as much as a launch.
 static const size_t kHostChunkMinBytes = 1u << 20;
 
+// Output bytes of a host GEMMs call up to which outputs in mapped
+// page-locked memory are written by the kernels themselves. Above it the
+// chunked copies win: the copy engines move large blocks over PCIe faster
+// than the kernels' 128-byte stores, and the first chunk's kernels are then
+// a small part of the call.
+#ifndef WB_HOST_DIRECT_MAX_BYTES
+#define WB_HOST_DIRECT_MAX_BYTES (32u << 20)
+#endif
+static const size_t kHostDirectMaxBytes = WB_HOST_DIRECT_MAX_BYTES;
+
+// The device address of page-locked host memory at p, if the current device
+// can address it.
+static bool host_mapped(const void *p, void **dev) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    if (a.type != cudaMemoryTypeHost || !a.devicePointer) return false;
+    *dev = a.devicePointer;
+    return true;
+}
+
+// Device addresses of the outputs when every one lies in page-locked host
+// memory the device can address (each run of contiguous outputs checked at
+// both ends); false otherwise.
+static bool mapped_outputs(float *const *ys, const size_t *y_lens, int n, std::vector<float *> &dys) {
+    dys.assign(n, nullptr);
+    for (int k = 0; k < n;) {
+        size_t len = y_lens[k];
+        int j = k + 1;
+        while (j < n && ys[j - 1] + y_lens[j - 1] == ys[j]) len += y_lens[j++];
+        if (len) {
+            void *d0 = nullptr, *d1 = nullptr;
+            if (!host_mapped(ys[k], &d0) || !host_mapped(ys[k] + len - 1, &d1) ||
+                (float *)d1 - (float *)d0 != (ptrdiff_t)(len - 1))
+                return false;
+            for (int i = k; i < j; i++) dys[i] = (float *)d0 + (ys[i] - ys[k]);
+        }
+        k = j;
+    }
+    return true;
+}
+
+// Outputs in mapped page-locked memory: the kernels store the results
+// there themselves, so they cross PCIe once, while the products run.
+static wc_status gemms_host_direct(const wc_cq *const *hs, int n, const float *x, size_t x_len,
+                                   const std::vector<float *> &dys, int rows) {
+    void *dx = nullptr;
+    WB_CUDA(t_scratch.get(0, x_len * sizeof(float), &dx));
+    wc_status st = WC_OK;
+    cudaError_t e = cudaMemcpyAsync(dx, x, x_len * sizeof(float), cudaMemcpyHostToDevice, t_pipe.comp);
+    if (e != cudaSuccess) st = cuda_error(e, "cq GEMMs host copy");
+    if (st == WC_OK) {
+        t_direct.on = true;
+        st = wc_cq_gemms(hs, n, (const float *)dx, dys.data(), rows, (wc_stream)t_pipe.comp);
+        t_direct.on = false;
+    }
+    // Nothing stays in flight into the caller's memory after return.
+    e = cudaStreamSynchronize(t_pipe.comp);
+    if (st != WC_OK) return st;
+    if (e != cudaSuccess) return cuda_error(e, "cq GEMMs host kernels");
+    return WC_OK;
+}
+
 extern "C" wc_status wc_cq_gemms_host(const wc_cq *const *hs, int n, const float *x, size_t x_len, float *const *ys,
                                       const size_t *y_lens, int rows) {
     if (n < 0 || (n > 0 && (!hs || !ys || !y_lens))) return set_error(WC_ERR_INVALID, "cq: GEMMs of a nil list");
@@ -622,10 +721,14 @@ extern "C" wc_status wc_cq_gemms_host(const wc_cq *const *hs, int n, const float
                              fmt("cq: GEMMs(len %zu, len %zu, %d rows) on [%d, %d]", y_lens[k], x_len, rows, out, in));
     }
     if (rows == 0 || n == 0) return WC_OK;
+    WB_CUDA(t_pipe.get());
     size_t total = 0;
     for (int k = 0; k < n; k++) total += y_lens[k];
+    if (total * sizeof(float) <= kHostDirectMaxBytes) {
+        std::vector<float *> direct;
+        if (mapped_outputs(ys, y_lens, n, direct)) return gemms_host_direct(hs, n, x, x_len, direct, rows);
+    }
     void *dx = nullptr, *dy = nullptr;
-    WB_CUDA(t_pipe.get());
     WB_CUDA(t_scratch.get(0, x_len * sizeof(float), &dx));
     WB_CUDA(t_scratch.get(1, (total ? total : 1) * sizeof(float), &dy));
     std::vector<float *> dys(n);

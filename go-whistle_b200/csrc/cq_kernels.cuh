@@ -50,14 +50,26 @@ struct StreamRun {
     int tpm;           // 32-row tiles per matrix
     int tile0;         // the run's first tile in the launch
 };
-struct StreamParams {
+// Launches of few runs use a parameter block of kSmallStreamRuns runs: the
+// block travels with every launch, and a small one launches faster.
+constexpr int kSmallStreamRuns = 4;
+template <int N>
+struct StreamParamsN {
     CqShape shape;
     const float *x;   // one activation [in]
     int nruns;
     int total_tiles;  // Σ count·tpm
     int smem_base;    // stream_smem_base() the launch was sized for
-    StreamRun runs[kMaxStreamRuns];
+    // Partial row sums between table passes: null keeps them in the
+    // outputs; otherwise [total_tiles][32] floats of device memory, so an
+    // output is written once, by the last pass (outputs in host memory).
+    float *part;
+    StreamRun runs[N];
 };
+using StreamParams = StreamParamsN<kMaxStreamRuns>;
+// Table passes of a stream launch (rows wider than one pass of byte tables
+// take several, the partial sums carried between them).
+int stream_passes(const CqShape &s);
 // The tensor-core GEMM (cq_gemm_tc.cu): operand images are pre-swizzled
 // 128 x 64 bf16 tiles.
 constexpr int kMaxTcMats = 16;  // matrices one grouped tensor-core launch carries

@@ -71,7 +71,8 @@ __device__ __forceinline__ void prefetch_l2(const void *addr, uint32_t bytes) {
 }
 
 // The run holding tile t.
-__device__ __forceinline__ int find_run(const StreamParams &p, int t) {
+template <class SP>
+__device__ __forceinline__ int find_run(const SP &p, int t) {
     int lo = 0, hi = p.nruns - 1;
     while (lo < hi) {
         int mid = (lo + hi + 1) >> 1;
@@ -84,7 +85,8 @@ __device__ __forceinline__ int find_run(const StreamParams &p, int t) {
 }
 
 // Tile t's run, trying k (the previous tile's) first.
-__device__ __forceinline__ int run_from(const StreamParams &p, int t, int k) {
+template <class SP>
+__device__ __forceinline__ int run_from(const SP &p, int t, int k) {
     if (k >= 0 && p.runs[k].tile0 <= t && t < p.runs[k].tile0 + p.runs[k].count * p.runs[k].tpm) return k;
     return find_run(p, t);
 }
@@ -95,7 +97,8 @@ struct TileLoc {
     float *y;
     int r0;
 };
-__device__ __forceinline__ TileLoc tile_loc(const StreamParams &p, int t, int k) {
+template <class SP>
+__device__ __forceinline__ TileLoc tile_loc(const SP &p, int t, int k) {
     const StreamRun &R = p.runs[k];
     const int u = t - R.tile0, i = u / R.tpm;
     TileLoc L;
@@ -199,8 +202,8 @@ __device__ void build_pass_tables(const CqShape &s, const float *xs, const float
 // Lane 0 of a warp asks L2 for tile t's index bytes and norms of
 // superchunks [sc0, sc0 + nsc_pass): 4 runs of 32 rows x 16 bytes and one
 // run of 32 rows x NG norms per superchunk, all inside the matrix.
-template <int NG>
-__device__ __forceinline__ void prefetch_tile(const StreamParams &p, int t, int sc0, int nsc_pass) {
+template <int NG, class SP>
+__device__ __forceinline__ void prefetch_tile(const SP &p, int t, int sc0, int nsc_pass) {
     const TileLoc L = tile_loc(p, t, find_run(p, t));
     const CqView &v = L.v;
     const int r0 = L.r0;
@@ -302,8 +305,9 @@ __device__ __forceinline__ void load_superchunk(const CqView &v, int sc, int R, 
     }
 }
 
-template <int GB>
-__global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const __grid_constant__ StreamParams p) {
+template <int GB, int NR>
+__global__ void __launch_bounds__(kStreamThreads, 1)
+    cq_lut_stream_kernel(const __grid_constant__ StreamParamsN<NR> p) {
     constexpr int P = GB / 2;    // byte pairs per group
     constexpr int NG = 32 / P;   // groups per 64-byte superchunk
     extern __shared__ __align__(16) unsigned char smem[];
@@ -411,9 +415,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const 
                     cbw[w] = word;
                 }
             }
+            // This pass reads the partial sums from, and writes them to, the
+            // output or the tile's row of p.part.
             float *yk = loc.y;
+            float *const pk = p.part ? p.part + (size_t)t * 32 + lane : nullptr;
+            float *const src = pk ? pk : yk + r;
+            float *const dst = pk && pass + 1 < npass ? pk : yk + r;
             float y = 0.0f;
-            if (pass > 0 && valid) y = yk[r];
+            if (pass > 0 && valid) y = *src;
 
             // The warp's next tile.
             const int tn = t + kStreamWarps;
@@ -442,7 +451,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) cq_lut_stream_kernel(const 
                 y = superchunk<GB, 3>(d3, n3, cbw, steps, wterms, lane, a_rot, sc0 + 3, y);
                 if (nxt) load_superchunk<NG>(ln.v, sc0 + 3, Rn, vn, d3, n3);
             }
-            if (valid) yk[r] = y;
+            if (valid) *dst = y;
             k = kn;
         }
     }
@@ -482,6 +491,8 @@ static size_t stream_small_bytes(const CqShape &s) {
     return (size_t)kNibBytes + sizeof(float) * ((size_t)kStreamWarps * ng * 32 + 2 * s.groups + s.pad);
 }
 
+int stream_passes(const CqShape &s) { return (s.row_bytes + kPassPositions - 1) / kPassPositions; }
+
 bool stream_eligible(const CqShape &s) {
     return (s.gb == 8 || s.gb == 16 || s.gb == 32 || s.gb == 64) && s.row_bytes % 64 == 0 && s.row_bytes >= 64;
 }
@@ -494,20 +505,34 @@ size_t stream_smem_bytes(const CqShape &s) {
     return (size_t)kTabAbs + kTabBytes - (size_t)b;
 }
 
-cudaError_t launch_stream(const StreamParams &p, int ctas, cudaStream_t st) {
+template <int NR>
+static cudaError_t launch_stream_n(const StreamParamsN<NR> &p, int ctas, cudaStream_t st) {
     size_t smem = stream_smem_bytes(p.shape);
-    void (*fn)(StreamParams);
+    void (*fn)(StreamParamsN<NR>);
     switch (p.shape.gb) {
-        case 8: fn = cq_lut_stream_kernel<8>; break;
-        case 16: fn = cq_lut_stream_kernel<16>; break;
-        case 32: fn = cq_lut_stream_kernel<32>; break;
-        default: fn = cq_lut_stream_kernel<64>; break;
+        case 8: fn = cq_lut_stream_kernel<8, NR>; break;
+        case 16: fn = cq_lut_stream_kernel<16, NR>; break;
+        case 32: fn = cq_lut_stream_kernel<32, NR>; break;
+        default: fn = cq_lut_stream_kernel<64, NR>; break;
     }
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     fn<<<ctas, kStreamThreads, smem, st>>>(p);
     count_launch();
     return cudaGetLastError();
+}
+
+cudaError_t launch_stream(const StreamParams &p, int ctas, cudaStream_t st) {
+    if (p.nruns > kSmallStreamRuns) return launch_stream_n(p, ctas, st);
+    StreamParamsN<kSmallStreamRuns> q;
+    q.shape = p.shape;
+    q.x = p.x;
+    q.nruns = p.nruns;
+    q.total_tiles = p.total_tiles;
+    q.smem_base = p.smem_base;
+    q.part = p.part;
+    for (int i = 0; i < kSmallStreamRuns; i++) q.runs[i] = i < p.nruns ? p.runs[i] : StreamRun{};
+    return launch_stream_n(q, ctas, st);
 }
 
 }  // namespace wb

@@ -180,7 +180,8 @@ wc_status wc_cq_gemm_tc_noalloc(const wc_cq *h, const float *x, float *y, int ro
 wc_status wc_device_status(int *code);
 
 /* GEMM on HOST slices with the reference's length check and panic text
- * (kernel.go:105-107): x_len = len(x), y_len = len(dst). Synchronous. */
+ * (kernel.go:105-107): x_len = len(x), y_len = len(dst). Synchronous; the
+ * result travels as wc_cq_gemms_host's does. */
 wc_status wc_cq_gemm_host(const wc_cq *h, const float *x, size_t x_len, float *y, size_t y_len, int rows);
 
 /*
@@ -193,7 +194,12 @@ wc_status wc_cq_gemm_host(const wc_cq *h, const float *x, size_t x_len, float *y
  */
 wc_status wc_cq_gemms(const wc_cq *const *hs, int n, const float *x, float *const *ys, int rows, wc_stream stream);
 
-/* GEMMs on HOST slices: y_lens[k] = len(dsts[k]). Synchronous. */
+/* GEMMs on HOST slices: y_lens[k] = len(dsts[k]). Synchronous. Outputs in
+ * page-locked host memory that the device can address (cudaHostAlloc, or
+ * cudaHostRegister under unified addressing) receive the results straight
+ * from the kernels, which overlaps the transfer with the products; other
+ * outputs are copied from device memory in chunks behind the kernels. The
+ * bits are the same either way. */
 wc_status wc_cq_gemms_host(const wc_cq *const *hs, int n, const float *x, size_t x_len, float *const *ys,
                            const size_t *y_lens, int rows);
 

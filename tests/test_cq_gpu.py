@@ -296,6 +296,45 @@ def test_gemms_host_chunked(wb, orc, cuda, rows, view_rows):
         assert bits_eq(flat[k].reshape(rows, view_rows), want[:, k])
 
 
+@pytest.mark.parametrize("in_,bits,rows,view_rows", [(512, 4, 1, 384), (2048, 4, 1, 96), (512, 2, 1, 16),
+                                                     (1024, 4, 3, 96)])
+def test_gemms_host_direct(wb, orc, cuda, in_, bits, rows, view_rows):
+    """GEMMs and GEMM on host slices in page-locked memory: the kernels store
+    the results there directly (the streaming kernel with one table pass,
+    and with four, its partial sums kept on the device; the small-product
+    kernels; several activations). Bit for bit the pageable-memory call's,
+    the device call's and the oracle's; a list mixing page-locked and
+    pageable outputs also matches."""
+    rng = np.random.default_rng(700 + in_ + bits + rows)
+    n = 64
+    base = wb.synth.random_packed(rng, n * view_rows, in_, 32, bits, "lloyd")
+    big = wb.cq.New(base)
+    views = [big.Rows(k * view_rows, (k + 1) * view_rows) for k in range(n)]
+    x = rng.normal(size=rows * in_).astype(np.float32)
+    pinned = cuda.full((n, rows * view_rows), float("nan"), dtype=cuda.float32).pin_memory().numpy()
+    wb.cq.GEMMs(views, [pinned[k] for k in range(n)], x, rows)
+    sep = [cuda.full((rows * view_rows,), float("nan"), dtype=cuda.float32).pin_memory().numpy() for _ in range(n)]
+    wb.cq.GEMMs(views, sep, x, rows)
+    pageable = np.full((n, rows * view_rows), np.nan, np.float32)
+    wb.cq.GEMMs(views, [pageable[k] for k in range(n)], x, rows)
+    mixed = [sep[k] if k % 2 else pageable[k] for k in range(n)]
+    for a in mixed:
+        a[:] = np.nan
+    wb.cq.GEMMs(views, mixed, x, rows)
+    yds = [cuda.empty(rows * view_rows, dtype=cuda.float32, device="cuda") for _ in views]
+    wb.cq.GEMMs(views, yds, cuda.from_numpy(x).cuda(), rows)
+    for k in range(n):
+        dev = yds[k].cpu().numpy()
+        assert bits_eq(pinned[k], dev) and bits_eq(sep[k], dev) and bits_eq(pageable[k], dev), k
+        assert bits_eq(mixed[k], dev), k
+    one = cuda.full((rows * view_rows,), float("nan"), dtype=cuda.float32).pin_memory().numpy()
+    views[5].GEMM(one, x, rows)
+    assert bits_eq(one, yds[5].cpu().numpy())
+    want = orc.gemm_lut(orc.OracleMatrix.of(base), x, rows, threads=8).reshape(rows, n, view_rows)
+    for k in (0, 17, n - 1):
+        assert bits_eq(pinned[k].reshape(rows, view_rows), want[:, k])
+
+
 def test_stream_runs(wb, orc, cuda):
     """GEMMs calls the streaming kernel carries as strided runs: a stack of
     views with a constant row step and contiguous outputs, one matrix
