@@ -58,7 +58,7 @@ def tc_gemm(wb, cuda, m, x):
 CASES = [(128, 128, 64, 32, 4), (300, 200, 512, 32, 4), (257, 96, 512, 128, 2), (129, 384, 512, 128, 2),
          (64, 1024, 512, 128, 2), (200, 512, 2048, 32, 4), (1000, 2048, 512, 32, 4), (130, 70, 200, 32, 2),
          (1024, 96, 512, 128, 2), (1500, 700, 200, 32, 2), (2500, 2048, 512, 32, 4), (1100, 512, 2048, 32, 4),
-         (24000, 384, 512, 128, 2)]
+         (24000, 384, 512, 128, 2), (1030, 130, 512, 32, 4)]
 
 
 @pytest.mark.parametrize("case", CASES, ids=[f"m{c[0]}_{c[1]}x{c[2]}g{c[3]}b{c[4]}" for c in CASES])
