@@ -605,12 +605,17 @@ extern "C" wc_status wc_cq_gemm_host(const wc_cq *h, const float *x, size_t x_le
     return wc_cq_gemms_host(&h, 1, x, x_len, &y, &y_len, rows);
 }
 
+// Most chunks one host GEMMs call is split into.
+#ifndef WB_HOST_CHUNKS
+#define WB_HOST_CHUNKS 8
+#endif
+
 // Streams and events of the host-slice entry points, one set per calling
 // thread: kernels run on `comp`, device-to-host copies on `copy`, so the copy
 // of one chunk of outputs overlaps the kernels of the next chunk.
 namespace {
 struct HostPipe {
-    static const int kChunks = 8;
+    static const int kChunks = WB_HOST_CHUNKS;
     cudaStream_t comp = nullptr, copy = nullptr;
     cudaEvent_t ev[kChunks] = {};
     int device = -1;
@@ -643,7 +648,10 @@ thread_local HostPipe t_pipe;
 
 // Output bytes per chunk below which a host GEMMs call is not split: one
 // chunk's copy then costs about as much as a launch.
-static const size_t kHostChunkMinBytes = 1u << 20;
+#ifndef WB_HOST_CHUNK_MIN_BYTES
+#define WB_HOST_CHUNK_MIN_BYTES (1u << 20)
+#endif
+static const size_t kHostChunkMinBytes = WB_HOST_CHUNK_MIN_BYTES;
 
 // Output bytes of a host GEMMs call up to which outputs in mapped
 // page-locked memory are written by the kernels themselves. Above it the
