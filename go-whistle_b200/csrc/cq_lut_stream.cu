@@ -305,7 +305,7 @@ __device__ __forceinline__ void load_superchunk(const CqView &v, int sc, int R, 
     }
 }
 
-template <int GB, int NR>
+template <int GB, int NR, int NSC>  // group bytes; run capacity; most superchunks a pass holds (1, 2 or 4)
 __global__ void __launch_bounds__(kStreamThreads, 1)
     cq_lut_stream_kernel(const __grid_constant__ StreamParamsN<NR> p) {
     constexpr int P = GB / 2;    // byte pairs per group
@@ -351,7 +351,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     for (int pass = 0; pass < npass; pass++) {
         const int j0 = pass * kPassPositions;
         const int npos = min(kPassPositions, s.row_bytes - j0);
-        const int sc0 = j0 / 64, nsc_pass = npos / 64;
+        const int sc0 = j0 / 64, nsc_pass = min(npos / 64, NSC);  // npos / 64 <= NSC by the launch
         if (pass > 0 && lane == 0 && t_begin + warp < t_end) prefetch_tile<NG>(p, t_begin + warp, sc0, nsc_pass);
         __syncthreads();
         build_pass_tables(s, xs, invs, j0, npos, nib, tab);
@@ -367,8 +367,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         // superchunk of the warp's next tile is loaded into them, so a
         // tile's worth of loads is in flight while the warp computes. With
         // 8-byte groups the extra live state would spill, so that variant
-        // loads each tile at the top of its iteration.
-        constexpr bool kRoll = GB > 8;
+        // loads each tile at the top of its iteration (unless a pass holds
+        // at most two superchunks).
+        constexpr bool kRoll = GB > 8 || NSC <= 2;
         int k = -1;
         uint4 d0[4], d1[4], d2[4], d3[4];
         uint32_t n0[4], n1[4], n2[4], n3[4];
@@ -378,9 +379,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
             const bool v0 = l0.r0 + lane < l0.v.out;
             const int R0 = l0.v.row0 + l0.r0 + lane;
             load_superchunk<NG>(l0.v, sc0, R0, v0, d0, n0);
-            if (nsc_pass > 1) load_superchunk<NG>(l0.v, sc0 + 1, R0, v0, d1, n1);
-            if (nsc_pass > 2) load_superchunk<NG>(l0.v, sc0 + 2, R0, v0, d2, n2);
-            if (nsc_pass > 3) load_superchunk<NG>(l0.v, sc0 + 3, R0, v0, d3, n3);
+            if (NSC > 1 && nsc_pass > 1) load_superchunk<NG>(l0.v, sc0 + 1, R0, v0, d1, n1);
+            if (NSC > 2 && nsc_pass > 2) load_superchunk<NG>(l0.v, sc0 + 2, R0, v0, d2, n2);
+            if (NSC > 3 && nsc_pass > 3) load_superchunk<NG>(l0.v, sc0 + 3, R0, v0, d3, n3);
         }
         for (int t = t_begin + warp; t < t_end; t += kStreamWarps) {
             k = run_from(p, t, k);
@@ -392,9 +393,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
             if (!kRoll) {
                 const int R = v.row0 + r;
                 load_superchunk<NG>(v, sc0, R, valid, d0, n0);
-                if (nsc_pass > 1) load_superchunk<NG>(v, sc0 + 1, R, valid, d1, n1);
-                if (nsc_pass > 2) load_superchunk<NG>(v, sc0 + 2, R, valid, d2, n2);
-                if (nsc_pass > 3) load_superchunk<NG>(v, sc0 + 3, R, valid, d3, n3);
+                if (NSC > 1 && nsc_pass > 1) load_superchunk<NG>(v, sc0 + 1, R, valid, d1, n1);
+                if (NSC > 2 && nsc_pass > 2) load_superchunk<NG>(v, sc0 + 2, R, valid, d2, n2);
+                if (NSC > 3 && nsc_pass > 3) load_superchunk<NG>(v, sc0 + 3, R, valid, d3, n3);
             }
 
             if (off != cached_off) {
@@ -439,15 +440,15 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
             }
             y = superchunk<GB, 0>(d0, n0, cbw, steps, wterms, lane, a_rot, sc0, y);
             if (nxt) load_superchunk<NG>(ln.v, sc0, Rn, vn, d0, n0);
-            if (nsc_pass > 1) {
+            if (NSC > 1 && nsc_pass > 1) {
                 y = superchunk<GB, 1>(d1, n1, cbw, steps, wterms, lane, a_rot, sc0 + 1, y);
                 if (nxt) load_superchunk<NG>(ln.v, sc0 + 1, Rn, vn, d1, n1);
             }
-            if (nsc_pass > 2) {
+            if (NSC > 2 && nsc_pass > 2) {
                 y = superchunk<GB, 2>(d2, n2, cbw, steps, wterms, lane, a_rot, sc0 + 2, y);
                 if (nxt) load_superchunk<NG>(ln.v, sc0 + 2, Rn, vn, d2, n2);
             }
-            if (nsc_pass > 3) {
+            if (NSC > 3 && nsc_pass > 3) {
                 y = superchunk<GB, 3>(d3, n3, cbw, steps, wterms, lane, a_rot, sc0 + 3, y);
                 if (nxt) load_superchunk<NG>(ln.v, sc0 + 3, Rn, vn, d3, n3);
             }
@@ -505,16 +506,23 @@ size_t stream_smem_bytes(const CqShape &s) {
     return (size_t)kTabAbs + kTabBytes - (size_t)b;
 }
 
+template <int NR, int NSC>
+static void (*stream_fn(int gb))(StreamParamsN<NR>) {
+    switch (gb) {
+        case 8: return cq_lut_stream_kernel<8, NR, NSC>;
+        case 16: return cq_lut_stream_kernel<16, NR, NSC>;
+        case 32: return cq_lut_stream_kernel<32, NR, NSC>;
+        default: return cq_lut_stream_kernel<64, NR, NSC>;
+    }
+}
+
 template <int NR>
 static cudaError_t launch_stream_n(const StreamParamsN<NR> &p, int ctas, cudaStream_t st) {
     size_t smem = stream_smem_bytes(p.shape);
-    void (*fn)(StreamParamsN<NR>);
-    switch (p.shape.gb) {
-        case 8: fn = cq_lut_stream_kernel<8, NR>; break;
-        case 16: fn = cq_lut_stream_kernel<16, NR>; break;
-        case 32: fn = cq_lut_stream_kernel<32, NR>; break;
-        default: fn = cq_lut_stream_kernel<64, NR>; break;
-    }
+    // Registers for as many superchunks as a pass holds.
+    const int nsc = p.shape.row_bytes / 64;
+    void (*fn)(StreamParamsN<NR>) =
+        nsc <= 1 ? stream_fn<NR, 1>(p.shape.gb) : nsc == 2 ? stream_fn<NR, 2>(p.shape.gb) : stream_fn<NR, 4>(p.shape.gb);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     fn<<<ctas, kStreamThreads, smem, st>>>(p);
