@@ -144,57 +144,54 @@ __device__ void rotate_and_bound(const CqShape &s, const float *x, float *xs, fl
     __syncthreads();
 }
 
-// Byte tables for byte positions [j0, j0 + npos) of the row.
+// Byte tables for byte positions [j0, j0 + npos) of the row (npos even).
 __device__ void build_pass_tables(const CqShape &s, const float *xs, const float *invs, int j0, int npos,
                                   uint16_t *nib, uint16_t *tab) {
     const int tid = threadIdx.x;
     const int G = s.group;
     // Nibble tables, biased: nib[e][c][j] for the lo (e = 0) and hi (e = 1)
     // nibble of byte position j0 + j (lut.go:248-255, 272-279).
-    for (int u = tid; u < 2 * kPassPositions; u += kStreamThreads) {
-        int e = u / kPassPositions, j = u % kPassPositions;
+    for (int u = tid; u < 2 * npos; u += kStreamThreads) {
+        const int e = u / npos, j = u % npos;
         uint16_t *dst = nib + e * 16 * kPassPositions + j;
-        if (j >= npos) {
-#pragma unroll
-            for (int c = 0; c < 16; c++) dst[c * kPassPositions] = (uint16_t)kEntryBias;
-            continue;
-        }
-        int np = 2 * (j0 + j) + e;  // nibble position in the row
+        const int np = 2 * (j0 + j) + e;  // nibble position in the row
         if (s.bits == 4) {
-            int g = np / G;
-            float a = __fmul_rn(xs[np], invs[g]);
+            const float a = __fmul_rn(xs[np], invs[np / G]);
 #pragma unroll
             for (int c = 0; c < 16; c++)
                 dst[c * kPassPositions] = (uint16_t)(__float2int_rn(__fmul_rn(s.cb[c], a)) + (int)kEntryBias);
         } else {
-            int g = (2 * np) / G;
-            float inv = invs[g];
-            float a = __fmul_rn(xs[2 * np], inv), b = __fmul_rn(xs[2 * np + 1], inv);
+            const float inv = invs[(2 * np) / G];
+            const float a = __fmul_rn(xs[2 * np], inv), b = __fmul_rn(xs[2 * np + 1], inv);
 #pragma unroll
             for (int c = 0; c < 16; c++) {
-                float v = __fadd_rn(__fmul_rn(s.cb[c & 3], a), __fmul_rn(s.cb[c >> 2], b));
+                const float v = __fadd_rn(__fmul_rn(s.cb[c & 3], a), __fmul_rn(s.cb[c >> 2], b));
                 dst[c * kPassPositions] = (uint16_t)(__float2int_rn(v) + (int)kEntryBias);
             }
         }
     }
     __syncthreads();
     // Byte tables: tab[blk][b][jj] = nib[0][b & 15][j] + nib[1][b >> 4][j],
-    // j = 128·blk + jj; 8 positions (16 bytes) per store, packed adds (no
-    // carry: each half stays below 2^15). Only the npos positions in use.
-    const int chunks = (npos + 7) / 8;
-    const int units = 256 * chunks;
-    for (int u = tid; u < units; u += kStreamThreads) {
-        int b = u / chunks, cg = u % chunks;
-        int blk = cg / 16, ch = cg % 16;
-        int j = 128 * blk + 8 * ch;
-        const uint4 lo = *reinterpret_cast<const uint4 *>(nib + (b & 15) * kPassPositions + j);
-        const uint4 hi = *reinterpret_cast<const uint4 *>(nib + 16 * kPassPositions + (b >> 4) * kPassPositions + j);
-        uint4 r;
-        r.x = lo.x + hi.x;
-        r.y = lo.y + hi.y;
-        r.z = lo.z + hi.z;
-        r.w = lo.w + hi.w;
-        *reinterpret_cast<uint4 *>(tab + ((size_t)blk * 256 + b) * 128 + 8 * ch) = r;
+    // j = 128·blk + jj. A thread takes two adjacent positions (one word of
+    // each nibble table row) and a quarter of the hi nibbles: 20 word loads,
+    // 64 word stores (packed adds carry nothing: each half stays below
+    // 2^15). A warp's loads and stores each cover one 128-byte row, so they
+    // are conflict-free.
+    const int npairs = npos / 2;
+    const uint32_t *nw = reinterpret_cast<const uint32_t *>(nib);
+    for (int u = tid; u < 4 * npairs; u += kStreamThreads) {
+        const int jp = u % npairs, hq = u / npairs, j = 2 * jp;
+        uint32_t lo[16], hi[4];
+#pragma unroll
+        for (int c = 0; c < 16; c++) lo[c] = nw[(c * kPassPositions + j) >> 1];
+#pragma unroll
+        for (int i = 0; i < 4; i++) hi[i] = nw[((16 + 4 * hq + i) * kPassPositions + j) >> 1];
+        uint32_t *dst = reinterpret_cast<uint32_t *>(tab + (size_t)(j >> 7) * 256 * 128 + (j & 127)) +
+                        (size_t)(4 * hq) * 16 * 64;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int c = 0; c < 16; c++) dst[(16 * i + c) * 64] = lo[c] + hi[i];
     }
     __syncthreads();
 }
@@ -336,15 +333,40 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         return;
     }
     float *wterms = terms + warp * NG * 32;
-    const int nsc = s.row_bytes / 64;
     const int npass = (s.row_bytes + kPassPositions - 1) / kPassPositions;
 
     // This CTA's tiles: a contiguous share of all matrices' 32-row tiles.
     const int t_begin = (int)(((long long)p.total_tiles * blockIdx.x) / gridDim.x);
     const int t_end = (int)(((long long)p.total_tiles * (blockIdx.x + 1)) / gridDim.x);
 
-    // The first tile's data streams into L2 while the tables are built.
-    if (lane == 0 && t_begin + warp < t_end) prefetch_tile<NG>(p, t_begin + warp, 0, min(nsc, kPassPositions / 64));
+    // Rolling prefetch: a warp's first tile of a pass is loaded into its
+    // registers before the pass's tables are built (for pass 0 before the
+    // rotation); afterwards, as soon as a superchunk's registers are
+    // consumed, the same superchunk of the warp's next tile is loaded into
+    // them, so a tile's worth of loads is in flight while the warp computes.
+    // With 8-byte groups and four superchunks a pass the extra live state
+    // would spill, so that variant loads each tile at the top of its
+    // iteration (its first tile streams into L2 during the table build).
+    constexpr bool kRoll = GB > 8 || NSC <= 2;
+    uint4 d0[4], d1[4], d2[4], d3[4];
+    uint32_t n0[4], n1[4], n2[4], n3[4];
+    const bool has_tile = t_begin + warp < t_end;
+    auto first_tile = [&](int sc0, int nsc_pass) {
+        if (kRoll) {
+            if (has_tile) {
+                const TileLoc l0 = tile_loc(p, t_begin + warp, find_run(p, t_begin + warp));
+                const bool v0 = l0.r0 + lane < l0.v.out;
+                const int R0 = l0.v.row0 + l0.r0 + lane;
+                load_superchunk<NG>(l0.v, sc0, R0, v0, d0, n0);
+                if (NSC > 1 && nsc_pass > 1) load_superchunk<NG>(l0.v, sc0 + 1, R0, v0, d1, n1);
+                if (NSC > 2 && nsc_pass > 2) load_superchunk<NG>(l0.v, sc0 + 2, R0, v0, d2, n2);
+                if (NSC > 3 && nsc_pass > 3) load_superchunk<NG>(l0.v, sc0 + 3, R0, v0, d3, n3);
+            }
+        } else if (lane == 0 && has_tile) {
+            prefetch_tile<NG>(p, t_begin + warp, sc0, nsc_pass);
+        }
+    };
+    first_tile(0, min(min(s.row_bytes, kPassPositions) / 64, NSC));
 
     rotate_and_bound(s, p.x, xs, steps, invs);
 
@@ -352,7 +374,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         const int j0 = pass * kPassPositions;
         const int npos = min(kPassPositions, s.row_bytes - j0);
         const int sc0 = j0 / 64, nsc_pass = min(npos / 64, NSC);  // npos / 64 <= NSC by the launch
-        if (pass > 0 && lane == 0 && t_begin + warp < t_end) prefetch_tile<NG>(p, t_begin + warp, sc0, nsc_pass);
+        if (pass > 0) first_tile(sc0, nsc_pass);
         __syncthreads();
         build_pass_tables(s, xs, invs, j0, npos, nib, tab);
 
@@ -361,28 +383,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 #pragma unroll
         for (int w = 0; w < 16; w++) cbw[w] = 0;
         int a_rot = 0;
-
-        // Rolling prefetch: a warp's first tile is loaded here; afterwards,
-        // as soon as a superchunk's registers are consumed, the same
-        // superchunk of the warp's next tile is loaded into them, so a
-        // tile's worth of loads is in flight while the warp computes. With
-        // 8-byte groups the extra live state would spill, so that variant
-        // loads each tile at the top of its iteration (unless a pass holds
-        // at most two superchunks).
-        constexpr bool kRoll = GB > 8 || NSC <= 2;
         int k = -1;
-        uint4 d0[4], d1[4], d2[4], d3[4];
-        uint32_t n0[4], n1[4], n2[4], n3[4];
-        if (kRoll && t_begin + warp < t_end) {
-            k = run_from(p, t_begin + warp, k);
-            const TileLoc l0 = tile_loc(p, t_begin + warp, k);
-            const bool v0 = l0.r0 + lane < l0.v.out;
-            const int R0 = l0.v.row0 + l0.r0 + lane;
-            load_superchunk<NG>(l0.v, sc0, R0, v0, d0, n0);
-            if (NSC > 1 && nsc_pass > 1) load_superchunk<NG>(l0.v, sc0 + 1, R0, v0, d1, n1);
-            if (NSC > 2 && nsc_pass > 2) load_superchunk<NG>(l0.v, sc0 + 2, R0, v0, d2, n2);
-            if (NSC > 3 && nsc_pass > 3) load_superchunk<NG>(l0.v, sc0 + 3, R0, v0, d3, n3);
-        }
         for (int t = t_begin + warp; t < t_end; t += kStreamWarps) {
             k = run_from(p, t, k);
             const TileLoc loc = tile_loc(p, t, k);
