@@ -335,6 +335,24 @@ def test_gemms_host_direct(wb, orc, cuda, in_, bits, rows, view_rows):
         assert bits_eq(pinned[k].reshape(rows, view_rows), want[:, k])
 
 
+def test_gemms_host_large_pinned(wb, cuda):
+    """Host GEMMs whose page-locked outputs exceed the direct-store limit
+    (34 MB): the products go to device memory in chunks and come back by
+    copies; bit for bit the device call's."""
+    rng = np.random.default_rng(808)
+    n, view_rows, rows = 64, 96, 1400
+    big = wb.cq.New(wb.synth.random_packed(rng, n * view_rows, 512, 32, 4, "lloyd"))
+    views = [big.Rows(k * view_rows, (k + 1) * view_rows) for k in range(n)]
+    x = rng.normal(size=rows * 512).astype(np.float32)
+    pinned = cuda.full((n, rows * view_rows), float("nan"), dtype=cuda.float32).pin_memory().numpy()
+    assert pinned.nbytes > 32 << 20
+    wb.cq.GEMMs(views, [pinned[k] for k in range(n)], x, rows)
+    yds = [cuda.empty(rows * view_rows, dtype=cuda.float32, device="cuda") for _ in views]
+    wb.cq.GEMMs(views, yds, cuda.from_numpy(x).cuda(), rows)
+    for k in range(n):
+        assert bits_eq(pinned[k], yds[k].cpu().numpy()), k
+
+
 def test_stream_runs(wb, orc, cuda):
     """GEMMs calls the streaming kernel carries as strided runs: a stack of
     views with a constant row step and contiguous outputs, one matrix
