@@ -403,17 +403,19 @@ def decode_gemm_component(pkg, torch, lib, streams=256, reps=20):
     through Whistle's self-attention projections (q 384, k 96, v 128, gate
     512 from x 512; CQ2 G128, one GEMMs call) and the 16384 x 512 CQ4 G32
     vocabulary head, with WC_GEMM_AUTO (tensor cores at this batch), each
-    call captured in a CUDA graph."""
+    call captured in a CUDA graph; and the head followed by the greedy step's
+    argmax (wc_head_argmax: one token id per stream)."""
     rng = np.random.default_rng(4000)
     peaks_gbs, _ = peaks()
     pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     tflops_peak = float(pk.get("bf16_tflops", 1590.0))
-    sets = [("qkvg 384+96+128+512 x512 CQ2 G128", [384, 96, 128, 512], 512, 128, 2),
-            ("head 16384x512 CQ4 G32", [16384], 512, 32, 4)]
+    sets = [("qkvg 384+96+128+512 x512 CQ2 G128", [384, 96, 128, 512], 512, 128, 2, False),
+            ("head 16384x512 CQ4 G32", [16384], 512, 32, 4, False),
+            ("head 16384x512 CQ4 G32 + argmax", [16384], 512, 32, 4, True)]
     st = torch.cuda.Stream()
     sptr = ctypes.c_void_p(st.cuda_stream)
     res = {}
-    for name, outs, in_, group, bits in sets:
+    for name, outs, in_, group, bits, argmax in sets:
         ps, ms = [], []
         for o in outs:
             p = pkg.synth.random_packed(rng, o, in_, group, bits)
@@ -426,10 +428,14 @@ def decode_gemm_component(pkg, torch, lib, streams=256, reps=20):
         ys = [torch.empty(streams, o, device="cuda", dtype=torch.float32) for o in outs]
         hs = (ctypes.c_void_p * len(ms))(*[m.handle.value for m in ms])
         yp = (ctypes.c_void_p * len(ms))(*[y.data_ptr() for y in ys])
+        idx = torch.empty(streams, device="cuda", dtype=torch.int32)
         n0 = lib.wc_launch_count()
 
         def call():
             pkg._lib.check(lib.wc_cq_gemms_ex(hs, len(ms), ctypes.c_void_p(x.data_ptr()), yp, streams, 2, sptr))
+            if argmax:
+                pkg._lib.check(lib.wc_head_argmax(ctypes.c_void_p(ys[0].data_ptr()), streams, outs[0], 1.0, None,
+                                                  ctypes.c_void_p(idx.data_ptr()), sptr))
 
         with torch.cuda.stream(st):
             call()
@@ -448,7 +454,7 @@ def decode_gemm_component(pkg, torch, lib, streams=256, reps=20):
         ms_call = e0.elapsed_time(e1) / reps
         del g
         algo = sum(pkg.synth.algorithmic_bytes_gemv(o, in_, group, bits) - 4 * in_ - 4 * o for o in outs)
-        algo += 4 * streams * in_ + 4 * streams * sum(outs)
+        algo += 4 * streams * in_ + 4 * streams * sum(outs) + (4 * streams if argmax else 0)
         flops = 2.0 * streams * in_ * sum(outs)
         t_roof = max(algo / (peaks_gbs * 1e9), flops / (tflops_peak * 1e12))
         res[name] = {"us": round(ms_call * 1e3, 2), "gbs": round(algo / (ms_call / 1e3) / 1e9, 1),

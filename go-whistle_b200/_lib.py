@@ -68,6 +68,7 @@ _SIGS = {
     "wc_cq_row_host": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_size]),
     "wc_quantize_rows": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p]),
     "wc_quantize_rows_host": (_c_int, [_c_void_p, _c_size, _c_int, _c_int, _c_void_p, _c_void_p]),
+    "wc_head_argmax": (_c_int, [_c_void_p, _c_int, _c_int, _c_float, _c_void_p, _c_void_p, _c_void_p]),
     "wc_attend_int8": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int,
                                 _c_int, _c_int, _c_void_p, _c_float, _c_int, _c_void_p, _c_void_p, _c_void_p]),
     "wc_attend_int8_host": (_c_int, [_c_void_p, _c_size, _c_int, _c_int, _c_void_p, _c_size, _c_void_p, _c_size,

@@ -1038,6 +1038,19 @@ extern "C" wc_status wc_quantize_rows(const float *x, int rows, int cols, int wi
     return e == cudaSuccess ? WC_OK : cuda_error(e, "quantize kernel");
 }
 
+extern "C" wc_status wc_head_argmax(const float *y, int rows, int vocab, float head, float *logits, int32_t *idx,
+                                    wc_stream stream) {
+    if (rows < 0 || vocab < 0) return set_error(WC_ERR_INVALID, fmt("decoder: head of %d rows of %d logits", rows, vocab));
+    if (rows == 0) return WC_OK;
+    if (!idx || (vocab > 0 && !y)) return set_error(WC_ERR_INVALID, "decoder: nil head buffer");
+    cudaError_t e;
+    if (vocab == 0)  // greedy.go:182 on an empty row: 0
+        e = cudaMemsetAsync(idx, 0, sizeof(int32_t) * (size_t)rows, (cudaStream_t)stream);
+    else
+        e = launch_head_argmax(y, rows, vocab, head, logits, idx, (cudaStream_t)stream);
+    return e == cudaSuccess ? WC_OK : cuda_error(e, "head argmax kernel");
+}
+
 extern "C" wc_status wc_quantize_rows_host(const float *x, size_t x_len, int cols, int width, int8_t *q, float *s) {
     if (width <= 0 || cols <= 0 || cols % width != 0)
         return set_error(WC_ERR_INVALID, fmt("needle: int8 rows of %d in chunks of %d", cols, width));

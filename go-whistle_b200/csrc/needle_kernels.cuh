@@ -39,6 +39,9 @@ struct BulkLayout {
 };
 
 cudaError_t launch_quantize_rows(const float *x, int chunks, int width, int8_t *q, float *s, cudaStream_t st);
+// The decoder head's scale and greedy argmax (decode_head.cu).
+cudaError_t launch_head_argmax(const float *y, int rows, int vocab, float head, float *logits, int32_t *idx,
+                               cudaStream_t st);
 size_t attend_smem_bytes(const AttendParams &p);
 cudaError_t launch_attend(const AttendParams &p, int streams, cudaStream_t st);
 size_t attend_any_smem_bytes(const AttendParams &p);

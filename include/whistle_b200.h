@@ -237,6 +237,19 @@ enum {
  */
 wc_status wc_quantize_rows(const float *x, int rows, int cols, int width, int8_t *q, float *s, wc_stream stream);
 
+/*
+ * The decoder's head scale and greedy choice for `rows` rows of `vocab`
+ * logits y (DEVICE memory), e.g. a wc_cq_gemm of the embedding matrix:
+ * internal/decoder/decoder.go:508-523 logits multiplies every logit by head
+ * when head != 1, and internal/decoder/greedy.go:182 argmax takes the first
+ * index of the largest value (a NaN at index 0 gives 0, later NaNs never
+ * win, +0 and -0 tie). logits (or NULL) receives the scaled logits and may
+ * be y itself; idx[rows] receives the argmax of each row (0 for an empty
+ * row). Enqueued on `stream`.
+ */
+wc_status wc_head_argmax(const float *y, int rows, int vocab, float head, float *logits, int32_t *idx,
+                         wc_stream stream);
+
 /* QuantizeRows on HOST memory (x_len values), with int8.go:108's checks. */
 wc_status wc_quantize_rows_host(const float *x, size_t x_len, int cols, int width, int8_t *q, float *s);
 

@@ -5,7 +5,7 @@ timed CPU baseline of ``bench.py``. Only ``tests/``, ``__graft_entry__.smoke()``
 and ``bench.py`` (its ``cpu_baseline`` leg and ``--impl reference``) may use
 it; the product (``go-whistle_b200``) never imports it.
 
-The C sources (``cq_oracle.c``, ``needle_oracle.c``) restate the reference's Go
+The C sources (``cq_oracle.c``, ``needle_oracle.c``, ``decoder_oracle.c``) restate the reference's Go
 routines operation for operation; each names the file:line it follows. The
 reference (a Go module) cannot be built in this image (no Go toolchain, and
 its third-party modules are not vendored), so there is no ``oracle/_ref``.
@@ -49,7 +49,7 @@ class Packed(ctypes.Structure):
 
 def build(force: bool = False) -> Path:
     """Compiles liboracle.so with the Makefile beside it (gcc, no GPU)."""
-    srcs = [HERE / n for n in ("cq_oracle.c", "needle_oracle.c", "oracle.h", "par.h", "Makefile")]
+    srcs = [HERE / n for n in ("cq_oracle.c", "needle_oracle.c", "decoder_oracle.c", "oracle.h", "par.h", "Makefile")]
     if force or not LIB_PATH.exists() or any(s.stat().st_mtime > LIB_PATH.stat().st_mtime for s in srcs):
         subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     return LIB_PATH
@@ -100,6 +100,7 @@ def lib() -> ctypes.CDLL:
         L.wo_attend_int8_streams_mt.argtypes = [ctypes.c_int, _f32p, ctypes.c_int, _i8p, _f32p, _i8p, _f32p,
                                                 ctypes.c_int, _i32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                 ctypes.c_float, _f32p, ctypes.c_int]
+        L.wo_head_argmax.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_float, _f32p, _i32p]
         _lib = L
     return _lib
 
@@ -274,3 +275,14 @@ def attend_streams(q, heads, k8, ks, v8, vs, cap, nkeys, kv_heads, qk, vd, scale
                                     _ptr(out, _f32p), threads)
     return out
 
+
+
+def head_argmax(y: np.ndarray, rows: int, vocab: int, head: float = 1.0):
+    """decoder.go:508 logits' head scale and greedy.go:182 argmax per row:
+    (logits [rows, vocab], idx [rows])."""
+    yy = _c(y, np.float32).reshape(-1)
+    assert yy.size == rows * vocab
+    logits = np.empty(rows * vocab, np.float32)
+    idx = np.empty(rows, np.int32)
+    lib().wo_head_argmax(_ptr(yy, _f32p), rows, vocab, float(head), _ptr(logits, _f32p), _ptr(idx, _i32p))
+    return logits.reshape(rows, vocab), idx

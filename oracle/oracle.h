@@ -113,6 +113,10 @@ void wo_attend_int8_spans_mt(const float *q, int t, int heads, const int8_t *k8,
                              const int32_t *spans, float scale, int quant_q, float *probs, float *out,
                              int threads);
 
+/* internal/decoder/decoder.go:508-523 logits' head scale (logits = y·head
+ * when head != 1, else y) and greedy.go:182 argmax per row of vocab values. */
+void wo_head_argmax(const float *y, int rows, int vocab, float head, float *logits, int32_t *idx);
+
 #ifdef __cplusplus
 }
 #endif
