@@ -161,8 +161,10 @@ def run_reference(args, world, rank):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8 index, int32 sums, f32",
         "data": "synthetic", "config": {"workload": WORKLOAD, "calls_per_shape_per_step": reps},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{sum(reps)} GEMV calls per step over the 8 sweep shapes, one matrix each, "
-                                   f"lut kernel restated in C (oracle/cq_oracle.c) with the reference's work split"},
+                         "sample": f"{sum(reps)} GEMV calls per step over the 8 sweep shapes, one matrix each "
+                                   f"(cache-warm, as the reference's own benchmarks run), the reference's amd64 lut "
+                                   f"path restated in C (oracle/: AVX2 lookup, tables and FWHT of lut_amd64.s) with "
+                                   f"its work split on a persistent thread pool"},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -196,7 +198,8 @@ def cpu_baseline(seconds_per_shape=1.2):
         calls += n
     return {"value": round(total_b / total_t / 1e9, 3), "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"{calls} GEMV calls over the 8 sweep shapes (~{seconds_per_shape}s each), one matrix per "
-                      f"shape, lut kernel restated in C with the reference's work split"}
+                      f"shape (cache-warm), the reference's amd64 lut path restated in C (AVX2 lookup, tables and "
+                      f"FWHT of lut_amd64.s) with its work split on a persistent thread pool"}
 
 
 # ------------------------------------------------------------------ b200 ----

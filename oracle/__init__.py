@@ -5,7 +5,7 @@ timed CPU baseline of ``bench.py``. Only ``tests/``, ``__graft_entry__.smoke()``
 and ``bench.py`` (its ``cpu_baseline`` leg and ``--impl reference``) may use
 it; the product (``go-whistle_b200``) never imports it.
 
-The C sources (``cq_oracle.c``, ``needle_oracle.c``, ``decoder_oracle.c``) restate the reference's Go
+The C sources (``cq_oracle.c``, ``lut_avx2.c``, ``needle_oracle.c``, ``decoder_oracle.c``) restate the reference's Go
 routines operation for operation; each names the file:line it follows. The
 reference (a Go module) cannot be built in this image (no Go toolchain, and
 its third-party modules are not vendored), so there is no ``oracle/_ref``.
@@ -49,7 +49,8 @@ class Packed(ctypes.Structure):
 
 def build(force: bool = False) -> Path:
     """Compiles liboracle.so with the Makefile beside it (gcc, no GPU)."""
-    srcs = [HERE / n for n in ("cq_oracle.c", "needle_oracle.c", "decoder_oracle.c", "oracle.h", "par.h", "Makefile")]
+    srcs = [HERE / n for n in ("cq_oracle.c", "lut_avx2.c", "needle_oracle.c", "decoder_oracle.c", "oracle.h", "par.h",
+                                "Makefile")]
     if force or not LIB_PATH.exists() or any(s.stat().st_mtime > LIB_PATH.stat().st_mtime for s in srcs):
         subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     return LIB_PATH
@@ -74,6 +75,10 @@ def lib() -> ctypes.CDLL:
             fn.restype = ctypes.c_float
             fn.argtypes = [ctypes.c_int, tp, _f32p, ctypes.c_int, _f32p, ctypes.c_float]
         L.wo_lut_lookup_blocked.argtypes = [_f32p, _u8p, _u8p, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        L.wo_lut_lookup_blocked_avx2.argtypes = L.wo_lut_lookup_blocked.argtypes
+        L.wo_fwht_avx2.argtypes = [_f32p, ctypes.c_int]
+        L.wo_lut_tables_planes_avx2.restype = ctypes.c_float
+        L.wo_lut_tables_planes_avx2.argtypes = [ctypes.c_int, _u8p, _f32p, ctypes.c_int, _f32p, ctypes.c_float]
         pp = ctypes.POINTER(Packed)
         L.wo_cq_gemm_lut.restype = ctypes.c_int
         L.wo_cq_gemm_lut.argtypes = [pp, _f32p, ctypes.c_int, _f32p]

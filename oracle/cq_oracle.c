@@ -220,8 +220,19 @@ static void lut_tables_act(const lut_matrix *m, const float *x, float *xh, uint8
     for (int k = m->in; k < pad; k++) xh[k] = 0.0f;
     for (int g = 0; g < m->groups; g++) {
         float *xg = xh + (size_t)g * m->group;
-        wo_fwht(xg, m->group);
-        float mm = lut_tables(m->bits, tab + (size_t)g * tab_bytes, NULL, xg, m->group, m->cb, m->cb_max);
+        float mm;
+#ifdef __AVX2__
+        /* lut_amd64.go:13 fwhtF32, :22 lutTables2, :35 lutTables4: the AVX2
+         * kernels for groups of 8 and more, as the reference dispatches. */
+        if (m->group >= 8) {
+            wo_fwht_avx2(xg, m->group);
+            mm = wo_lut_tables_planes_avx2(m->bits, tab + (size_t)g * tab_bytes, xg, m->group, m->cb, m->cb_max);
+        } else
+#endif
+        {
+            wo_fwht(xg, m->group);
+            mm = lut_tables(m->bits, tab + (size_t)g * tab_bytes, NULL, xg, m->group, m->cb, m->cb_max);
+        }
         steps[g] = mm * m->lut_step;
     }
 }
@@ -230,8 +241,15 @@ static void lut_tables_act(const lut_matrix *m, const float *x, float *xh, uint8
 static void lut_apply(const lut_matrix *m, const uint8_t *tab, const float *steps, float *ybuf, float *y, int b_lo,
                       int b_hi) {
     int ib = m->row_bytes * LUT_ROWS, nbk = m->groups * LUT_ROWS;
+    /* lut_amd64.go:46 lutLookup: the AVX2 kernel where the host has it, as
+     * the reference dispatches (the same bits as the generic kernel). */
+#ifdef __AVX2__
+    wo_lut_lookup_blocked_avx2(ybuf, m->idx + (size_t)b_lo * ib, tab, m->norm + (size_t)b_lo * nbk, steps,
+                               b_hi - b_lo, m->groups, m->gb);
+#else
     wo_lut_lookup_blocked(ybuf, m->idx + (size_t)b_lo * ib, tab, m->norm + (size_t)b_lo * nbk, steps, b_hi - b_lo,
                           m->groups, m->gb);
+#endif
     int r0 = b_lo * LUT_ROWS, r1 = b_hi * LUT_ROWS;
     if (r1 > m->out) r1 = m->out;
     if (r1 > r0) memcpy(y + r0, ybuf, (size_t)(r1 - r0) * sizeof(float));

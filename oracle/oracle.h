@@ -49,6 +49,17 @@ float wo_lut_tables_int(int bits, int16_t *tab, const float *x, int n, const flo
 void wo_lut_lookup_blocked(float *y, const uint8_t *idx, const uint8_t *tab, const float *norm,
                            const float *steps, int blocks, int groups, int gb);
 
+/* internal/cq/lut_amd64.s:236 lutLookupAVX2, restated with AVX2 intrinsics:
+ * the same products as wo_lut_lookup_blocked, bit for bit (asm_test.go). */
+void wo_lut_lookup_blocked_avx2(float *y, const uint8_t *idx, const uint8_t *tab, const float *norm,
+                                const float *steps, int blocks, int groups, int gb);
+
+/* lut_amd64.s:20 fwhtAVX2 (n a power of two >= 8) and :127/:184
+ * lutTables2AVX2 / lutTables4AVX2 (n a multiple of 8), restated: the same
+ * bits as wo_fwht and wo_lut_tables_planes. */
+void wo_fwht_avx2(float *x, int n);
+float wo_lut_tables_planes_avx2(int bits, uint8_t *tab, const float *x, int n, const float *cb, float cb_max);
+
 /*
  * A CQ matrix as cact.Packed holds it (internal/cact/packed.go:18-40): index
  * = out rows of row_bytes LSB-first bytes, norms16 = [out][groups] FP16,

@@ -33,6 +33,16 @@ def test_fwht_matches_sylvester(orc):
         x = (rng.integers(0, 17, n) - 8).astype(np.float32)
         want = (refmath.sylvester(n) @ x.astype(np.float64)).astype(np.float32)
         assert np.array_equal(orc.fwht(x), want), n
+    # lut_amd64.s:20 fwhtAVX2 restated: the same bits as fwht (asm_test.go)
+    import ctypes
+
+    f = ctypes.POINTER(ctypes.c_float)
+    for n in (8, 16, 32, 64, 128, 256, 1024):
+        for trial in range(3):
+            x = rng.normal(size=n).astype(np.float32) * np.float32(10.0 ** (trial - 1))
+            y = x.copy()
+            orc.lib().wo_fwht_avx2(y.ctypes.data_as(f), n)
+            assert np.array_equal(y.view(np.uint32), orc.fwht(x).view(np.uint32)), n
 
 
 def test_float16_known_answers(orc):
@@ -108,6 +118,15 @@ def test_lut_tables(orc, bits):
                 x[:] = 0
             m, planes = orc.lut_tables_planes(bits, x, cb, cb_max)
             m2, ints = orc.lut_tables_int(bits, x, cb, cb_max)
+            # lut_amd64.s:127/184 lutTables2AVX2/lutTables4AVX2 restated: the same planes
+            import ctypes
+
+            planes2 = np.zeros_like(planes)
+            m3 = orc.lib().wo_lut_tables_planes_avx2(bits, planes2.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)),
+                                                     x.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n,
+                                                     cb.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                                     float(cb_max))
+            assert np.float32(m3) == m and np.array_equal(planes2, planes), (n, trial)
             mn, vn = numpy_tables(bits, x, cb, cb_max)
             assert m == m2 == mn
             assert np.array_equal(ints.astype(np.int32), vn)
@@ -153,6 +172,11 @@ def test_lut_lookup_blocked(orc):
                         coef = norm.reshape(blocks, groups, 32)[b, g] * steps[g]
                         want[b * 32:(b + 1) * 32] = want[b * 32:(b + 1) * 32] + (s.astype(np.float32) * coef)
                 assert np.array_equal(y, want), (gb, groups, blocks)
+                # lut_amd64.s:236 lutLookupAVX2 restated: the same bits (asm_test.go)
+                y2 = np.full(blocks * 32, np.nan, np.float32)
+                L.wo_lut_lookup_blocked_avx2(y2.ctypes.data_as(f), idx.ctypes.data_as(u), tab.ctypes.data_as(u),
+                                             norm.ctypes.data_as(f), steps.ctypes.data_as(f), blocks, groups, gb)
+                assert np.array_equal(y2.view(np.uint32), y.view(np.uint32)), (gb, groups, blocks)
 
 
 @pytest.mark.parametrize("shape", TEST_SHAPES)
