@@ -34,7 +34,6 @@ namespace {
 constexpr int kTcM = 128;         // UMMA M (cta_group::1)
 constexpr int kTcN = 128;         // UMMA N, TMEM columns
 constexpr int kTcK = 64;          // bf16 elements per 128-byte row of a chunk
-constexpr int kStages = 2;
 constexpr int kChunkBytes = kTcM * 128;  // one 128 x 64 bf16 tile, A and B alike
 constexpr int kTcThreads = 192;
 constexpr uint32_t kSpinLimit = 1u << 22;
@@ -116,7 +115,11 @@ __device__ __forceinline__ uint32_t swz(int row, int k) {
     return (uint32_t)row * 128u + ((uint32_t)(((k >> 3) ^ (row & 7)) & 7) << 4) + (uint32_t)(k & 7) * 2u;
 }
 
-__global__ void __launch_bounds__(kTcThreads, 3) cq_gemm_tc_kernel(const __grid_constant__ TcParams p) {
+// kStages ring stages: 2 with three CTAs per SM; a launch of few tiles (one
+// or two per SM) takes a deeper ring, more of its loads in flight at once.
+template <int kStages>
+__global__ void __launch_bounds__(kTcThreads, kStages <= 2 ? 3 : kStages <= 3 ? 2 : 1)
+    cq_gemm_tc_kernel(const __grid_constant__ TcParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte alignment for the swizzle atoms.
     unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -656,7 +659,8 @@ cudaError_t launch_rotate_bf16(const CqShape &s, const float *x, int m, unsigned
     return cudaGetLastError();
 }
 
-size_t tc_smem_bytes() { return 1024 + 2 * kStages * kChunkBytes + 8 * (2 * kStages + 1) + 16; }
+static size_t tc_smem_bytes_st(int stages) { return 1024 + 2 * (size_t)stages * kChunkBytes + 8 * (2 * stages + 1) + 16; }
+size_t tc_smem_bytes() { return tc_smem_bytes_st(2); }
 
 // ---- the no-allocation entry point's scratch --------------------------------
 //
@@ -762,13 +766,20 @@ int tc_total_tiles(const TcParams &p) {
 // on st: its CTAs may start while the rotation drains, and the producer
 // waits for it before reading the x̂ image (griddepcontrol.wait).
 cudaError_t launch_gemm_tc(const TcParams &p, cudaStream_t st) {
-    const size_t smem = tc_smem_bytes();
-    cudaError_t e = cudaFuncSetAttribute(cq_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int ntiles = tc_total_tiles(p), mtiles = (p.m + kTcM - 1) / kTcM;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // The deepest ring that still holds the CTAs one wave needs per SM.
+    const long long per_sm = ((long long)ntiles * mtiles + sms - 1) / sms;
+    const int stages = per_sm <= 1 ? 6 : per_sm <= 2 ? 3 : 2;
+    void (*fn)(TcParams) = stages == 6 ? cq_gemm_tc_kernel<6> : stages == 3 ? cq_gemm_tc_kernel<3> : cq_gemm_tc_kernel<2>;
+    const size_t smem = tc_smem_bytes_st(stages);
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     TcParams q = p;
     q.pdl = 1;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((unsigned)tc_total_tiles(p), (unsigned)((p.m + kTcM - 1) / kTcM));
+    cfg.gridDim = dim3((unsigned)ntiles, (unsigned)mtiles);
     cfg.blockDim = dim3(kTcThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -777,7 +788,7 @@ cudaError_t launch_gemm_tc(const TcParams &p, cudaStream_t st) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, cq_gemm_tc_kernel, q);
+    e = cudaLaunchKernelEx(&cfg, fn, q);
     count_launch();
     return e != cudaSuccess ? e : cudaGetLastError();
 }

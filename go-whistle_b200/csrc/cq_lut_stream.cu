@@ -112,10 +112,11 @@ __device__ __forceinline__ TileLoc tile_loc(const SP &p, int t, int k) {
 // Rotation, group bounds, 8191/M and steps for one activation (lut.go:160-178).
 __device__ void rotate_and_bound(const CqShape &s, const float *x, float *xs, float *steps, float *invs) {
     const int tid = threadIdx.x, pad = s.pad, G = s.group, half = G >> 1;
-    for (int k = tid; k < pad; k += kStreamThreads) xs[k] = k < s.in ? x[k] : 0.0f;
+    const int nt = blockDim.x;
+    for (int k = tid; k < pad; k += nt) xs[k] = k < s.in ? x[k] : 0.0f;
     __syncthreads();
     for (int h = 1; h < G; h <<= 1) {
-        for (int b = tid; b < pad / 2; b += kStreamThreads) {
+        for (int b = tid; b < pad / 2; b += nt) {
             int g = b / half, t = b % half;
             int j = g * G + (t / h) * 2 * h + (t % h);
             float a = xs[j], c = xs[j + h];
@@ -125,7 +126,7 @@ __device__ void rotate_and_bound(const CqShape &s, const float *x, float *xs, fl
         __syncthreads();
     }
     const int warp = tid >> 5, lane = tid & 31;
-    for (int g = warp; g < s.groups; g += kStreamWarps) {
+    for (int g = warp; g < s.groups; g += nt / 32) {
         const float *xg = xs + g * G;
         float mx = 0.0f;
         if (s.bits == 2) {
@@ -151,7 +152,7 @@ __device__ void build_pass_tables(const CqShape &s, const float *xs, const float
     const int G = s.group;
     // Nibble tables, biased: nib[e][c][j] for the lo (e = 0) and hi (e = 1)
     // nibble of byte position j0 + j (lut.go:248-255, 272-279).
-    for (int u = tid; u < 2 * npos; u += kStreamThreads) {
+    for (int u = tid; u < 2 * npos; u += (int)blockDim.x) {
         const int e = u / npos, j = u % npos;
         uint16_t *dst = nib + e * 16 * kPassPositions + j;
         const int np = 2 * (j0 + j) + e;  // nibble position in the row
@@ -179,7 +180,7 @@ __device__ void build_pass_tables(const CqShape &s, const float *xs, const float
     // are conflict-free.
     const int npairs = npos / 2;
     const uint32_t *nw = reinterpret_cast<const uint32_t *>(nib);
-    for (int u = tid; u < 4 * npairs; u += kStreamThreads) {
+    for (int u = tid; u < 4 * npairs; u += (int)blockDim.x) {
         const int jp = u % npairs, hq = u / npairs, j = 2 * jp;
         uint32_t lo[16], hi[4];
 #pragma unroll
@@ -302,9 +303,16 @@ __device__ __forceinline__ void load_superchunk(const CqView &v, int sc, int R, 
     }
 }
 
+// Threads of an instance: 512, or 384 for 8-byte groups with four
+// superchunks a pass, whose rolling prefetch needs more than 128 registers
+// (registers are shared per quarter-SM: three warps a quarter leave 168).
+template <int GB, int NSC>
+__host__ __device__ constexpr int stream_threads() { return GB == 8 && NSC == 4 ? 384 : kStreamThreads; }
+
 template <int GB, int NR, int NSC>  // group bytes; run capacity; most superchunks a pass holds (1, 2 or 4)
-__global__ void __launch_bounds__(kStreamThreads, 1)
+__global__ void __launch_bounds__(stream_threads<GB, NSC>(), 1)
     cq_lut_stream_kernel(const __grid_constant__ StreamParamsN<NR> p) {
+    constexpr int NW = stream_threads<GB, NSC>() / 32;  // warps
     constexpr int P = GB / 2;    // byte pairs per group
     constexpr int NG = 32 / P;   // groups per 64-byte superchunk
     extern __shared__ __align__(16) unsigned char smem[];
@@ -325,7 +333,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         // Not the layout the host sized: leave NaN, never a wrong number.
         const int t_b = (int)(((long long)p.total_tiles * blockIdx.x) / gridDim.x);
         const int t_e = (int)(((long long)p.total_tiles * (blockIdx.x + 1)) / gridDim.x);
-        for (int t = t_b + warp; t < t_e; t += kStreamWarps) {
+        for (int t = t_b + warp; t < t_e; t += NW) {
             const TileLoc L = tile_loc(p, t, find_run(p, t));
             const int r = L.r0 + lane;
             if (r < L.v.out) L.y[r] = __int_as_float(0x7fc00000);
@@ -344,10 +352,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     // rotation); afterwards, as soon as a superchunk's registers are
     // consumed, the same superchunk of the warp's next tile is loaded into
     // them, so a tile's worth of loads is in flight while the warp computes.
-    // With 8-byte groups and four superchunks a pass the extra live state
-    // would spill, so that variant loads each tile at the top of its
-    // iteration (its first tile streams into L2 during the table build).
-    constexpr bool kRoll = GB > 8 || NSC <= 2;
+    constexpr bool kRoll = true;
     uint4 d0[4], d1[4], d2[4], d3[4];
     uint32_t n0[4], n1[4], n2[4], n3[4];
     const bool has_tile = t_begin + warp < t_end;
@@ -384,7 +389,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         for (int w = 0; w < 16; w++) cbw[w] = 0;
         int a_rot = 0;
         int k = -1;
-        for (int t = t_begin + warp; t < t_end; t += kStreamWarps) {
+        for (int t = t_begin + warp; t < t_end; t += NW) {
             k = run_from(p, t, k);
             const TileLoc loc = tile_loc(p, t, k);
             const CqView &v = loc.v;
@@ -427,7 +432,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
             if (pass > 0 && valid) y = *src;
 
             // The warp's next tile.
-            const int tn = t + kStreamWarps;
+            const int tn = t + NW;
             const bool nxt = kRoll && tn < t_end;
             int kn = k;
             TileLoc ln = loc;
@@ -526,7 +531,8 @@ static cudaError_t launch_stream_n(const StreamParamsN<NR> &p, int ctas, cudaStr
         nsc <= 1 ? stream_fn<NR, 1>(p.shape.gb) : nsc == 2 ? stream_fn<NR, 2>(p.shape.gb) : stream_fn<NR, 4>(p.shape.gb);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    fn<<<ctas, kStreamThreads, smem, st>>>(p);
+    const int threads = p.shape.gb == 8 && nsc >= 3 ? stream_threads<8, 4>() : kStreamThreads;
+    fn<<<ctas, threads, smem, st>>>(p);
     count_launch();
     return cudaGetLastError();
 }
