@@ -65,11 +65,6 @@ __device__ __forceinline__ int32_t lds_tab(uint32_t addr) {
     return (int32_t)v;
 }
 
-// Hint: fetch [addr, addr + bytes) into L2 (bytes a multiple of 16, > 0).
-__device__ __forceinline__ void prefetch_l2(const void *addr, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(addr), "r"(bytes) : "memory");
-}
-
 // The run holding tile t.
 template <class SP>
 __device__ __forceinline__ int find_run(const SP &p, int t) {
@@ -195,29 +190,6 @@ __device__ void build_pass_tables(const CqShape &s, const float *xs, const float
             for (int c = 0; c < 16; c++) dst[(16 * i + c) * 64] = lo[c] + hi[i];
     }
     __syncthreads();
-}
-
-// Lane 0 of a warp asks L2 for tile t's index bytes and norms of
-// superchunks [sc0, sc0 + nsc_pass): 4 runs of 32 rows x 16 bytes and one
-// run of 32 rows x NG norms per superchunk, all inside the matrix.
-template <int NG, class SP>
-__device__ __forceinline__ void prefetch_tile(const SP &p, int t, int sc0, int nsc_pass) {
-    const TileLoc L = tile_loc(p, t, find_run(p, t));
-    const CqView &v = L.v;
-    const int r0 = L.r0;
-    const int rows = min(32, v.out - r0);
-    const int R0 = v.row0 + r0;
-    for (int scl = 0; scl < nsc_pass; scl++) {
-        const int sc = sc0 + scl;
-#pragma unroll
-        for (int i = 0; i < 4; i++) prefetch_l2(v.idx + (((size_t)sc * 4 + i) * v.ld + R0) * 16, (uint32_t)rows * 16);
-        // The norm run may start off a 16-byte boundary: prefetch its aligned
-        // interior only, which stays inside the run.
-        const uintptr_t a0 = (uintptr_t)(v.nrm + ((size_t)sc * v.ld + R0) * NG);
-        const uintptr_t a1 = a0 + (uintptr_t)rows * NG * 2;
-        const uintptr_t s0 = (a0 + 15) & ~(uintptr_t)15, s1 = a1 & ~(uintptr_t)15;
-        if (s1 > s0) prefetch_l2(reinterpret_cast<const void *>(s0), (uint32_t)(s1 - s0));
-    }
 }
 
 // One superchunk of a 32-row tile: 32 slots of two table lookups each, one
@@ -352,23 +324,18 @@ __global__ void __launch_bounds__(stream_threads<GB, NSC>(), 1)
     // rotation); afterwards, as soon as a superchunk's registers are
     // consumed, the same superchunk of the warp's next tile is loaded into
     // them, so a tile's worth of loads is in flight while the warp computes.
-    constexpr bool kRoll = true;
     uint4 d0[4], d1[4], d2[4], d3[4];
     uint32_t n0[4], n1[4], n2[4], n3[4];
     const bool has_tile = t_begin + warp < t_end;
     auto first_tile = [&](int sc0, int nsc_pass) {
-        if (kRoll) {
-            if (has_tile) {
-                const TileLoc l0 = tile_loc(p, t_begin + warp, find_run(p, t_begin + warp));
-                const bool v0 = l0.r0 + lane < l0.v.out;
-                const int R0 = l0.v.row0 + l0.r0 + lane;
-                load_superchunk<NG>(l0.v, sc0, R0, v0, d0, n0);
-                if (NSC > 1 && nsc_pass > 1) load_superchunk<NG>(l0.v, sc0 + 1, R0, v0, d1, n1);
-                if (NSC > 2 && nsc_pass > 2) load_superchunk<NG>(l0.v, sc0 + 2, R0, v0, d2, n2);
-                if (NSC > 3 && nsc_pass > 3) load_superchunk<NG>(l0.v, sc0 + 3, R0, v0, d3, n3);
-            }
-        } else if (lane == 0 && has_tile) {
-            prefetch_tile<NG>(p, t_begin + warp, sc0, nsc_pass);
+        if (has_tile) {
+            const TileLoc l0 = tile_loc(p, t_begin + warp, find_run(p, t_begin + warp));
+            const bool v0 = l0.r0 + lane < l0.v.out;
+            const int R0 = l0.v.row0 + l0.r0 + lane;
+            load_superchunk<NG>(l0.v, sc0, R0, v0, d0, n0);
+            if (NSC > 1 && nsc_pass > 1) load_superchunk<NG>(l0.v, sc0 + 1, R0, v0, d1, n1);
+            if (NSC > 2 && nsc_pass > 2) load_superchunk<NG>(l0.v, sc0 + 2, R0, v0, d2, n2);
+            if (NSC > 3 && nsc_pass > 3) load_superchunk<NG>(l0.v, sc0 + 3, R0, v0, d3, n3);
         }
     };
     first_tile(0, min(min(s.row_bytes, kPassPositions) / 64, NSC));
@@ -396,13 +363,6 @@ __global__ void __launch_bounds__(stream_threads<GB, NSC>(), 1)
             const int r = loc.r0 + lane;
             const bool valid = r < v.out;
             const int off = v.row0 & 31;
-            if (!kRoll) {
-                const int R = v.row0 + r;
-                load_superchunk<NG>(v, sc0, R, valid, d0, n0);
-                if (NSC > 1 && nsc_pass > 1) load_superchunk<NG>(v, sc0 + 1, R, valid, d1, n1);
-                if (NSC > 2 && nsc_pass > 2) load_superchunk<NG>(v, sc0 + 2, R, valid, d2, n2);
-                if (NSC > 3 && nsc_pass > 3) load_superchunk<NG>(v, sc0 + 3, R, valid, d3, n3);
-            }
 
             if (off != cached_off) {
                 cached_off = off;
@@ -433,7 +393,7 @@ __global__ void __launch_bounds__(stream_threads<GB, NSC>(), 1)
 
             // The warp's next tile.
             const int tn = t + NW;
-            const bool nxt = kRoll && tn < t_end;
+            const bool nxt = tn < t_end;
             int kn = k;
             TileLoc ln = loc;
             int Rn = 0;
