@@ -108,6 +108,39 @@ __device__ __forceinline__ TileLoc tile_loc(const SP &p, int t, int k) {
 __device__ void rotate_and_bound(const CqShape &s, const float *x, float *xs, float *steps, float *invs) {
     const int tid = threadIdx.x, pad = s.pad, G = s.group, half = G >> 1;
     const int nt = blockDim.x;
+    if (G <= 32) {
+        // Groups within a warp: lane l of chunk c holds element 32c + l; the
+        // butterflies (the same stages and operand order as below) and the
+        // group's bound run by shuffles, with no block barrier between.
+        const int lane = tid & 31;
+        for (int c = tid >> 5; c * 32 < pad; c += nt >> 5) {
+            const int k = c * 32 + lane;
+            float v = k < s.in ? x[k] : 0.0f;
+            for (int h = 1; h < G; h <<= 1) {
+                const float o = __shfl_xor_sync(0xffffffffu, v, h);
+                v = (lane & h) ? __fsub_rn(o, v) : __fadd_rn(v, o);
+            }
+            if (k < pad) xs[k] = v;
+            const float a = fabsf(v);
+            float mv;
+            if (s.bits == 2) {  // |x[2q]| + |x[2q+1]|, the even element first
+                const float pa = __shfl_xor_sync(0xffffffffu, a, 1);
+                mv = (lane & 1) ? __fadd_rn(pa, a) : __fadd_rn(a, pa);
+            } else {
+                mv = a;
+            }
+            mv = fmaxf(0.0f, mv);
+            for (int o = 1; o < G; o <<= 1) mv = fmaxf(mv, __shfl_xor_sync(0xffffffffu, mv, o));
+            if ((lane & (G - 1)) == 0 && k < pad) {
+                const int g = k / G;
+                const float m = __fmul_rn(s.cb_max, mv);
+                invs[g] = m > 0.0f ? __fdiv_rn((float)kLutQ, m) : 0.0f;
+                steps[g] = __fmul_rn(m, s.lut_step);
+            }
+        }
+        __syncthreads();
+        return;
+    }
     for (int k = tid; k < pad; k += nt) xs[k] = k < s.in ? x[k] : 0.0f;
     __syncthreads();
     for (int h = 1; h < G; h <<= 1) {

@@ -231,7 +231,8 @@ def test_bytes(wb, cuda):
 # several table passes (rows of 256 and 1024 index bytes), and GEMMs over
 # views that start inside a 32-row tile.
 STREAM_CASES = [(16384, 512, 32, 4), (8199, 512, 128, 4), (16384, 512, 32, 2), (8192, 2048, 32, 4),
-                (8192, 2048, 32, 2), (20000, 512, 128, 2), (4096, 2048, 128, 4)]
+                (8192, 2048, 32, 2), (20000, 512, 128, 2), (4096, 2048, 128, 4), (16384, 512, 16, 4),
+                (16384, 512, 64, 2)]
 
 
 @pytest.mark.parametrize("case", STREAM_CASES, ids=[f"{o}x{i}g{g}b{b}" for o, i, g, b in STREAM_CASES])
@@ -239,6 +240,7 @@ def test_stream_kernel_bit_exact(wb, orc, cuda, case):
     out, in_, group, bits = case
     rng, p, m, om = make(wb, orc, out + in_ + group + bits, out, in_, group, bits, "lloyd")
     x = rng.normal(size=in_).astype(np.float32)
+    x[group:2 * group] = 0.0  # a group whose bound M is 0 (lut.go:219: 8191/M taken as 0)
     want = orc.gemm_lut(om, x, 1, threads=8).reshape(-1)
     xd = cuda.from_numpy(x).cuda()
     yd = cuda.full((out,), float("nan"), dtype=cuda.float32, device="cuda")
