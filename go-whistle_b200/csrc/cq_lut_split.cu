@@ -130,38 +130,69 @@ __global__ void __launch_bounds__(kSplitThreads) cq_lut_split_kernel(const __gri
     // This CTA's columns of the activation, zero past In (lut.go:163-165),
     // and the FWHT of each of its groups (kernel.go:384), stage by stage.
     const float *x = p.x + (size_t)act * s.in;
-    for (int c = tid; c < gn * G; c += kSplitThreads) {
-        const int col = g0 * G + c;
-        xs[c] = col < s.in ? x[col] : 0.0f;
-    }
-    __syncthreads();
-    const int half = G >> 1;
-    for (int h = 1; h < G; h <<= 1) {
-        for (int b = tid; b < gn * half; b += kSplitThreads) {
-            const int g = b / half, t = b % half;
-            const int j = g * G + (t / h) * 2 * h + (t % h);
-            const float a = xs[j], c = xs[j + h];
-            xs[j] = __fadd_rn(a, c);
-            xs[j + h] = __fsub_rn(a, c);
+    if (G <= 32) {
+        // Groups within a warp: butterflies (same stages, same operand
+        // order) and bounds by shuffles, no block barrier between stages.
+        const int lane = tid & 31, ncol = gn * G;
+        for (int c = tid >> 5; c * 32 < ncol; c += kSplitThreads / 32) {
+            const int lc = c * 32 + lane, col = g0 * G + lc;
+            float v = lc < ncol && col < s.in ? x[col] : 0.0f;
+            for (int h = 1; h < G; h <<= 1) {
+                const float o = __shfl_xor_sync(0xffffffffu, v, h);
+                v = (lane & h) ? __fsub_rn(o, v) : __fadd_rn(v, o);
+            }
+            if (lc < ncol) xs[lc] = v;
+            const float a = fabsf(v);
+            float mv;
+            if (s.bits == 2) {  // |x[2q]| + |x[2q+1]|, the even element first
+                const float pa = __shfl_xor_sync(0xffffffffu, a, 1);
+                mv = (lane & 1) ? __fadd_rn(pa, a) : __fadd_rn(a, pa);
+            } else {
+                mv = a;
+            }
+            mv = fmaxf(0.0f, mv);
+            for (int o = 1; o < G; o <<= 1) mv = fmaxf(mv, __shfl_xor_sync(0xffffffffu, mv, o));
+            if ((lane & (G - 1)) == 0 && lc < ncol) {
+                const int g = lc / G;
+                const float m = __fmul_rn(s.cb_max, mv);
+                invs[g] = m > 0.0f ? __fdiv_rn((float)kLutQ, m) : 0.0f;
+                steps[g] = __fmul_rn(m, s.lut_step);
+            }
+        }
+    } else {
+        for (int c = tid; c < gn * G; c += kSplitThreads) {
+            const int col = g0 * G + c;
+            xs[c] = col < s.in ? x[col] : 0.0f;
         }
         __syncthreads();
-    }
-    // Bounds M (lut.go:241-245, 264-269), 8191/M and the step per group.
-    const int warp = tid >> 5, lane = tid & 31;
-    for (int g = warp; g < gn; g += kSplitThreads / 32) {
-        const float *xg = xs + g * G;
-        float mx = 0.0f;
-        if (s.bits == 2) {
-            for (int q = lane; q < half; q += 32) mx = fmaxf(mx, __fadd_rn(fabsf(xg[2 * q]), fabsf(xg[2 * q + 1])));
-        } else {
-            for (int q = lane; q < G; q += 32) mx = fmaxf(mx, fabsf(xg[q]));
+        const int half = G >> 1;
+        for (int h = 1; h < G; h <<= 1) {
+            for (int b = tid; b < gn * half; b += kSplitThreads) {
+                const int g = b / half, t = b % half;
+                const int j = g * G + (t / h) * 2 * h + (t % h);
+                const float a = xs[j], c = xs[j + h];
+                xs[j] = __fadd_rn(a, c);
+                xs[j + h] = __fsub_rn(a, c);
+            }
+            __syncthreads();
         }
+        // Bounds M (lut.go:241-245, 264-269), 8191/M and the step per group.
+        const int warp = tid >> 5, lane = tid & 31;
+        for (int g = warp; g < gn; g += kSplitThreads / 32) {
+            const float *xg = xs + g * G;
+            float mx = 0.0f;
+            if (s.bits == 2) {
+                for (int q = lane; q < half; q += 32) mx = fmaxf(mx, __fadd_rn(fabsf(xg[2 * q]), fabsf(xg[2 * q + 1])));
+            } else {
+                for (int q = lane; q < G; q += 32) mx = fmaxf(mx, fabsf(xg[q]));
+            }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (lane == 0) {
-            const float m = __fmul_rn(s.cb_max, mx);
-            invs[g] = m > 0.0f ? __fdiv_rn((float)kLutQ, m) : 0.0f;
-            steps[g] = __fmul_rn(m, s.lut_step);
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (lane == 0) {
+                const float m = __fmul_rn(s.cb_max, mx);
+                invs[g] = m > 0.0f ? __fdiv_rn((float)kLutQ, m) : 0.0f;
+                steps[g] = __fmul_rn(m, s.lut_step);
+            }
         }
     }
     __syncthreads();
