@@ -530,6 +530,102 @@ __global__ void __launch_bounds__(256) rotate_bf16_kernel(const float *__restric
     }
 }
 
+// The segment-per-lane rotation of rotate_bf16_kernel with both of its
+// memory sides staged through shared memory, for activations whose rows
+// are whole chunks (In = kpad, so a warp's 32 segments are 1024
+// consecutive floats of x): each warp loads its floats as consecutive
+// 16-byte pieces (512 bytes an instruction) and stores its 16 image rows
+// of 128 bytes as whole rows (four per instruction), instead of one
+// 128-byte stride per lane on both sides. The butterflies are
+// rotate_bf16_kernel's.
+constexpr int kRotSeg = 36;  // floats per staged segment (32 + 4: conflict-free 16-byte reads)
+__global__ void __launch_bounds__(256) rotate_bf16_v3_kernel(const float *__restrict__ x, int m, int G, int kpad,
+                                                             int kchunks, int mtiles,
+                                                             unsigned char *__restrict__ a) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    __shared__ __align__(16) float sx[8][32 * kRotSeg];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int segs = kpad / 32;
+    const long seg0 = ((long)blockIdx.x * 8 + warp) * 32;  // the warp's first segment
+    const long total = (long)mtiles * kTcM * segs;
+    if (seg0 >= total) return;  // whole warps: total is a multiple of 32 segments (kpad % 64 == 0, 128 rows)
+    float *buf = sx[warp];
+    const long xend = (long)m * kpad;  // floats of x (In = kpad)
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        const int f4 = e * 32 + lane;  // 16-byte piece of the warp's 1024 floats
+        const long L = seg0 * 32 + 4L * f4;
+        float4 val = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (L < xend) val = __ldg(reinterpret_cast<const float4 *>(x + L));
+        *reinterpret_cast<float4 *>(buf + (f4 >> 3) * kRotSeg + (f4 & 7) * 4) = val;
+    }
+    __syncwarp();
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        const float4 f = *reinterpret_cast<const float4 *>(buf + lane * kRotSeg + 4 * q);
+        v[4 * q] = f.x;
+        v[4 * q + 1] = f.y;
+        v[4 * q + 2] = f.z;
+        v[4 * q + 3] = f.w;
+    }
+    const long seg = seg0 + lane;
+    const int sg = (int)(seg % segs);
+    const int gin = G < 32 ? G : 32;  // butterflies inside the segment
+#pragma unroll
+    for (int h = 1; h < 32; h <<= 1) {
+        if (h < gin) {
+#pragma unroll
+            for (int e = 0; e < 32; e++) {
+                if ((e & h) == 0) {
+                    const float a0 = v[e], b0 = v[e + h];
+                    v[e] = a0 + b0;
+                    v[e + h] = a0 - b0;
+                }
+            }
+        }
+    }
+    for (int h = 32; h < G; h <<= 1) {  // across the lanes of a group
+        const int pl = h / 32;
+#pragma unroll
+        for (int e = 0; e < 32; e++) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[e], pl);
+            v[e] = (sg & pl) ? o - v[e] : v[e] + o;
+        }
+    }
+    // Lanes 2j and 2j+1 fill image row j of the warp (144-byte stride): the
+    // two 64-byte halves of one 128-byte chunk row, in swizzled order.
+    __syncwarp();
+    unsigned char *ob = reinterpret_cast<unsigned char *>(buf);
+    const long row = seg / segs;
+    const int r = (int)(row % kTcM), half = lane & 1;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        uint4 w;
+        __nv_bfloat162 t0 = __floats2bfloat162_rn(v[8 * c], v[8 * c + 1]);
+        __nv_bfloat162 t1 = __floats2bfloat162_rn(v[8 * c + 2], v[8 * c + 3]);
+        __nv_bfloat162 t2 = __floats2bfloat162_rn(v[8 * c + 4], v[8 * c + 5]);
+        __nv_bfloat162 t3 = __floats2bfloat162_rn(v[8 * c + 6], v[8 * c + 7]);
+        w.x = *reinterpret_cast<uint32_t *>(&t0);
+        w.y = *reinterpret_cast<uint32_t *>(&t1);
+        w.z = *reinterpret_cast<uint32_t *>(&t2);
+        w.w = *reinterpret_cast<uint32_t *>(&t3);
+        *reinterpret_cast<uint4 *>(ob + (lane >> 1) * 144 + (((half * 4 + c) ^ (r & 7)) << 4)) = w;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const int u = e * 32 + lane, j = u >> 3, wc = u & 7;  // image row j of the warp, 16-byte chunk wc
+        const long sj = seg0 + 2 * j;
+        const long rowj = sj / segs;
+        const int kc = (int)(sj % segs) / 2;
+        unsigned char *dst = a + (((size_t)(rowj / kTcM) * kchunks + kc) * kChunkBytes) +
+                             (size_t)(rowj % kTcM) * 128 + wc * 16;
+        *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(ob + j * 144 + wc * 16);
+    }
+}
+
+
 // The same image with four columns per lane: a warp's loads are 512
 // contiguous bytes of one row, the butterflies with h < 4 run in registers
 // and those with h >= 4 between lanes (xor h/4), and each lane stores its
@@ -654,6 +750,11 @@ cudaError_t launch_rotate_bf16(const CqShape &s, const float *x, int m, unsigned
     }
     const long threads = (long)mtiles * kTcM * (kpad / 32);
     if (threads == 0) return cudaSuccess;
+    if (s.in == kpad && (((uintptr_t)x) & 15) == 0) {  // rows of whole chunks: staged, coalesced
+        rotate_bf16_v3_kernel<<<(int)((threads + 255) / 256), 256, 0, st>>>(x, m, s.group, kpad, kchunks, mtiles, a);
+        count_launch();
+        return cudaGetLastError();
+    }
     rotate_bf16_kernel<<<(int)((threads + 255) / 256), 256, 0, st>>>(x, m, s.in, s.group, kpad, kchunks, mtiles, a);
     count_launch();
     return cudaGetLastError();
