@@ -10,7 +10,7 @@ larger than L2; no flush needed). The 1000 calls of a shape share their
 input x and run as cq.GEMMs (internal/cq/kernel.go:134) through the C ABI,
 captured once in a CUDA graph and replayed per step.
 
-value = algorithmic bytes of all calls (SURVEY's B = Out*RowBytes +
+value = algorithmic bytes of all calls (B = Out*RowBytes +
 2*Out*Groups + 4*In + 4*Out + 4*2^bits per GEMV) / device time, summed over
 ranks (weak scaling: every rank runs the full sweep on its own GPU).
 
