@@ -337,6 +337,33 @@ def test_gemms_host_direct(wb, orc, cuda, in_, bits, rows, view_rows):
         assert bits_eq(pinned[k].reshape(rows, view_rows), want[:, k])
 
 
+def test_gemms_host_direct_mixed(wb, orc, cuda):
+    """Page-locked host outputs for a list that mixes shared-table matrices,
+    another codebook, an Exact view and an empty view (kernel.go:134's
+    GEMMs cases): every kernel stores into host memory directly, the empty
+    output stays untouched; bit for bit the oracle's."""
+    rng = np.random.default_rng(383)
+    ps = [wb.synth.random_packed(rng, o, 512, 128, 2, "lloyd") for o in (384, 96, 128, 512)]
+    other = wb.synth.random_packed(rng, 64, 512, 128, 2, "reference")
+    ms = [wb.cq.New(p) for p in ps] + [wb.cq.New(other)]
+    ms.append(ms[0].Exact().Rows(3, 40))
+    ms.append(ms[1].Rows(5, 5))
+    oms = [orc.OracleMatrix.of(p) for p in ps] + [orc.OracleMatrix.of(other)]
+    for rows in (1, 3):
+        x = rng.normal(size=rows * 512).astype(np.float32)
+        total = sum(rows * m.Out() for m in ms)
+        flat = cuda.full((total,), float("nan"), dtype=cuda.float32).pin_memory().numpy()
+        dsts, off = [], 0
+        for m in ms:
+            dsts.append(flat[off:off + rows * m.Out()])
+            off += rows * m.Out()
+        wb.cq.GEMMs(ms, dsts, x, rows)
+        for k, om in enumerate(oms):
+            assert bits_eq(dsts[k], orc.gemm_lut(om, x, rows).reshape(-1)), k
+        assert bits_eq(dsts[5].reshape(rows, -1), orc.gemm_exact(oms[0], x, rows)[:, 3:40])
+        assert dsts[6].size == 0
+
+
 def test_gemms_host_large_pinned(wb, cuda):
     """Host GEMMs whose page-locked outputs exceed the direct-store limit
     (34 MB): the products go to device memory in chunks and come back by
