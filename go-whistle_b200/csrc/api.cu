@@ -351,6 +351,8 @@ struct HostDirect {
 thread_local HostDirect t_direct;
 }  // namespace
 
+static int *device_err_word();
+
 // The streaming kernel for one activation, if every matrix has the stream
 // layout and the products are large enough; returns false otherwise.
 static bool try_stream(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows, cudaStream_t st,
@@ -377,6 +379,7 @@ static bool try_stream(const wc_cq *const *ms, int n, const float *x, float *con
         p->x = x;
         p->smem_base = stream_smem_base();
         p->part = nullptr;
+        p->err = device_err_word();
         cudaError_t e = cudaSuccess;
         if (t_direct.on && stream_passes(p->shape) > 1) e = t_direct.get((size_t)p->total_tiles * 32, &p->part);
         const int ctas = p->total_tiles < sms ? p->total_tiles : sms;
@@ -873,6 +876,14 @@ extern "C" wc_status wc_device_status(int *code) {
     if (!w) return set_error(WC_ERR_NOMEM, "cuda: error word");
     WB_CUDA(cudaMemcpy(code, w, sizeof(int), cudaMemcpyDeviceToHost));
     WB_CUDA(cudaMemset(w, 0, sizeof(int)));
+    // The no-allocation GEMM's own word (its calls with err = NULL): the
+    // first code recorded on either word is reported, and both are cleared.
+    if (int *nw = noalloc_err_word()) {
+        int c = 0;
+        WB_CUDA(cudaMemcpy(&c, nw, sizeof(int), cudaMemcpyDeviceToHost));
+        WB_CUDA(cudaMemset(nw, 0, sizeof(int)));
+        if (*code == 0) *code = c;
+    }
     return WC_OK;
 }
 
@@ -1033,7 +1044,8 @@ extern "C" wc_status wc_cq_gemm_tc_noalloc(const wc_cq *h, const float *x, float
     if (!wimg)
         return set_error(WC_ERR_INVALID,
                          "cq: matrix has no tensor-core weight image: call wc_cq_prepare_tc at load time first");
-    cudaError_t e = gemm_tc_noalloc(h->shape, wimg, x, y, rows, h->out, err, (cudaStream_t)stream);
+    cudaError_t e =
+        gemm_tc_noalloc(h->shape, wimg, x, y, rows, h->out, err, rows >= kTcPersistRows, (cudaStream_t)stream);
     return e == cudaSuccess ? WC_OK : cuda_error(e, "cq tensor-core kernel (no allocation)");
 }
 

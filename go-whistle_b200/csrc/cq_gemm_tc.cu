@@ -168,6 +168,7 @@ __global__ void __launch_bounds__(kTcThreads, kStages <= 2 ? 3 : kStages <= 3 ? 
         // it (and its writes of the x̂ image) before the first copy; the
         // set-up above already overlapped its tail.
         if (p.pdl) asm volatile("griddepcontrol.wait;" ::: "memory");
+        int issued = 0;
         for (int kc = 0; kc < kchunks; kc++) {
             const int s = kc % kStages, round = kc / kStages;
             if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
@@ -178,7 +179,12 @@ __global__ void __launch_bounds__(kTcThreads, kStages <= 2 ? 3 : kStages <= 3 ? 
             mbar_expect_tx(&full[s], 2 * kChunkBytes);
             bulk_g2s(sa + s * kChunkBytes, ga + (size_t)kc * kChunkBytes, kChunkBytes, &full[s]);
             bulk_g2s(sb + s * kChunkBytes, gb + (size_t)kc * kChunkBytes, kChunkBytes, &full[s]);
+            issued = kc + 1;
         }
+        // Nothing may land in shared memory after exit: wait (bounded) for
+        // the copies of the last chunk issued on each stage.
+        for (int q = issued - kStages < 0 ? 0 : issued - kStages; q < issued; q++)
+            if (!mbar_wait(&full[q % kStages], (q / kStages) & 1)) atomicExch(p.err, 4);
     } else if (warp == 1 && lane == 0) {
         // MMA issuer.
         bool ok = true;
@@ -776,41 +782,56 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 size_t noalloc_scratch_bytes() { return kNoAllocScratchBytes; }
 
+// The array's device address per device, looked up on first use.
+static unsigned char *g_noalloc_addr[64];
+static std::mutex g_noalloc_mu;
+
+static bool noalloc_ready(int dev) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    return g_noalloc_addr[dev] != nullptr;
+}
+
 // The array's device address on the current device (set-up on first use).
 static cudaError_t noalloc_scratch(unsigned char **out) {
-    static unsigned char *addr[64];
-    static std::mutex mu;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) return e;
-        addr[dev] = static_cast<unsigned char *>(p);
+        g_noalloc_addr[dev] = static_cast<unsigned char *>(p);
     }
-    *out = addr[dev];
+    *out = g_noalloc_addr[dev];
     return cudaSuccess;
+}
+
+// The error word inside the array on the current device, or null when no
+// no-allocation call has set the array up there yet (wc_device_status
+// reads and clears it).
+int *noalloc_err_word() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    unsigned char *base = nullptr;
+    if (!noalloc_ready(dev) || noalloc_scratch(&base) != cudaSuccess) return nullptr;
+    return reinterpret_cast<int *>(base + kNoAllocScratchBytes);
 }
 
 // Rotation into the static image, then the tensor-core GEMM, with no
 // allocation. The caller has checked that the image fits
 // (tc_a_bytes(rows, kchunks) <= kNoAllocScratchBytes) and that the weight
 // image wimg exists. err: a device int for the bounded waits' error code,
-// or null for the array's own word (cleared here on every call).
+// or null for the array's own word, which accumulates the codes until
+// wc_device_status reads and clears it. persistent: the kernel
+// wc_cq_gemm_ex picks for this many rows.
 cudaError_t gemm_tc_noalloc(const CqShape &s, const unsigned char *wimg, const float *x, float *y, int rows, int n,
-                            int *err, cudaStream_t st) {
+                            int *err, bool persistent, cudaStream_t st) {
     unsigned char *base = nullptr;
     cudaError_t e = noalloc_scratch(&base);
     if (e != cudaSuccess) return e;
-    int *word = reinterpret_cast<int *>(base + kNoAllocScratchBytes);
-    if (!err) {
-        e = cudaMemsetAsync(word, 0, sizeof(int), st);
-        if (e != cudaSuccess) return e;
-        err = word;
-    }
+    if (!err) err = reinterpret_cast<int *>(base + kNoAllocScratchBytes);
     e = launch_rotate_bf16(s, x, rows, base, st);
     if (e != cudaSuccess) return e;
     TcParams p{};
@@ -820,7 +841,7 @@ cudaError_t gemm_tc_noalloc(const CqShape &s, const unsigned char *wimg, const f
     p.err = err;
     p.nmats = 1;
     p.mats[0] = TcMat{wimg, y, n, n, 0};
-    return launch_gemm_tc(p, st);
+    return persistent ? launch_gemm_tc_persistent(p, st) : launch_gemm_tc(p, st);
 }
 
 size_t tc_persistent_smem_bytes() {

@@ -64,6 +64,9 @@ struct StreamParamsN {
     // outputs; otherwise [total_tiles][32] floats of device memory, so an
     // output is written once, by the last pass (outputs in host memory).
     float *part;
+    // Device error word: the kernel records code 20 there when the shared
+    // window does not start where the host sized it (and leaves NaN).
+    int *err;
     StreamRun runs[N];
 };
 using StreamParams = StreamParamsN<kMaxStreamRuns>;
@@ -103,7 +106,10 @@ cudaError_t launch_gemm_tc_persistent(const TcParams &p, cudaStream_t st);
 // wc_cq_gemm_tc_noalloc's core: the same kernels on a static scratch array.
 size_t noalloc_scratch_bytes();
 cudaError_t gemm_tc_noalloc(const CqShape &s, const unsigned char *wimg, const float *x, float *y, int rows, int n,
-                            int *err, cudaStream_t st);
+                            int *err, bool persistent, cudaStream_t st);
+// The static array's error word on the current device (null before the
+// first no-allocation call there).
+int *noalloc_err_word();
 
 int stream_smem_base();
 bool stream_eligible(const CqShape &s);

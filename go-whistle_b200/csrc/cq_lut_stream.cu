@@ -335,7 +335,9 @@ __global__ void __launch_bounds__(stream_threads<GB, NSC>(), 1)
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (base != p.smem_base) {
-        // Not the layout the host sized: leave NaN, never a wrong number.
+        // Not the layout the host sized: leave NaN, never a wrong number,
+        // and record it in the error word (wc_device_status).
+        if (tid == 0 && p.err) atomicExch(p.err, 20);
         const int t_b = (int)(((long long)p.total_tiles * blockIdx.x) / gridDim.x);
         const int t_e = (int)(((long long)p.total_tiles * (blockIdx.x + 1)) / gridDim.x);
         for (int t = t_b + warp; t < t_e; t += NW) {
@@ -539,6 +541,7 @@ cudaError_t launch_stream(const StreamParams &p, int ctas, cudaStream_t st) {
     q.total_tiles = p.total_tiles;
     q.smem_base = p.smem_base;
     q.part = p.part;
+    q.err = p.err;
     for (int i = 0; i < kSmallStreamRuns; i++) q.runs[i] = i < p.nruns ? p.runs[i] : StreamRun{};
     return launch_stream_n(q, ctas, st);
 }

@@ -168,15 +168,22 @@ wc_status wc_cq_prepare_tc(const wc_cq *h);
  *    different threads without ordering) race and corrupt each other.
  *  - err: a device int that receives the error code of the kernels' bounded
  *    waits (0 = none; the caller clears it), or NULL to use a word inside
- *    the array, cleared by each call.
- * x [rows][In] and y [rows][Out] are fp32 DEVICE memory; y as
- * wc_cq_gemm_ex with WC_GEMM_TENSOR_CORES computes it.
+ *    the array. That word keeps the first code of any call until
+ *    wc_device_status reports and clears it, so a caller passing NULL
+ *    learns of an expired wait from wc_device_status (which synchronises,
+ *    and so belongs outside the real-time loop, e.g. once per utterance).
+ *    After an expired wait y is incomplete.
+ * x [rows][In] and y [rows][Out] are fp32 DEVICE memory; y is what
+ * wc_cq_gemm_ex with WC_GEMM_TENSOR_CORES computes, bit for bit: the same
+ * kernels are chosen for the same number of rows (the persistent one from
+ * 1,024 rows).
  */
 wc_status wc_cq_gemm_tc_noalloc(const wc_cq *h, const float *x, float *y, int rows, int *err, wc_stream stream);
 
-/* Synchronises the current device and reports (and clears) the error word
- * of the kernels' bounded waits: *code = 0 if none expired. A diagnostic
- * with no reference counterpart. */
+/* Synchronises the current device and reports (and clears) the error words
+ * of the kernels' bounded waits — the library's word and the
+ * no-allocation GEMM's — : *code = 0 if none expired. A diagnostic with no
+ * reference counterpart. */
 wc_status wc_device_status(int *code);
 
 /* GEMM on HOST slices with the reference's length check and panic text

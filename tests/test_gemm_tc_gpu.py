@@ -153,3 +153,61 @@ def test_auto_dispatch(wb, orc, cuda):
             tc = tc_gemms(wb, cuda, ms, x, WC_GEMM_TENSOR_CORES)
             for g, t in zip(got, tc):
                 assert np.array_equal(g.view(np.uint32), t.view(np.uint32))
+
+
+# BASELINE configs[2] at full size: 64 streams × 375 frames = 24,000 rows
+# through the encoder's FFN up/down and fused QKV (4-bit, group 32), and
+# Whistle's own q/k/v/gate set (2-bit, group 128) as one GEMMs call.
+PREFILL = [("up", 2048, 512, 32, 4), ("down", 512, 2048, 32, 4), ("qkv", 1536, 512, 32, 4)]
+
+# The reference's accept for its lut kernel (internal/cq/cq_test.go:196-254
+# TestKernels: cosine >= 0.99999 against the float64 product), applied to
+# every row of the tensor-core product.
+TC_COSINE = 0.99999
+
+
+def _rows_cosine(a, b):
+    num = np.einsum("ij,ij->i", a, b)
+    return num / (np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1))
+
+
+def _check_prefill(orc, p, x, got):
+    xh, w = rotated_operands(p, x.astype(np.float64))
+    want = xh @ w.T
+    gamma = 2.0 ** -7 + (w.shape[1] + np.log2(p.group) + 4) * 2.0 ** -24
+    bound = gamma * (np.abs(xh) @ np.abs(w).T)
+    assert np.all(np.isfinite(got))
+    assert np.all(np.abs(got - want) <= bound)
+    cos = _rows_cosine(got.astype(np.float64), want)
+    assert cos.min() >= TC_COSINE, f"worst row cosine {cos.min():.9f}"
+    # Sampled rows against the oracle's lut product (the reference's own
+    # kernel): the two differ by at most the tensor-core bound plus the lut
+    # kernel's own distance to the float64 product.
+    sample = np.arange(0, x.shape[0], x.shape[0] // 48)
+    lut = orc.gemm_lut(orc.OracleMatrix.of(p), np.ascontiguousarray(x[sample]), len(sample))
+    lut_err = np.abs(lut.astype(np.float64) - want[sample])
+    assert np.all(np.abs(got[sample] - lut) <= bound[sample] + lut_err)
+    assert _rows_cosine(got[sample].astype(np.float64), lut.astype(np.float64)).min() >= TC_COSINE
+
+
+@pytest.mark.parametrize("case", PREFILL, ids=[c[0] for c in PREFILL])
+def test_tc_gemm_configs2_full_size(wb, orc, cuda, case):
+    _, out, in_, group, bits = case
+    rng = np.random.default_rng(2000 + out + in_)
+    p = wb.synth.random_packed(rng, out, in_, group, bits, "baseline")
+    m = wb.cq.New(p)
+    x = rng.normal(size=(24000, in_)).astype(np.float32)
+    got = tc_gemm(wb, cuda, m, x)
+    _check_prefill(orc, p, x, got)
+
+
+def test_tc_gemms_configs2_whistle_qkvg(wb, orc, cuda):
+    rng = np.random.default_rng(2100)
+    ps = [wb.synth.random_packed(rng, o, 512, 128, 2, "lloyd") for o in (384, 96, 128, 512)]
+    for q in ps[1:]:
+        q.Codebook = ps[0].Codebook
+    ms = [wb.cq.New(p) for p in ps]
+    x = rng.normal(size=(24000, 512)).astype(np.float32)
+    got = tc_gemms(wb, cuda, ms, x, WC_GEMM_TENSOR_CORES)
+    for p, g in zip(ps, got):
+        _check_prefill(orc, p, x, g)

@@ -42,9 +42,13 @@ def _bf16_bound(p, x, want_rows):
     return xh @ w.T, gamma * (np.abs(xh) @ np.abs(w).T)
 
 
-@pytest.mark.parametrize("shape", [(512, 512, 32, 4), (1120, 512, 128, 2), (300, 2048, 32, 4)])
+# (out, in, group, bits, row counts of the calls in a row). A smaller call
+# after a larger one finds the larger one's rotated rows in the array; from
+# 1024 rows both entry points run the persistent kernel.
+@pytest.mark.parametrize("shape", [(512, 512, 32, 4, (1000, 200)), (1120, 512, 128, 2, (1000, 200)),
+                                   (300, 2048, 32, 4, (1000, 200)), (512, 512, 32, 4, (4096, 1500))])
 def test_no_alloc_matches_allocating_entry_point(wb, cuda, shape):
-    out, in_, group, bits = shape
+    out, in_, group, bits, calls = shape
     lib = wb._lib.lib()
     rng = np.random.default_rng(out + in_)
     p = wb.synth.random_packed(rng, out, in_, group, bits, "lloyd")
@@ -54,7 +58,7 @@ def test_no_alloc_matches_allocating_entry_point(wb, cuda, shape):
     err = cuda.zeros(1, dtype=cuda.int32, device="cuda")
     # Two calls in a row with different inputs: the second must not see the
     # first's scratch contents.
-    for rows in (200, 1000):
+    for rows in calls:
         x = cuda.randn(rows, in_, device="cuda", dtype=cuda.float32)
         want = cuda.empty(rows, out, device="cuda", dtype=cuda.float32)
         got = cuda.full((rows, out), float("nan"), device="cuda", dtype=cuda.float32)
@@ -89,3 +93,30 @@ def test_no_alloc_limits(wb, cuda):
     wb._lib.check(lib.wc_cq_gemm_tc_noalloc(m.handle, _ptr(x), _ptr(y), 4096, None, None))
     cuda.cuda.synchronize()
     assert bool((y[:4096] == 0.0).all()) and bool((y[4096:] == 7.0).all())
+
+
+def test_no_alloc_allocates_nothing(wb, cuda):
+    """Device memory stays where it was across repeated calls (after the
+    one-time look-up of the array's address), both in torch's view and in
+    the driver's free-memory count."""
+    lib = wb._lib.lib()
+    rng = np.random.default_rng(9)
+    p = wb.synth.random_packed(rng, 1024, 512, 32, 4, "lloyd")
+    m = wb.cq.New(p)
+    wb._lib.check(lib.wc_cq_prepare_tc(m.handle))
+    x = cuda.randn(2048, 512, device="cuda", dtype=cuda.float32)
+    y = cuda.empty(2048, 1024, device="cuda", dtype=cuda.float32)
+    # Warm-up: module load, the address look-up, kernel attributes.
+    wb._lib.check(lib.wc_cq_gemm_tc_noalloc(m.handle, _ptr(x), _ptr(y), 2048, None, None))
+    cuda.cuda.synchronize()
+    free0, _ = cuda.cuda.mem_get_info()
+    alloc0 = cuda.cuda.memory_allocated()
+    for rows in (2048, 100, 1024, 7):
+        wb._lib.check(lib.wc_cq_gemm_tc_noalloc(m.handle, _ptr(x), _ptr(y), rows, None, None))
+    cuda.cuda.synchronize()
+    free1, _ = cuda.cuda.mem_get_info()
+    assert free1 == free0, f"free device memory moved by {free0 - free1} bytes"
+    assert cuda.cuda.memory_allocated() == alloc0
+    code = ctypes.c_int(-1)
+    wb._lib.check(lib.wc_device_status(ctypes.byref(code)))
+    assert code.value == 0
