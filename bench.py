@@ -353,7 +353,7 @@ def prefill_component(pkg, torch, lib, frames=24000, reps=5):
         res[name] = {"us": round(ms * 1e3, 2), "gbs": round(algo / (ms / 1e3) / 1e9, 1),
                      "tflops": round(flops / (ms / 1e3) / 1e12, 1), "roofline_frac": round(t_roof / (ms / 1e3), 3),
                      "algorithmic_bytes": algo}
-    return {"workload": f"configs[2]: {frames} x in fp32 ~N(0,1) prefill rows, tensor cores (bf16 operands in the "
+    return {"workload": f"configs[2]: {frames} x in fp32 ~N(0,1) prefill rows, tensor cores (fp16 operands in the "
                         f"rotated domain, fp32 accumulate)", "per_matrix": res,
             "roofline": "max(algorithmic bytes / measured HBM, flops / measured bf16 peak)"}
 
@@ -464,7 +464,7 @@ def decode_gemm_component(pkg, torch, lib, streams=256, reps=20):
                      "tflops": round(flops / (ms_call / 1e3) / 1e12, 1),
                      "roofline_frac": round(t_roof / (ms_call / 1e3), 3), "algorithmic_bytes": algo,
                      "launches": launches}
-    return {"workload": f"{streams} decode streams: one activation row each, WC_GEMM_AUTO (tensor cores, bf16 "
+    return {"workload": f"{streams} decode streams: one activation row each, WC_GEMM_AUTO (tensor cores, fp16 "
                         f"operands, fp32 accumulate)", "per_set": res,
             "roofline": "max(algorithmic bytes / measured HBM, flops / measured bf16 peak); launch-bound at "
                         "this size"}

@@ -59,6 +59,7 @@ struct CqStorage {
     uint8_t *sidx = nullptr;  // stream layout (cq_lut_stream.cu), or null
     __half *snrm = nullptr;
     size_t idx_bytes = 0, nrm_bytes = 0, sidx_bytes = 0, snrm_bytes = 0;
+    float nrm_max = 0.0f;  // largest |norm| (the tensor-core image's scale)
     int device = 0;
     ~CqStorage() {
         int cur = 0;
@@ -77,6 +78,7 @@ struct TcImage {
     std::mutex mu;
     unsigned char *b = nullptr;
     size_t bytes = 0;
+    float ws = 1.0f;  // 1 / the image's power-of-two scale
     int device = 0;
     ~TcImage() {
         if (!b) return;
@@ -228,6 +230,10 @@ extern "C" wc_status wc_cq_create(const uint8_t *index, size_t index_len, const 
             memcpy(&idx[((size_t)g * out + r) * gb], index + (size_t)r * row_bytes + (size_t)g * gb, gb);
             const uint8_t *p = norms + 2 * ((size_t)r * groups + g);
             nrm[(size_t)g * out + r] = (uint16_t)(p[0] | (p[1] << 8));  // little-endian FP16
+            __half_raw hr;
+            hr.x = nrm[(size_t)g * out + r];
+            const float nv = std::fabs(__half2float(__half(hr)));
+            if (nv > storage->nrm_max) storage->nrm_max = nv;  // NaN never wins
         }
     }
     storage->idx_bytes = idx.size() > 0 ? idx.size() : 16;
@@ -890,6 +896,8 @@ extern "C" wc_status wc_device_status(int *code) {
 static wc_status tc_supported(const wc_cq *h) {
     if (h->shape.group > 256)
         return set_error(WC_ERR_UNSUPPORTED, fmt("cq: tensor-core GEMM of group %d (at most 256)", h->shape.group));
+    if (tc_kchunks(h->shape) > 64)
+        return set_error(WC_ERR_UNSUPPORTED, fmt("cq: tensor-core GEMM of %d input columns (at most 4096)", h->shape.in));
     int dev = 0, limit = 0;
     WB_CUDA(cudaGetDevice(&dev));
     WB_CUDA(cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
@@ -907,8 +915,18 @@ extern "C" wc_status wc_cq_prepare_tc(const wc_cq *h) {
     const int kchunks = tc_kchunks(h->shape);
     const size_t bytes = tc_b_bytes(h->out, kchunks);
     unsigned char *b = nullptr;
+    // The image's power-of-two scale: its largest |ŵ| = max|cb|·max|n|/√G
+    // times wsc lies in [2^13, 2^14), well inside fp16's range.
+    const double wmax = (double)h->shape.cb_max * (double)h->st->nrm_max * (double)h->shape.inv_sqrt;
+    int ew = 0;
+    if (wmax > 0.0 && std::isfinite(wmax)) {
+        int k = 0;
+        std::frexp(wmax, &k);  // wmax < 2^k
+        ew = std::min(120, std::max(-120, 14 - k));
+    }
+    const float wsc = std::ldexp(1.0f, ew);
     WB_CUDA(cudaMalloc(&b, bytes));
-    cudaError_t e = launch_dequant_bf16(h->shape, h->view(), b, nullptr);
+    cudaError_t e = launch_dequant_f16(h->shape, h->view(), wsc, b, nullptr);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         cudaFree(b);
@@ -916,6 +934,7 @@ extern "C" wc_status wc_cq_prepare_tc(const wc_cq *h) {
     }
     h->tc->b = b;
     h->tc->bytes = bytes;
+    h->tc->ws = std::ldexp(1.0f, -ew);
     WB_CUDA(cudaGetDevice(&h->tc->device));
     return WC_OK;
 }
@@ -946,10 +965,11 @@ static wc_status run_tc(const wc_cq *const *ms, int n, const float *x, float *co
         const int kchunks = tc_kchunks(sh);
         void *a = nullptr;
         WB_CUDA(t_scratch.get(3, tc_a_bytes(rows, kchunks), &a));
-        cudaError_t e = launch_rotate_bf16(sh, x, rows, (unsigned char *)a, s);
+        cudaError_t e = launch_rotate_f16(sh, x, rows, (unsigned char *)a, s);
         if (e != cudaSuccess) return cuda_error(e, "cq rotate kernel");
         TcParams p{};
         p.a = (const unsigned char *)a;
+        p.rs = reinterpret_cast<const float *>((const unsigned char *)a + tc_a_image_bytes(rows, kchunks));
         p.m = rows;
         p.kchunks = kchunks;
         p.err = err;
@@ -967,6 +987,7 @@ static wc_status run_tc(const wc_cq *const *ms, int n, const float *x, float *co
             {
                 std::lock_guard<std::mutex> lock(m->tc->mu);
                 t.b = m->tc->b;
+                t.ws = m->tc->ws;
             }
             t.y = ys[j];
             t.n = m->out;
@@ -1031,21 +1052,26 @@ extern "C" wc_status wc_cq_gemm_tc_noalloc(const wc_cq *h, const float *x, float
     if ((st = tc_supported(h)) != WC_OK) return st;
     const int kchunks = tc_kchunks(h->shape);
     const size_t need = tc_a_bytes(rows, kchunks), have = noalloc_scratch_bytes();
-    if (need > have)
+    if (need > have) {
+        int most = 0;  // the most rows (a multiple of 128) whose image and scales fit
+        while (tc_a_bytes(most + 128, kchunks) <= have) most += 128;
         return set_error(WC_ERR_INVALID,
                          fmt("cq: %d rows of %d columns need %zu bytes of scratch; the no-allocation GEMM has %zu "
-                             "(at most %zu rows at this width)",
-                             rows, kchunks * 64, need, have, (have / (size_t)(kchunks * 64 * 2)) / 128 * 128));
+                             "(at most %d rows at this width)",
+                             rows, kchunks * 64, need, have, most));
+    }
     const unsigned char *wimg = nullptr;
+    float ws = 1.0f;
     {
         std::lock_guard<std::mutex> lock(h->tc->mu);
         wimg = h->tc->b;
+        ws = h->tc->ws;
     }
     if (!wimg)
         return set_error(WC_ERR_INVALID,
                          "cq: matrix has no tensor-core weight image: call wc_cq_prepare_tc at load time first");
     cudaError_t e =
-        gemm_tc_noalloc(h->shape, wimg, x, y, rows, h->out, err, rows >= kTcPersistRows, (cudaStream_t)stream);
+        gemm_tc_noalloc(h->shape, wimg, ws, x, y, rows, h->out, err, rows >= kTcPersistRows, (cudaStream_t)stream);
     return e == cudaSuccess ? WC_OK : cuda_error(e, "cq tensor-core kernel (no allocation)");
 }
 

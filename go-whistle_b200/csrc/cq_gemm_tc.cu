@@ -4,14 +4,18 @@
 // The product is taken in the rotated domain, where a CQ matrix needs no
 // Hadamard transform (internal/cq/matrix.go:1-13):
 //   y[m, r] = Σ_k x̂[m, k] · ŵ[r, k],   x̂_g = H·x_g,   ŵ[r, k] = cb[idx[r,k]]·n[r,g]/√G
-// Both operands go to bf16 (x̂ per activation by `rotate_bf16_kernel`, ŵ once
-// per matrix by `dequant_bf16_kernel`) and the tensor cores accumulate in
-// fp32. This is not the reference's lut arithmetic, so it is not bit-exact:
-// every element is within the bf16 bound stated in tests/test_gemm_tc_gpu.py
-// of the float64 product. It is only used when asked for
-// (wc_cq_gemm_ex with WC_GEMM_TENSOR_CORES).
+// Both operands go to fp16 (x̂ per activation by `rotate_f16_kernel`, ŵ once
+// per matrix by `dequant_f16_kernel`), each scaled by an exact power of two
+// — per activation row for x̂, per matrix for ŵ — so that its largest value
+// sits just under 2^15 (no overflow, fp16's full 11-bit precision at any
+// input range); the tensor cores accumulate in fp32 and the epilogue
+// multiplies the scales back out, exactly. This is not the reference's lut
+// arithmetic, so it is not bit-exact: every element is within the fp16
+// bound stated in include/whistle_b200.h (WC_GEMM_TENSOR_CORES) of the
+// float64 product. It is only used when asked for (wc_cq_gemm_ex with
+// WC_GEMM_TENSOR_CORES, or WC_GEMM_AUTO from 32 rows).
 //
-// Operand images in global memory are pre-swizzled 128 x 64 bf16 tiles
+// Operand images in global memory are pre-swizzled 128 x 64 fp16 tiles
 // (K-major, 128-byte swizzle: 16-byte chunk c of row r at chunk c ^ (r & 7)),
 // so a stage of the main loop is two 1-D bulk copies (cp.async.bulk, no
 // tensor map, no multicast). One CTA computes a 128 x 128 tile of y:
@@ -20,7 +24,7 @@
 //   warps 2-5       epilogue: TMEM -> registers -> y (fp32)
 // Every wait on an mbarrier is bounded; on timeout the CTA records an error
 // code, skips its remaining work, frees its TMEM and returns.
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <mutex>
 
@@ -33,8 +37,8 @@ namespace {
 
 constexpr int kTcM = 128;         // UMMA M (cta_group::1)
 constexpr int kTcN = 128;         // UMMA N, TMEM columns
-constexpr int kTcK = 64;          // bf16 elements per 128-byte row of a chunk
-constexpr int kChunkBytes = kTcM * 128;  // one 128 x 64 bf16 tile, A and B alike
+constexpr int kTcK = 64;          // fp16 elements per 128-byte row of a chunk
+constexpr int kChunkBytes = kTcM * 128;  // one 128 x 64 fp16 tile, A and B alike
 constexpr int kTcThreads = 192;
 constexpr uint32_t kSpinLimit = 1u << 22;
 
@@ -80,11 +84,12 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// Instruction descriptor: D f32, A and B bf16, both K-major, N = kTcN, M = kTcM.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcN >> 3) << 17) |
+// Instruction descriptor: D f32, A and B f16 (formats 0), both K-major,
+// N = kTcN, M = kTcM.
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kTcN >> 3) << 17) |
                             ((uint32_t)(kTcM >> 4) << 24);
 
-__device__ __forceinline__ void umma_bf16(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void umma_f16(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
@@ -110,7 +115,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Byte offset of element (row, k) of a 128 x 64 bf16 swizzled chunk.
+// Byte offset of element (row, k) of a 128 x 64 fp16 swizzled chunk.
 __device__ __forceinline__ uint32_t swz(int row, int k) {
     return (uint32_t)row * 128u + ((uint32_t)(((k >> 3) ^ (row & 7)) & 7) << 4) + (uint32_t)(k & 7) * 2u;
 }
@@ -200,7 +205,7 @@ __global__ void __launch_bounds__(kTcThreads, kStages <= 2 ? 3 : kStages <= 3 ? 
             const uint32_t a0 = smem_u32(sa + s * kChunkBytes), b0 = smem_u32(sb + s * kChunkBytes);
 #pragma unroll
             for (int k = 0; k < kTcK / 16; k++)
-                umma_bf16(tmem, umma_desc(a0 + 32 * k), umma_desc(b0 + 32 * k), (kc > 0 || k > 0) ? 1u : 0u);
+                umma_f16(tmem, umma_desc(a0 + 32 * k), umma_desc(b0 + 32 * k), (kc > 0 || k > 0) ? 1u : 0u);
             umma_commit(&empty[s]);
         }
         umma_commit(done);
@@ -240,7 +245,10 @@ __global__ void __launch_bounds__(kTcThreads, kStages <= 2 ? 3 : kStages <= 3 ? 
                 for (int rr = (warp - 2) * 2 + sub; rr < kTcM; rr += 8) {
                     const int row = mt * kTcM + rr, col = col0 + c4;
                     if (row < p.m && col < mat.n) {
-                        const float4 v = *reinterpret_cast<const float4 *>(stage + rr * kPad + c4);
+                        float4 v = *reinterpret_cast<const float4 *>(stage + rr * kPad + c4);
+                        // Undo the row's and the matrix's power-of-two scales (exact).
+                        const float f = __fmul_rn(p.rs[row], mat.ws);
+                        v = make_float4(__fmul_rn(v.x, f), __fmul_rn(v.y, f), __fmul_rn(v.z, f), __fmul_rn(v.w, f));
                         float *y = mat.y + (size_t)row * mat.ldy + col;
                         if (col + 4 <= mat.n && (mat.ldy & 3) == 0 && (((uintptr_t)y) & 15) == 0) {
                             *reinterpret_cast<float4 *>(y) = v;
@@ -281,10 +289,10 @@ constexpr int kPStages = 3;
 constexpr int kPStageBytes = 3 * kChunkBytes;  // x̂ 16 KB + ŵ 32 KB
 constexpr int kPThreads = 320;  // producer, MMA, eight epilogue warps
 constexpr int kPStgStride = 36;  // floats per staged row (32 + 4)
-constexpr uint32_t kPIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kPN >> 3) << 17) |
+constexpr uint32_t kPIdesc = (1u << 4) | ((uint32_t)(kPN >> 3) << 17) |
                              ((uint32_t)(kTcM >> 4) << 24);
 
-__device__ __forceinline__ void umma_bf16_n256(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void umma_f16_n256(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
@@ -394,7 +402,7 @@ __global__ void __launch_bounds__(kPThreads, 1) cq_gemm_tc_persistent_kernel(con
                 const uint32_t b0 = a0 + kChunkBytes;
 #pragma unroll
                 for (int k = 0; k < kTcK / 16; k++)
-                    umma_bf16_n256(d, umma_desc(a0 + 32 * k), umma_desc(b0 + 32 * k), (kc > 0 || k > 0) ? 1u : 0u);
+                    umma_f16_n256(d, umma_desc(a0 + 32 * k), umma_desc(b0 + 32 * k), (kc > 0 || k > 0) ? 1u : 0u);
                 umma_commit(&empty[s]);
             }
             if (!ok) break;
@@ -436,7 +444,9 @@ __global__ void __launch_bounds__(kPThreads, 1) cq_gemm_tc_persistent_kernel(con
                 for (int rr = sub; rr < 32; rr += 4) {
                     const int row = mt * kTcM + part * 32 + rr, col = col_base + cc + c4;
                     if (row < p.m && col < mat.n) {
-                        const float4 v = *reinterpret_cast<const float4 *>(mystg + rr * kPStgStride + c4);
+                        float4 v = *reinterpret_cast<const float4 *>(mystg + rr * kPStgStride + c4);
+                        const float f = __fmul_rn(p.rs[row], mat.ws);
+                        v = make_float4(__fmul_rn(v.x, f), __fmul_rn(v.y, f), __fmul_rn(v.z, f), __fmul_rn(v.w, f));
                         float *y = mat.y + (size_t)row * mat.ldy + col;
                         if (col + 4 <= mat.n && (mat.ldy & 3) == 0 && (((uintptr_t)y) & 15) == 0) {
                             *reinterpret_cast<float4 *>(y) = v;
@@ -462,249 +472,126 @@ __global__ void __launch_bounds__(kPThreads, 1) cq_gemm_tc_persistent_kernel(con
     }
 }
 
-// x̂ = H·x per group of G (no 1/√G: it is in ŵ), bf16, into the swizzled
-// image [m_tile][kc][128 rows][128 B]; rows past m and columns past In are
-// zero. Each lane owns a 32-column segment of one row (four 16-byte chunks
-// of the image): the butterflies with h < 32 run in registers, those with
-// h >= 32 (G > 32) between the lanes of a group by shuffles; for G < 32 a
-// segment holds 32/G whole groups. Same butterflies as fwht.
-__global__ void __launch_bounds__(256) rotate_bf16_kernel(const float *__restrict__ x, int m, int in, int G,
-                                                          int kpad, int kchunks, int mtiles,
-                                                          unsigned char *__restrict__ a) {
+// x̂ = H·x per group of G (no 1/√G: it is in ŵ), scaled by a power of two
+// per row, fp16, into the swizzled image [m_tile][kc][128 rows][128 B];
+// rows past m and columns past In are zero. One warp per image row: lane l
+// holds the columns 128·j + 4·l .. +3 (j < J), loaded as float4s (512
+// contiguous bytes per warp load). The row's largest |x| fixes its scale
+// 2^e, the largest with G·max|x|·2^e < 2^14, so no |x̂·2^e| reaches fp16's
+// 65504 and the row keeps fp16's 11-bit precision however large or small
+// its values are; rs[row] = 2^-e undoes it exactly in the GEMM's epilogue.
+// The butterflies are fwht's (kernel.go:384), stage by stage: h < 4 inside
+// a lane's float4, 4 <= h < 128 between lanes (xor h/4), h >= 128 between
+// a lane's float4s. Each lane stores its four fp16 values as 8 bytes of a
+// 128-byte chunk row.
+template <int J>
+__global__ void __launch_bounds__(256) rotate_f16_kernel(const float *__restrict__ x, int m, int in, int G,
+                                                         int log2g, int kpad, int kchunks, long rows_total,
+                                                         int vec, unsigned char *__restrict__ a,
+                                                         float *__restrict__ rs) {
     // A GEMM launched as this kernel's programmatic dependent may start its
     // set-up now; it waits for this grid's completion before reading a.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const int segs = kpad / 32;                       // segments per row (kpad: multiple of 32)
-    const long seg = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    const long total = (long)mtiles * kTcM * segs;
-    // Whole warps stay in the loop so the shuffles see every lane.
-    const bool live = seg < total;
-    const int row = live ? (int)(seg / segs) : 0, sg = live ? (int)(seg % segs) : 0;
-    const int k0 = sg * 32;
-    float v[32];
-    if (live && row < m && k0 + 32 <= in && (in & 3) == 0 && (((uintptr_t)x) & 15) == 0) {
-        const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)row * in + k0);
+    const int lane = threadIdx.x & 31;
+    const long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows_total) return;  // whole warps
+    float v[J][4];
+    const bool real = row < m;
 #pragma unroll
-        for (int q = 0; q < 8; q++) {
-            const float4 f = __ldg(src + q);
-            v[4 * q] = f.x;
-            v[4 * q + 1] = f.y;
-            v[4 * q + 2] = f.z;
-            v[4 * q + 3] = f.w;
-        }
-    } else {
-#pragma unroll
-        for (int e = 0; e < 32; e++) v[e] = (live && row < m && k0 + e < in) ? x[(size_t)row * in + k0 + e] : 0.0f;
-    }
-    const int gin = G < 32 ? G : 32;  // butterflies inside the segment
-#pragma unroll
-    for (int h = 1; h < 32; h <<= 1) {
-        if (h < gin) {
-#pragma unroll
-            for (int e = 0; e < 32; e++) {
-                if ((e & h) == 0) {
-                    const float a0 = v[e], b0 = v[e + h];
-                    v[e] = a0 + b0;
-                    v[e + h] = a0 - b0;
-                }
-            }
-        }
-    }
-    for (int h = 32; h < G; h <<= 1) {  // across the lanes of a group
-        const int pl = h / 32;
-#pragma unroll
-        for (int e = 0; e < 32; e++) {
-            const float o = __shfl_xor_sync(0xffffffffu, v[e], pl);
-            v[e] = (sg & pl) ? o - v[e] : v[e] + o;
-        }
-    }
-    if (!live) return;
-    const int mtile = row / kTcM, r = row % kTcM, kc = k0 / kTcK;
-    unsigned char *base = a + ((size_t)mtile * kchunks + kc) * kChunkBytes;
-#pragma unroll
-    for (int c = 0; c < 4; c++) {
-        uint4 w;
-        __nv_bfloat162 t0 = __floats2bfloat162_rn(v[8 * c], v[8 * c + 1]);
-        __nv_bfloat162 t1 = __floats2bfloat162_rn(v[8 * c + 2], v[8 * c + 3]);
-        __nv_bfloat162 t2 = __floats2bfloat162_rn(v[8 * c + 4], v[8 * c + 5]);
-        __nv_bfloat162 t3 = __floats2bfloat162_rn(v[8 * c + 6], v[8 * c + 7]);
-        w.x = *reinterpret_cast<uint32_t *>(&t0);
-        w.y = *reinterpret_cast<uint32_t *>(&t1);
-        w.z = *reinterpret_cast<uint32_t *>(&t2);
-        w.w = *reinterpret_cast<uint32_t *>(&t3);
-        *reinterpret_cast<uint4 *>(base + swz(r, (k0 % kTcK) + 8 * c)) = w;
-    }
-}
-
-// The segment-per-lane rotation of rotate_bf16_kernel with both of its
-// memory sides staged through shared memory, for activations whose rows
-// are whole chunks (In = kpad, so a warp's 32 segments are 1024
-// consecutive floats of x): each warp loads its floats as consecutive
-// 16-byte pieces (512 bytes an instruction) and stores its 16 image rows
-// of 128 bytes as whole rows (four per instruction), instead of one
-// 128-byte stride per lane on both sides. The butterflies are
-// rotate_bf16_kernel's.
-constexpr int kRotSeg = 36;  // floats per staged segment (32 + 4: conflict-free 16-byte reads)
-__global__ void __launch_bounds__(256) rotate_bf16_v3_kernel(const float *__restrict__ x, int m, int G, int kpad,
-                                                             int kchunks, int mtiles,
-                                                             unsigned char *__restrict__ a) {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    __shared__ __align__(16) float sx[8][32 * kRotSeg];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int segs = kpad / 32;
-    const long seg0 = ((long)blockIdx.x * 8 + warp) * 32;  // the warp's first segment
-    const long total = (long)mtiles * kTcM * segs;
-    if (seg0 >= total) return;  // whole warps: total is a multiple of 32 segments (kpad % 64 == 0, 128 rows)
-    float *buf = sx[warp];
-    const long xend = (long)m * kpad;  // floats of x (In = kpad)
-#pragma unroll
-    for (int e = 0; e < 8; e++) {
-        const int f4 = e * 32 + lane;  // 16-byte piece of the warp's 1024 floats
-        const long L = seg0 * 32 + 4L * f4;
-        float4 val = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (L < xend) val = __ldg(reinterpret_cast<const float4 *>(x + L));
-        *reinterpret_cast<float4 *>(buf + (f4 >> 3) * kRotSeg + (f4 & 7) * 4) = val;
-    }
-    __syncwarp();
-    float v[32];
-#pragma unroll
-    for (int q = 0; q < 8; q++) {
-        const float4 f = *reinterpret_cast<const float4 *>(buf + lane * kRotSeg + 4 * q);
-        v[4 * q] = f.x;
-        v[4 * q + 1] = f.y;
-        v[4 * q + 2] = f.z;
-        v[4 * q + 3] = f.w;
-    }
-    const long seg = seg0 + lane;
-    const int sg = (int)(seg % segs);
-    const int gin = G < 32 ? G : 32;  // butterflies inside the segment
-#pragma unroll
-    for (int h = 1; h < 32; h <<= 1) {
-        if (h < gin) {
-#pragma unroll
-            for (int e = 0; e < 32; e++) {
-                if ((e & h) == 0) {
-                    const float a0 = v[e], b0 = v[e + h];
-                    v[e] = a0 + b0;
-                    v[e + h] = a0 - b0;
-                }
-            }
-        }
-    }
-    for (int h = 32; h < G; h <<= 1) {  // across the lanes of a group
-        const int pl = h / 32;
-#pragma unroll
-        for (int e = 0; e < 32; e++) {
-            const float o = __shfl_xor_sync(0xffffffffu, v[e], pl);
-            v[e] = (sg & pl) ? o - v[e] : v[e] + o;
-        }
-    }
-    // Lanes 2j and 2j+1 fill image row j of the warp (144-byte stride): the
-    // two 64-byte halves of one 128-byte chunk row, in swizzled order.
-    __syncwarp();
-    unsigned char *ob = reinterpret_cast<unsigned char *>(buf);
-    const long row = seg / segs;
-    const int r = (int)(row % kTcM), half = lane & 1;
-#pragma unroll
-    for (int c = 0; c < 4; c++) {
-        uint4 w;
-        __nv_bfloat162 t0 = __floats2bfloat162_rn(v[8 * c], v[8 * c + 1]);
-        __nv_bfloat162 t1 = __floats2bfloat162_rn(v[8 * c + 2], v[8 * c + 3]);
-        __nv_bfloat162 t2 = __floats2bfloat162_rn(v[8 * c + 4], v[8 * c + 5]);
-        __nv_bfloat162 t3 = __floats2bfloat162_rn(v[8 * c + 6], v[8 * c + 7]);
-        w.x = *reinterpret_cast<uint32_t *>(&t0);
-        w.y = *reinterpret_cast<uint32_t *>(&t1);
-        w.z = *reinterpret_cast<uint32_t *>(&t2);
-        w.w = *reinterpret_cast<uint32_t *>(&t3);
-        *reinterpret_cast<uint4 *>(ob + (lane >> 1) * 144 + (((half * 4 + c) ^ (r & 7)) << 4)) = w;
-    }
-    __syncwarp();
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-        const int u = e * 32 + lane, j = u >> 3, wc = u & 7;  // image row j of the warp, 16-byte chunk wc
-        const long sj = seg0 + 2 * j;
-        const long rowj = sj / segs;
-        const int kc = (int)(sj % segs) / 2;
-        unsigned char *dst = a + (((size_t)(rowj / kTcM) * kchunks + kc) * kChunkBytes) +
-                             (size_t)(rowj % kTcM) * 128 + wc * 16;
-        *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(ob + j * 144 + wc * 16);
-    }
-}
-
-
-// The same image with four columns per lane: a warp's loads are 512
-// contiguous bytes of one row, the butterflies with h < 4 run in registers
-// and those with h >= 4 between lanes (xor h/4), and each lane stores its
-// four bf16 values as 8 bytes of the swizzled chunk. Rows are padded to a
-// whole number of warps (lanes past kpad hold zeros and store nothing), so
-// a group (G <= 128: at most 32 lanes) never straddles two warps.
-__global__ void __launch_bounds__(256) rotate_bf16_v2_kernel(const float *__restrict__ x, int m, int in, int G,
-                                                             int kpad, int kchunks, int mtiles,
-                                                             unsigned char *__restrict__ a) {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const int lanes_row = ((kpad / 4) + 31) & ~31;
-    const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    const long total = (long)mtiles * kTcM * lanes_row;
-    const bool live = t < total;
-    const int row = live ? (int)(t / lanes_row) : 0;
-    const int c0 = live ? (int)(t % lanes_row) * 4 : kpad;
-    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    if (live && row < m && c0 < in) {
-        const float *src = x + (size_t)row * in + c0;
-        if (c0 + 4 <= in && (((uintptr_t)src) & 15) == 0) {
-            const float4 f = __ldg(reinterpret_cast<const float4 *>(src));
-            v[0] = f.x;
-            v[1] = f.y;
-            v[2] = f.z;
-            v[3] = f.w;
+    for (int j = 0; j < J; j++) {
+        const int c0 = 128 * j + 4 * lane;
+        if (real && vec && c0 + 4 <= in) {
+            const float4 f = __ldg(reinterpret_cast<const float4 *>(x + (size_t)row * in + c0));
+            v[j][0] = f.x;
+            v[j][1] = f.y;
+            v[j][2] = f.z;
+            v[j][3] = f.w;
         } else {
 #pragma unroll
-            for (int e = 0; e < 4; e++) v[e] = c0 + e < in ? src[e] : 0.0f;
+            for (int e = 0; e < 4; e++) v[j][e] = (real && c0 + e < in) ? x[(size_t)row * in + c0 + e] : 0.0f;
         }
     }
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < J; j++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) amax = fmaxf(amax, fabsf(v[j][e]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    int sh = 0;  // the row's scale exponent e
+    if (amax > 0.0f && amax <= 3.402823466e38f) {
+        int k;
+        frexpf(amax, &k);  // amax < 2^k
+        sh = 14 - k - log2g;
+        sh = sh < -120 ? -120 : sh > 120 ? 120 : sh;
+    }
+    // Butterflies inside a float4 (h = 1, 2).
 #pragma unroll
     for (int h = 1; h < 4; h <<= 1) {
         if (h < G) {
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                if ((e & h) == 0) {
-                    const float a0 = v[e], b0 = v[e + h];
-                    v[e] = a0 + b0;
-                    v[e + h] = a0 - b0;
-                }
-            }
-        }
-    }
-    for (int h = 4; h < G; h <<= 1) {
-        const int pl = h / 4;
+            for (int j = 0; j < J; j++)
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const float o = __shfl_xor_sync(0xffffffffu, v[e], pl);
-            v[e] = (c0 & h) ? o - v[e] : v[e] + o;
+                for (int e = 0; e < 4; e++)
+                    if ((e & h) == 0) {
+                        const float a0 = v[j][e], b0 = v[j][e + h];
+                        v[j][e] = a0 + b0;
+                        v[j][e + h] = a0 - b0;
+                    }
         }
     }
-    if (!live || c0 >= kpad) return;
-    const int mtile = row / kTcM, r = row % kTcM, kc = c0 / kTcK;
-    unsigned char *base = a + ((size_t)mtile * kchunks + kc) * kChunkBytes;
-    __nv_bfloat162 p0 = __floats2bfloat162_rn(v[0], v[1]);
-    __nv_bfloat162 p1 = __floats2bfloat162_rn(v[2], v[3]);
-    uint2 w;
-    w.x = *reinterpret_cast<uint32_t *>(&p0);
-    w.y = *reinterpret_cast<uint32_t *>(&p1);
-    *reinterpret_cast<uint2 *>(base + swz(r, c0 % kTcK)) = w;
+    // Between lanes (h = 4 .. 64).
+    for (int h = 4; h < G && h < 128; h <<= 1) {
+        const int pl = h >> 2;
+#pragma unroll
+        for (int j = 0; j < J; j++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float o = __shfl_xor_sync(0xffffffffu, v[j][e], pl);
+                v[j][e] = (lane & pl) ? o - v[j][e] : v[j][e] + o;
+            }
+    }
+    // Between float4s: h = 128 (G = 256, the largest group taken).
+    if (G > 128) {
+#pragma unroll
+        for (int j = 0; j + 1 < J; j += 2)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float a0 = v[j][e], b0 = v[j + 1][e];
+                v[j][e] = a0 + b0;
+                v[j + 1][e] = a0 - b0;
+            }
+    }
+    const float p2 = __int_as_float((127 + sh) << 23);
+    const int mtile = (int)(row / kTcM), r = (int)(row % kTcM);
+#pragma unroll
+    for (int j = 0; j < J; j++) {
+        const int c0 = 128 * j + 4 * lane;
+        if (c0 >= kpad) continue;
+        const __half2 h0 = __floats2half2_rn(__fmul_rn(v[j][0], p2), __fmul_rn(v[j][1], p2));
+        const __half2 h1 = __floats2half2_rn(__fmul_rn(v[j][2], p2), __fmul_rn(v[j][3], p2));
+        uint2 w;
+        w.x = *reinterpret_cast<const uint32_t *>(&h0);
+        w.y = *reinterpret_cast<const uint32_t *>(&h1);
+        unsigned char *base = a + ((size_t)mtile * kchunks + c0 / kTcK) * kChunkBytes;
+        *reinterpret_cast<uint2 *>(base + swz(r, c0 % kTcK)) = w;
+    }
+    if (lane == 0) rs[row] = __int_as_float((127 - sh) << 23);
 }
 
-// ŵ[r, k] = cb[idx]·n[r, g]·(1/√G) in bf16, swizzled [n_tile][kc][128][128 B];
-// rows past Out are zero. One thread per (row, 8 columns).
-__global__ void dequant_bf16_kernel(const __grid_constant__ CqShape s, const CqView v, int ntiles, int kchunks,
-                                    unsigned char *__restrict__ b) {
+// ŵ[r, k] = cb[idx]·n[r, g]·(1/√G)·wsc in fp16, swizzled
+// [n_tile][kc][128][128 B]; rows past Out are zero. wsc is the matrix's
+// power-of-two scale (its largest |ŵ| just under 2^15), undone in the
+// epilogue. One thread per (row, 8 columns).
+__global__ void dequant_f16_kernel(const __grid_constant__ CqShape s, const CqView v, float wsc, int ntiles,
+                                   int kchunks, unsigned char *__restrict__ b) {
     const int units = ntiles * kTcN * (kchunks * kTcK / 8);
     const int u = blockIdx.x * blockDim.x + threadIdx.x;
     if (u >= units) return;
     const int per_row = kchunks * kTcK / 8;
     const int row = u / per_row, k0 = (u % per_row) * 8;
     const int ntile = row / kTcN, r = row % kTcN, kc = k0 / kTcK;
-    __align__(16) __nv_bfloat16 out[8];
+    __align__(16) __half out[8];
 #pragma unroll
     for (int e = 0; e < 8; e++) {
         const int k = k0 + e;
@@ -714,9 +601,9 @@ __global__ void dequant_bf16_kernel(const __grid_constant__ CqShape s, const CqV
             const size_t lrow = (size_t)g * v.ld + (size_t)(v.row0 + row);
             const int bit = kin * s.bits;
             const uint32_t code = (v.idx[lrow * s.gb + (bit >> 3)] >> (bit & 7)) & ((1u << s.bits) - 1u);
-            w = s.cb[code] * __half2float(v.nrm[lrow]) * s.inv_sqrt;
+            w = __fmul_rn(__fmul_rn(__fmul_rn(s.cb[code], __half2float(v.nrm[lrow])), s.inv_sqrt), wsc);
         }
-        out[e] = __float2bfloat16_rn(w);
+        out[e] = __float2half_rn(w);
     }
     unsigned char *base = b + ((size_t)ntile * kchunks + kc) * kChunkBytes;
     *reinterpret_cast<uint4 *>(base + swz(r, k0 % kTcK)) = *reinterpret_cast<const uint4 *>(out);
@@ -724,46 +611,54 @@ __global__ void dequant_bf16_kernel(const __grid_constant__ CqShape s, const CqV
 
 }  // namespace
 
-size_t tc_a_bytes(int m, int kchunks) { return (size_t)((m + kTcM - 1) / kTcM) * kchunks * kChunkBytes; }
+// The x̂ image, then the rows' scales (one float per image row).
+size_t tc_a_image_bytes(int m, int kchunks) { return (size_t)((m + kTcM - 1) / kTcM) * kchunks * kChunkBytes; }
+size_t tc_a_bytes(int m, int kchunks) {
+    return tc_a_image_bytes(m, kchunks) + (size_t)((m + kTcM - 1) / kTcM) * kTcM * sizeof(float);
+}
 // Weight images hold an even number of 128-row tiles (rows past Out are
 // zero), so the persistent kernel's 256-row tiles never read past them.
 static int tc_b_tiles(int n) { return ((n + 2 * kTcN - 1) / (2 * kTcN)) * 2; }
 size_t tc_b_bytes(int n, int kchunks) { return (size_t)tc_b_tiles(n) * kchunks * kChunkBytes; }
 int tc_kchunks(const CqShape &s) { return (s.pad + kTcK - 1) / kTcK; }
 
-cudaError_t launch_dequant_bf16(const CqShape &s, const CqView &v, unsigned char *b, cudaStream_t st) {
+cudaError_t launch_dequant_f16(const CqShape &s, const CqView &v, float wsc, unsigned char *b, cudaStream_t st) {
     const int kchunks = tc_kchunks(s), ntiles = tc_b_tiles(v.out);
     const long units = (long)ntiles * kTcN * (kchunks * kTcK / 8);
     if (units == 0) return cudaSuccess;
-    dequant_bf16_kernel<<<(int)((units + 255) / 256), 256, 0, st>>>(s, v, ntiles, kchunks, b);
+    dequant_f16_kernel<<<(int)((units + 255) / 256), 256, 0, st>>>(s, v, wsc, ntiles, kchunks, b);
     count_launch();
     return cudaGetLastError();
 }
 
-cudaError_t launch_rotate_bf16(const CqShape &s, const float *x, int m, unsigned char *a, cudaStream_t st) {
-    const int kchunks = tc_kchunks(s), mtiles = (m + kTcM - 1) / kTcM;
-    // Segments cover kchunks·64 columns: the padding past groups·G is zero
-    // (x is zero there, and H of zeros is zero within a group of G <= 32;
-    // for larger G the padding is whole groups of zeros).
-    const int kpad = kchunks * kTcK;
-    if (s.group <= 128 && m < 1024) {  // few rows: four columns per lane, more lanes in flight
-        const long threads = (long)mtiles * kTcM * (((kpad / 4) + 31) & ~31);
-        if (threads == 0) return cudaSuccess;
-        rotate_bf16_v2_kernel<<<(int)((threads + 255) / 256), 256, 0, st>>>(x, m, s.in, s.group, kpad, kchunks,
-                                                                             mtiles, a);
-        count_launch();
-        return cudaGetLastError();
-    }
-    const long threads = (long)mtiles * kTcM * (kpad / 32);
-    if (threads == 0) return cudaSuccess;
-    if (s.in == kpad && (((uintptr_t)x) & 15) == 0) {  // rows of whole chunks: staged, coalesced
-        rotate_bf16_v3_kernel<<<(int)((threads + 255) / 256), 256, 0, st>>>(x, m, s.group, kpad, kchunks, mtiles, a);
-        count_launch();
-        return cudaGetLastError();
-    }
-    rotate_bf16_kernel<<<(int)((threads + 255) / 256), 256, 0, st>>>(x, m, s.in, s.group, kpad, kchunks, mtiles, a);
+template <int J>
+static cudaError_t launch_rotate_j(const CqShape &s, const float *x, int m, int kpad, int kchunks, long rows,
+                                   unsigned char *a, float *rs, cudaStream_t st) {
+    int log2g = 0;
+    while ((1 << log2g) < s.group) log2g++;
+    const int vec = (s.in % 4 == 0) && (((uintptr_t)x) & 15) == 0;
+    rotate_f16_kernel<J><<<(int)((rows + 7) / 8), 256, 0, st>>>(x, m, s.in, s.group, log2g, kpad, kchunks, rows, vec,
+                                                               a, rs);
     count_launch();
     return cudaGetLastError();
+}
+
+cudaError_t launch_rotate_f16(const CqShape &s, const float *x, int m, unsigned char *a, cudaStream_t st) {
+    const int kchunks = tc_kchunks(s), mtiles = (m + kTcM - 1) / kTcM;
+    // The image covers kchunks·64 columns: the padding past groups·G is
+    // zero (x is zero there, and H of zeros is zero within a group of
+    // G <= 64; for larger G the padding is whole groups of zeros).
+    const int kpad = kchunks * kTcK;
+    const long rows = (long)mtiles * kTcM;
+    if (rows == 0) return cudaSuccess;
+    float *rs = reinterpret_cast<float *>(a + tc_a_image_bytes(m, kchunks));
+    const int j = (kpad + 127) / 128;
+    if (j <= 1) return launch_rotate_j<1>(s, x, m, kpad, kchunks, rows, a, rs, st);
+    if (j <= 2) return launch_rotate_j<2>(s, x, m, kpad, kchunks, rows, a, rs, st);
+    if (j <= 4) return launch_rotate_j<4>(s, x, m, kpad, kchunks, rows, a, rs, st);
+    if (j <= 8) return launch_rotate_j<8>(s, x, m, kpad, kchunks, rows, a, rs, st);
+    if (j <= 16) return launch_rotate_j<16>(s, x, m, kpad, kchunks, rows, a, rs, st);
+    return launch_rotate_j<32>(s, x, m, kpad, kchunks, rows, a, rs, st);
 }
 
 static size_t tc_smem_bytes_st(int stages) { return 1024 + 2 * (size_t)stages * kChunkBytes + 8 * (2 * stages + 1) + 16; }
@@ -772,12 +667,15 @@ size_t tc_smem_bytes() { return tc_smem_bytes_st(2); }
 // ---- the no-allocation entry point's scratch --------------------------------
 //
 // One file-scope device array holds the rotated-activation image of
-// wc_cq_gemm_tc_noalloc (kNoAllocScratchBytes) followed by its error word.
+// wc_cq_gemm_tc_noalloc and its rows' scales (kNoAllocScratchBytes),
+// followed by its error word.
 // Every GPU that loads the library carries it until the process exits.
 // Host code cannot use the array's name as a device address (it names a
 // host-side shadow), so each device's address is looked up once with
 // cudaGetSymbolAddress, with that device current, and handed to the kernels.
-constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;
+// 16 MiB for the x̂ image and 512 KiB for its rows' scales (the most rows
+// a 16 MiB image holds, at 64 columns, is 131,072).
+constexpr size_t kNoAllocScratchBytes = ((size_t)16 << 20) + ((size_t)512 << 10);
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes + 256];
 
 size_t noalloc_scratch_bytes() { return kNoAllocScratchBytes; }
@@ -826,13 +724,13 @@ int *noalloc_err_word() {
 // or null for the array's own word, which accumulates the codes until
 // wc_device_status reads and clears it. persistent: the kernel
 // wc_cq_gemm_ex picks for this many rows.
-cudaError_t gemm_tc_noalloc(const CqShape &s, const unsigned char *wimg, const float *x, float *y, int rows, int n,
-                            int *err, bool persistent, cudaStream_t st) {
+cudaError_t gemm_tc_noalloc(const CqShape &s, const unsigned char *wimg, float ws, const float *x, float *y, int rows,
+                            int n, int *err, bool persistent, cudaStream_t st) {
     unsigned char *base = nullptr;
     cudaError_t e = noalloc_scratch(&base);
     if (e != cudaSuccess) return e;
     if (!err) err = reinterpret_cast<int *>(base + kNoAllocScratchBytes);
-    e = launch_rotate_bf16(s, x, rows, base, st);
+    e = launch_rotate_f16(s, x, rows, base, st);
     if (e != cudaSuccess) return e;
     TcParams p{};
     p.a = base;
@@ -840,7 +738,8 @@ cudaError_t gemm_tc_noalloc(const CqShape &s, const unsigned char *wimg, const f
     p.kchunks = tc_kchunks(s);
     p.err = err;
     p.nmats = 1;
-    p.mats[0] = TcMat{wimg, y, n, n, 0};
+    p.rs = reinterpret_cast<const float *>(base + tc_a_image_bytes(rows, p.kchunks));
+    p.mats[0] = TcMat{wimg, y, n, n, 0, ws};
     return persistent ? launch_gemm_tc_persistent(p, st) : launch_gemm_tc(p, st);
 }
 

@@ -74,16 +74,18 @@ using StreamParams = StreamParamsN<kMaxStreamRuns>;
 // take several, the partial sums carried between them).
 int stream_passes(const CqShape &s);
 // The tensor-core GEMM (cq_gemm_tc.cu): operand images are pre-swizzled
-// 128 x 64 bf16 tiles.
+// 128 x 64 fp16 tiles, each scaled by a power of two.
 constexpr int kMaxTcMats = 16;  // matrices one grouped tensor-core launch carries
 struct TcMat {
     const unsigned char *b;  // ŵ image [n_tiles][kchunks][128][128 B]
     float *y;                // [m][ldy] fp32
     int n, ldy;
     int tile0;               // first n-tile of this matrix in the launch's grid
+    float ws;                // 1 / the image's scale (a power of two)
 };
 struct TcParams {
     const unsigned char *a;  // x̂ image [m_tiles][kchunks][128][128 B], shared by the matrices
+    const float *rs;         // [m_tiles·128]: 1 / each x̂ row's scale (a power of two)
     int m, kchunks;
     int *err;                // device error word (bounded waits)
     int nmats;               // matrices in this launch (1 .. kMaxTcMats)
@@ -91,11 +93,16 @@ struct TcParams {
     TcMat mats[kMaxTcMats];
 };
 int tc_kchunks(const CqShape &s);
+// The x̂ image of m rows alone, and with the rows' scales behind it (the
+// buffer a rotation writes: tc_a_bytes).
+size_t tc_a_image_bytes(int m, int kchunks);
 size_t tc_a_bytes(int m, int kchunks);
 size_t tc_b_bytes(int n, int kchunks);
 size_t tc_smem_bytes();
-cudaError_t launch_dequant_bf16(const CqShape &s, const CqView &v, unsigned char *b, cudaStream_t st);
-cudaError_t launch_rotate_bf16(const CqShape &s, const float *x, int m, unsigned char *a, cudaStream_t st);
+// ŵ·wsc into the image b (wsc a power of two).
+cudaError_t launch_dequant_f16(const CqShape &s, const CqView &v, float wsc, unsigned char *b, cudaStream_t st);
+// x̂ of m rows into the buffer a (tc_a_bytes): the image, then the scales.
+cudaError_t launch_rotate_f16(const CqShape &s, const float *x, int m, unsigned char *a, cudaStream_t st);
 // Total n-tiles of a launch: mats[nmats - 1].tile0 + its tiles.
 int tc_total_tiles(const TcParams &p);
 cudaError_t launch_gemm_tc(const TcParams &p, cudaStream_t st);
@@ -105,8 +112,8 @@ size_t tc_persistent_smem_bytes();
 cudaError_t launch_gemm_tc_persistent(const TcParams &p, cudaStream_t st);
 // wc_cq_gemm_tc_noalloc's core: the same kernels on a static scratch array.
 size_t noalloc_scratch_bytes();
-cudaError_t gemm_tc_noalloc(const CqShape &s, const unsigned char *wimg, const float *x, float *y, int rows, int n,
-                            int *err, bool persistent, cudaStream_t st);
+cudaError_t gemm_tc_noalloc(const CqShape &s, const unsigned char *wimg, float ws, const float *x, float *y, int rows,
+                            int n, int *err, bool persistent, cudaStream_t st);
 // The static array's error word on the current device (null before the
 // first no-allocation call there).
 int *noalloc_err_word();

@@ -108,13 +108,19 @@ wc_status wc_cq_gemm(const wc_cq *h, const float *x, float *y, int rows, wc_stre
 
 /* Flags of wc_cq_gemm_ex and wc_cq_gemms_ex. */
 enum {
-    /* Run the product on the tensor cores (tcgen05, bf16 operands in the
-     * rotated domain, fp32 accumulation) instead of the bit-exact lut
-     * kernel: for many rows (encoder prefill, batched decode). Not
+    /* Run the product on the tensor cores (tcgen05, fp16 operands in the
+     * rotated domain, each scaled by an exact power of two — per activation
+     * row and per matrix — and fp32 accumulation) instead of the bit-exact
+     * lut kernel: for many rows (encoder prefill, batched decode). Not
      * bit-exact: each output y is within
-     * (2^-7 + (K + log2 G + 4)·2^-24) · Σ_k |x̂_k|·|ŵ_k| of the exact
-     * product (K = In rounded up to the group, x̂ and ŵ the rotated
-     * activation and weights). */
+     *   (2^-10 + (K + log2 G + 6)·2^-24) · Σ_k |x̂_k|·|ŵ_k|
+     *   + 2^-37 · (G·max|x| · Σ_k |ŵ_k| + max|ŵ| · Σ_k |x̂_k|)
+     * of the exact product (K = In rounded up to the group, x̂ and ŵ the
+     * rotated activation row and weight row, max|x| over the activation
+     * row, max|ŵ| over the matrix; the second line covers fp16's
+     * subnormals), and every row of y has cosine >= 0.99999 with the exact
+     * product on the reference's test distributions, its lut kernel's
+     * accept (internal/cq/cq_test.go:196-254). In <= 4096. */
     WC_GEMM_TENSOR_CORES = 1,
     /* The tensor cores from 32 rows on, the bit-exact lut kernel below:
      * the choice a batched caller (multi-stream decode, prefill) makes. */
@@ -123,7 +129,7 @@ enum {
 
 /*
  * wc_cq_gemm with options (flags above). With WC_GEMM_TENSOR_CORES the first
- * call on a matrix builds its bf16 weight image on the device (or call
+ * call on a matrix builds its fp16 weight image on the device (or call
  * wc_cq_prepare_tc first, outside any stream capture), and each call uses a
  * per-thread device buffer for the rotated activations, grown on demand: a
  * thread's tensor-core calls must not overlap on the GPU (use one stream
@@ -151,12 +157,13 @@ wc_status wc_cq_prepare_tc(const wc_cq *h);
  * stall a decode step for milliseconds; or a serving process that reserves
  * its GPU memory once at start-up, next to other models, and cannot let a
  * call grow it. This entry point calls no cudaMalloc, cudaFree or other
- * allocating routine: the rotated activations go to a fixed 16 MiB array
+ * allocating routine: the rotated activations go to a fixed 16.5 MiB array
  * that the library keeps on every GPU it is loaded on, until the process
  * exits. It has no counterpart in the reference.
  *
- *  - rows · K · 2 bytes must fit in 16 MiB, K = In rounded up to the group
- *    and to 64 (16,384 rows at In = 512, 4,096 at In = 2048); larger calls
+ *  - R · (K · 2 + 4) bytes must fit in 16.5 MiB, R = rows rounded up to
+ *    128 and K = In rounded up to the group and to 64 (16,896 rows at
+ *    In = 512, 4,096 at In = 2048); larger calls
  *    fail with WC_ERR_INVALID and leave y alone.
  *  - h must already have its weight image: call wc_cq_prepare_tc when the
  *    matrix is loaded (that call allocates; this one does not).

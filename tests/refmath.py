@@ -86,3 +86,26 @@ def lut_bound(p, x) -> np.ndarray:
         mx = v.max()
         bound += 1.01 * n[:, g] * per * cb_max * mx / (2 * LUT_Q * np.sqrt(G))
     return bound
+
+
+def tc_bound(p, x):
+    """The tensor-core GEMM's rotated operands and per-element error bound
+    (WC_GEMM_TENSOR_CORES in include/whistle_b200.h): returns (y64, bound),
+    the float64 product of x [rows][In] with p and the bound on
+    |y_tc - y64|. fp16 operands rounded once each (2^-10 for a product),
+    the fp32 rotation, scaling and K-term accumulation, and fp16's
+    subnormals below the power-of-two scales (the 2^-37 term)."""
+    G = p.group
+    groups = (p.in_ + G - 1) // G
+    rows = x.shape[0]
+    xp = np.zeros((rows, groups * G))
+    xp[:, : p.in_] = x
+    xh = np.einsum("jk,rgk->rgj", sylvester(G), xp.reshape(rows, groups, G)).reshape(rows, groups * G)
+    cb = np.asarray(p.codebook, np.float64)
+    w = (cb[unpack(p)].reshape(p.out, groups, G) * norms(p)[:, :, None] / np.sqrt(G)).reshape(p.out, groups * G)
+    K = w.shape[1]
+    gamma = 2.0 ** -10 + (K + np.log2(G) + 6) * 2.0 ** -24
+    aw, ax = np.abs(w), np.abs(xh)
+    amax = np.abs(x).max(axis=1, initial=0.0)[:, None]
+    sub = 2.0 ** -37 * (G * amax * aw.sum(axis=1)[None, :] + aw.max(initial=0.0) * ax.sum(axis=1)[:, None])
+    return xh @ w.T, gamma * (ax @ aw.T) + sub

@@ -29,19 +29,6 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr())
 
 
-def _bf16_bound(p, x, want_rows):
-    """The tensor-core tests' per-element bound (test_gemm_tc_gpu.py)."""
-    G = p.group
-    groups = (p.in_ + G - 1) // G
-    xp = np.zeros((x.shape[0], groups * G))
-    xp[:, : p.in_] = x
-    xh = np.einsum("jk,rgk->rgj", refmath.sylvester(G), xp.reshape(x.shape[0], groups, G)).reshape(x.shape[0], -1)
-    cb = np.asarray(p.codebook, np.float64)
-    w = (cb[refmath.unpack(p)].reshape(p.out, groups, G) * refmath.norms(p)[:, :, None] / np.sqrt(G)).reshape(p.out, -1)
-    gamma = 2.0 ** -7 + (w.shape[1] + np.log2(G) + 4) * 2.0 ** -24
-    return xh @ w.T, gamma * (np.abs(xh) @ np.abs(w).T)
-
-
 # (out, in, group, bits, row counts of the calls in a row). A smaller call
 # after a larger one finds the larger one's rotated rows in the array; from
 # 1024 rows both entry points run the persistent kernel.
@@ -70,7 +57,7 @@ def test_no_alloc_matches_allocating_entry_point(wb, cuda, shape):
         # Same kernels on the same inputs: the same bits, and so within the
         # tensor-core bound of the float64 product.
         assert np.array_equal(g.view(np.uint32), w.view(np.uint32))
-        ref, bound = _bf16_bound(p, x.cpu().numpy().astype(np.float64), rows)
+        ref, bound = refmath.tc_bound(p, x.cpu().numpy().astype(np.float64))
         assert np.all(np.abs(g - ref) <= bound)
 
 
