@@ -77,6 +77,15 @@ _SIGS = {
     "wc_attend_int8_streams": (_c_int, [_c_int, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                         _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float, _c_int, _c_void_p,
                                         _c_void_p]),
+    "wc_decoder_create": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_void_p)]),
+    "wc_decoder_destroy": (None, [_c_void_p]),
+    "wc_decoder_memory": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_void_p]),
+    "wc_decoder_extend": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "wc_decoder_greedy": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
+                                   _c_void_p, _c_void_p, _c_void_p]),
+    "wc_decoder_len": (_c_int, [_c_void_p]),
+    "wc_decoder_memory_of": (_c_int, [_c_void_p, _c_int, ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p),
+                                      ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p)]),
 }
 
 _lib = None

@@ -85,7 +85,10 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     objs = []
     for src in sources():
         obj = OBJ / (src.stem + ".o")
-        cmd = [cc, *ARCH, *NVFLAGS, "-c", str(src), "-o", str(obj)]
+        # The decoder's elementwise arithmetic must keep every float
+        # rounding the reference makes: no multiply-add contraction there.
+        extra = ["--fmad=false"] if src.name == "decoder.cu" else []
+        cmd = [cc, *ARCH, *NVFLAGS, *extra, "-c", str(src), "-o", str(obj)]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
         r = subprocess.run(cmd, capture_output=True, text=True)

@@ -951,7 +951,8 @@ static const int kTcPersistRows = 1024;
 // kMaxTcMats matrices of that G. The image lives in the calling thread's
 // scratch, so one thread's calls must not overlap on the GPU (one stream
 // per thread, as the header states).
-static wc_status run_tc(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows, cudaStream_t s) {
+static wc_status run_tc(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows, cudaStream_t s,
+                        void *ext = nullptr, size_t ext_bytes = 0) {
     for (int k = 0; k < n; k++) {
         wc_status st = wc_cq_prepare_tc(ms[k]);
         if (st != WC_OK) return st;
@@ -963,8 +964,12 @@ static wc_status run_tc(const wc_cq *const *ms, int n, const float *x, float *co
         if (done[i] || ms[i]->out == 0) continue;
         const CqShape &sh = ms[i]->shape;
         const int kchunks = tc_kchunks(sh);
-        void *a = nullptr;
-        WB_CUDA(t_scratch.get(3, tc_a_bytes(rows, kchunks), &a));
+        void *a = ext;
+        if (ext) {
+            if (tc_a_bytes(rows, kchunks) > ext_bytes) return set_error(WC_ERR_INVALID, "cq: tensor-core buffer too small");
+        } else {
+            WB_CUDA(t_scratch.get(3, tc_a_bytes(rows, kchunks), &a));
+        }
         cudaError_t e = launch_rotate_f16(sh, x, rows, (unsigned char *)a, s);
         if (e != cudaSuccess) return cuda_error(e, "cq rotate kernel");
         TcParams p{};
@@ -1040,6 +1045,20 @@ extern "C" wc_status wc_cq_gemms_ex(const wc_cq *const *hs, int n, const float *
     if (rows == 0 || n == 0) return WC_OK;
     return run_tc(hs, n, x, ys, rows, (cudaStream_t)stream);
 }
+
+namespace wb {
+// GEMMs on device memory for the library's own callers (the decoder): the
+// bit-exact lut kernels, or the tensor cores with the rotated image in the
+// caller's buffer, so that a captured graph never points at a per-thread
+// scratch that a later call could grow and free.
+wc_status gemms_device(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows, bool tc,
+                       void *tc_buf, size_t tc_bytes, cudaStream_t st) {
+    if (rows == 0 || n == 0) return WC_OK;
+    if (!tc) return wc_cq_gemms(ms, n, x, ys, rows, st);
+    return run_tc(ms, n, x, ys, rows, st, tc_buf, tc_bytes);
+}
+int *err_word() { return device_err_word(); }
+}  // namespace wb
 
 // Tensor-core GEMM without any allocation: see whistle_b200.h.
 extern "C" wc_status wc_cq_gemm_tc_noalloc(const wc_cq *h, const float *x, float *y, int rows, int *err,

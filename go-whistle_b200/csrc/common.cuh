@@ -57,6 +57,12 @@ wc_status set_error(wc_status st, const std::string &msg);
 wc_status cuda_error(cudaError_t e, const char *what);
 // Counts one kernel launch (wc_launch_count).
 void count_launch();
+// The current device's error word of the kernels' bounded waits.
+int *err_word();
+// GEMMs on device memory (api.cu): lut, or tensor cores with the rotated
+// image in tc_buf (at least tc_a_bytes of the rows and widths).
+wc_status gemms_device(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows, bool tc,
+                       void *tc_buf, size_t tc_bytes, cudaStream_t st);
 }  // namespace wb
 
 #define WB_CUDA(call)                                            \

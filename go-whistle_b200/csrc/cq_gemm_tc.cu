@@ -225,6 +225,9 @@ __global__ void __launch_bounds__(kTcThreads, kStages <= 2 ? 3 : kStages <= 3 ? 
         float *stage = reinterpret_cast<float *>(sa);
         constexpr int kHalf = 64, kPad = kHalf + 4;
         const int erow = part * 32 + lane;  // this thread's TMEM lane / tile row
+        // Undo the row's and the matrix's power-of-two scales (exact) as the
+        // accumulator leaves TMEM: one factor per thread, its tile row.
+        const float fsc = __fmul_rn(p.rs[mt * kTcM + erow], mat.ws);
         for (int h = 0; h < kTcN; h += kHalf) {
             if (ok) {
 #pragma unroll
@@ -233,8 +236,11 @@ __global__ void __launch_bounds__(kTcThreads, kStages <= 2 ? 3 : kStages <= 3 ? 
                     tmem_ld32(tmem + ((uint32_t)(part * 32) << 16) + (uint32_t)(h + c), r);
 #pragma unroll
                     for (int q = 0; q < 8; q++)
-                        *reinterpret_cast<uint4 *>(stage + erow * kPad + c + 4 * q) =
-                            make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+                        *reinterpret_cast<float4 *>(stage + erow * kPad + c + 4 * q) =
+                            make_float4(__fmul_rn(__uint_as_float(r[4 * q]), fsc),
+                                        __fmul_rn(__uint_as_float(r[4 * q + 1]), fsc),
+                                        __fmul_rn(__uint_as_float(r[4 * q + 2]), fsc),
+                                        __fmul_rn(__uint_as_float(r[4 * q + 3]), fsc));
                 }
             }
             asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -245,10 +251,7 @@ __global__ void __launch_bounds__(kTcThreads, kStages <= 2 ? 3 : kStages <= 3 ? 
                 for (int rr = (warp - 2) * 2 + sub; rr < kTcM; rr += 8) {
                     const int row = mt * kTcM + rr, col = col0 + c4;
                     if (row < p.m && col < mat.n) {
-                        float4 v = *reinterpret_cast<const float4 *>(stage + rr * kPad + c4);
-                        // Undo the row's and the matrix's power-of-two scales (exact).
-                        const float f = __fmul_rn(p.rs[row], mat.ws);
-                        v = make_float4(__fmul_rn(v.x, f), __fmul_rn(v.y, f), __fmul_rn(v.z, f), __fmul_rn(v.w, f));
+                        const float4 v = *reinterpret_cast<const float4 *>(stage + rr * kPad + c4);
                         float *y = mat.y + (size_t)row * mat.ldy + col;
                         if (col + 4 <= mat.n && (mat.ldy & 3) == 0 && (((uintptr_t)y) & 15) == 0) {
                             *reinterpret_cast<float4 *>(y) = v;
@@ -428,14 +431,19 @@ __global__ void __launch_bounds__(kPThreads, 1) cq_gemm_tc_persistent_kernel(con
             const int nt = t % ntg, mt = t / ntg;
             const TcMat &mat = p.mats[p_matrix(p, nt)];
             const int col_base = (nt - mat.tile0) * kPN;
+            // The scales of this lane's accumulator row (TMEM lane = tile row).
+            const float fsc = __fmul_rn(p.rs[mt * kTcM + part * 32 + lane], mat.ws);
             for (int cc = half * (kPN / 2); cc < (half + 1) * (kPN / 2); cc += 32) {
                 {
                     uint32_t r[32];
                     tmem_ld32(tmem + ((uint32_t)(part * 32) << 16) + (uint32_t)(b * kPN + cc), r);
 #pragma unroll
                     for (int q = 0; q < 8; q++)
-                        *reinterpret_cast<uint4 *>(mystg + lane * kPStgStride + 4 * q) =
-                            make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+                        *reinterpret_cast<float4 *>(mystg + lane * kPStgStride + 4 * q) =
+                            make_float4(__fmul_rn(__uint_as_float(r[4 * q]), fsc),
+                                        __fmul_rn(__uint_as_float(r[4 * q + 1]), fsc),
+                                        __fmul_rn(__uint_as_float(r[4 * q + 2]), fsc),
+                                        __fmul_rn(__uint_as_float(r[4 * q + 3]), fsc));
                 }
                 __syncwarp();
                 // The warp's 32 rows x 32 columns: 8 lanes per row, four rows
@@ -444,9 +452,7 @@ __global__ void __launch_bounds__(kPThreads, 1) cq_gemm_tc_persistent_kernel(con
                 for (int rr = sub; rr < 32; rr += 4) {
                     const int row = mt * kTcM + part * 32 + rr, col = col_base + cc + c4;
                     if (row < p.m && col < mat.n) {
-                        float4 v = *reinterpret_cast<const float4 *>(mystg + rr * kPStgStride + c4);
-                        const float f = __fmul_rn(p.rs[row], mat.ws);
-                        v = make_float4(__fmul_rn(v.x, f), __fmul_rn(v.y, f), __fmul_rn(v.z, f), __fmul_rn(v.w, f));
+                        const float4 v = *reinterpret_cast<const float4 *>(mystg + rr * kPStgStride + c4);
                         float *y = mat.y + (size_t)row * mat.ldy + col;
                         if (col + 4 <= mat.n && (mat.ldy & 3) == 0 && (((uintptr_t)y) & 15) == 0) {
                             *reinterpret_cast<float4 *>(y) = v;
@@ -485,7 +491,7 @@ __global__ void __launch_bounds__(kPThreads, 1) cq_gemm_tc_persistent_kernel(con
 // a lane's float4s. Each lane stores its four fp16 values as 8 bytes of a
 // 128-byte chunk row.
 template <int J>
-__global__ void __launch_bounds__(256) rotate_f16_kernel(const float *__restrict__ x, int m, int in, int G,
+__global__ void __launch_bounds__(128) rotate_f16_kernel(const float *__restrict__ x, int m, int in, int G,
                                                          int log2g, int kpad, int kchunks, long rows_total,
                                                          int vec, unsigned char *__restrict__ a,
                                                          float *__restrict__ rs) {
@@ -637,7 +643,9 @@ static cudaError_t launch_rotate_j(const CqShape &s, const float *x, int m, int 
     int log2g = 0;
     while ((1 << log2g) < s.group) log2g++;
     const int vec = (s.in % 4 == 0) && (((uintptr_t)x) & 15) == 0;
-    rotate_f16_kernel<J><<<(int)((rows + 7) / 8), 256, 0, st>>>(x, m, s.in, s.group, log2g, kpad, kchunks, rows, vec,
+    // Four rows (warps) per block: a call of few rows still spreads over
+    // many SMs.
+    rotate_f16_kernel<J><<<(int)((rows + 3) / 4), 128, 0, st>>>(x, m, s.in, s.group, log2g, kpad, kchunks, rows, vec,
                                                                a, rs);
     count_launch();
     return cudaGetLastError();

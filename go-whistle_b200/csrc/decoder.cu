@@ -1,0 +1,1300 @@
+// decoder.cu — Whistle's text decoder step on the device (wc_decoder_*):
+// internal/decoder's Decoder.Extend (decoder.go:252) with the Best()
+// hypothesis and the engine's int8 numerics, for many independent streams
+// at once, every stream's state resident in HBM.
+//
+// One step (one token per stream) is, per layer l (decoder.go:446 layer):
+//   mhc_in        RMSUnit of the 4-lane stream, int8 fake-quant (mHC φ input)
+//   GEMMs         φ_pre, φ_post, φ_res (CQ4, 2048 in)
+//   mhc_block_in  mHC heads: sigmoids, Sinkhorn, u = Σ h_pre·lane; engram
+//                 gate at the sites; norm_in
+//   GEMMs         q, k, v, gate (CQ2)
+//   self_prep     causal taps, q/k ZCRMSNorm, RoPE, int8 append of k and v
+//   attention     the int8 KV kernel (exact reference order)
+//   gate          σ(gate) ⊙ attention
+//   GEMM          out_proj
+//   post_attn     post_attn_norm, gated residual, cross_norm
+//   GEMMs         cross q, cross gate
+//   cross_q       cross q norm
+//   attention     over the int8 memory
+//   gate, GEMM    σ(gate) ⊙, cross out_proj
+//   block_out     post_cross_norm, residual, pre_hada norm, HadamardMLP,
+//                 mHC mix back into the lanes
+// then the lane mean, final norm, the tied head GEMM and the argmax. The
+// engram keys and values of both sites are computed once per step before
+// the layers (decoder.go:276-285).
+//
+// Elementwise phases run one 512-thread CTA per stream, one thread per
+// model column. Every float32 operation is a separate IEEE rounding in the
+// reference's order: this file is compiled with --fmad=false, and the few
+// sums whose order matters in float32 (the engram gate's dot product, the
+// HadamardMLP's condition and Kronecker products) run sequentially per
+// output, as algo-tensor's loops do. The float64 sums of squares of the
+// norms run as a tree instead of the reference's four partial sums: a
+// float64 sum's rounding can change the float32 result only when it lies
+// within about 2^-44 (relative) of a float32 rounding boundary.
+//
+// Positions live in device memory, so a step can be captured once as a
+// CUDA graph and replayed.
+#include <cmath>
+#include <cstdarg>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "cq_kernels.cuh"
+#include "needle_kernels.cuh"
+
+namespace wb {
+
+namespace {
+
+constexpr int kD = 512;        // model width this build's kernels take
+constexpr int kLanes = 4;      // mHC lanes
+constexpr int kQK = 48;        // query/key head width
+constexpr int kVD = 64;        // value head width
+constexpr int kNA = 16, kNB = 32, kRank = 8;  // HadamardMLP
+constexpr int kThreads = 512;  // one thread per model column
+constexpr float kEps = 1e-6f;  // internal/needle/norm.go:9 normEps as float32
+
+// One layer's device tensors and constants.
+struct LayerK {
+    const float *g_norm_in, *g_post, *g_pre_hada;  // gains 1 + scale [dim]
+    const float *q_taps, *k_taps, *v_taps;         // [taps][width]
+    const float *g_qn, *g_kn;                      // [qk]
+    const float *d1, *d2, *b2, *d3, *d4;           // [na·nb]
+    const float *wa[3], *wb[3];                    // [na][na], [nb][nb]
+    const float *cond_v, *cond_u;                  // [dim][rank], [rank][na·nb]
+    const float *g_xn, *g_xpost, *g_xqn, *g_xkn;
+    const float *b_pre, *b_post, *b_res;
+    float gate;    // σ(attn_gate) (block.go:60)
+    float xresid;  // σ(cross_gate) (cross.go:148)
+    float a_pre, a_post, a_res;
+    int lane;      // layer mod lanes: its pre/post offsets (mhc.go:123 laneOffsets)
+};
+
+__device__ __forceinline__ float sigm(float x) { return (float)(1.0 / (1.0 + exp(-(double)x))); }
+
+// Σ of one double per thread over the CTA (warp shuffles, then the warps'
+// sums in warp order), returned to every thread.
+__device__ double block_sum(double v, double *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < nw; w++) t += red[w];
+        red[32] = t;
+    }
+    __syncthreads();
+    const double t = red[32];
+    __syncthreads();
+    return t;
+}
+
+__device__ float block_max(float v, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int w = 0; w < nw; w++) t = fmaxf(t, red[w]);
+        red[32] = t;
+    }
+    __syncthreads();
+    const float t = red[32];
+    __syncthreads();
+    return t;
+}
+
+// norm.go:104 meanSquare of the CTA's row (one value per thread, n values).
+__device__ float mean_square(float x, int n, double *red) {
+    const double s = block_sum((double)x * (double)x, red);
+    return (float)(s / (double)n);
+}
+
+// norm.go:60 ZCRMSNorm.Apply on the CTA's row of kD values: (g·x)/rms.
+__device__ float zc_norm_row(float x, float g, double *red) {
+    const float ms = mean_square(x, kD, red) + kEps;
+    const float rms = (float)sqrt((double)ms);
+    return __fdiv_rn(g * x, rms);
+}
+
+// The same per head of 48 inside one warp: lane l < 24 holds elements l and
+// l + 24 of the head. Returns the mean square + eps as float32.
+__device__ float head_ms48(float a, float b, int lane) {
+    double v = lane < 24 ? (double)a * (double)a + (double)b * (double)b : 0.0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return (float)(v / 48.0) + kEps;
+}
+
+// int8.go:36 QuantizeRow's rounding of one value with scale s.
+__device__ __forceinline__ int8_t quant8(float x, float s) {
+    float r = rintf(__fdiv_rn(x, s));
+    r = fminf(fmaxf(r, -128.0f), 127.0f);
+    return (int8_t)(int)r;
+}
+
+// ---------------------------------------------------------------- kernels
+
+// Embedding row × √dim into every lane (decoder.go:270-283, mhc.go:131
+// ExpandLanes); the self-attention's key count for this step.
+__global__ void __launch_bounds__(kThreads) embed_kernel(const float *__restrict__ row, float scale,
+                                                         const int32_t *__restrict__ pos, int32_t *nk_self,
+                                                         float *__restrict__ stream) {
+    const int s = blockIdx.x, c = threadIdx.x;
+    const float v = row[(size_t)s * kD + c] * scale;
+#pragma unroll
+    for (int k = 0; k < kLanes; k++) stream[((size_t)s * kLanes + k) * kD + c] = v;
+    if (c == 0) nk_self[s] = pos[s] + 1;
+}
+
+// engram.go:141 ngramHash and IndicesAt for the fed token: the table rows
+// the step gathers (−1, a zero row, before order − 1 positions).
+__global__ void engram_rows_kernel(const int32_t *__restrict__ tok, const int32_t *__restrict__ tokhist, int ring,
+                                   const int32_t *__restrict__ pos, const int32_t *__restrict__ orders, int n_tables,
+                                   int slots, int32_t *__restrict__ rows) {
+    const int s = blockIdx.x, c = threadIdx.x;
+    if (c >= n_tables) return;
+    const int p = pos[s], order = orders[c];
+    int32_t r = -1;
+    if (p + 1 >= order) {
+        uint32_t acc = 0x9E3779B9u * (uint32_t)(c + 1);
+        for (int j = 0; j < order; j++) {
+            uint32_t t = 0;
+            if (j == 0)
+                t = (uint32_t)tok[s];
+            else if (p - j >= 0)
+                t = (uint32_t)tokhist[(size_t)s * ring + (p - j) % ring];
+            acc = (acc ^ t) * 0x01000193u;
+        }
+        acc ^= acc >> 15;
+        r = c * slots + (int32_t)(acc % (uint32_t)slots);
+    }
+    rows[(size_t)s * n_tables + c] = r;
+}
+
+// cache.go:196-205: the dilated taps over the raw values of the last
+// (taps − 1)·dil positions (a ring indexed by position) and this step's.
+__global__ void __launch_bounds__(kThreads) engram_taps_kernel(const float *__restrict__ vraw, float *__restrict__ ring,
+                                                               const float *__restrict__ taps, int ntaps, int dil,
+                                                               const int32_t *__restrict__ pos,
+                                                               float *__restrict__ ev) {
+    const int s = blockIdx.x, c = threadIdx.x;
+    const int p = pos[s], R = (ntaps - 1) * dil;
+    const float z = vraw[(size_t)s * kD + c];
+    float out = 0.0f;
+    out = out + taps[c] * z;
+    for (int j = 1; j < ntaps; j++) {
+        const int q = p - dil * j;
+        if (q < 0) break;
+        out = out + taps[(size_t)j * kD + c] * ring[((size_t)s * R + q % R) * kD + c];
+    }
+    ev[(size_t)s * kD + c] = out;
+    if (R > 0) ring[((size_t)s * R + p % R) * kD + c] = z;
+}
+
+// mhc.go:193 nx = RMSUnit(stream) over all lanes, then linear.go:108's
+// int8 fake-quant of the row (the φ products' shared quantised input).
+__global__ void __launch_bounds__(kThreads) mhc_in_kernel(const float *__restrict__ stream, float *__restrict__ xq) {
+    __shared__ double red[33];
+    __shared__ float redf[33];
+    const int s = blockIdx.x, c = threadIdx.x;
+    float v[kLanes];
+    double sq = 0.0;
+#pragma unroll
+    for (int k = 0; k < kLanes; k++) {
+        v[k] = stream[((size_t)s * kLanes + k) * kD + c];
+        sq += (double)v[k] * (double)v[k];
+    }
+    const double tot = block_sum(sq, red);
+    const float ms = (float)(tot / (double)(kLanes * kD)) + kEps;
+    const float inv = (float)(1.0 / sqrt((double)ms));
+    float m = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kLanes; k++) {
+        v[k] = v[k] * inv;
+        m = fmaxf(m, fabsf(v[k]));
+    }
+    m = block_max(m, redf);
+    const float sc = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
+#pragma unroll
+    for (int k = 0; k < kLanes; k++)
+        xq[((size_t)s * kLanes + k) * kD + c] = (float)quant8(v[k], sc) * sc;
+}
+
+// mhc.go:316 sinkhornExp / :374 sinkhornLog on a 4×4 matrix held by lanes
+// 0..15 of one warp (lane e: row e/4, column e%4); every row and column sum
+// is formed in the reference's order by each lane of that row or column.
+__device__ float sinkhorn_lane(float k, int lane) {
+    const unsigned full = 0x0000ffffu;  // lanes 0..15 only
+    float lo = k, hi = k;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+        lo = fminf(lo, __shfl_xor_sync(full, lo, o, 16));
+        hi = fmaxf(hi, __shfl_xor_sync(full, hi, o, 16));
+    }
+    const double spread = (double)hi - (double)lo;
+    const int r = (lane & 15) >> 2, c = lane & 3;
+    const bool exp_path =
+        !(isinf(spread) || isnan(spread) || spread + 2.0 * 20.0 * log(4.0) > 700.0);
+    if (exp_path) {
+        double e = exp((double)k - (double)hi);
+        for (int it = 0; it < 20; it++) {
+            double v0 = __shfl_sync(full, e, r * 4 + 0, 16), v1 = __shfl_sync(full, e, r * 4 + 1, 16);
+            double v2 = __shfl_sync(full, e, r * 4 + 2, 16), v3 = __shfl_sync(full, e, r * 4 + 3, 16);
+            double sum = 0.0;
+            sum += v0;
+            sum += v1;
+            sum += v2;
+            sum += v3;
+            e = e / sum;
+            v0 = __shfl_sync(full, e, 0 * 4 + c, 16), v1 = __shfl_sync(full, e, 1 * 4 + c, 16);
+            v2 = __shfl_sync(full, e, 2 * 4 + c, 16), v3 = __shfl_sync(full, e, 3 * 4 + c, 16);
+            sum = 0.0;
+            sum += v0;
+            sum += v1;
+            sum += v2;
+            sum += v3;
+            e = e / sum;
+        }
+        return (float)e;
+    }
+    float x = k;
+    for (int it = 0; it < 20; it++) {
+        for (int phase = 0; phase < 2; phase++) {
+            float v[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) v[j] = __shfl_sync(full, x, phase == 0 ? r * 4 + j : j * 4 + c, 16);
+            float m = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; j++) m = fmaxf(m, v[j]);
+            if (isinf(m)) m = 0.0f;
+            float sum = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; j++) sum += (float)exp((double)(v[j] - m));
+            x = x - (m + (float)log((double)sum));
+        }
+    }
+    return (float)exp((double)x);
+}
+
+// mhc.go:241 logits and :205-221 (sigmoids, u, Sinkhorn), then block.go:148
+// run up to the attention: the engram gate (block.go:231 applyEngram) at a
+// site, and norm_in.
+__global__ void __launch_bounds__(kThreads)
+    mhc_block_in_kernel(const LayerK L, const float *__restrict__ stream, const float *__restrict__ phi_pre,
+                        const float *__restrict__ phi_post, const float *__restrict__ phi_res,
+                        const float *__restrict__ ek, const float *__restrict__ ev, float *__restrict__ u_out,
+                        float *__restrict__ h_out, float *__restrict__ n_out, float *__restrict__ hp_out,
+                        float *__restrict__ hr_out) {
+    __shared__ double red[33];
+    __shared__ float pre[kLanes], post[kLanes], res[kLanes * kLanes];
+    __shared__ float ux[kD], uk[kD];
+    __shared__ float alpha;
+    const int s = blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
+    if (warp == 0) {
+        if (lane < kLanes) {
+            const float pre_off = lane == L.lane ? 4.0f : -4.0f, post_off = lane == L.lane ? 0.0f : -4.0f;
+            const float t = L.a_pre * phi_pre[(size_t)s * kLanes + lane];
+            pre[lane] = sigm(t + L.b_pre[lane] + pre_off);
+            const float t2 = L.a_post * phi_post[(size_t)s * kLanes + lane];
+            post[lane] = 2.0f * sigm(t2 + L.b_post[lane] + post_off);
+        }
+        if (lane < kLanes * kLanes) {
+            const float t = L.a_res * phi_res[(size_t)s * kLanes * kLanes + lane];
+            res[lane] = sinkhorn_lane(t + L.b_res[lane], lane);
+        }
+    }
+    __syncthreads();
+    float u = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kLanes; k++) u = u + pre[k] * stream[((size_t)s * kLanes + k) * kD + c];
+    float h = u;
+    if (ek) {
+        const float e = ek[(size_t)s * kD + c];
+        const float msx = mean_square(h, kD, red) + kEps;
+        const float msk = mean_square(e, kD, red) + kEps;
+        ux[c] = h * (float)(1.0 / sqrt((double)msx));
+        uk[c] = e * (float)(1.0 / sqrt((double)msk));
+        __syncthreads();
+        if (c == 0) {
+            float dp = 0.0f;  // algo-tensor DotProduct, index order
+            for (int i = 0; i < kD; i++) dp = dp + ux[i] * uk[i];
+            alpha = sigm(__fdiv_rn(dp, (float)sqrt((double)kD)));
+        }
+        __syncthreads();
+        h = h + alpha * ev[(size_t)s * kD + c];
+    }
+    const float n = zc_norm_row(h, L.g_norm_in[c], red);
+    u_out[(size_t)s * kD + c] = u;
+    h_out[(size_t)s * kD + c] = h;
+    n_out[(size_t)s * kD + c] = n;
+    if (c < kLanes) hp_out[(size_t)s * kLanes + c] = post[c];
+    if (c < kLanes * kLanes) hr_out[(size_t)s * kLanes * kLanes + c] = res[c];
+}
+
+// cache.go:78-139 Attention.Extend up to the attention: the causal taps
+// over the raw q/k/v history (cache.go:185 extendTaps), the per-head q/k
+// ZCRMSNorm and RoPE at the position (attention.go:300 normRotate), and the
+// int8 append of the key and value row (int8.go:125 Append).
+__global__ void __launch_bounds__(kThreads)
+    self_prep_kernel(const LayerK L, const float *__restrict__ q, const float *__restrict__ k,
+                     const float *__restrict__ v, float *__restrict__ hist, int ntaps, int heads, int kv_heads,
+                     const int32_t *__restrict__ pos, const float *__restrict__ rcos, const float *__restrict__ rsin,
+                     int8_t *__restrict__ k8, float *__restrict__ ks, int8_t *__restrict__ v8,
+                     float *__restrict__ vs, int cap, float *__restrict__ qo) {
+    extern __shared__ float z[];  // [qw + kw + vw]
+    const int s = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int qw = heads * kQK, kw = kv_heads * kQK, vw = kv_heads * kVD, W = qw + kw + vw;
+    const int p = pos[s], th = ntaps - 1;
+    for (int col = t; col < W; col += blockDim.x) {
+        float raw;
+        const float *tap;
+        int tw, tc;
+        if (col < qw) {
+            raw = q[(size_t)s * qw + col], tap = L.q_taps, tw = qw, tc = col;
+        } else if (col < qw + kw) {
+            raw = k[(size_t)s * kw + col - qw], tap = L.k_taps, tw = kw, tc = col - qw;
+        } else {
+            raw = v[(size_t)s * vw + col - qw - kw], tap = L.v_taps, tw = vw, tc = col - qw - kw;
+        }
+        float out = 0.0f;
+        out = out + tap[tc] * raw;
+        for (int j = 1; j < ntaps; j++) {
+            if (p - j < 0) break;
+            out = out + tap[(size_t)j * tw + tc] * hist[((size_t)s * th + (p - j) % th) * W + col];
+        }
+        if (th > 0) hist[((size_t)s * th + p % th) * W + col] = raw;
+        z[col] = out;
+    }
+    __syncthreads();
+    // q heads, then k heads: a warp per head.
+    const int nh = heads + kv_heads;
+    const int half = kQK / 2;
+    for (int hd = warp; hd < nh; hd += blockDim.x >> 5) {
+        const int base = hd < heads ? hd * kQK : qw + (hd - heads) * kQK;
+        const float *g = hd < heads ? L.g_qn : L.g_kn;
+        float a = 0.0f, b = 0.0f;
+        if (lane < half) {
+            a = z[base + lane];
+            b = z[base + lane + half];
+        }
+        const float rms = (float)sqrt((double)head_ms48(a, b, lane));
+        if (lane < half) {
+            a = __fdiv_rn(g[lane] * a, rms);
+            b = __fdiv_rn(g[lane + half] * b, rms);
+            const float cs = rcos[(size_t)p * half + lane], sn = rsin[(size_t)p * half + lane];
+            const float ac = a * cs, bs = b * sn, bc = b * cs, as = a * sn;
+            z[base + lane] = ac - bs;
+            z[base + lane + half] = bc + as;
+        }
+    }
+    __syncthreads();
+    for (int col = t; col < qw; col += blockDim.x) qo[(size_t)s * qw + col] = z[col];
+    // int8 codes and scales of the new key (heads of 48) and value (64) row.
+    for (int hd = warp; hd < 2 * kv_heads; hd += blockDim.x >> 5) {
+        const bool isk = hd < kv_heads;
+        const int w = isk ? kQK : kVD, h2 = isk ? hd : hd - kv_heads;
+        const int base = isk ? qw + h2 * kQK : qw + kw + h2 * kVD;
+        const float a = lane < w / 2 ? z[base + lane] : 0.0f, b = lane < w / 2 ? z[base + lane + w / 2] : 0.0f;
+        float m = fmaxf(fabsf(a), fabsf(b));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const float sc = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
+        const size_t rowi = (size_t)s * cap + p;
+        if (lane < w / 2) {
+            int8_t *dst = isk ? k8 + rowi * kw + h2 * kQK : v8 + rowi * vw + h2 * kVD;
+            dst[lane] = quant8(a, sc);
+            dst[lane + w / 2] = quant8(b, sc);
+        }
+        if (lane == 0) (isk ? ks : vs)[rowi * kv_heads + h2] = sc;
+    }
+}
+
+// attention.go:243 output's gate: out ⊙ σ(gate).
+__global__ void __launch_bounds__(kThreads) gate_kernel(float *__restrict__ out, const float *__restrict__ g, int w) {
+    const int s = blockIdx.x;
+    for (int i = threadIdx.x; i < w; i += blockDim.x) {
+        const size_t o = (size_t)s * w + i;
+        out[o] = out[o] * sigm(g[o]);
+    }
+}
+
+// block.go:193-199 post_attn_norm and the gated residual, then cross.go:212
+// cross_norm of the result (the cross-attention's input).
+__global__ void __launch_bounds__(kThreads) post_attn_kernel(const LayerK L, const float *__restrict__ a,
+                                                             float *__restrict__ h, float *__restrict__ x) {
+    __shared__ double red[33];
+    const int s = blockIdx.x, c = threadIdx.x;
+    const float an = zc_norm_row(a[(size_t)s * kD + c], L.g_post[c], red);
+    const float hv = h[(size_t)s * kD + c] + L.gate * an;
+    h[(size_t)s * kD + c] = hv;
+    x[(size_t)s * kD + c] = zc_norm_row(hv, L.g_xn[c], red);
+}
+
+// cross.go:218 the cross-attention's q norm, per head.
+__global__ void __launch_bounds__(kThreads) cross_q_kernel(const LayerK L, const float *__restrict__ q, int heads,
+                                                           float *__restrict__ qo) {
+    const int s = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, half = kQK / 2;
+    for (int hd = warp; hd < heads; hd += blockDim.x >> 5) {
+        const size_t base = (size_t)s * heads * kQK + hd * kQK;
+        float a = 0.0f, b = 0.0f;
+        if (lane < half) {
+            a = q[base + lane];
+            b = q[base + lane + half];
+        }
+        const float rms = (float)sqrt((double)head_ms48(a, b, lane));
+        if (lane < half) {
+            qo[base + lane] = __fdiv_rn(L.g_xqn[lane] * a, rms);
+            qo[base + lane + half] = __fdiv_rn(L.g_xqn[lane + half] * b, rms);
+        }
+    }
+}
+
+// hadamard.go:300 kronApply (+ :281 mix's permutation for stages 0 and 1)
+// of z (shared, n = 512) into dst (shared): Yᵀ = bᵀ·Zᵀ, then out = aᵀ·Y,
+// each output a sequential sum as tensor.MatMulTransB forms it.
+__device__ void kron_mix(const float *__restrict__ wa, const float *__restrict__ wb, const int *__restrict__ perm,
+                         const float *z, float *yT, float *kb, float *dst) {
+    const int t = threadIdx.x;
+    {
+        const int i = t / kNA, j = t % kNA;  // yT[i][j], i < nb, j < na
+        float acc = 0.0f;
+        for (int l = 0; l < kNB; l++) acc = acc + wb[l * kNB + i] * z[j * kNB + l];
+        yT[i * kNA + j] = acc;
+    }
+    __syncthreads();
+    {
+        const int kk = t / kNB, l2 = t % kNB;  // out[kk][l2], kk < na, l2 < nb
+        float acc = 0.0f;
+        for (int l = 0; l < kNA; l++) acc = acc + wa[l * kNA + kk] * yT[l2 * kNA + l];
+        (perm ? kb : dst)[t] = acc;
+    }
+    __syncthreads();
+    if (perm) {
+        dst[t] = kb[perm[t]];
+        __syncthreads();
+    }
+}
+
+// cross.go:236-248 post_cross_norm, the σ(cross_gate) residual; block.go:
+// 203-214 pre_hada norm, HadamardMLP (hadamard.go:211 rows), the MLP
+// residual; mhc.go:229 y = block(u) − u and :270 mix into the lanes.
+__global__ void __launch_bounds__(kThreads)
+    block_out_kernel(const LayerK L, const int *__restrict__ p1, const int *__restrict__ p2,
+                     const float *__restrict__ cy, const float *__restrict__ h, const float *__restrict__ u,
+                     const float *__restrict__ hp, const float *__restrict__ hr, float *__restrict__ stream) {
+    __shared__ double red[33];
+    __shared__ float pv[kD], z[kD], o[kD], yT[kD], kb[kD];
+    __shared__ float lg[kRank];
+    const int s = blockIdx.x, c = threadIdx.x;
+    const float y = L.xresid * zc_norm_row(cy[(size_t)s * kD + c], L.g_xpost[c], red);
+    const float h2 = h[(size_t)s * kD + c] + y;
+    const float p = zc_norm_row(h2, L.g_pre_hada[c], red);
+    pv[c] = p;
+    __syncthreads();
+    // cond = 1 + softmax(p @ cond_v) @ cond_u
+    if (c < kRank) {
+        float acc = 0.0f;
+        for (int i = 0; i < kD; i++) acc = acc + pv[i] * L.cond_v[i * kRank + c];
+        lg[c] = acc;
+    }
+    __syncthreads();
+    if (c == 0) {  // load.go:127 softmaxInPlace with exp.go:238 expSubSumGeneric
+        float m = -INFINITY;
+        for (int r = 0; r < kRank; r++) m = fmaxf(m, lg[r]);
+        float sum = 0.0f;
+        for (int r = 0; r < kRank; r++) {
+            const float e = (float)exp((double)(lg[r] - m));
+            lg[r] = e;
+            sum = sum + e;
+        }
+        for (int r = 0; r < kRank; r++) lg[r] = __fdiv_rn(lg[r], sum);
+    }
+    __syncthreads();
+    float cond = 0.0f;
+    for (int r = 0; r < kRank; r++) cond = cond + lg[r] * L.cond_u[r * kD + c];
+    cond = cond + 1.0f;
+    z[c] = L.d1[c] * p;
+    __syncthreads();
+    kron_mix(L.wa[0], L.wb[0], p1, z, yT, kb, o);
+    {
+        const float a2 = L.d2[c] * cond * o[c] + L.b2[c];
+        z[c] = a2 * sigm(a2);
+    }
+    __syncthreads();
+    kron_mix(L.wa[1], L.wb[1], p2, z, yT, kb, o);
+    z[c] = L.d3[c] * o[c];
+    __syncthreads();
+    kron_mix(L.wa[2], L.wb[2], nullptr, z, yT, kb, o);
+    const float m = o[c] * L.d4[c] + h2;
+    const float Y = m - u[(size_t)s * kD + c];
+    float st[kLanes], out[kLanes];
+#pragma unroll
+    for (int b = 0; b < kLanes; b++) st[b] = stream[((size_t)s * kLanes + b) * kD + c];
+#pragma unroll
+    for (int a = 0; a < kLanes; a++) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int b = 0; b < kLanes; b++) acc = acc + hr[(size_t)s * kLanes * kLanes + a * kLanes + b] * st[b];
+        out[a] = acc + hp[(size_t)s * kLanes + a] * Y;
+    }
+#pragma unroll
+    for (int a = 0; a < kLanes; a++) stream[((size_t)s * kLanes + a) * kD + c] = out[a];
+}
+
+// mhc.go:140 CollapseLanes and decoder.go:510 final_norm: the head's input.
+__global__ void __launch_bounds__(kThreads) final_kernel(const float *__restrict__ stream, const float *__restrict__ g,
+                                                         float *__restrict__ fin) {
+    __shared__ double red[33];
+    const int s = blockIdx.x, c = threadIdx.x;
+    float m = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kLanes; k++) m = m + stream[((size_t)s * kLanes + k) * kD + c];
+    m = __fdiv_rn(m, (float)kLanes);
+    fin[(size_t)s * kD + c] = zc_norm_row(m, g[c], red);
+}
+
+// The step's bookkeeping: the fed token into the engram history, the
+// position forward.
+__global__ void advance_kernel(const int32_t *__restrict__ tok, int32_t *__restrict__ tokhist, int ring,
+                               int32_t *__restrict__ pos, int streams) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= streams) return;
+    const int p = pos[s];
+    if (ring > 0) tokhist[(size_t)s * ring + p % ring] = tok[s];
+    pos[s] = p + 1;
+}
+
+// cross.go:188-201: the memory keys' per-head norm and the int8 codes and
+// scales of keys and values, one CTA per (stream, frame) row, a warp per
+// head.
+__global__ void __launch_bounds__(256) xmem_kernel(const float *__restrict__ kp, const float *__restrict__ vp,
+                                                   const float *__restrict__ g_xkn, int heads,
+                                                   int8_t *__restrict__ k8, float *__restrict__ ks,
+                                                   int8_t *__restrict__ v8, float *__restrict__ vs) {
+    const size_t r = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, half = kQK / 2;
+    for (int hd = warp; hd < heads; hd += blockDim.x >> 5) {
+        const size_t kb = r * heads * kQK + hd * kQK;
+        float a = 0.0f, b = 0.0f;
+        if (lane < half) {
+            a = kp[kb + lane];
+            b = kp[kb + lane + half];
+        }
+        const float rms = (float)sqrt((double)head_ms48(a, b, lane));
+        if (lane < half) {
+            a = __fdiv_rn(g_xkn[lane] * a, rms);
+            b = __fdiv_rn(g_xkn[lane + half] * b, rms);
+        }
+        float m = fmaxf(fabsf(a), fabsf(b));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float sc = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
+        if (lane < half) {
+            k8[kb + lane] = quant8(a, sc);
+            k8[kb + lane + half] = quant8(b, sc);
+        }
+        if (lane == 0) ks[r * heads + hd] = sc;
+        const size_t vb = r * heads * kVD + hd * kVD;
+        a = vp[vb + lane];
+        b = vp[vb + lane + 32];
+        m = fmaxf(fabsf(a), fabsf(b));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        sc = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
+        v8[vb + lane] = quant8(a, sc);
+        v8[vb + lane + 32] = quant8(b, sc);
+        if (lane == 0) vs[r * heads + hd] = sc;
+    }
+}
+
+// greedy.go:81 language: the largest logit among the language tokens (the
+// first on ties); it is the next token.
+__global__ void lang_kernel(const float *__restrict__ logits, int vocab, const int32_t *__restrict__ langs, int n,
+                            int32_t *__restrict__ tok, int32_t *__restrict__ lang, int streams) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= streams) return;
+    const float *l = logits + (size_t)s * vocab;
+    int best = 0;
+    for (int i = 1; i < n; i++)
+        if (l[langs[i]] > l[langs[best]]) best = i;
+    tok[s] = langs[best];
+    lang[s] = langs[best];
+}
+
+// greedy.go:58-66: record the argmax (already in tok) unless the stream has
+// ended; EOS ends it.
+__global__ void record_kernel(const int32_t *__restrict__ tok, int eos, int max_out, int32_t *__restrict__ tokens,
+                              int32_t *__restrict__ counts, int32_t *__restrict__ eos_hit, int32_t *__restrict__ done,
+                              int streams) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= streams || done[s]) return;
+    const int t = tok[s];
+    if (t == eos) {
+        done[s] = 1;
+        eos_hit[s] = 1;
+        return;
+    }
+    const int n = counts[s];
+    if (n < max_out) tokens[(size_t)s * max_out + n] = t;
+    counts[s] = n + 1;
+}
+
+__global__ void greedy_init_kernel(int32_t *tok, int bos, int32_t *tokens, int max_out, int32_t *counts,
+                                   int32_t *eos_hit, int32_t *done, int streams) {
+    const int s = blockIdx.x;
+    if (s >= streams) return;
+    for (int i = threadIdx.x; i < max_out; i += blockDim.x) tokens[(size_t)s * max_out + i] = -1;
+    if (threadIdx.x == 0) {
+        tok[s] = bos;
+        counts[s] = 0;
+        eos_hit[s] = 0;
+        done[s] = 0;
+    }
+}
+
+__global__ void fill_kernel(int32_t *p, int32_t v, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) p[i] = v;
+}
+
+}  // namespace
+
+}  // namespace wb
+
+using namespace wb;
+
+// A device allocation freed with the decoder.
+struct DevBuf {
+    void *p = nullptr;
+    size_t bytes = 0;
+};
+
+struct wc_decoder {
+    wc_decoder_desc d{};  // sizes (pointers not kept)
+    int max_streams = 0, max_frames = 0, cap = 0, flags = 0, device = 0;
+    int streams = 0, frames = 0, len = 0;
+    int ring_t = 0;  // token history ring: max_order − 1
+    bool tc = false;
+    std::vector<DevBuf> bufs;
+    // views of the caller's matrices (they keep the storage alive)
+    std::vector<wc_cq *> views;
+    wc_cq *emb = nullptr;
+    struct Layer {
+        LayerK k;
+        wc_cq *q, *kk, *v, *g, *o, *xq, *xk, *xv, *xg, *xo, *ppre, *ppost, *pres;
+    };
+    std::vector<Layer> layers;
+    struct Site {
+        wc_cq *tables, *key, *value;
+        const float *taps;
+        int layer;
+    };
+    std::vector<Site> sites;
+    const float *g_final = nullptr;
+    const int *p1 = nullptr, *p2 = nullptr;
+    const int32_t *orders = nullptr;
+    const float *rcos = nullptr, *rsin = nullptr;
+    float in_scale = 1.0f, att_scale = 1.0f, xatt_scale = 1.0f;
+    // per-stream state and step buffers
+    float *stream = nullptr, *xq = nullptr, *phi_pre = nullptr, *phi_post = nullptr, *phi_res = nullptr;
+    float *u = nullptr, *h = nullptr, *n = nullptr, *hp = nullptr, *hr = nullptr;
+    float *q = nullptr, *k = nullptr, *v = nullptr, *g = nullptr, *qo = nullptr, *att = nullptr, *a = nullptr;
+    float *x = nullptr, *cq = nullptr, *cg = nullptr, *cqn = nullptr, *catt = nullptr, *cy = nullptr;
+    float *fin = nullptr, *logits = nullptr, *row = nullptr, *erow = nullptr, *vraw = nullptr;
+    float *ek = nullptr, *ev = nullptr, *evring = nullptr, *hist = nullptr;
+    int32_t *tok = nullptr, *pos = nullptr, *nk_self = nullptr, *nk_x = nullptr, *erows = nullptr;
+    int32_t *tokhist = nullptr, *done = nullptr, *langs = nullptr;
+    int32_t langs_host[64] = {};
+    int8_t *k8 = nullptr, *v8 = nullptr, *xk8 = nullptr, *xv8 = nullptr;
+    float *ks = nullptr, *vs = nullptr, *xks = nullptr, *xvs = nullptr;
+    float *mk = nullptr, *mv = nullptr;  // memory projection outputs [streams·frames][x_heads·x_qk | x_vd]
+    void *tcbuf = nullptr;
+    size_t tcbytes = 0;
+    cudaGraphExec_t graph = nullptr;
+    cudaStream_t graph_stream = nullptr;
+    int graph_streams = 0;
+
+    ~wc_decoder() {
+        int cur = 0;
+        cudaGetDevice(&cur);
+        if (cur != device) cudaSetDevice(device);
+        if (graph) cudaGraphExecDestroy(graph);
+        for (auto &b : bufs) cudaFree(b.p);
+        for (auto *vw : views) wc_cq_destroy(vw);
+        if (cur != device) cudaSetDevice(cur);
+    }
+
+    template <typename T>
+    wc_status alloc(T **p, size_t count) {
+        void *q = nullptr;
+        const size_t bytes = (count > 0 ? count : 1) * sizeof(T);
+        cudaError_t e = cudaMalloc(&q, bytes);
+        if (e != cudaSuccess) return set_error(WC_ERR_NOMEM, std::string("decoder: device memory: ") + cudaGetErrorString(e));
+        bufs.push_back({q, bytes});
+        *p = static_cast<T *>(q);
+        return WC_OK;
+    }
+    // A host float array copied to the device (n values).
+    wc_status upload(const float **dst, const float *src, size_t n, bool gain = false) {
+        float *p = nullptr;
+        wc_status st = alloc(&p, n);
+        if (st != WC_OK) return st;
+        std::vector<float> tmp(src, src + n);
+        if (gain)
+            for (auto &x : tmp) x = 1.0f + x;  // norm.go:22 NewZCRMSNorm
+        WB_CUDA(cudaMemcpy(p, tmp.data(), n * sizeof(float), cudaMemcpyHostToDevice));
+        *dst = p;
+        return WC_OK;
+    }
+    wc_status view(const wc_cq *h, wc_cq **out) {
+        wc_status st = wc_cq_rows(h, 0, wc_cq_out(h), out);
+        if (st == WC_OK) views.push_back(*out);
+        return st;
+    }
+};
+
+namespace {
+
+std::string fmt(const char *f, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, f);
+    vsnprintf(buf, sizeof buf, f, ap);
+    va_end(ap);
+    return buf;
+}
+
+float sigmoid_host(float x) { return (float)(1.0 / (1.0 + std::exp(-(double)x))); }
+
+wc_status check_matrix(const wc_cq *m, const char *what, int layer, int out, int in) {
+    if (!m) return set_error(WC_ERR_INVALID, fmt("decoder: layer %d %s: nil matrix", layer, what));
+    if (wc_cq_out(m) != out || wc_cq_in(m) != in)
+        return set_error(WC_ERR_INVALID, fmt("decoder: layer %d %s has shape (%d, %d), want (%d, %d)", layer, what,
+                                             wc_cq_out(m), wc_cq_in(m), out, in));
+    return WC_OK;
+}
+
+// The products of one GEMMs call.
+wc_status gemms(wc_decoder *d, std::initializer_list<const wc_cq *> ms, const float *x,
+                std::initializer_list<float *> ys, int rows, cudaStream_t st) {
+    std::vector<const wc_cq *> m(ms);
+    std::vector<float *> y(ys);
+    return gemms_device(m.data(), (int)m.size(), x, y.data(), rows, d->tc, d->tcbuf, d->tcbytes, st);
+}
+
+#define DEC_LAUNCH(...)                                                 \
+    do {                                                                \
+        __VA_ARGS__;                                                    \
+        count_launch();                                                 \
+        cudaError_t e_ = cudaGetLastError();                            \
+        if (e_ != cudaSuccess) return cuda_error(e_, "decoder kernel"); \
+    } while (0)
+
+#define DEC_ST(call)                        \
+    do {                                    \
+        wc_status s_ = (call);              \
+        if (s_ != WC_OK) return s_;         \
+    } while (0)
+
+// One decoder step for every stream (decoder.go:252 Extend with one token
+// each, the token in d->tok): up to the logits in d->logits, the position
+// advanced.
+wc_status step_body(wc_decoder *d, cudaStream_t st) {
+    const int S = d->streams;
+    const wc_decoder_desc &D = d->d;
+    // Embedding gather (matrix.go:161 Row), × √dim, into every lane.
+    DEC_ST(wc_cq_row_gather(d->emb, d->tok, S, d->row, nullptr, st));
+    DEC_LAUNCH(embed_kernel<<<S, kThreads, 0, st>>>(d->row, d->in_scale, d->pos, d->nk_self, d->stream));
+    // Engram keys and values of every site (cache.go:166 Engram.Extend).
+    if (!d->sites.empty()) {
+        DEC_LAUNCH(engram_rows_kernel<<<S, 32, 0, st>>>(d->tok, d->tokhist, d->ring_t, d->pos, d->orders, D.n_tables,
+                                                        D.slots, d->erows));
+        for (size_t i = 0; i < d->sites.size(); i++) {
+            const auto &site = d->sites[i];
+            DEC_ST(wc_cq_row_gather(site.tables, d->erows, S * D.n_tables, d->erow, nullptr, st));
+            float *ek = d->ek + i * (size_t)S * kD, *ev = d->ev + i * (size_t)S * kD;
+            DEC_ST(gemms(d, {site.key, site.value}, d->erow, {ek, d->vraw}, S, st));
+            const int R = (D.etaps - 1) * (D.n_tables > 0 ? d->ring_t + 1 : 1);
+            DEC_LAUNCH(engram_taps_kernel<<<S, kThreads, 0, st>>>(
+                d->vraw, d->evring + i * (size_t)S * (R > 0 ? R : 1) * kD, site.taps, D.etaps, d->ring_t + 1, d->pos,
+                ev));
+        }
+    }
+    const int qw = D.heads * kQK, kw = D.kv_heads * kQK, vw = D.kv_heads * kVD, W = qw + kw + vw;
+    const int th = D.taps - 1 > 0 ? D.taps - 1 : 1;
+    for (int l = 0; l < D.layers; l++) {
+        auto &L = d->layers[l];
+        int site = -1;
+        for (size_t i = 0; i < d->sites.size(); i++)
+            if (d->sites[i].layer == l) site = (int)i;
+        DEC_LAUNCH(mhc_in_kernel<<<S, kThreads, 0, st>>>(d->stream, d->xq));
+        DEC_ST(gemms(d, {L.ppre, L.ppost, L.pres}, d->xq, {d->phi_pre, d->phi_post, d->phi_res}, S, st));
+        const float *ek = site >= 0 ? d->ek + (size_t)site * S * kD : nullptr;
+        const float *ev = site >= 0 ? d->ev + (size_t)site * S * kD : nullptr;
+        DEC_LAUNCH(mhc_block_in_kernel<<<S, kThreads, 0, st>>>(L.k, d->stream, d->phi_pre, d->phi_post, d->phi_res, ek,
+                                                               ev, d->u, d->h, d->n, d->hp, d->hr));
+        DEC_ST(gemms(d, {L.q, L.kk, L.v, L.g}, d->n, {d->q, d->k, d->v, d->g}, S, st));
+        const size_t cap = (size_t)d->cap;
+        int8_t *k8 = d->k8 + (size_t)l * d->max_streams * cap * kw;
+        int8_t *v8 = d->v8 + (size_t)l * d->max_streams * cap * vw;
+        float *ks = d->ks + (size_t)l * d->max_streams * cap * D.kv_heads;
+        float *vs = d->vs + (size_t)l * d->max_streams * cap * D.kv_heads;
+        DEC_LAUNCH(self_prep_kernel<<<S, kThreads, W * sizeof(float), st>>>(
+            L.k, d->q, d->k, d->v, d->hist + (size_t)l * d->max_streams * th * W, D.taps, D.heads, D.kv_heads, d->pos,
+            d->rcos, d->rsin, k8, ks, v8, vs, d->cap, d->qo));
+        DEC_ST(wc_attend_int8_streams(S, d->qo, D.heads, k8, ks, v8, vs, d->cap, d->nk_self, D.kv_heads, kQK, kVD,
+                                      d->att_scale, WC_ATTEND_QUANT_Q, d->att, st));
+        DEC_LAUNCH(gate_kernel<<<S, kThreads, 0, st>>>(d->att, d->g, D.heads * kVD));
+        DEC_ST(gemms(d, {L.o}, d->att, {d->a}, S, st));
+        DEC_LAUNCH(post_attn_kernel<<<S, kThreads, 0, st>>>(L.k, d->a, d->h, d->x));
+        DEC_ST(gemms(d, {L.xq, L.xg}, d->x, {d->cq, d->cg}, S, st));
+        DEC_LAUNCH(cross_q_kernel<<<S, kThreads, 0, st>>>(L.k, d->cq, D.x_heads, d->cqn));
+        const size_t F = (size_t)d->frames;
+        const size_t xoff = (size_t)l * d->max_streams * d->max_frames;
+        DEC_ST(wc_attend_int8_streams(S, d->cqn, D.x_heads, d->xk8 + xoff * D.x_heads * kQK, d->xks + xoff * D.x_heads,
+                                      d->xv8 + xoff * D.x_heads * kVD, d->xvs + xoff * D.x_heads, (int)F, d->nk_x,
+                                      D.x_heads, kQK, kVD, d->xatt_scale, WC_ATTEND_QUANT_Q, d->catt, st));
+        DEC_LAUNCH(gate_kernel<<<S, kThreads, 0, st>>>(d->catt, d->cg, D.x_heads * kVD));
+        DEC_ST(gemms(d, {L.xo}, d->catt, {d->cy}, S, st));
+        DEC_LAUNCH(block_out_kernel<<<S, kThreads, 0, st>>>(L.k, d->p1, d->p2, d->cy, d->h, d->u, d->hp, d->hr,
+                                                            d->stream));
+    }
+    DEC_LAUNCH(final_kernel<<<S, kThreads, 0, st>>>(d->stream, d->g_final, d->fin));
+    DEC_ST(gemms(d, {d->emb}, d->fin, {d->logits}, S, st));
+    DEC_LAUNCH(advance_kernel<<<(S + 127) / 128, 128, 0, st>>>(d->tok, d->tokhist, d->ring_t, d->pos, S));
+    return WC_OK;
+}
+
+// The step, replayed from a CUDA graph captured on first use (per stream
+// count), or launched eagerly.
+wc_status run_step(wc_decoder *d, cudaStream_t st) {
+    if (d->len >= d->cap || d->len >= d->d.rope_len)
+        return set_error(WC_ERR_INVALID, fmt("decoder: %d positions exceed the cache's %d or the RoPE tables' %d",
+                                             d->len + 1, d->cap, d->d.rope_len));
+    if (d->flags & WC_DECODER_NO_GRAPH) {
+        DEC_ST(step_body(d, st));
+        d->len++;
+        return WC_OK;
+    }
+    if (!d->graph || d->graph_streams != d->streams) {
+        if (d->graph) {
+            cudaGraphExecDestroy(d->graph);
+            d->graph = nullptr;
+        }
+        // The first step runs eagerly: it sets kernel attributes and the
+        // library's one-time device words outside any capture.
+        if (d->len == 0 && d->graph_streams != -d->streams) {
+            d->graph_streams = -d->streams;
+            DEC_ST(step_body(d, st));
+            d->len++;
+            return WC_OK;
+        }
+        cudaStream_t cs = nullptr;
+        WB_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+        cudaGraph_t g = nullptr;
+        WB_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+        wc_status s = step_body(d, cs);
+        cudaError_t e = cudaStreamEndCapture(cs, &g);
+        if (s == WC_OK && e == cudaSuccess) e = cudaGraphInstantiate(&d->graph, g, 0);
+        if (g) cudaGraphDestroy(g);
+        cudaStreamDestroy(cs);
+        if (s != WC_OK) return s;
+        if (e != cudaSuccess) return cuda_error(e, "decoder step graph");
+        d->graph_streams = d->streams;
+    }
+    WB_CUDA(cudaGraphLaunch(d->graph, st));
+    count_launch();
+    d->len++;
+    return WC_OK;
+}
+
+}  // namespace
+
+extern "C" wc_status wc_decoder_create(const wc_decoder_desc *desc, int max_streams, int max_frames, int max_positions,
+                                       int flags, wc_decoder **out) {
+    if (!out) return set_error(WC_ERR_INVALID, "decoder: nil handle pointer");
+    *out = nullptr;
+    if (!desc) return set_error(WC_ERR_INVALID, "decoder: nil description");
+    const wc_decoder_desc &D = *desc;
+    if (D.dim != kD || D.lanes != kLanes || D.qk != kQK || D.vd != kVD || D.x_qk != kQK || D.x_vd != kVD ||
+        D.na != kNA || D.nb != kNB || D.rank != kRank)
+        return set_error(WC_ERR_UNSUPPORTED,
+                         fmt("decoder: this build's kernels take width 512 in 4 lanes, heads of 48/64 and a 16 x 32 "
+                             "HadamardMLP of rank 8 (got width %d, %d lanes, heads %d/%d, cross %d/%d, %d x %d rank %d)",
+                             D.dim, D.lanes, D.qk, D.vd, D.x_qk, D.x_vd, D.na, D.nb, D.rank));
+    if (D.layers <= 0 || D.vocab <= 0 || D.heads <= 0 || D.kv_heads <= 0 || D.heads % D.kv_heads != 0 ||
+        D.taps < 1 || D.x_heads <= 0 || D.heads * kVD > 4 * kThreads)
+        return set_error(WC_ERR_INVALID, fmt("decoder: %d layers, vocab %d, %d query heads over %d KV heads, %d taps",
+                                             D.layers, D.vocab, D.heads, D.kv_heads, D.taps));
+    if (D.heads * kVD != kD || D.x_heads * kVD != kD)
+        return set_error(WC_ERR_UNSUPPORTED, "decoder: the attention outputs must be as wide as the model (heads·64 = 512)");
+    if (max_streams <= 0 || max_streams > 65535 || max_frames <= 0 || max_positions <= 0)
+        return set_error(WC_ERR_INVALID, fmt("decoder: room for %d streams, %d frames, %d positions", max_streams,
+                                             max_frames, max_positions));
+    if (D.n_sites < 0 || (D.n_sites > 0 && (!D.site || !D.orders || D.n_tables <= 0 || D.n_tables > 32 ||
+                                            D.slots <= 0 || D.etaps < 1 || D.n_tables * D.sub != kD)))
+        return set_error(WC_ERR_INVALID, fmt("decoder: %d engram sites of %d tables x %d slots x %d", D.n_sites,
+                                             D.n_tables, D.slots, D.sub));
+    if (!D.layer || !D.embedding || !D.final_norm || !D.hada_p1 || !D.hada_p2 || D.rope_len <= 0)
+        return set_error(WC_ERR_INVALID, "decoder: nil tensor");
+
+    std::unique_ptr<wc_decoder> d(new (std::nothrow) wc_decoder);
+    if (!d) return set_error(WC_ERR_NOMEM, "decoder: out of host memory");
+    WB_CUDA(cudaGetDevice(&d->device));
+    d->d = D;
+    d->d.layer = nullptr;
+    d->d.site = nullptr;
+    d->d.orders = d->d.hada_p1 = d->d.hada_p2 = nullptr;
+    d->d.final_norm = nullptr;
+    d->d.embedding = nullptr;
+    d->max_streams = max_streams;
+    d->max_frames = max_frames;
+    d->cap = (max_positions + 1) & ~1;  // an even row count keeps the bulk attention's scale chunks aligned
+    d->flags = flags;
+    d->tc = (flags & WC_DECODER_TENSOR_CORES) != 0;
+    const int qw = D.heads * kQK, kw = D.kv_heads * kQK, vw = D.kv_heads * kVD;
+    const int xqw = D.x_heads * kQK, xvw = D.x_heads * kVD;
+
+    // Matrices.
+    if (wc_cq_out(D.embedding) != D.vocab || wc_cq_in(D.embedding) != kD)
+        return set_error(WC_ERR_INVALID, fmt("decoder: embedding has shape (%d, %d), want (%d, %d)",
+                                             wc_cq_out(D.embedding), wc_cq_in(D.embedding), D.vocab, kD));
+    DEC_ST(d->view(D.embedding, &d->emb));
+    for (int l = 0; l < D.layers; l++) {
+        const wc_decoder_layer &S = D.layer[l];
+        DEC_ST(check_matrix(S.q_proj, "q_proj", l, qw, kD));
+        DEC_ST(check_matrix(S.k_proj, "k_proj", l, kw, kD));
+        DEC_ST(check_matrix(S.v_proj, "v_proj", l, vw, kD));
+        DEC_ST(check_matrix(S.gate_proj, "gate_proj", l, D.heads * kVD, kD));
+        DEC_ST(check_matrix(S.out_proj, "out_proj", l, kD, D.heads * kVD));
+        DEC_ST(check_matrix(S.x_q_proj, "cross q_proj", l, xqw, kD));
+        DEC_ST(check_matrix(S.x_k_proj, "cross k_proj", l, xqw, kD));
+        DEC_ST(check_matrix(S.x_v_proj, "cross v_proj", l, xvw, kD));
+        DEC_ST(check_matrix(S.x_gate_proj, "cross gate_proj", l, xvw, kD));
+        DEC_ST(check_matrix(S.x_out_proj, "cross out_proj", l, kD, xvw));
+        DEC_ST(check_matrix(S.phi_pre, "mhc_phi_pre", l, kLanes, kLanes * kD));
+        DEC_ST(check_matrix(S.phi_post, "mhc_phi_post", l, kLanes, kLanes * kD));
+        DEC_ST(check_matrix(S.phi_res, "mhc_phi_res", l, kLanes * kLanes, kLanes * kD));
+        const float *vecs[] = {S.norm_in, S.post_norm, S.pre_hada, S.q_taps, S.k_taps, S.v_taps, S.q_norm, S.k_norm,
+                               S.d1, S.d2, S.b2, S.d3, S.d4, S.w1a, S.w1b, S.w2a, S.w2b, S.w3a, S.w3b, S.cond_v,
+                               S.cond_u, S.x_norm_in, S.x_post_norm, S.x_q_norm, S.x_k_norm, S.b_pre, S.b_post,
+                               S.b_res};
+        for (const float *p : vecs)
+            if (!p) return set_error(WC_ERR_INVALID, fmt("decoder: layer %d: nil tensor", l));
+        wc_decoder::Layer L{};
+        DEC_ST(d->view(S.q_proj, &L.q));
+        DEC_ST(d->view(S.k_proj, &L.kk));
+        DEC_ST(d->view(S.v_proj, &L.v));
+        DEC_ST(d->view(S.gate_proj, &L.g));
+        DEC_ST(d->view(S.out_proj, &L.o));
+        DEC_ST(d->view(S.x_q_proj, &L.xq));
+        DEC_ST(d->view(S.x_k_proj, &L.xk));
+        DEC_ST(d->view(S.x_v_proj, &L.xv));
+        DEC_ST(d->view(S.x_gate_proj, &L.xg));
+        DEC_ST(d->view(S.x_out_proj, &L.xo));
+        DEC_ST(d->view(S.phi_pre, &L.ppre));
+        DEC_ST(d->view(S.phi_post, &L.ppost));
+        DEC_ST(d->view(S.phi_res, &L.pres));
+        LayerK &K = L.k;
+        const int nn = kNA * kNB;
+        DEC_ST(d->upload(&K.g_norm_in, S.norm_in, kD, true));
+        DEC_ST(d->upload(&K.g_post, S.post_norm, kD, true));
+        DEC_ST(d->upload(&K.g_pre_hada, S.pre_hada, kD, true));
+        DEC_ST(d->upload(&K.q_taps, S.q_taps, (size_t)D.taps * qw));
+        DEC_ST(d->upload(&K.k_taps, S.k_taps, (size_t)D.taps * kw));
+        DEC_ST(d->upload(&K.v_taps, S.v_taps, (size_t)D.taps * vw));
+        DEC_ST(d->upload(&K.g_qn, S.q_norm, kQK, true));
+        DEC_ST(d->upload(&K.g_kn, S.k_norm, kQK, true));
+        DEC_ST(d->upload(&K.d1, S.d1, nn));
+        DEC_ST(d->upload(&K.d2, S.d2, nn));
+        DEC_ST(d->upload(&K.b2, S.b2, nn));
+        DEC_ST(d->upload(&K.d3, S.d3, nn));
+        DEC_ST(d->upload(&K.d4, S.d4, nn));
+        const float *wa[3] = {S.w1a, S.w2a, S.w3a}, *wbb[3] = {S.w1b, S.w2b, S.w3b};
+        for (int i = 0; i < 3; i++) {
+            DEC_ST(d->upload(&K.wa[i], wa[i], kNA * kNA));
+            DEC_ST(d->upload(&K.wb[i], wbb[i], kNB * kNB));
+        }
+        DEC_ST(d->upload(&K.cond_v, S.cond_v, (size_t)kD * kRank));
+        DEC_ST(d->upload(&K.cond_u, S.cond_u, (size_t)kRank * nn));
+        DEC_ST(d->upload(&K.g_xn, S.x_norm_in, kD, true));
+        DEC_ST(d->upload(&K.g_xpost, S.x_post_norm, kD, true));
+        DEC_ST(d->upload(&K.g_xqn, S.x_q_norm, kQK, true));
+        DEC_ST(d->upload(&K.g_xkn, S.x_k_norm, kQK, true));
+        DEC_ST(d->upload(&K.b_pre, S.b_pre, kLanes));
+        DEC_ST(d->upload(&K.b_post, S.b_post, kLanes));
+        DEC_ST(d->upload(&K.b_res, S.b_res, kLanes * kLanes));
+        K.gate = sigmoid_host(S.attn_gate);
+        K.xresid = sigmoid_host(S.x_attn_gate);
+        K.a_pre = S.a_pre;
+        K.a_post = S.a_post;
+        K.a_res = S.a_res;
+        K.lane = l % kLanes;
+        d->layers.push_back(L);
+    }
+    for (int i = 0; i < D.n_sites; i++) {
+        const wc_engram_site &S = D.site[i];
+        if (S.layer < 0 || S.layer >= D.layers || !S.taps)
+            return set_error(WC_ERR_INVALID, fmt("decoder: engram site %d at layer %d", i, S.layer));
+        if (!S.tables || wc_cq_out(S.tables) != D.n_tables * D.slots || wc_cq_in(S.tables) != D.sub)
+            return set_error(WC_ERR_INVALID, fmt("decoder: engram site %d tables: want (%d, %d)", i,
+                                                 D.n_tables * D.slots, D.sub));
+        if (!S.key_proj || wc_cq_out(S.key_proj) != kD || wc_cq_in(S.key_proj) != kD || !S.value_proj ||
+            wc_cq_out(S.value_proj) != kD || wc_cq_in(S.value_proj) != kD)
+            return set_error(WC_ERR_INVALID, fmt("decoder: engram site %d projections: want (%d, %d)", i, kD, kD));
+        wc_decoder::Site st{};
+        DEC_ST(d->view(S.tables, &st.tables));
+        DEC_ST(d->view(S.key_proj, &st.key));
+        DEC_ST(d->view(S.value_proj, &st.value));
+        DEC_ST(d->upload(&st.taps, S.taps, (size_t)D.etaps * kD));
+        st.layer = S.layer;
+        d->sites.push_back(st);
+    }
+    int max_order = 1;
+    if (D.n_sites > 0) {
+        for (int c = 0; c < D.n_tables; c++) {
+            if (D.orders[c] < 1) return set_error(WC_ERR_INVALID, fmt("decoder: engram order %d", D.orders[c]));
+            max_order = std::max(max_order, (int)D.orders[c]);
+        }
+        int32_t *o = nullptr;
+        DEC_ST(d->alloc(&o, D.n_tables));
+        WB_CUDA(cudaMemcpy(o, D.orders, D.n_tables * sizeof(int32_t), cudaMemcpyHostToDevice));
+        d->orders = o;
+    }
+    d->ring_t = max_order - 1;
+    d->d.etaps = D.etaps;
+    {
+        std::vector<int> seen(kNA * kNB, 0);
+        for (const int32_t *pp : {D.hada_p1, D.hada_p2}) {
+            std::fill(seen.begin(), seen.end(), 0);
+            for (int i = 0; i < kNA * kNB; i++) {
+                if (pp[i] < 0 || pp[i] >= kNA * kNB || seen[pp[i]])
+                    return set_error(WC_ERR_INVALID, fmt("needle: hada_p is not a permutation of %d (entry %d = %d)",
+                                                         kNA * kNB, i, pp[i]));
+                seen[pp[i]] = 1;
+            }
+        }
+        int32_t *p = nullptr;
+        DEC_ST(d->alloc(&p, 2 * kNA * kNB));
+        WB_CUDA(cudaMemcpy(p, D.hada_p1, kNA * kNB * sizeof(int32_t), cudaMemcpyHostToDevice));
+        WB_CUDA(cudaMemcpy(p + kNA * kNB, D.hada_p2, kNA * kNB * sizeof(int32_t), cudaMemcpyHostToDevice));
+        d->p1 = p;
+        d->p2 = p + kNA * kNB;
+    }
+    DEC_ST(d->upload(&d->g_final, D.final_norm, kD, true));
+    // rope.go:20 NewRope, in the same float32 steps (the host's libm).
+    {
+        const int half = kQK / 2;
+        std::vector<float> freqs(half), c((size_t)D.rope_len * half), s((size_t)D.rope_len * half);
+        for (int i = 0; i < half; i++) {
+            const float e = (float)(2 * i) / (float)kQK;
+            freqs[i] = 1.0f / (float)std::pow(D.rope_theta, (double)e);
+        }
+        for (int t = 0; t < D.rope_len; t++)
+            for (int i = 0; i < half; i++) {
+                const double angle = (double)((float)t * freqs[i]);
+                c[(size_t)t * half + i] = (float)std::cos(angle);
+                s[(size_t)t * half + i] = (float)std::sin(angle);
+            }
+        DEC_ST(d->upload(&d->rcos, c.data(), c.size()));
+        DEC_ST(d->upload(&d->rsin, s.data(), s.size()));
+    }
+    d->in_scale = (float)std::sqrt((double)kD);    // decoder.go:313 ScaleSqrtDim
+    d->att_scale = (float)std::sqrt((double)kQK);  // attention.go:407 attendScale
+    d->xatt_scale = (float)std::sqrt((double)kQK); // cross.go:276
+
+    // State and step buffers.
+    const size_t S = (size_t)max_streams, cap = (size_t)d->cap, F = (size_t)max_frames, L = (size_t)D.layers;
+    const int th = D.taps - 1 > 0 ? D.taps - 1 : 1;
+    const int W = qw + kw + vw;
+    DEC_ST(d->alloc(&d->stream, S * kLanes * kD));
+    DEC_ST(d->alloc(&d->xq, S * kLanes * kD));
+    DEC_ST(d->alloc(&d->phi_pre, S * kLanes));
+    DEC_ST(d->alloc(&d->phi_post, S * kLanes));
+    DEC_ST(d->alloc(&d->phi_res, S * kLanes * kLanes));
+    for (float **p : {&d->u, &d->h, &d->n, &d->att, &d->a, &d->x, &d->cg, &d->catt, &d->cy, &d->fin, &d->row,
+                      &d->erow, &d->vraw, &d->g})
+        DEC_ST(d->alloc(p, S * kD));
+    DEC_ST(d->alloc(&d->hp, S * kLanes));
+    DEC_ST(d->alloc(&d->hr, S * kLanes * kLanes));
+    DEC_ST(d->alloc(&d->q, S * qw));
+    DEC_ST(d->alloc(&d->qo, S * qw));
+    DEC_ST(d->alloc(&d->k, S * kw));
+    DEC_ST(d->alloc(&d->v, S * vw));
+    DEC_ST(d->alloc(&d->cq, S * xqw));
+    DEC_ST(d->alloc(&d->cqn, S * xqw));
+    DEC_ST(d->alloc(&d->logits, S * D.vocab));
+    const size_t sites = D.n_sites > 0 ? D.n_sites : 1;
+    DEC_ST(d->alloc(&d->ek, sites * S * kD));
+    DEC_ST(d->alloc(&d->ev, sites * S * kD));
+    const int R = (D.etaps - 1) * max_order;
+    DEC_ST(d->alloc(&d->evring, sites * S * (R > 0 ? R : 1) * kD));
+    DEC_ST(d->alloc(&d->hist, L * S * th * W));
+    DEC_ST(d->alloc(&d->tok, S));
+    DEC_ST(d->alloc(&d->pos, S));
+    DEC_ST(d->alloc(&d->nk_self, S));
+    DEC_ST(d->alloc(&d->nk_x, S));
+    DEC_ST(d->alloc(&d->done, S));
+    DEC_ST(d->alloc(&d->langs, 64));
+    DEC_ST(d->alloc(&d->erows, S * (D.n_tables > 0 ? D.n_tables : 1)));
+    DEC_ST(d->alloc(&d->tokhist, S * (d->ring_t > 0 ? d->ring_t : 1)));
+    DEC_ST(d->alloc(&d->k8, L * S * cap * kw));
+    DEC_ST(d->alloc(&d->v8, L * S * cap * vw));
+    DEC_ST(d->alloc(&d->ks, L * S * cap * D.kv_heads));
+    DEC_ST(d->alloc(&d->vs, L * S * cap * D.kv_heads));
+    DEC_ST(d->alloc(&d->xk8, L * S * F * xqw));
+    DEC_ST(d->alloc(&d->xv8, L * S * F * xvw));
+    DEC_ST(d->alloc(&d->xks, L * S * F * D.x_heads));
+    DEC_ST(d->alloc(&d->xvs, L * S * F * D.x_heads));
+    DEC_ST(d->alloc(&d->mk, S * F * xqw));
+    DEC_ST(d->alloc(&d->mv, S * F * xvw));
+    if (d->tc) {
+        // The largest rotated image any product needs: S·F rows at 512 in
+        // (the memory), S rows at 2048 in (φ).
+        const size_t a = tc_a_bytes((int)(S * F), (kD + 63) / 64), b = tc_a_bytes((int)S, (kLanes * kD + 63) / 64);
+        d->tcbytes = std::max(a, b);
+        unsigned char *p = nullptr;
+        DEC_ST(d->alloc(&p, d->tcbytes));
+        d->tcbuf = p;
+        for (auto &L2 : d->layers)
+            for (wc_cq *m : {L2.q, L2.kk, L2.v, L2.g, L2.o, L2.xq, L2.xk, L2.xv, L2.xg, L2.xo, L2.ppre, L2.ppost,
+                             L2.pres})
+                DEC_ST(wc_cq_prepare_tc(m));
+        for (auto &st : d->sites) {
+            DEC_ST(wc_cq_prepare_tc(st.key));
+            DEC_ST(wc_cq_prepare_tc(st.value));
+        }
+        DEC_ST(wc_cq_prepare_tc(d->emb));
+    }
+    if (!err_word()) return set_error(WC_ERR_NOMEM, "cuda: error word");
+    WB_CUDA(cudaDeviceSynchronize());
+    *out = d.release();
+    return WC_OK;
+}
+
+extern "C" void wc_decoder_destroy(wc_decoder *d) { delete d; }
+
+extern "C" int wc_decoder_len(const wc_decoder *d) { return d ? d->len : 0; }
+
+static wc_status dec_check(const wc_decoder *d) {
+    if (!d) return set_error(WC_ERR_INVALID, "decoder: nil decoder");
+    int dev = 0;
+    WB_CUDA(cudaGetDevice(&dev));
+    if (dev != d->device)
+        return set_error(WC_ERR_DEVICE, fmt("decoder: created on device %d, called on device %d", d->device, dev));
+    return WC_OK;
+}
+
+extern "C" wc_status wc_decoder_memory(wc_decoder *d, const float *enc, int streams, int frames, wc_stream stream) {
+    DEC_ST(dec_check(d));
+    if (streams <= 0 || streams > d->max_streams || frames <= 0 || frames > d->max_frames || !enc)
+        return set_error(WC_ERR_INVALID, fmt("decoder: encoder output of %d streams x %d frames (room for %d x %d)",
+                                             streams, frames, d->max_streams, d->max_frames));
+    cudaStream_t st = (cudaStream_t)stream;
+    const wc_decoder_desc &D = d->d;
+    const size_t rows = (size_t)streams * frames;
+    if (rows > (size_t)INT32_MAX) return set_error(WC_ERR_INVALID, "decoder: memory too large");
+    for (int l = 0; l < D.layers; l++) {
+        auto &L = d->layers[l];
+        DEC_ST(gemms(d, {L.xk, L.xv}, enc, {d->mk, d->mv}, (int)rows, st));
+        const size_t xoff = (size_t)l * d->max_streams * d->max_frames;
+        // Memory rows of stream b start at b·frames (cap = frames for the
+        // attention), so the layer's block is contiguous.
+        DEC_LAUNCH(xmem_kernel<<<(unsigned)rows, 256, 0, st>>>(d->mk, d->mv, L.k.g_xkn, D.x_heads,
+                                                               d->xk8 + xoff * D.x_heads * kQK, d->xks + xoff * D.x_heads,
+                                                               d->xv8 + xoff * D.x_heads * kVD,
+                                                               d->xvs + xoff * D.x_heads));
+    }
+    DEC_LAUNCH(fill_kernel<<<(streams + 255) / 256, 256, 0, st>>>(d->nk_x, frames, streams));
+    DEC_LAUNCH(fill_kernel<<<(streams + 255) / 256, 256, 0, st>>>(d->pos, 0, streams));
+    if (d->streams != streams || d->frames != frames) {
+        if (d->graph) cudaGraphExecDestroy(d->graph);
+        d->graph = nullptr;
+        d->graph_streams = 0;
+    }
+    d->streams = streams;
+    d->frames = frames;
+    d->len = 0;
+    return WC_OK;
+}
+
+extern "C" wc_status wc_decoder_memory_of(const wc_decoder *d, int l, const int8_t **k8, const float **ks,
+                                          const int8_t **v8, const float **vs) {
+    DEC_ST(dec_check(d));
+    if (l < 0 || l >= d->d.layers || !k8 || !ks || !v8 || !vs)
+        return set_error(WC_ERR_INVALID, fmt("decoder: memory of layer %d", l));
+    const size_t xoff = (size_t)l * d->max_streams * d->max_frames;
+    *k8 = d->xk8 + xoff * d->d.x_heads * kQK;
+    *ks = d->xks + xoff * d->d.x_heads;
+    *v8 = d->xv8 + xoff * d->d.x_heads * kVD;
+    *vs = d->xvs + xoff * d->d.x_heads;
+    return WC_OK;
+}
+
+extern "C" wc_status wc_decoder_extend(wc_decoder *d, const int32_t *tokens, float *logits, int32_t *next,
+                                       wc_stream stream) {
+    DEC_ST(dec_check(d));
+    if (d->streams == 0) return set_error(WC_ERR_INVALID, "decoder: no memory (call wc_decoder_memory first)");
+    if (!tokens) return set_error(WC_ERR_INVALID, "decoder: nil tokens");
+    cudaStream_t st = (cudaStream_t)stream;
+    const int S = d->streams;
+    WB_CUDA(cudaMemcpyAsync(d->tok, tokens, S * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
+    DEC_ST(run_step(d, st));
+    if (logits)
+        WB_CUDA(cudaMemcpyAsync(logits, d->logits, (size_t)S * d->d.vocab * sizeof(float), cudaMemcpyDeviceToDevice,
+                                st));
+    if (next) {
+        cudaError_t e = launch_head_argmax(d->logits, S, d->d.vocab, 1.0f, nullptr, next, st);
+        if (e != cudaSuccess) return cuda_error(e, "decoder argmax");
+    }
+    return WC_OK;
+}
+
+extern "C" wc_status wc_decoder_greedy(wc_decoder *d, int bos, const int32_t *langs, int n_langs, int eos,
+                                       int max_tokens, int32_t *tokens, int32_t *counts, int32_t *lang,
+                                       int32_t *eos_hit, wc_stream stream) {
+    DEC_ST(dec_check(d));
+    if (d->streams == 0) return set_error(WC_ERR_INVALID, "decoder: no memory (call wc_decoder_memory first)");
+    if (!langs || n_langs <= 0 || n_langs > 64 || max_tokens < 1 || !tokens || !counts || !lang || !eos_hit)
+        return set_error(WC_ERR_INVALID, fmt("decoder: greedy with %d languages and %d tokens", n_langs, max_tokens));
+    const wc_decoder_desc &D = d->d;
+    if (bos < 0 || bos >= D.vocab || eos < 0 || eos >= D.vocab)
+        return set_error(WC_ERR_INVALID, fmt("decoder: token %d out of range [0, %d)", bos < 0 || bos >= D.vocab ? bos : eos,
+                                             D.vocab));
+    for (int i = 0; i < n_langs; i++)
+        if (langs[i] < 0 || langs[i] >= D.vocab)
+            return set_error(WC_ERR_INVALID, fmt("decoder: token %d out of range [0, %d)", langs[i], D.vocab));
+    if (d->len + max_tokens > d->cap || d->len + max_tokens > D.rope_len)
+        return set_error(WC_ERR_INVALID, fmt("decoder: %d positions exceed the cache's %d or the RoPE tables' %d",
+                                             d->len + max_tokens, d->cap, D.rope_len));
+    cudaStream_t st = (cudaStream_t)stream;
+    const int S = d->streams, out_w = max_tokens > 1 ? max_tokens - 1 : 1;
+    // The language ids: a small device copy (the stream orders it before
+    // the kernel that reads it; the host array may be reused after return
+    // only once the stream has reached the copy, so copy from a staging
+    // array the decoder owns).
+    std::memcpy(d->langs_host, langs, n_langs * sizeof(int32_t));
+    WB_CUDA(cudaMemcpyAsync(d->langs, d->langs_host, n_langs * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    int32_t *dl = d->langs;
+    DEC_LAUNCH(greedy_init_kernel<<<S, 128, 0, st>>>(d->tok, bos, tokens, out_w, counts, eos_hit, d->done, S));
+    DEC_ST(run_step(d, st));
+    DEC_LAUNCH(lang_kernel<<<(S + 127) / 128, 128, 0, st>>>(d->logits, D.vocab, dl, n_langs, d->tok, lang, S));
+    for (int step = 0; step < max_tokens - 1; step++) {
+        DEC_ST(run_step(d, st));
+        cudaError_t e = launch_head_argmax(d->logits, S, D.vocab, 1.0f, nullptr, d->tok, st);
+        if (e != cudaSuccess) return cuda_error(e, "decoder argmax");
+        DEC_LAUNCH(record_kernel<<<(S + 127) / 128, 128, 0, st>>>(d->tok, eos, out_w, tokens, counts, eos_hit, d->done,
+                                                                  S));
+    }
+    return WC_OK;
+}

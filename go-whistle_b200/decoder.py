@@ -10,7 +10,7 @@ import ctypes
 
 from ._lib import Panic, WC_ERR_INVALID, check, lib
 
-__all__ = ["HeadArgmax"]
+__all__ = ["HeadArgmax", "Decoder"]
 
 
 def HeadArgmax(y, rows: int, vocab: int, head: float = 1.0, logits=None, idx=None):
@@ -36,3 +36,173 @@ def HeadArgmax(y, rows: int, vocab: int, head: float = 1.0, logits=None, idx=Non
                                ctypes.c_void_p(logits.data_ptr()) if logits is not None else None,
                                ctypes.c_void_p(idx.data_ptr()), stream))
     return idx
+
+
+# ------------------------------------------------------------------ Decoder
+#
+# internal/decoder's Decoder (decoder.go:25) on the device: Load builds it
+# from a weight set, Memory projects the encoder output (decoder.go:157),
+# Extend feeds one token per stream (decoder.go:252), GreedyMemory runs
+# greedy.go:40 for every stream without leaving the device.
+
+_f32p = ctypes.c_void_p
+
+
+class _Layer(ctypes.Structure):
+    """wc_decoder_layer (include/whistle_b200.h)."""
+    _fields_ = ([(k, _f32p) for k in ("norm_in", "post_norm", "pre_hada")] + [("attn_gate", ctypes.c_float)]
+                + [(k, ctypes.c_void_p) for k in ("q_proj", "k_proj", "v_proj", "gate_proj", "out_proj")]
+                + [(k, _f32p) for k in ("q_taps", "k_taps", "v_taps", "q_norm", "k_norm", "d1", "d2", "b2", "d3",
+                                        "d4", "w1a", "w1b", "w2a", "w2b", "w3a", "w3b", "cond_v", "cond_u",
+                                        "x_norm_in", "x_post_norm", "x_q_norm", "x_k_norm")]
+                + [("x_attn_gate", ctypes.c_float)]
+                + [(k, ctypes.c_void_p) for k in ("x_q_proj", "x_k_proj", "x_v_proj", "x_gate_proj", "x_out_proj")]
+                + [(k, ctypes.c_float) for k in ("a_pre", "a_post", "a_res")]
+                + [(k, _f32p) for k in ("b_pre", "b_post", "b_res")]
+                + [(k, ctypes.c_void_p) for k in ("phi_pre", "phi_post", "phi_res")])
+
+
+class _Site(ctypes.Structure):
+    _fields_ = [("tables", ctypes.c_void_p), ("key_proj", ctypes.c_void_p), ("value_proj", ctypes.c_void_p),
+                ("taps", _f32p), ("layer", ctypes.c_int)]
+
+
+class _Desc(ctypes.Structure):
+    _fields_ = ([(k, ctypes.c_int) for k in ("dim", "lanes", "layers", "vocab", "heads", "kv_heads", "qk", "vd",
+                                             "taps", "x_heads", "x_qk", "x_vd", "na", "nb", "rank", "n_sites",
+                                             "n_tables", "slots", "sub", "etaps")]
+                + [("orders", ctypes.c_void_p), ("hada_p1", ctypes.c_void_p), ("hada_p2", ctypes.c_void_p),
+                   ("rope_theta", ctypes.c_double), ("rope_len", ctypes.c_int), ("embedding", ctypes.c_void_p),
+                   ("final_norm", _f32p), ("layer", ctypes.POINTER(_Layer)), ("site", ctypes.POINTER(_Site))])
+
+
+WC_DECODER_TENSOR_CORES = 1
+WC_DECODER_NO_GRAPH = 2
+
+
+class Decoder:
+    """Whistle's decoder (decoder.go:25) with int8 numerics on the GPU, for
+    up to ``max_streams`` independent streams.
+
+    ``w`` is a weight set with the attributes of ``synth.DecoderWeights``
+    (CQ tensors as ``cq.Packed``, float tensors as arrays); the CQ tensors
+    are uploaded once here (cq.New), the float tensors copied by the
+    library. flags: ``WC_DECODER_TENSOR_CORES``, ``WC_DECODER_NO_GRAPH``.
+    """
+
+    def __init__(self, w, max_streams: int, max_frames: int = 375, max_positions: int = 80, flags: int = 0):
+        import numpy as np
+
+        from . import cq
+
+        self.w, self.flags = w, flags
+        self._keep = []
+
+        def f(a):
+            a = np.ascontiguousarray(a, np.float32).reshape(-1)
+            self._keep.append(a)
+            return a.ctypes.data
+
+        def m(p):
+            mat = cq.New(p)
+            self._keep.append(mat)
+            return mat.handle.value
+
+        def rows(p, lo, hi):
+            mat = cq.New(p) if id(p) not in self._stacked else self._stacked[id(p)]
+            self._stacked[id(p)] = mat
+            v = mat.Rows(lo, hi)
+            self._keep.append(v)
+            return v.handle.value
+
+        self._stacked = {}
+        L = (_Layer * len(w.layers))()
+        for l, src in enumerate(w.layers):
+            d = L[l]
+            for k in ("norm_in", "post_norm", "pre_hada", "q_taps", "k_taps", "v_taps", "q_norm", "k_norm", "d1",
+                      "d2", "b2", "d3", "d4", "w1a", "w1b", "w2a", "w2b", "w3a", "w3b", "cond_v", "cond_u",
+                      "x_norm_in", "x_post_norm", "x_q_norm", "x_k_norm", "b_pre", "b_post", "b_res"):
+                setattr(d, k, f(src[k]))
+            for k in ("attn_gate", "x_attn_gate", "a_pre", "a_post", "a_res"):
+                setattr(d, k, float(src[k]))
+            for k in ("q_proj", "k_proj", "v_proj", "gate_proj", "out_proj", "x_q_proj", "x_k_proj", "x_v_proj",
+                      "x_gate_proj", "x_out_proj"):
+                setattr(d, k, m(src[k]))
+            for k in ("phi_pre", "phi_post", "phi_res"):
+                lo, hi = w.phi_rows(k, l)
+                setattr(d, k, rows(getattr(w, k), lo, hi))
+        S = (_Site * max(1, len(w.sites)))()
+        for i, src in enumerate(w.sites):
+            S[i].tables, S[i].key_proj, S[i].value_proj = (m(src[k]) for k in ("tables", "key_proj", "value_proj"))
+            S[i].taps = f(src["taps"])
+            S[i].layer = src["layer"]
+        orders = np.ascontiguousarray(w.orders, np.int32)
+        p1, p2 = np.ascontiguousarray(w.hada_p1, np.int32), np.ascontiguousarray(w.hada_p2, np.int32)
+        self._keep += [orders, p1, p2, L, S]
+        desc = _Desc(w.dim, w.lanes, len(w.layers), w.vocab, w.heads, w.kv_heads, w.qk, w.vd, w.taps, w.x_heads,
+                     w.x_qk, w.x_vd, w.na, w.nb, w.rank, len(w.sites), w.n_tables, w.slots, w.sub, w.etaps)
+        desc.orders, desc.hada_p1, desc.hada_p2 = orders.ctypes.data, p1.ctypes.data, p2.ctypes.data
+        desc.rope_theta, desc.rope_len = float(w.rope_theta), int(w.rope_len)
+        desc.embedding = m(w.embedding)
+        desc.final_norm = f(w.final_norm)
+        desc.layer, desc.site = L, S
+        h = ctypes.c_void_p()
+        check(lib().wc_decoder_create(ctypes.byref(desc), max_streams, max_frames, max_positions, flags,
+                                      ctypes.byref(h)))
+        self.handle = h
+        self.streams = 0
+
+    def __del__(self):
+        if getattr(self, "handle", None) and self.handle.value:
+            lib().wc_decoder_destroy(self.handle)
+            self.handle = None
+
+    @staticmethod
+    def _stream():
+        import torch
+
+        return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def Memory(self, enc):
+        """decoder.go:157 Memory + NewState for every stream: enc is a CUDA
+        float32 tensor [streams, frames, dim]."""
+        streams, frames = enc.shape[0], enc.shape[1]
+        check(lib().wc_decoder_memory(self.handle, ctypes.c_void_p(enc.data_ptr()), streams, frames, self._stream()))
+        self.streams = streams
+
+    def memory_of(self, l: int):
+        """Layer l's device memory pointers (k8, ks, v8, vs)."""
+        ps = [ctypes.c_void_p() for _ in range(4)]
+        check(lib().wc_decoder_memory_of(self.handle, l, *[ctypes.byref(p) for p in ps]))
+        return [p.value for p in ps]
+
+    def Extend(self, tokens, logits=None, next_=None):
+        """decoder.go:252 Extend with one token per stream (CUDA int32
+        [streams]); logits (CUDA float32 [streams, vocab]) and next_ (CUDA
+        int32 [streams], the argmax) are filled when given."""
+        check(lib().wc_decoder_extend(self.handle, ctypes.c_void_p(tokens.data_ptr()),
+                                      ctypes.c_void_p(logits.data_ptr()) if logits is not None else None,
+                                      ctypes.c_void_p(next_.data_ptr()) if next_ is not None else None,
+                                      self._stream()))
+
+    def Len(self) -> int:
+        return lib().wc_decoder_len(self.handle)
+
+    def GreedyMemory(self, bos: int, langs, eos: int, max_tokens: int):
+        """greedy.go:40 GreedyMemory for every stream, on the device: returns
+        CUDA tensors (tokens [streams, max_tokens − 1] padded with −1,
+        counts, lang, eos_hit)."""
+        import numpy as np
+        import torch
+
+        S = self.streams
+        out_w = max(1, max_tokens - 1)
+        dev = torch.device("cuda")
+        tokens = torch.empty((S, out_w), dtype=torch.int32, device=dev)
+        counts, lang, eos_hit = (torch.empty(S, dtype=torch.int32, device=dev) for _ in range(3))
+        lg = np.ascontiguousarray(langs, np.int32)
+        check(lib().wc_decoder_greedy(self.handle, int(bos), lg.ctypes.data, lg.size, int(eos), int(max_tokens),
+                                      ctypes.c_void_p(tokens.data_ptr()), ctypes.c_void_p(counts.data_ptr()),
+                                      ctypes.c_void_p(lang.data_ptr()), ctypes.c_void_p(eos_hit.data_ptr()),
+                                      self._stream()))
+        return tokens, counts, lang, eos_hit

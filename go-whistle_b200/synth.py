@@ -73,3 +73,128 @@ def random_kv(rng: np.random.Generator, rows: int, kv_heads: int, width: int):
     q = rng.integers(-127, 128, size=rows * kv_heads * width, dtype=np.int8)
     s = rng.uniform(0.01, 0.05, size=rows * kv_heads).astype(np.float32)
     return q, s
+
+
+# ------------------------------------------------------------------ decoder
+#
+# Whistle's decoder as whistle.cact lays it out (internal/cact/testdata/
+# whistle_names.txt): 8 layers of width 512 in 4 mHC lanes; self-attention
+# 8 query heads / 2 KV heads of 48 (values 64) with 3 causal taps; a gated
+# cross-attention of 8 heads (48 / 64); a HadamardMLP of 16 × 32 Kronecker
+# factors with a rank-8 condition; engram sites at layers 3 and 7 with
+# orders (2, 3) × 2 hashes = 4 tables of 18432 slots × 128; RoPE θ = 1e5.
+# CQ tensors use one codebook per width (the .cact header's cb2/cb4), group
+# 128: CQ4 for the embedding / head and the mHC φ, CQ2 for every other
+# product. Values: CQ rows and float tensors ~N(0, 0.02) in scale, norm
+# gains near 1 (scales ~N(0, 0.02)), as the benchmark configuration asks.
+
+WHISTLE_LANGS = list(range(8192, 8199))  # "<|en|>" … "<|pl|>" (decoder.go:58)
+WHISTLE_BOS, WHISTLE_EOS = 1, 2
+
+
+def _cq_tensor(rng, out, in_, bits, group, cb, rms=0.02):
+    """A CQ tensor whose rows have the given RMS: norms ≈ rms·√G (the
+    codebook holds unit-variance levels over √G), spread ±25 %."""
+    groups = (in_ + group - 1) // group
+    row_bytes = groups * group * bits // 8
+    index = rng.integers(0, 256, size=out * row_bytes, dtype=np.uint8)
+    n = (rms * np.sqrt(group) * rng.uniform(0.8, 1.25, size=out * groups)).astype(np.float16)
+    return Packed(Out=out, In=in_, Group=group, Bits=bits, Width=bits, Codebook=cb, Index=index,
+                  Norms=n.view(np.uint16).astype("<u2").view(np.uint8))
+
+
+class DecoderWeights:
+    """A synthetic Whistle decoder: sizes as attributes, CQ tensors as
+    Packed, float tensors as float32 arrays; per-layer tensors in
+    ``layers[l]`` (dicts keyed by the .cact names without the prefix) and
+    the engram sites in ``sites``."""
+
+    def __init__(self, seed: int = 4000, vocab: int = 16384, layers: int = 8, slots: int = 18432):
+        rng = np.random.default_rng(seed)
+        self.seed = seed
+        self.dim, self.lanes, self.n_layers, self.vocab = 512, 4, layers, vocab
+        self.heads, self.kv_heads, self.qk, self.vd, self.taps = 8, 2, 48, 64, 3
+        self.x_heads, self.x_qk, self.x_vd = 8, 48, 64
+        self.na, self.nb, self.rank = 16, 32, 8
+        self.orders = [2, 2, 3, 3]
+        self.n_tables, self.slots, self.sub, self.etaps = 4, slots, 128, 4
+        self.max_order = 3
+        self.site_layers = [3, 7] if layers > 7 else [min(3, layers - 1)]
+        self.rope_theta, self.rope_len = 1e5, 512
+        G = 128
+        self.cb2, self.cb4 = lloyd_max_codebook(2, G), lloyd_max_codebook(4, G)
+        D, n = self.dim, self.lanes
+
+        def vec(k, mean=0.0, sd=0.02):
+            return (mean + rng.normal(0.0, sd, size=k)).astype(np.float32)
+
+        # The tied embedding at a smaller scale than the other products, so
+        # that the blocks, not the fed token alone, decide the next token.
+        self.embedding = _cq_tensor(rng, vocab, D, 4, G, self.cb4, rms=0.005)
+        self.final_norm = vec(D)
+        self.hada_p1 = rng.permutation(self.na * self.nb).astype(np.int32)
+        self.hada_p2 = rng.permutation(self.na * self.nb).astype(np.int32)
+        # The stacked mHC heads (mhc_*: one row block per layer).
+        self.phi_pre = _cq_tensor(rng, layers * n, n * D, 4, G, self.cb4)
+        self.phi_post = _cq_tensor(rng, layers * n, n * D, 4, G, self.cb4)
+        self.phi_res = _cq_tensor(rng, layers * n * n, n * D, 4, G, self.cb4)
+        self.layers = []
+        for _ in range(layers):
+            L = {}
+            for k in ("norm_in", "post_norm", "pre_hada", "q_norm", "k_norm"):
+                L[k] = vec(self.qk if k in ("q_norm", "k_norm") else D)
+            L["attn_gate"] = float(rng.normal(0.0, 0.5))
+            qw, kw, vw = self.heads * self.qk, self.kv_heads * self.qk, self.kv_heads * self.vd
+            for k, o in (("q_proj", qw), ("k_proj", kw), ("v_proj", vw), ("gate_proj", self.heads * self.vd),
+                         ("out_proj", D)):
+                L[k] = _cq_tensor(rng, o, D if k != "out_proj" else self.heads * self.vd, 2, G, self.cb2)
+            for k, w in (("q_taps", qw), ("k_taps", kw), ("v_taps", vw)):
+                t = rng.normal(0.0, 0.1, size=(self.taps, w)).astype(np.float32)
+                t[0] += 1.0
+                L[k] = t
+            nn_ = self.na * self.nb
+            for k in ("d1", "d2", "d3", "d4"):
+                L[k] = vec(nn_, 1.0)
+            L["b2"] = vec(nn_)
+            for s in range(3):
+                L[f"w{s + 1}a"] = rng.normal(0.0, 1.0 / np.sqrt(self.na), size=(self.na, self.na)).astype(np.float32)
+                L[f"w{s + 1}b"] = rng.normal(0.0, 1.0 / np.sqrt(self.nb), size=(self.nb, self.nb)).astype(np.float32)
+            L["cond_v"] = rng.normal(0.0, 0.02, size=(D, self.rank)).astype(np.float32)
+            L["cond_u"] = rng.normal(0.0, 0.02, size=(self.rank, nn_)).astype(np.float32)
+            # cross-attention (crossNN.*)
+            for k in ("x_norm_in", "x_post_norm"):
+                L[k] = vec(D)
+            for k in ("x_q_norm", "x_k_norm"):
+                L[k] = vec(self.x_qk)
+            L["x_attn_gate"] = float(rng.normal(0.0, 0.5))
+            xq, xv = self.x_heads * self.x_qk, self.x_heads * self.x_vd
+            for k, o, i in (("x_q_proj", xq, D), ("x_k_proj", xq, D), ("x_v_proj", xv, D), ("x_gate_proj", xv, D),
+                            ("x_out_proj", D, xv)):
+                L[k] = _cq_tensor(rng, o, i, 2, G, self.cb2)
+            # this layer's mHC scalars and biases (mhc_a_*, mhc_b_*)
+            L["a_pre"], L["a_post"], L["a_res"] = (float(v) for v in 0.1 + rng.normal(0.0, 0.02, size=3))
+            L["b_pre"], L["b_post"] = vec(n, 0.0, 0.1), vec(n, 0.0, 0.1)
+            L["b_res"] = (2.0 * np.eye(n) + rng.normal(0.0, 0.1, size=(n, n))).astype(np.float32).reshape(-1)
+            self.layers.append(L)
+        self.sites = []
+        for lay in self.site_layers:
+            S = {"layer": lay,
+                 "tables": _cq_tensor(rng, self.n_tables * slots, self.sub, 2, G, self.cb2),
+                 "key_proj": _cq_tensor(rng, D, self.n_tables * self.sub, 2, G, self.cb2),
+                 "value_proj": _cq_tensor(rng, D, self.n_tables * self.sub, 2, G, self.cb2)}
+            t = rng.normal(0.0, 0.1, size=(self.etaps, D)).astype(np.float32)
+            t[0] += 1.0
+            S["taps"] = t
+            self.sites.append(S)
+
+    def phi_rows(self, name: str, l: int):
+        """Layer l's row range of a stacked φ (mhc.go:94-96)."""
+        n = self.lanes
+        per = n * n if name == "phi_res" else n
+        return l * per, (l + 1) * per
+
+
+def encoder_output(rng: np.random.Generator, streams: int, frames: int = 375, dim: int = 512) -> np.ndarray:
+    """Synthetic encoder outputs [streams][frames][dim] (the final-normed
+    memory the decoder reads), ~N(0, 1)."""
+    return rng.normal(0.0, 1.0, size=(streams, frames, dim)).astype(np.float32)

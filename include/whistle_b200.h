@@ -316,6 +316,132 @@ wc_status wc_attend_int8_streams(int streams, const float *q, int heads, const i
                                  const int8_t *v8, const float *vs, int cap, const int32_t *nkeys, int kv_heads,
                                  int qk, int vd, float scale, int flags, float *out, wc_stream stream);
 
+/* ----------------------------------------------------------- decoder ---- */
+
+/*
+ * Whistle's text decoder on the device: internal/decoder's Decoder with the
+ * Best() hypothesis (decoder/hypothesis.go:199: cross-attention after the
+ * self-attention, ZC q/k norms, sigmoid gates and residual, √dim input
+ * scale, tied head, final norm, engram on, no cross RoPE) and the engine's
+ * int8 numerics (needle.Int8{Act: true, KV: true}, whistle.WithInt8). Many
+ * independent sequences ("streams") advance together, one token each per
+ * step; every stream's state — the mHC lanes, the int8 self-attention
+ * caches with their tap history, the engram caches and the int8
+ * cross-attention memory — stays in device memory.
+ *
+ * The tensors are the reference's, as its loaders read them from
+ * whistle.cact (decoder.go:76 LoadInt8, needle.LoadBlock/LoadMHC/
+ * LoadEngram): CQ matrices as wc_cq handles (the decoder keeps views of
+ * them), float tensors as HOST arrays (copied at creation), norm vectors as
+ * the stored scales (gain = 1 + scale), gates as their raw parameters.
+ */
+typedef struct wc_decoder wc_decoder;
+
+/* One decoder layer: layerNN.* (needle.Block, block.go:21; Attention,
+ * attention.go:38; HadamardMLP, hadamard.go:28), crossNN.* (cross.go:26)
+ * and the layer's mHC heads (mhc.go:30; phi_* are this layer's row views of
+ * the stacked mhc_phi_*, mhc.go:94-96). */
+typedef struct wc_decoder_layer {
+    const float *norm_in, *post_norm, *pre_hada; /* [dim] */
+    float attn_gate;
+    const wc_cq *q_proj, *k_proj, *v_proj, *gate_proj, *out_proj;
+    const float *q_taps, *k_taps, *v_taps; /* [taps][heads·qk | kv_heads·qk | kv_heads·vd] */
+    const float *q_norm, *k_norm;          /* [qk] */
+    const float *d1, *d2, *b2, *d3, *d4;   /* [na·nb] */
+    const float *w1a, *w1b, *w2a, *w2b, *w3a, *w3b; /* [na][na], [nb][nb] */
+    const float *cond_v; /* [dim][rank] */
+    const float *cond_u; /* [rank][na·nb] */
+    const float *x_norm_in, *x_post_norm, *x_q_norm, *x_k_norm;
+    float x_attn_gate;
+    const wc_cq *x_q_proj, *x_k_proj, *x_v_proj, *x_gate_proj, *x_out_proj;
+    float a_pre, a_post, a_res;
+    const float *b_pre, *b_post; /* [lanes] */
+    const float *b_res;          /* [lanes][lanes] */
+    const wc_cq *phi_pre, *phi_post, *phi_res;
+} wc_decoder_layer;
+
+/* One engram site: engramN.* (needle/engram.go:35) and its layer. */
+typedef struct wc_engram_site {
+    const wc_cq *tables;            /* [n_tables·slots][sub] */
+    const wc_cq *key_proj, *value_proj; /* [dim][n_tables·sub] */
+    const float *taps;              /* [etaps][dim] */
+    int layer;
+} wc_engram_site;
+
+typedef struct wc_decoder_desc {
+    int dim, lanes, layers, vocab;
+    int heads, kv_heads, qk, vd, taps;
+    int x_heads, x_qk, x_vd;
+    int na, nb, rank;
+    int n_sites, n_tables, slots, sub, etaps;
+    const int32_t *orders;           /* [n_tables]: table c's n-gram order */
+    const int32_t *hada_p1, *hada_p2; /* [na·nb] */
+    double rope_theta;
+    int rope_len;
+    const wc_cq *embedding;          /* [vocab][dim], also the head */
+    const float *final_norm;         /* [dim] */
+    const wc_decoder_layer *layer;   /* [layers] */
+    const wc_engram_site *site;      /* [n_sites] */
+} wc_decoder_desc;
+
+/* Flags of wc_decoder_create. */
+enum {
+    /* Every CQ product on the tensor cores (WC_GEMM_TENSOR_CORES' fp16
+     * bound) instead of the bit-exact lut kernels. */
+    WC_DECODER_TENSOR_CORES = 1,
+    /* Run each step as eager launches instead of a captured CUDA graph. */
+    WC_DECODER_NO_GRAPH = 2,
+};
+
+/*
+ * Builds a decoder (decoder.go:76 LoadInt8) with device room for up to
+ * max_streams sequences of up to max_positions tokens against memories of
+ * up to max_frames encoder frames. Validates the shapes with the loaders'
+ * messages ("decoder: …", "needle: …"). This build's kernels take
+ * Whistle's widths: dim 512 in 4 lanes, qk 48, vd 64, HadamardMLP 16 × 32.
+ */
+wc_status wc_decoder_create(const wc_decoder_desc *desc, int max_streams, int max_frames, int max_positions,
+                            int flags, wc_decoder **out);
+void wc_decoder_destroy(wc_decoder *d);
+
+/*
+ * decoder.go:157 Memory and :194 NewState for `streams` streams: enc is
+ * DEVICE [streams][frames][dim] (each stream's encoder output); every
+ * layer's cross-attention keys and values (cross.go:181 project: the k/v
+ * products, the per-head k norm, QuantizeRows) go to the device memory,
+ * and every stream starts an empty sequence.
+ */
+wc_status wc_decoder_memory(wc_decoder *d, const float *enc, int streams, int frames, wc_stream stream);
+
+/*
+ * decoder.go:252 Extend with one token per stream: tokens DEVICE [streams];
+ * logits (or NULL) DEVICE [streams][vocab] receives the next-token logits
+ * (decoder.go:508 logits); next (or NULL) DEVICE [streams] their argmax
+ * (greedy.go:182).
+ */
+wc_status wc_decoder_extend(wc_decoder *d, const int32_t *tokens, float *logits, int32_t *next, wc_stream stream);
+
+/*
+ * decoder/greedy.go:40 GreedyMemory for every stream: the prompt [bos], the
+ * language token (the largest logit among langs, the first on ties,
+ * greedy.go:81), then argmax tokens until eos or max_tokens − 1 steps.
+ * All on the device, with no host synchronisation between steps. DEVICE
+ * outputs: tokens [streams][max_tokens − 1] (each stream's text tokens,
+ * then −1), counts [streams], lang [streams] (the language token),
+ * eos_hit [streams]. langs is a HOST array of n_langs token ids.
+ */
+wc_status wc_decoder_greedy(wc_decoder *d, int bos, const int32_t *langs, int n_langs, int eos, int max_tokens,
+                            int32_t *tokens, int32_t *counts, int32_t *lang, int32_t *eos_hit, wc_stream stream);
+
+/* Positions fed so far (every stream advances together). */
+int wc_decoder_len(const wc_decoder *d);
+
+/* Layer l's int8 cross-attention memory for the tests: device pointers to
+ * k8 [streams][frames][x_heads·x_qk], ks [streams][frames][x_heads], v8, vs
+ * (layouts as wc_attend_int8_streams reads them, cap = frames). */
+wc_status wc_decoder_memory_of(const wc_decoder *d, int l, const int8_t **k8, const float **ks, const int8_t **v8,
+                               const float **vs);
+
 #ifdef __cplusplus
 }
 #endif

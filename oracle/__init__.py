@@ -5,7 +5,8 @@ timed CPU baseline of ``bench.py``. Only ``tests/``, ``__graft_entry__.smoke()``
 and ``bench.py`` (its ``cpu_baseline`` leg and ``--impl reference``) may use
 it; the product (``go-whistle_b200``) never imports it.
 
-The C sources (``cq_oracle.c``, ``lut_avx2.c``, ``needle_oracle.c``, ``decoder_oracle.c``) restate the reference's Go
+The C sources (``cq_oracle.c``, ``lut_avx2.c``, ``needle_oracle.c``, ``decoder_oracle.c``,
+``whistle_oracle.c``) restate the reference's Go
 routines operation for operation; each names the file:line it follows. The
 reference (a Go module) cannot be built in this image (no Go toolchain, and
 its third-party modules are not vendored), so there is no ``oracle/_ref``.
@@ -49,8 +50,8 @@ class Packed(ctypes.Structure):
 
 def build(force: bool = False) -> Path:
     """Compiles liboracle.so with the Makefile beside it (gcc, no GPU)."""
-    srcs = [HERE / n for n in ("cq_oracle.c", "lut_avx2.c", "needle_oracle.c", "decoder_oracle.c", "oracle.h", "par.h",
-                                "Makefile")]
+    srcs = [HERE / n for n in ("cq_oracle.c", "lut_avx2.c", "needle_oracle.c", "decoder_oracle.c", "whistle_oracle.c",
+                                "oracle.h", "par.h", "Makefile")]
     if force or not LIB_PATH.exists() or any(s.stat().st_mtime > LIB_PATH.stat().st_mtime for s in srcs):
         subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     return LIB_PATH
@@ -291,3 +292,247 @@ def head_argmax(y: np.ndarray, rows: int, vocab: int, head: float = 1.0):
     idx = np.empty(rows, np.int32)
     lib().wo_head_argmax(_ptr(yy, _f32p), rows, vocab, float(head), _ptr(logits, _f32p), _ptr(idx, _i32p))
     return logits.reshape(rows, vocab), idx
+
+
+# ---------------------------------------------------------------- decoder
+#
+# whistle_oracle.c: Whistle's decoder step (internal/decoder, Best(), int8
+# numerics) on the CPU, over a synthetic weight set (any object with the
+# attributes of go-whistle_b200's synth.DecoderWeights).
+
+_i32 = ctypes.c_int
+
+
+class _DecLayer(ctypes.Structure):
+    _fields_ = ([(k, _f32p) for k in ("norm_in", "post_norm", "pre_hada")] + [("attn_gate", ctypes.c_float)]
+                + [(k, Packed) for k in ("q_proj", "k_proj", "v_proj", "gate_proj", "out_proj")]
+                + [(k, _f32p) for k in ("q_taps", "k_taps", "v_taps", "q_norm", "k_norm", "d1", "d2", "b2", "d3",
+                                        "d4")]
+                + [("hada_w", (_f32p * 2) * 3), ("cond_v", _f32p), ("cond_u", _f32p)]
+                + [(k, _f32p) for k in ("x_norm_in", "x_post_norm", "x_q_norm", "x_k_norm")]
+                + [("x_attn_gate", ctypes.c_float)]
+                + [(k, Packed) for k in ("x_q_proj", "x_k_proj", "x_v_proj", "x_gate_proj", "x_out_proj")]
+                + [(k, ctypes.c_float) for k in ("a_pre", "a_post", "a_res")]
+                + [(k, _f32p) for k in ("b_pre", "b_post", "b_res")]
+                + [(k, Packed) for k in ("phi_pre", "phi_post", "phi_res")])
+
+
+class _EngramSite(ctypes.Structure):
+    _fields_ = [("tables", Packed), ("key_proj", Packed), ("value_proj", Packed), ("taps", _f32p), ("layer", _i32)]
+
+
+class _Decoder(ctypes.Structure):
+    _fields_ = ([(k, _i32) for k in ("dim", "lanes", "layers", "vocab", "heads", "kv_heads", "qk", "vd", "taps",
+                                     "x_heads", "x_qk", "x_vd", "na", "nb", "rank", "n_sites", "n_tables", "slots",
+                                     "sub", "etaps", "max_order")]
+                + [("orders", _i32p), ("hada_p1", _i32p), ("hada_p2", _i32p), ("rope_cos", _f32p),
+                   ("rope_sin", _f32p), ("rope_len", _i32), ("embedding", Packed), ("final_norm", _f32p),
+                   ("layer", ctypes.POINTER(_DecLayer)), ("site", ctypes.POINTER(_EngramSite))])
+
+
+def _dec_lib():
+    L = lib()
+    if not getattr(L, "_dec_ready", False):
+        dp, sp = ctypes.POINTER(_Decoder), ctypes.c_void_p
+        L.wo_rope_tables.argtypes = [_i32, _i32, ctypes.c_double, _f32p, _f32p]
+        L.wo_sinkhorn.argtypes = [_f32p, _i32]
+        L.wo_dec_new.restype = sp
+        L.wo_dec_new.argtypes = [dp, _i32, _i32]
+        L.wo_dec_free.argtypes = [sp]
+        L.wo_dec_memory.argtypes = [dp, sp, _f32p, _i32]
+        L.wo_dec_memory_of.argtypes = [dp, sp, _i32, ctypes.POINTER(_i8p), ctypes.POINTER(_f32p),
+                                       ctypes.POINTER(_i8p), ctypes.POINTER(_f32p)]
+        L.wo_dec_extend.restype = _i32
+        L.wo_dec_extend.argtypes = [dp, sp, _i32, _f32p]
+        L.wo_dec_greedy.restype = _i32
+        L.wo_dec_greedy.argtypes = [dp, sp, _i32, _i32p, _i32, _i32, _i32, _i32p, _i32p, _i32p, _f32p]
+        L.wo_ngram_hash.restype = ctypes.c_uint32
+        L.wo_ngram_hash.argtypes = [_i32, _i32, _i32p, _i32]
+        L.wo_zc_norm.argtypes = [_f32p, _f32p, _i32, _i32, _f32p]
+        L.wo_rms_unit.argtypes = [_f32p, _f32p, _i32, _i32]
+        L.wo_rope_apply.argtypes = [_f32p, _i32, _f32p, _f32p]
+        L.wo_sinkhorn_iters.argtypes = [_f32p, _i32, _i32]
+        L.wo_dec_greedy_streams_mt.argtypes = [dp, _i32, _f32p, _i32, _i32, _i32p, _i32, _i32, _i32, _i32p, _i32p,
+                                               _i32p, _i32p, _i32]
+        L._dec_ready = True
+    return L
+
+
+def rope_tables(head_dim: int, length: int, theta: float):
+    """rope.go:20 NewRope's cos and sin tables [length][head_dim/2]."""
+    c = np.zeros(length * (head_dim // 2), np.float32)
+    s = np.zeros_like(c)
+    _dec_lib().wo_rope_tables(head_dim, length, float(theta), _ptr(c, _f32p), _ptr(s, _f32p))
+    return c, s
+
+
+def sinkhorn(k: np.ndarray, iters: int = 20) -> np.ndarray:
+    """mhc.go:300 sinkhorn on an n×n matrix of logits."""
+    k = _c(k, np.float32).copy()
+    n = int(round(np.sqrt(k.size)))
+    _dec_lib().wo_sinkhorn_iters(_ptr(k.reshape(-1), _f32p), n, iters)
+    return k
+
+
+def ngram_hash(c: int, order: int, hist) -> int:
+    """engram.go:141 ngramHash."""
+    h = _c(hist if len(hist) else [0], np.int32)
+    return int(_dec_lib().wo_ngram_hash(c, order, _ptr(h, _i32p), len(hist)))
+
+
+def zc_norm(x: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    """norm.go:60 ZCRMSNorm.Apply on rows of len(scale)."""
+    x, sc = _c(x, np.float32).reshape(-1), _c(scale, np.float32)
+    out = np.zeros_like(x)
+    _dec_lib().wo_zc_norm(_ptr(out, _f32p), _ptr(x, _f32p), x.size // sc.size, sc.size, _ptr(sc, _f32p))
+    return out
+
+
+def rms_unit(x: np.ndarray, dim: int) -> np.ndarray:
+    """norm.go:82 RMSUnit."""
+    x = _c(x, np.float32).reshape(-1)
+    out = np.zeros_like(x)
+    _dec_lib().wo_rms_unit(_ptr(out, _f32p), _ptr(x, _f32p), x.size // dim, dim)
+    return out
+
+
+def rope_apply(x: np.ndarray, cos_row: np.ndarray, sin_row: np.ndarray) -> np.ndarray:
+    """rope.go:73 apply at one position (its table rows)."""
+    x = _c(x, np.float32).copy()
+    c, s = _c(cos_row, np.float32), _c(sin_row, np.float32)
+    _dec_lib().wo_rope_apply(_ptr(x, _f32p), x.size // 2, _ptr(c, _f32p), _ptr(s, _f32p))
+    return x
+
+
+class OracleDecoder:
+    """The CPU restatement of Whistle's decoder over weights ``w``."""
+
+    def __init__(self, w):
+        self._keep = []
+
+        def arr(a, dt=np.float32):
+            a = _c(a, dt).reshape(-1)
+            self._keep.append(a)
+            return a
+
+        def f(a):
+            return _ptr(arr(a), _f32p)
+
+        def pk(p, lo=None, hi=None):
+            m = OracleMatrix.of(p)
+            self._keep.append(m)
+            if lo is None:
+                return m.s
+            return lib().wo_rows_py(m, lo, hi) if False else _rows(m, lo, hi)
+
+        def _rows(m, lo, hi):
+            groups = (m.in_ + m.group - 1) // m.group
+            rb = groups * m.group * m.bits // 8
+            return Packed(hi - lo, m.in_, m.group, m.bits, _ptr(m.index[lo * rb:], _u8p),
+                          _ptr(m.norms16[lo * groups:], _u16p), _ptr(m.cb, _f32p))
+
+        self.w = w
+        n = len(w.layers)
+        layers = (_DecLayer * n)()
+        for l, L in enumerate(w.layers):
+            d = layers[l]
+            for k in ("norm_in", "post_norm", "pre_hada", "q_taps", "k_taps", "v_taps", "q_norm", "k_norm", "d1",
+                      "d2", "b2", "d3", "d4", "cond_v", "cond_u", "x_norm_in", "x_post_norm", "x_q_norm",
+                      "x_k_norm", "b_pre", "b_post", "b_res"):
+                setattr(d, k, f(L[k]))
+            for k in ("attn_gate", "x_attn_gate", "a_pre", "a_post", "a_res"):
+                setattr(d, k, float(L[k]))
+            for k in ("q_proj", "k_proj", "v_proj", "gate_proj", "out_proj", "x_q_proj", "x_k_proj", "x_v_proj",
+                      "x_gate_proj", "x_out_proj"):
+                setattr(d, k, pk(L[k]))
+            for s in range(3):
+                d.hada_w[s][0] = f(L[f"w{s + 1}a"])
+                d.hada_w[s][1] = f(L[f"w{s + 1}b"])
+            for k in ("phi_pre", "phi_post", "phi_res"):
+                lo, hi = w.phi_rows(k, l)
+                setattr(d, k, pk(getattr(w, k), lo, hi))
+        sites = (_EngramSite * max(1, len(w.sites)))()
+        for i, S in enumerate(w.sites):
+            sites[i].tables, sites[i].key_proj, sites[i].value_proj = (pk(S[k]) for k in ("tables", "key_proj",
+                                                                                          "value_proj"))
+            sites[i].taps = f(S["taps"])
+            sites[i].layer = S["layer"]
+        self._layers, self._sites = layers, sites
+        self.rope_cos, self.rope_sin = rope_tables(w.qk, w.rope_len, w.rope_theta)
+        D = _Decoder(w.dim, w.lanes, n, w.vocab, w.heads, w.kv_heads, w.qk, w.vd, w.taps, w.x_heads, w.x_qk,
+                     w.x_vd, w.na, w.nb, w.rank, len(w.sites), w.n_tables, w.slots, w.sub, w.etaps, w.max_order)
+        D.orders = _ptr(arr(w.orders, np.int32), _i32p)
+        D.hada_p1 = _ptr(arr(w.hada_p1, np.int32), _i32p)
+        D.hada_p2 = _ptr(arr(w.hada_p2, np.int32), _i32p)
+        D.rope_cos, D.rope_sin = _ptr(self.rope_cos, _f32p), _ptr(self.rope_sin, _f32p)
+        D.rope_len = w.rope_len
+        D.embedding = pk(w.embedding)
+        D.final_norm = f(w.final_norm)
+        D.layer = layers
+        D.site = sites
+        self.d = D
+
+    def state(self, cap: int, frames: int) -> "OracleState":
+        return OracleState(self, cap, frames)
+
+    def greedy_streams(self, enc: np.ndarray, bos: int, langs, eos: int, max_tok: int, threads: int = 1):
+        """GreedyMemory for every stream of enc [streams][frames][dim]:
+        (tokens [streams][max_tok] (−1 past each count), counts, langs, eos)."""
+        enc = _c(enc, np.float32)
+        streams, frames = enc.shape[0], enc.shape[1]
+        lg = _c(langs, np.int32)
+        tok = np.full((streams, max_tok), -1, np.int32)
+        cnt, lang, eh = (np.zeros(streams, np.int32) for _ in range(3))
+        _dec_lib().wo_dec_greedy_streams_mt(ctypes.byref(self.d), streams, _ptr(enc, _f32p), frames, bos,
+                                            _ptr(lg, _i32p), lg.size, eos, max_tok, _ptr(tok, _i32p),
+                                            _ptr(cnt, _i32p), _ptr(lang, _i32p), _ptr(eh, _i32p), threads)
+        for b in range(streams):
+            tok[b, cnt[b]:] = -1
+        return tok, cnt, lang, eh
+
+
+class OracleState:
+    """One sequence (decoder.go:173 State) with its memory."""
+
+    def __init__(self, dec: OracleDecoder, cap: int, frames: int):
+        self.dec, self.frames = dec, frames
+        self.h = _dec_lib().wo_dec_new(ctypes.byref(dec.d), cap, frames)
+
+    def memory(self, enc: np.ndarray) -> None:
+        enc = _c(enc, np.float32)
+        self._enc = enc
+        _dec_lib().wo_dec_memory(ctypes.byref(self.dec.d), self.h, _ptr(enc, _f32p), enc.shape[0])
+
+    def memory_of(self, l: int):
+        """Layer l's int8 memory (k8, ks, v8, vs) as numpy copies."""
+        w = self.dec.w
+        k8, ks, v8, vs = _i8p(), _f32p(), _i8p(), _f32p()
+        _dec_lib().wo_dec_memory_of(ctypes.byref(self.dec.d), self.h, l, ctypes.byref(k8), ctypes.byref(ks),
+                                    ctypes.byref(v8), ctypes.byref(vs))
+        F = self.frames
+        return (np.ctypeslib.as_array(k8, (F * w.x_heads * w.x_qk,)).copy(),
+                np.ctypeslib.as_array(ks, (F * w.x_heads,)).copy(),
+                np.ctypeslib.as_array(v8, (F * w.x_heads * w.x_vd,)).copy(),
+                np.ctypeslib.as_array(vs, (F * w.x_heads,)).copy())
+
+    def extend(self, tok: int) -> np.ndarray:
+        logits = np.zeros(self.dec.w.vocab, np.float32)
+        if _dec_lib().wo_dec_extend(ctypes.byref(self.dec.d), self.h, int(tok), _ptr(logits, _f32p)) != 0:
+            raise ValueError(f"oracle: token {tok} out of range or cache full")
+        return logits
+
+    def greedy(self, bos: int, langs, eos: int, max_tok: int):
+        lg = _c(langs, np.int32)
+        tok = np.zeros(max_tok, np.int32)
+        lang, eh = ctypes.c_int(0), ctypes.c_int(0)
+        margins = np.zeros(max_tok, np.float32)
+        n = _dec_lib().wo_dec_greedy(ctypes.byref(self.dec.d), self.h, bos, _ptr(lg, _i32p), lg.size, eos, max_tok,
+                                     _ptr(tok, _i32p), ctypes.byref(lang), ctypes.byref(eh), _ptr(margins, _f32p))
+        if n < 0:
+            raise ValueError("oracle: greedy decode failed")
+        return tok[:n], lang.value, bool(eh.value), margins
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            _dec_lib().wo_dec_free(self.h)
+            self.h = None

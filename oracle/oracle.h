@@ -128,6 +128,107 @@ void wo_attend_int8_spans_mt(const float *q, int t, int heads, const int8_t *k8,
  * when head != 1, else y) and greedy.go:182 argmax per row of vocab values. */
 void wo_head_argmax(const float *y, int rows, int vocab, float head, float *logits, int32_t *idx);
 
+/* ------------------------------------------------------------------
+ * Whistle's decoder step (whistle_oracle.c): internal/decoder with the
+ * Best() hypothesis (decoder/hypothesis.go:199) and needle.Int8{Act, KV}.
+ */
+
+/* Rows [lo, hi) of p sharing its storage (matrix.go:133 Rows). */
+wo_packed wo_rows(const wo_packed *p, int lo, int hi);
+
+/* internal/needle/rope.go:20 NewRope's tables [len][head_dim/2]. */
+void wo_rope_tables(int head_dim, int len, double theta, float *cos_t, float *sin_t);
+
+/* internal/needle/mhc.go:300 sinkhorn (20 iterations) on an n×n matrix. */
+void wo_sinkhorn(float *k, int n);
+
+/* The decoder step's pieces, for the reference's known-answer tests:
+ * engram.go:141 ngramHash over hist[0..len) (hist[len-1] the current
+ * token), norm.go:60 ZCRMSNorm.Apply (scale, not gain), norm.go:82 RMSUnit,
+ * rope.go:73 apply with one position's tables, mhc.go:300 sinkhorn with a
+ * chosen iteration count. */
+uint32_t wo_ngram_hash(int c, int order, const int *hist, int len);
+void wo_zc_norm(float *dst, const float *x, int rows, int d, const float *scale);
+void wo_rms_unit(float *dst, const float *x, int rows, int d);
+void wo_rope_apply(float *x, int half, const float *cs, const float *sn);
+void wo_sinkhorn_iters(float *k, int n, int iters);
+
+/* One decoder layer's weights: needle.Block (block.go:21), its Attention
+ * (attention.go:38), HadamardMLP (hadamard.go:28), the layer's cross
+ * (decoder/cross.go:26) and its mHC heads (mhc.go:30). Norm vectors are the
+ * stored scales (gain = 1 + scale); gates are the raw parameters. */
+typedef struct {
+    const float *norm_in, *post_norm, *pre_hada; /* [dim] */
+    float attn_gate;
+    wo_packed q_proj, k_proj, v_proj, gate_proj, out_proj;
+    const float *q_taps, *k_taps, *v_taps; /* [taps][width] */
+    const float *q_norm, *k_norm;          /* [qk] */
+    const float *d1, *d2, *b2, *d3, *d4;   /* [na·nb] */
+    const float *hada_w[3][2];             /* stage s: a [na][na], b [nb][nb] */
+    const float *cond_v;                   /* [dim][rank] */
+    const float *cond_u;                   /* [rank][na·nb] */
+    const float *x_norm_in, *x_post_norm, *x_q_norm, *x_k_norm;
+    float x_attn_gate;
+    wo_packed x_q_proj, x_k_proj, x_v_proj, x_gate_proj, x_out_proj;
+    float a_pre, a_post, a_res;
+    const float *b_pre, *b_post; /* [lanes] */
+    const float *b_res;          /* [lanes·lanes] */
+    wo_packed phi_pre, phi_post, phi_res; /* this layer's rows of the stacked φ */
+} wo_dec_layer;
+
+/* One engram site (needle/engram.go:35 Engram) and its decoder layer. */
+typedef struct {
+    wo_packed tables;                /* [n_tables·slots][sub] */
+    wo_packed key_proj, value_proj;  /* [dim][n_tables·sub] */
+    const float *taps;               /* [etaps][dim] */
+    int layer;
+} wo_engram_site;
+
+typedef struct {
+    int dim, lanes, layers, vocab;
+    int heads, kv_heads, qk, vd, taps; /* self-attention */
+    int x_heads, x_qk, x_vd;           /* cross-attention */
+    int na, nb, rank;                  /* HadamardMLP */
+    int n_sites, n_tables, slots, sub, etaps, max_order;
+    const int *orders;                 /* [n_tables]: the n-gram order of table c */
+    const int *hada_p1, *hada_p2;      /* [na·nb] */
+    const float *rope_cos, *rope_sin;  /* [rope_len][qk/2] */
+    int rope_len;
+    wo_packed embedding;               /* [vocab][dim], also the tied head */
+    const float *final_norm;           /* [dim] */
+    const wo_dec_layer *layer;         /* [layers] */
+    const wo_engram_site *site;        /* [n_sites] */
+} wo_decoder;
+
+typedef struct wo_dec_state wo_dec_state;
+
+/* A sequence with room for cap positions and a memory of frames rows. */
+wo_dec_state *wo_dec_new(const wo_decoder *d, int cap, int frames);
+void wo_dec_free(wo_dec_state *s);
+int wo_dec_len(const wo_dec_state *s);
+
+/* decoder.go:157 Memory for enc [frames][dim] (cross.go:181 project per
+ * layer); starts the sequence afresh (decoder.go:194 NewState). */
+void wo_dec_memory(const wo_decoder *d, wo_dec_state *s, const float *enc, int frames);
+
+/* Layer l's int8 memory: k8 [frames][x_heads·x_qk], ks [frames][x_heads],
+ * v8 [frames][x_heads·x_vd], vs. */
+void wo_dec_memory_of(const wo_decoder *d, const wo_dec_state *s, int l, const int8_t **k8, const float **ks,
+                      const int8_t **v8, const float **vs);
+
+/* decoder.go:252 Extend with one token; logits [vocab]. -1 on a bad token
+ * or a full cache. */
+int wo_dec_extend(const wo_decoder *d, wo_dec_state *s, int tok, float *logits);
+
+/* greedy.go:40 GreedyMemory with the language detected among langs. */
+int wo_dec_greedy(const wo_decoder *d, wo_dec_state *s, int bos, const int *langs, int nlangs, int eos,
+                  int max_tok, int *tokens, int *lang, int *eos_hit, float *margins);
+
+/* GreedyMemory for many streams (enc [streams][frames][dim]) on threads. */
+void wo_dec_greedy_streams_mt(const wo_decoder *d, int streams, const float *enc, int frames, int bos,
+                              const int *langs, int nlangs, int eos, int max_tok, int *tokens, int *counts,
+                              int *lang, int *eos_hit, int threads);
+
 #ifdef __cplusplus
 }
 #endif
