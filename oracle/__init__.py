@@ -352,6 +352,11 @@ def _dec_lib():
         L.wo_rms_unit.argtypes = [_f32p, _f32p, _i32, _i32]
         L.wo_rope_apply.argtypes = [_f32p, _i32, _f32p, _f32p]
         L.wo_sinkhorn_iters.argtypes = [_f32p, _i32, _i32]
+        L.wo_dec_states_mt.restype = sp
+        L.wo_dec_states_mt.argtypes = [dp, _i32, _f32p, _i32, _i32, _i32]
+        L.wo_dec_states_free.argtypes = [sp, _i32]
+        L.wo_dec_greedy_states_mt.argtypes = [dp, sp, _i32, _i32, _i32p, _i32, _i32, _i32, _i32p, _i32p, _i32p,
+                                              _i32p, _i32]
         L.wo_dec_greedy_streams_mt.argtypes = [dp, _i32, _f32p, _i32, _i32, _i32p, _i32, _i32, _i32, _i32p, _i32p,
                                                _i32p, _i32p, _i32]
         L._dec_ready = True
@@ -489,6 +494,27 @@ class OracleDecoder:
         for b in range(streams):
             tok[b, cnt[b]:] = -1
         return tok, cnt, lang, eh
+
+
+def timed_greedy(dec: "OracleDecoder", enc: np.ndarray, bos: int, langs, eos: int, max_tok: int, threads: int):
+    """The CPU baseline of the decoder: every stream's memory on threads
+    (untimed), then their greedy decodes on threads, timed by the wall
+    clock. Returns (seconds, tokens [streams][max_tok], counts, langs, eos)."""
+    import time
+
+    L = _dec_lib()
+    enc = _c(enc, np.float32)
+    streams, frames = enc.shape[0], enc.shape[1]
+    st = L.wo_dec_states_mt(ctypes.byref(dec.d), streams, _ptr(enc, _f32p), frames, max_tok + 1, threads)
+    lg = _c(langs, np.int32)
+    tok = np.full((streams, max_tok), -1, np.int32)
+    cnt, lang, eh = (np.zeros(streams, np.int32) for _ in range(3))
+    t0 = time.perf_counter()
+    L.wo_dec_greedy_states_mt(ctypes.byref(dec.d), st, streams, bos, _ptr(lg, _i32p), lg.size, eos, max_tok,
+                              _ptr(tok, _i32p), _ptr(cnt, _i32p), _ptr(lang, _i32p), _ptr(eh, _i32p), threads)
+    secs = time.perf_counter() - t0
+    L.wo_dec_states_free(st, streams)
+    return secs, tok, cnt, lang, eh
 
 
 class OracleState:

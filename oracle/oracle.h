@@ -229,6 +229,15 @@ void wo_dec_greedy_streams_mt(const wo_decoder *d, int streams, const float *enc
                               const int *langs, int nlangs, int eos, int max_tok, int *tokens, int *counts,
                               int *lang, int *eos_hit, int threads);
 
+/* The same in two phases (the timed CPU baseline): every stream's memory
+ * on threads (states with room for cap positions), then their greedy
+ * decodes on threads. */
+wo_dec_state **wo_dec_states_mt(const wo_decoder *d, int streams, const float *enc, int frames, int cap, int threads);
+void wo_dec_states_free(wo_dec_state **st, int streams);
+void wo_dec_greedy_states_mt(const wo_decoder *d, wo_dec_state **st, int streams, int bos, const int *langs,
+                             int nlangs, int eos, int max_tok, int *tokens, int *counts, int *lang, int *eos_hit,
+                             int threads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -758,3 +758,54 @@ void wo_rope_apply(float *x, int half, const float *cs, const float *sn) { rope_
 void wo_sinkhorn_iters(float *k, int n, int iters) {
     if (!sinkhorn_exp(k, n, iters)) sinkhorn_log(k, n, iters);
 }
+
+/* The CPU baseline in two phases, so that the decode rate excludes the
+ * memory projection (the reference's decode rate starts after the first
+ * text token; whistle/strategy.go:33 clock): the memories of many streams
+ * on threads, then their greedy decodes on threads. */
+typedef struct {
+    const wo_decoder *d;
+    wo_dec_state **st;
+    const float *enc;
+    int frames, cap;
+} states_job;
+
+static void states_task(int b, void *arg) {
+    const states_job *j = arg;
+    j->st[b] = wo_dec_new(j->d, j->cap, j->frames);
+    wo_dec_memory(j->d, j->st[b], j->enc + (size_t)b * j->frames * j->d->dim, j->frames);
+}
+
+wo_dec_state **wo_dec_states_mt(const wo_decoder *d, int streams, const float *enc, int frames, int cap, int threads) {
+    wo_dec_state **st = calloc((size_t)(streams > 0 ? streams : 1), sizeof *st);
+    states_job job = {d, st, enc, frames, cap};
+    wo_parallel_for(streams, threads < 1 ? 1 : threads, states_task, &job);
+    return st;
+}
+
+void wo_dec_states_free(wo_dec_state **st, int streams) {
+    if (!st) return;
+    for (int b = 0; b < streams; b++) wo_dec_free(st[b]);
+    free(st);
+}
+
+typedef struct {
+    const wo_decoder *d;
+    wo_dec_state **st;
+    int bos, nlangs, eos, max_tok;
+    const int *langs;
+    int *tokens, *counts, *lang, *eos_hit;
+} greedy_states_job;
+
+static void greedy_states_task(int b, void *arg) {
+    const greedy_states_job *j = arg;
+    j->counts[b] = wo_dec_greedy(j->d, j->st[b], j->bos, j->langs, j->nlangs, j->eos, j->max_tok,
+                                 j->tokens + (size_t)b * j->max_tok, &j->lang[b], &j->eos_hit[b], NULL);
+}
+
+void wo_dec_greedy_states_mt(const wo_decoder *d, wo_dec_state **st, int streams, int bos, const int *langs,
+                             int nlangs, int eos, int max_tok, int *tokens, int *counts, int *lang, int *eos_hit,
+                             int threads) {
+    greedy_states_job job = {d, st, bos, nlangs, eos, max_tok, langs, tokens, counts, lang, eos_hit};
+    wo_parallel_for(streams, threads < 1 ? 1 : threads, greedy_states_task, &job);
+}
