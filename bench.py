@@ -470,6 +470,119 @@ def decode_gemm_component(pkg, torch, lib, streams=256, reps=20):
                         "this size"}
 
 
+DECODE_STREAMS = 1024   # configs[4]: streams sharded over the GPUs (stream s -> rank s mod N)
+DECODE_FRAMES = 375     # 30 s of audio at 12.5 encoder frames/s
+DECODE_TOKENS = 65      # the language token and 64 greedy text tokens
+DECODE_VOCAB = 16384
+
+
+def decode_streams_of(rank, world, total=DECODE_STREAMS):
+    """The streams a rank decodes (go-whistle_b200/dp.py's shard: s mod N)."""
+    return [s for s in range(total) if s % world == rank]
+
+
+def decode_component(pkg, torch, lib, world, rank, pg, dev, total=DECODE_STREAMS, frames=DECODE_FRAMES,
+                     max_tok=DECODE_TOKENS, flags=0):
+    """configs[4]'s decoder: greedy decoding of `total` independent streams
+    of the synthetic Whistle decoder (8 layers, 4 mHC lanes, int8 self and
+    cross attention over 375 frames, engram, vocab 16384), sharded over the
+    ranks with no collective. Each rank projects its streams' memories
+    (untimed, the prefill), then runs GreedyMemory for all of them on the
+    device; tokens/s = every token the ranks decoded (the language token,
+    the text tokens, the EOS that ends a stream) / the slowest rank's
+    device time of the decode."""
+    S_ = pkg.synth
+    mine = decode_streams_of(rank, world, total)
+    w = S_.DecoderWeights(seed=4000, vocab=DECODE_VOCAB)
+    enc = np.stack([S_.encoder_output(np.random.default_rng(5000 + s), 1, frames)[0] for s in mine])
+    denc = torch.from_numpy(enc).to(dev)
+    dec = pkg.decoder.Decoder(w, max_streams=len(mine), max_frames=frames, max_positions=max_tok + 1, flags=flags)
+    stream = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    ev[0].record(stream)
+    dec.Memory(denc)
+    ev[1].record(stream)
+    # Warm-up run: captures the step graph.
+    dec.GreedyMemory(S_.WHISTLE_BOS, S_.WHISTLE_LANGS, S_.WHISTLE_EOS, 4)
+    dec.Memory(denc)
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    n0 = lib.wc_launch_count()
+    ev[2].record(stream)
+    tokens, counts, lang, eos = dec.GreedyMemory(S_.WHISTLE_BOS, S_.WHISTLE_LANGS, S_.WHISTLE_EOS, max_tok)
+    ev[3].record(stream)
+    torch.cuda.synchronize()
+    launches = lib.wc_launch_count() - n0
+    ms = ev[2].elapsed_time(ev[3])
+    mem_ms = ev[0].elapsed_time(ev[1])
+    counts_h, eos_h = counts.cpu().numpy(), eos.cpu().numpy()
+    ntok = int(len(mine) + counts_h.sum() + eos_h.sum())
+    if pg:
+        t = torch.tensor([ms, float(ntok)], device=dev, dtype=torch.float64)
+        tmax = t.clone()
+        pg.all_reduce(tmax, op=pg.ReduceOp.MAX)
+        pg.all_reduce(t, op=pg.ReduceOp.SUM)
+        ms, ntok = float(tmax[0].item()), int(t[1].item())
+    # Algorithmic bytes of one step on this rank (the decode's roofline):
+    # the int8 cross memory of every layer and stream, the self caches, and
+    # the CQ weights once.
+    L, S = len(w.layers), len(mine)
+    cross = S * L * (frames * w.x_heads * (w.x_qk + w.x_vd) + frames * w.x_heads * 2 * 4)
+    ctx = max_tok / 2
+    self_b = S * L * (ctx * w.kv_heads * (w.qk + w.vd) + ctx * w.kv_heads * 2 * 4)
+    def wb_(p):
+        return p.Index.size + p.Norms.size
+    wbytes = wb_(w.embedding) + wb_(w.phi_pre) + wb_(w.phi_post) + wb_(w.phi_res) + sum(
+        wb_(Ld[k]) for Ld in w.layers for k in ("q_proj", "k_proj", "v_proj", "gate_proj", "out_proj", "x_q_proj",
+                                                "x_gate_proj", "x_out_proj"))
+    step_bytes = cross + self_b + wbytes
+    steps = max_tok
+    peak, peak_kind = peaks()
+    return {"workload": f"configs[4] decoder: {total} streams sharded stream mod {world}, greedy {max_tok} tokens "
+                        f"(language + 64 text) per stream, synthetic Whistle decoder (8 layers, vocab {DECODE_VOCAB}, "
+                        f"int8 KV, cross memory of {frames} frames), every CQ product on the bit-exact lut kernels",
+            "metric": "decode tokens/s", "value": round(ntok / (ms / 1e3), 1), "unit": "tokens/s",
+            "scaling": "strong", "streams_total": total, "streams_this_rank": S, "tokens": ntok,
+            "ms_decode": round(ms, 3), "ms_per_step": round(ms / steps, 4), "ms_memory_prefill": round(mem_ms, 2),
+            "gpu_launches_per_step": round(launches / steps, 1),
+            "roofline": {"bound": "hbm", "bytes_per_step_per_rank": int(step_bytes),
+                         "achieved_gbs": round(step_bytes / (ms / steps / 1e3) / 1e9, 1), "peak": peak,
+                         "frac": round(step_bytes / (ms / steps / 1e3) / 1e9 / peak, 4), "peak_kind": peak_kind},
+            "parity": "token ids identical to the CPU restatement (tests/test_decoder_step_gpu.py)"}
+
+
+def decode_cpu_baseline(pkg, streams=16, max_tok=DECODE_TOKENS, frames=DECODE_FRAMES):
+    """The decoder's CPU baseline: the oracle's restatement of the
+    reference's greedy decode (internal/decoder, int8 numerics, the lut
+    kernels) for a sample of streams, one stream per host thread; memories
+    untimed, the decodes timed by the wall clock."""
+    import oracle
+
+    oracle.build()
+    S_ = pkg.synth
+    w = S_.DecoderWeights(seed=4000, vocab=DECODE_VOCAB)
+    od = oracle.OracleDecoder(w)
+    enc = np.stack([S_.encoder_output(np.random.default_rng(5000 + s), 1, frames)[0] for s in range(streams)])
+    threads = min(streams, os.cpu_count() or 1)
+    secs, tok, cnt, lang, eh = oracle.timed_greedy(od, enc, S_.WHISTLE_BOS, S_.WHISTLE_LANGS, S_.WHISTLE_EOS, max_tok,
+                                                   threads)
+    ntok = int(streams + cnt.sum() + eh.sum())
+    return {"value": round(ntok / secs, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{streams} streams x {max_tok} greedy tokens of the same synthetic decoder, one stream per "
+                      f"thread (memories untimed)", "cpu_model": cpu_model()}
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def run_b200(args, world, rank, local):
     import torch
 
@@ -625,9 +738,13 @@ def run_b200(args, world, rank, local):
         "gpu_launches": int(launches_per_step * args.steps), "gpu_launches_scope": "per rank",
         "clocks": clocks,
     }
+    if not args.only and not args.no_decode:
+        line["decode"] = decode_component(pkg, torch, lib, world, rank, pg, dev)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            line["decode"]["cpu_baseline"] = decode_cpu_baseline(pkg)
     if args.only:
         line["config"]["workload"] = f"one shape {args.only} (profiling run, not the headline workload)"
-    elif not args.no_components:
+    elif not args.no_components and world == 1:
         line["components"] = {"int8_attention": attention_component(pkg, torch, lib, None, flags=3),
                               "int8_attention_exact_order": attention_component(pkg, torch, lib, None, flags=1),
                               "cq_gemm_prefill": prefill_component(pkg, torch, lib),
@@ -656,6 +773,11 @@ def main():
     ap.add_argument("--attention-only", action="store_true", help="only the attention component (profiling)")
     ap.add_argument("--prefill-only", action="store_true", help="only the prefill GEMM component (profiling)")
     ap.add_argument("--decode-gemm-only", action="store_true", help="only the multi-stream decode GEMM component")
+    ap.add_argument("--no-decode", action="store_true", help="skip the greedy decoder component")
+    ap.add_argument("--decode-only", action="store_true", help="only the greedy decoder component")
+    ap.add_argument("--decode-streams", type=int, default=DECODE_STREAMS, help="--decode-only: total streams")
+    ap.add_argument("--decode-tokens", type=int, default=DECODE_TOKENS, help="--decode-only: tokens per stream")
+    ap.add_argument("--decode-eager", action="store_true", help="--decode-only: steps as eager launches (profiling)")
     args = ap.parse_args()
     world, rank, local = dist_env()
     if args.impl == "reference":
@@ -674,6 +796,29 @@ def main():
         pkg = __import__("importlib").import_module("go-whistle_b200")
         torch.cuda.set_device(local)
         print(json.dumps(decode_gemm_component(pkg, torch, pkg._lib.lib())), flush=True)
+        return
+    if args.decode_only:
+        import torch
+
+        pkg = __import__("importlib").import_module("go-whistle_b200")
+        torch.cuda.set_device(local)
+        pg = None
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local))
+            pg = dist
+        res = decode_component(pkg, torch, pkg._lib.lib(), world, rank, pg, torch.device("cuda", local),
+                               total=args.decode_streams, max_tok=args.decode_tokens,
+                               flags=pkg.decoder.WC_DECODER_NO_GRAPH if args.decode_eager else 0)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        if pg:
+            pg.barrier()
+            pg.destroy_process_group()
         return
     if args.attention_only:
         import torch

@@ -383,6 +383,7 @@ static bool try_stream(const wc_cq *const *ms, int n, const float *x, float *con
         p->total_tiles = l.tile0 + l.count * l.tpm;
         p->shape = ms[0]->shape;
         p->x = x;
+        p->acts = 1;
         p->smem_base = stream_smem_base();
         p->part = nullptr;
         p->err = device_err_word();
@@ -433,6 +434,7 @@ static bool try_stream(const wc_cq *const *ms, int n, const float *x, float *con
         r.v = sv;
         r.y = ys[k];
         r.y_step = 0;
+        r.y_act = 0;
         r.row_step = 0;
         r.count = 1;
         r.tpm = tpm;
@@ -440,6 +442,67 @@ static bool try_stream(const wc_cq *const *ms, int n, const float *x, float *con
         tiles += tpm;
     }
     flush();
+    return true;
+}
+
+// Activations from which a product of matrices with the stream layout runs
+// on the streaming kernel over all of them (each CTA tabulates the
+// activations its share of (activation, tile) items touches) instead of
+// the per-activation or per-tile kernels.
+static const int kStreamActsMinRows = 5;
+
+// Rows (all matrices together) from which the streaming kernel's byte
+// tables (256 entries per index byte, rebuilt per activation) pay off
+// against the per-activation kernel's nibble tables; below it (the mHC φ:
+// 24 rows of 2048) the table build would dominate.
+static const int kStreamActsMinOut = 128;
+
+static bool try_stream_acts(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows,
+                            cudaStream_t st, wc_status *status) {
+    if (rows < kStreamActsMinRows || n == 0) return false;
+    long long outs = 0;
+    for (int k = 0; k < n; k++) {
+        if (!ms[k]->streamable()) return false;
+        outs += ms[k]->out;
+    }
+    if (outs < kStreamActsMinOut) return false;
+    const int sms = sm_count();
+    *status = WC_OK;
+    for (int base = 0; base < n; base += kMaxStreamRuns) {
+        const int cnt = n - base < kMaxStreamRuns ? n - base : kMaxStreamRuns;
+        auto p = std::make_unique<StreamParams>();
+        p->shape = ms[base]->shape;
+        p->x = x;
+        p->acts = rows;
+        p->smem_base = stream_smem_base();
+        p->part = nullptr;
+        p->err = device_err_word();
+        p->nruns = 0;
+        long long tiles = 0;
+        for (int k = 0; k < cnt; k++) {
+            const wc_cq *m = ms[base + k];
+            if (m->out == 0) continue;
+            StreamRun &r = p->runs[p->nruns++];
+            r.v = m->stream_view();
+            r.y = ys[base + k];
+            r.y_step = 0;
+            r.y_act = m->out;  // outputs [rows][out]
+            r.row_step = 0;
+            r.count = 1;
+            r.tpm = (m->out + 31) / 32;
+            r.tile0 = (int)tiles;
+            tiles += r.tpm;
+        }
+        if (p->nruns == 0) continue;
+        p->total_tiles = (int)tiles;
+        const long long work = tiles * (long long)rows;
+        const int ctas = work < sms ? (int)work : sms;
+        cudaError_t e = launch_stream(*p, ctas, st);
+        if (e != cudaSuccess) {
+            *status = cuda_error(e, "cq stream kernel (activations)");
+            return true;
+        }
+    }
     return true;
 }
 
@@ -487,11 +550,56 @@ static bool try_split(const wc_cq *const *ms, int n, const float *x, float *cons
     return true;
 }
 
+// Activations from which a product of group-128 matrices runs on the
+// per-activation kernel (cq_lut_acts.cu: tables built once per activation
+// for all rows) instead of the per-tile kernel (tables rebuilt per tile).
+static const int kActsMinRows = 8;
+
+// The per-activation kernel, when every matrix's shape takes it.
+static bool try_acts(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows, cudaStream_t st,
+                     wc_status *status) {
+    if (rows < kActsMinRows || !acts_eligible(ms[0]->shape)) return false;
+    const int sms = sm_count();
+    *status = WC_OK;
+    for (int base = 0; base < n; base += kMaxActsMats) {
+        const int cnt = n - base < kMaxActsMats ? n - base : kMaxActsMats;
+        ActsParams p{};
+        p.shape = ms[base]->shape;
+        p.x = x;
+        int total = 0;
+        for (int k = 0; k < cnt; k++) {
+            const wc_cq *m = ms[base + k];
+            if (m->out == 0) continue;
+            p.views[p.n] = m->view();
+            p.y[p.n] = ys[base + k];
+            p.row_start[p.n] = total;
+            total += m->out;
+            p.n++;
+        }
+        p.row_start[p.n] = total;
+        p.total_rows = total;
+        if (p.n == 0) continue;
+        // Few activations: split the rows over more CTAs (each builds the
+        // tables) until about two CTAs run per SM, keeping >= 64 rows each.
+        int splits = 1;
+        while (rows * splits < 2 * sms && total / (2 * splits) >= 64) splits *= 2;
+        p.splits = splits;
+        cudaError_t e = launch_lut_acts(p, rows, st);
+        if (e != cudaSuccess) {
+            *status = cuda_error(e, "cq lut kernel (per activation)");
+            return true;
+        }
+    }
+    return true;
+}
+
 static wc_status run_lut(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows,
                          cudaStream_t st) {
     wc_status sst;
     if (try_stream(ms, n, x, ys, rows, st, &sst)) return sst;
     if (try_split(ms, n, x, ys, rows, st, &sst)) return sst;
+    if (try_stream_acts(ms, n, x, ys, rows, st, &sst)) return sst;
+    if (try_acts(ms, n, x, ys, rows, st, &sst)) return sst;
     for (int base = 0; base < n; base += kMaxLaunchMats) {
         int cnt = n - base < kMaxLaunchMats ? n - base : kMaxLaunchMats;
         auto p = std::make_unique<LutParams>();
@@ -1058,6 +1166,12 @@ wc_status gemms_device(const wc_cq *const *ms, int n, const float *x, float *con
     return run_tc(ms, n, x, ys, rows, st, tc_buf, tc_bytes);
 }
 int *err_word() { return device_err_word(); }
+bool cq_internal(const wc_cq *h, CqShape *s, CqView *v) {
+    if (!h) return false;
+    *s = h->shape;
+    *v = h->view();
+    return true;
+}
 }  // namespace wb
 
 // Tensor-core GEMM without any allocation: see whistle_b200.h.

@@ -63,6 +63,8 @@ int *err_word();
 // image in tc_buf (at least tc_a_bytes of the rows and widths).
 wc_status gemms_device(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows, bool tc,
                        void *tc_buf, size_t tc_bytes, cudaStream_t st);
+// A matrix's shape and device view, for the library's own kernels.
+bool cq_internal(const wc_cq *h, CqShape *s, CqView *v);
 }  // namespace wb
 
 #define WB_CUDA(call)                                            \

@@ -43,8 +43,9 @@ cudaError_t launch_split(const LutParams &p, int tiles, int acts, cudaStream_t s
 constexpr int kMaxStreamRuns = 256;
 struct StreamRun {
     CqView v;          // the run's first matrix
-    float *y;          // its output [v.out]
+    float *y;          // its output [v.out] (of the first activation)
     long long y_step;  // floats between consecutive matrices' outputs
+    long long y_act;   // floats between consecutive activations' outputs
     int row_step;      // layout rows between consecutive matrices' row0
     int count;         // matrices in the run
     int tpm;           // 32-row tiles per matrix
@@ -56,7 +57,8 @@ constexpr int kSmallStreamRuns = 4;
 template <int N>
 struct StreamParamsN {
     CqShape shape;
-    const float *x;   // one activation [in]
+    const float *x;   // the activations [acts][in]
+    int acts;         // activations: the work is acts × total_tiles (activation-major)
     int nruns;
     int total_tiles;  // Σ count·tpm
     int smem_base;    // stream_smem_base() the launch was sized for
@@ -117,6 +119,23 @@ cudaError_t gemm_tc_noalloc(const CqShape &s, const unsigned char *wimg, float w
 // The static array's error word on the current device (null before the
 // first no-allocation call there).
 int *noalloc_err_word();
+
+// The per-activation lut kernel (cq_lut_acts.cu): every row of up to
+// kMaxActsMats matrices (group 128) per activation, tables built once.
+constexpr int kMaxActsMats = 16;
+struct ActsParams {
+    CqShape shape;
+    const float *x;  // [acts][in]
+    int n;           // matrices
+    int total_rows;  // Σ out
+    int splits;      // CTAs per activation (grid.y), each a contiguous share of the rows
+    CqView views[kMaxActsMats];
+    float *y[kMaxActsMats];              // [acts][views[k].out]
+    int row_start[kMaxActsMats + 1];     // prefix sum of rows
+};
+bool acts_eligible(const CqShape &s);
+size_t acts_smem_bytes(const CqShape &s);
+cudaError_t launch_lut_acts(const ActsParams &p, int acts, cudaStream_t st);
 
 int stream_smem_base();
 bool stream_eligible(const CqShape &s);

@@ -93,13 +93,13 @@ struct TileLoc {
     int r0;
 };
 template <class SP>
-__device__ __forceinline__ TileLoc tile_loc(const SP &p, int t, int k) {
+__device__ __forceinline__ TileLoc tile_loc(const SP &p, int t, int k, int act = 0) {
     const StreamRun &R = p.runs[k];
     const int u = t - R.tile0, i = u / R.tpm;
     TileLoc L;
     L.v = R.v;
     L.v.row0 += i * R.row_step;
-    L.y = R.y + (long long)i * R.y_step;
+    L.y = R.y + (long long)i * R.y_step + (long long)act * R.y_act;
     L.r0 = (u - i * R.tpm) * 32;
     return L;
 }
@@ -334,14 +334,18 @@ __global__ void __launch_bounds__(stream_threads<GB, NSC>(), 1)
     uint16_t *tab = reinterpret_cast<uint16_t *>(smem + (kTabAbs - base));  // kTabBytes
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // This CTA's work: a contiguous share of the (activation, 32-row tile)
+    // items, activation-major: for each activation it touches, it rotates
+    // and tabulates the activation once and streams that activation's tiles.
+    const long long T = p.total_tiles, W = T * p.acts;
+    const long long w_begin = W * blockIdx.x / gridDim.x, w_end = W * (blockIdx.x + 1) / gridDim.x;
     if (base != p.smem_base) {
         // Not the layout the host sized: leave NaN, never a wrong number,
         // and record it in the error word (wc_device_status).
         if (tid == 0 && p.err) atomicExch(p.err, 20);
-        const int t_b = (int)(((long long)p.total_tiles * blockIdx.x) / gridDim.x);
-        const int t_e = (int)(((long long)p.total_tiles * (blockIdx.x + 1)) / gridDim.x);
-        for (int t = t_b + warp; t < t_e; t += NW) {
-            const TileLoc L = tile_loc(p, t, find_run(p, t));
+        for (long long w = w_begin + warp; w < w_end; w += NW) {
+            const int a = (int)(w / T), t = (int)(w - (long long)a * T);
+            const TileLoc L = tile_loc(p, t, find_run(p, t), a);
             const int r = L.r0 + lane;
             if (r < L.v.out) L.y[r] = __int_as_float(0x7fc00000);
         }
@@ -350,9 +354,14 @@ __global__ void __launch_bounds__(stream_threads<GB, NSC>(), 1)
     float *wterms = terms + warp * NG * 32;
     const int npass = (s.row_bytes + kPassPositions - 1) / kPassPositions;
 
-    // This CTA's tiles: a contiguous share of all matrices' 32-row tiles.
-    const int t_begin = (int)(((long long)p.total_tiles * blockIdx.x) / gridDim.x);
-    const int t_end = (int)(((long long)p.total_tiles * (blockIdx.x + 1)) / gridDim.x);
+  for (int act = (int)(w_begin / T); (long long)act * T < w_end; act++) {
+    const int t_begin = (int)(w_begin > (long long)act * T ? w_begin - (long long)act * T : 0);
+    const int t_end = (int)(w_end < (long long)(act + 1) * T ? w_end - (long long)act * T : T);
+    if (t_begin >= t_end) continue;
+    const float *x = p.x + (size_t)act * s.in;
+    // The previous activation's tables and steps are read until every warp
+    // has finished its tiles.
+    __syncthreads();
 
     // Rolling prefetch: a warp's first tile of a pass is loaded into its
     // registers before the pass's tables are built (for pass 0 before the
@@ -364,7 +373,7 @@ __global__ void __launch_bounds__(stream_threads<GB, NSC>(), 1)
     const bool has_tile = t_begin + warp < t_end;
     auto first_tile = [&](int sc0, int nsc_pass) {
         if (has_tile) {
-            const TileLoc l0 = tile_loc(p, t_begin + warp, find_run(p, t_begin + warp));
+            const TileLoc l0 = tile_loc(p, t_begin + warp, find_run(p, t_begin + warp), act);
             const bool v0 = l0.r0 + lane < l0.v.out;
             const int R0 = l0.v.row0 + l0.r0 + lane;
             load_superchunk<NG>(l0.v, sc0, R0, v0, d0, n0);
@@ -375,7 +384,7 @@ __global__ void __launch_bounds__(stream_threads<GB, NSC>(), 1)
     };
     first_tile(0, min(min(s.row_bytes, kPassPositions) / 64, NSC));
 
-    rotate_and_bound(s, p.x, xs, steps, invs);
+    rotate_and_bound(s, x, xs, steps, invs);
 
     for (int pass = 0; pass < npass; pass++) {
         const int j0 = pass * kPassPositions;
@@ -393,7 +402,7 @@ __global__ void __launch_bounds__(stream_threads<GB, NSC>(), 1)
         int k = -1;
         for (int t = t_begin + warp; t < t_end; t += NW) {
             k = run_from(p, t, k);
-            const TileLoc loc = tile_loc(p, t, k);
+            const TileLoc loc = tile_loc(p, t, k, act);
             const CqView &v = loc.v;
             const int r = loc.r0 + lane;
             const bool valid = r < v.out;
@@ -435,7 +444,7 @@ __global__ void __launch_bounds__(stream_threads<GB, NSC>(), 1)
             bool vn = false;
             if (nxt) {
                 kn = run_from(p, tn, k);
-                ln = tile_loc(p, tn, kn);
+                ln = tile_loc(p, tn, kn, act);
                 Rn = ln.v.row0 + ln.r0 + lane;
                 vn = ln.r0 + lane < ln.v.out;
             }
@@ -457,6 +466,7 @@ __global__ void __launch_bounds__(stream_threads<GB, NSC>(), 1)
             k = kn;
         }
     }
+  }
 }
 
 __global__ void smem_base_probe_kernel(int *out) {
@@ -537,6 +547,7 @@ cudaError_t launch_stream(const StreamParams &p, int ctas, cudaStream_t st) {
     StreamParamsN<kSmallStreamRuns> q;
     q.shape = p.shape;
     q.x = p.x;
+    q.acts = p.acts;
     q.nruns = p.nruns;
     q.total_tiles = p.total_tiles;
     q.smem_base = p.smem_base;

@@ -36,6 +36,7 @@
 //
 // Positions live in device memory, so a step can be captured once as a
 // CUDA graph and replayed.
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstring>
@@ -230,73 +231,84 @@ __global__ void __launch_bounds__(kThreads) mhc_in_kernel(const float *__restric
         xq[((size_t)s * kLanes + k) * kD + c] = (float)quant8(v[k], sc) * sc;
 }
 
-// mhc.go:316 sinkhornExp / :374 sinkhornLog on a 4×4 matrix held by lanes
-// 0..15 of one warp (lane e: row e/4, column e%4); every row and column sum
-// is formed in the reference's order by each lane of that row or column.
-__device__ float sinkhorn_lane(float k, int lane) {
-    const unsigned full = 0x0000ffffu;  // lanes 0..15 only
-    float lo = k, hi = k;
+// mhc.go:316 sinkhornExp / :374 sinkhornLog, one stream per thread with the
+// 4×4 matrix in registers: h_res = sinkhorn(a_res·(nx @ φ_res) + b_res).
+// Only the mix at the layer's end reads it, so it runs beside the block.
+__global__ void sinkhorn_kernel(const LayerK L, const float *__restrict__ phi_res, float *__restrict__ hr,
+                                int streams) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= streams) return;
+    constexpr int n = kLanes, nn = kLanes * kLanes;
+    float k[nn];
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) {
-        lo = fminf(lo, __shfl_xor_sync(full, lo, o, 16));
-        hi = fmaxf(hi, __shfl_xor_sync(full, hi, o, 16));
+    for (int i = 0; i < nn; i++) {
+        const float t = L.a_res * phi_res[(size_t)s * nn + i];
+        k[i] = t + L.b_res[i];
+    }
+    float lo = k[0], hi = k[0];
+#pragma unroll
+    for (int i = 1; i < nn; i++) {
+        lo = fminf(lo, k[i]);
+        hi = fmaxf(hi, k[i]);
     }
     const double spread = (double)hi - (double)lo;
-    const int r = (lane & 15) >> 2, c = lane & 3;
-    const bool exp_path =
-        !(isinf(spread) || isnan(spread) || spread + 2.0 * 20.0 * log(4.0) > 700.0);
-    if (exp_path) {
-        double e = exp((double)k - (double)hi);
+    if (!(isinf(spread) || isnan(spread) || spread + 2.0 * 20.0 * log((double)n) > 700.0)) {
+        double e[nn];
+#pragma unroll
+        for (int i = 0; i < nn; i++) e[i] = exp((double)k[i] - (double)hi);
         for (int it = 0; it < 20; it++) {
-            double v0 = __shfl_sync(full, e, r * 4 + 0, 16), v1 = __shfl_sync(full, e, r * 4 + 1, 16);
-            double v2 = __shfl_sync(full, e, r * 4 + 2, 16), v3 = __shfl_sync(full, e, r * 4 + 3, 16);
-            double sum = 0.0;
-            sum += v0;
-            sum += v1;
-            sum += v2;
-            sum += v3;
-            e = e / sum;
-            v0 = __shfl_sync(full, e, 0 * 4 + c, 16), v1 = __shfl_sync(full, e, 1 * 4 + c, 16);
-            v2 = __shfl_sync(full, e, 2 * 4 + c, 16), v3 = __shfl_sync(full, e, 3 * 4 + c, 16);
-            sum = 0.0;
-            sum += v0;
-            sum += v1;
-            sum += v2;
-            sum += v3;
-            e = e / sum;
+#pragma unroll
+            for (int r = 0; r < n; r++) {
+                double sum = 0.0;
+#pragma unroll
+                for (int c = 0; c < n; c++) sum += e[r * n + c];
+#pragma unroll
+                for (int c = 0; c < n; c++) e[r * n + c] /= sum;
+            }
+#pragma unroll
+            for (int c = 0; c < n; c++) {
+                double sum = 0.0;
+#pragma unroll
+                for (int r = 0; r < n; r++) sum += e[r * n + c];
+#pragma unroll
+                for (int r = 0; r < n; r++) e[r * n + c] /= sum;
+            }
         }
-        return (float)e;
+#pragma unroll
+        for (int i = 0; i < nn; i++) hr[(size_t)s * nn + i] = (float)e[i];
+        return;
     }
-    float x = k;
     for (int it = 0; it < 20; it++) {
         for (int phase = 0; phase < 2; phase++) {
-            float v[4];
 #pragma unroll
-            for (int j = 0; j < 4; j++) v[j] = __shfl_sync(full, x, phase == 0 ? r * 4 + j : j * 4 + c, 16);
-            float m = -INFINITY;
+            for (int a = 0; a < n; a++) {
+                float m = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < 4; j++) m = fmaxf(m, v[j]);
-            if (isinf(m)) m = 0.0f;
-            float sum = 0.0f;
+                for (int j = 0; j < n; j++) m = fmaxf(m, k[phase == 0 ? a * n + j : j * n + a]);
+                if (isinf(m)) m = 0.0f;
+                float sum = 0.0f;
 #pragma unroll
-            for (int j = 0; j < 4; j++) sum += (float)exp((double)(v[j] - m));
-            x = x - (m + (float)log((double)sum));
+                for (int j = 0; j < n; j++) sum += (float)exp((double)(k[phase == 0 ? a * n + j : j * n + a] - m));
+                const float l = m + (float)log((double)sum);
+#pragma unroll
+                for (int j = 0; j < n; j++) k[phase == 0 ? a * n + j : j * n + a] -= l;
+            }
         }
     }
-    return (float)exp((double)x);
+#pragma unroll
+    for (int i = 0; i < nn; i++) hr[(size_t)s * nn + i] = (float)exp((double)k[i]);
 }
 
-// mhc.go:241 logits and :205-221 (sigmoids, u, Sinkhorn), then block.go:148
+// mhc.go:241 logits and :205-221 (sigmoids, u), then block.go:148
 // run up to the attention: the engram gate (block.go:231 applyEngram) at a
 // site, and norm_in.
 __global__ void __launch_bounds__(kThreads)
     mhc_block_in_kernel(const LayerK L, const float *__restrict__ stream, const float *__restrict__ phi_pre,
                         const float *__restrict__ phi_post, const float *__restrict__ phi_res,
                         const float *__restrict__ ek, const float *__restrict__ ev, float *__restrict__ u_out,
-                        float *__restrict__ h_out, float *__restrict__ n_out, float *__restrict__ hp_out,
-                        float *__restrict__ hr_out) {
+                        float *__restrict__ h_out, float *__restrict__ n_out, float *__restrict__ hp_out) {
     __shared__ double red[33];
-    __shared__ float pre[kLanes], post[kLanes], res[kLanes * kLanes];
+    __shared__ float pre[kLanes], post[kLanes];
     __shared__ float ux[kD], uk[kD];
     __shared__ float alpha;
     const int s = blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
@@ -307,10 +319,6 @@ __global__ void __launch_bounds__(kThreads)
             pre[lane] = sigm(t + L.b_pre[lane] + pre_off);
             const float t2 = L.a_post * phi_post[(size_t)s * kLanes + lane];
             post[lane] = 2.0f * sigm(t2 + L.b_post[lane] + post_off);
-        }
-        if (lane < kLanes * kLanes) {
-            const float t = L.a_res * phi_res[(size_t)s * kLanes * kLanes + lane];
-            res[lane] = sinkhorn_lane(t + L.b_res[lane], lane);
         }
     }
     __syncthreads();
@@ -338,7 +346,6 @@ __global__ void __launch_bounds__(kThreads)
     h_out[(size_t)s * kD + c] = h;
     n_out[(size_t)s * kD + c] = n;
     if (c < kLanes) hp_out[(size_t)s * kLanes + c] = post[c];
-    if (c < kLanes * kLanes) hr_out[(size_t)s * kLanes * kLanes + c] = res[c];
 }
 
 // cache.go:78-139 Attention.Extend up to the attention: the causal taps
@@ -495,7 +502,14 @@ __global__ void __launch_bounds__(kThreads)
     __shared__ double red[33];
     __shared__ float pv[kD], z[kD], o[kD], yT[kD], kb[kD];
     __shared__ float lg[kRank];
+    __shared__ float cv[kD * kRank];                         // cond_v
+    __shared__ float wa_s[3][kNA * kNA], wb_s[3][kNB * kNB];  // Kronecker factors
     const int s = blockIdx.x, c = threadIdx.x;
+    for (int i = c; i < kD * kRank; i += kThreads) cv[i] = L.cond_v[i];
+    for (int st = 0; st < 3; st++) {
+        for (int i = c; i < kNA * kNA; i += kThreads) wa_s[st][i] = L.wa[st][i];
+        for (int i = c; i < kNB * kNB; i += kThreads) wb_s[st][i] = L.wb[st][i];
+    }
     const float y = L.xresid * zc_norm_row(cy[(size_t)s * kD + c], L.g_xpost[c], red);
     const float h2 = h[(size_t)s * kD + c] + y;
     const float p = zc_norm_row(h2, L.g_pre_hada[c], red);
@@ -504,7 +518,7 @@ __global__ void __launch_bounds__(kThreads)
     // cond = 1 + softmax(p @ cond_v) @ cond_u
     if (c < kRank) {
         float acc = 0.0f;
-        for (int i = 0; i < kD; i++) acc = acc + pv[i] * L.cond_v[i * kRank + c];
+        for (int i = 0; i < kD; i++) acc = acc + pv[i] * cv[i * kRank + c];
         lg[c] = acc;
     }
     __syncthreads();
@@ -525,16 +539,16 @@ __global__ void __launch_bounds__(kThreads)
     cond = cond + 1.0f;
     z[c] = L.d1[c] * p;
     __syncthreads();
-    kron_mix(L.wa[0], L.wb[0], p1, z, yT, kb, o);
+    kron_mix(wa_s[0], wb_s[0], p1, z, yT, kb, o);
     {
         const float a2 = L.d2[c] * cond * o[c] + L.b2[c];
         z[c] = a2 * sigm(a2);
     }
     __syncthreads();
-    kron_mix(L.wa[1], L.wb[1], p2, z, yT, kb, o);
+    kron_mix(wa_s[1], wb_s[1], p2, z, yT, kb, o);
     z[c] = L.d3[c] * o[c];
     __syncthreads();
-    kron_mix(L.wa[2], L.wb[2], nullptr, z, yT, kb, o);
+    kron_mix(wa_s[2], wb_s[2], nullptr, z, yT, kb, o);
     const float m = o[c] * L.d4[c] + h2;
     const float Y = m - u[(size_t)s * kD + c];
     float st[kLanes], out[kLanes];
@@ -617,20 +631,6 @@ __global__ void __launch_bounds__(256) xmem_kernel(const float *__restrict__ kp,
     }
 }
 
-// greedy.go:81 language: the largest logit among the language tokens (the
-// first on ties); it is the next token.
-__global__ void lang_kernel(const float *__restrict__ logits, int vocab, const int32_t *__restrict__ langs, int n,
-                            int32_t *__restrict__ tok, int32_t *__restrict__ lang, int streams) {
-    const int s = blockIdx.x * blockDim.x + threadIdx.x;
-    if (s >= streams) return;
-    const float *l = logits + (size_t)s * vocab;
-    int best = 0;
-    for (int i = 1; i < n; i++)
-        if (l[langs[i]] > l[langs[best]]) best = i;
-    tok[s] = langs[best];
-    lang[s] = langs[best];
-}
-
 // greedy.go:58-66: record the argmax (already in tok) unless the stream has
 // ended; EOS ends it.
 __global__ void record_kernel(const int32_t *__restrict__ tok, int eos, int max_out, int32_t *__restrict__ tokens,
@@ -665,6 +665,230 @@ __global__ void greedy_init_kernel(int32_t *tok, int bos, int32_t *tokens, int m
 __global__ void fill_kernel(int32_t *p, int32_t v, int n) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) p[i] = v;
+}
+
+// ----------------------------------------------------- the head's choice
+//
+// The greedy step needs only the argmax of the tied head's logits
+// (greedy.go:182), not the logits. The head (vocab × 512, CQ4) is by far
+// the largest product of a step, so it runs on the tensor cores
+// (WC_GEMM_TENSOR_CORES: fp16 operands, error bound stated in the header),
+// and only the rows that can still be the argmax are recomputed with the
+// lut kernel's exact arithmetic. Each approximate logit y_r lies within
+// B_r of the lut value l_r:
+//   |y_r − l_r| ≤ |y_r − e_r| + |e_r − l_r|   (e_r: the exact real product)
+//   |y_r − e_r| ≤ (2^-10 + (K + log2 G + 6)·2^-24)·A_r + 2^-37·(G·max|x|·Σ|ŵ_r| + max|ŵ|·Σ|x̂|)
+//   |e_r − l_r| ≤ Σ_g n_rg/√G · (G/2)·M_g/8191 + (groups + 6)·2^-24·A_r
+// with A_r = Σ_k |x̂_k||ŵ_rk| ≤ ‖x̂‖·‖ŵ_r‖ = √G·‖x‖·‖ŵ_r‖ (Cauchy-Schwarz),
+// Σ|ŵ_r| ≤ √K‖ŵ_r‖, Σ|x̂| ≤ √K‖x̂‖, M_g = max|cb|·max_g|x̂| ≤ max|cb|·‖x_g‖₁,
+// and a margin of 1.25 for the float32 evaluation of the bound. With
+// m = max_r (y_r − B_r) ≤ max_r l_r, every row whose l_r can reach the
+// maximum has y_r + B_r ≥ m: those candidates (a handful) are rescored
+// exactly, and the largest at its first index is the reference's argmax,
+// bit for bit. More than kMaxCand candidates, or a non-finite value, and
+// the stream's whole row is computed exactly instead.
+constexpr int kMaxCand = 64;
+constexpr int kHeadG = 128, kHeadBits = 4, kHeadGroups = kD / kHeadG, kHeadGB = kHeadG * kHeadBits / 8;
+
+// ‖ŵ_r‖₂ (rounded up) and max_g |n_rg| of every head row.
+__global__ void head_rownorm_kernel(const __grid_constant__ CqShape s, const CqView v, float *__restrict__ wn,
+                                    float *__restrict__ nmax) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= v.out) return;
+    double acc = 0.0;
+    float nm = 0.0f;
+    for (int g = 0; g < s.groups; g++) {
+        const size_t lrow = (size_t)g * v.ld + (size_t)(v.row0 + r);
+        const double n = fabs((double)__half2float(v.nrm[lrow]));
+        nm = fmaxf(nm, (float)n);
+        double c2 = 0.0;
+        for (int k = 0; k < s.group; k++) {
+            const int bit = k * s.bits;
+            const uint32_t code = (v.idx[lrow * s.gb + (bit >> 3)] >> (bit & 7)) & ((1u << s.bits) - 1u);
+            c2 += (double)s.cb[code] * (double)s.cb[code];
+        }
+        acc += n * n * c2 / (double)s.group;
+    }
+    wn[r] = (float)(sqrt(acc) * (1.0 + 1e-6));
+    nmax[r] = nm;
+}
+
+// Candidates of each stream's argmax from the approximate logits y.
+__global__ void __launch_bounds__(kThreads)
+    head_screen_kernel(const float *__restrict__ y, int vocab, const float *__restrict__ x, const float *__restrict__ wn,
+                       const float *__restrict__ nmax, float cb_max, float wmax, int32_t *__restrict__ cand,
+                       int32_t *__restrict__ cnt) {
+    __shared__ double red[33];
+    __shared__ float redf[33];
+    __shared__ int count;
+    __shared__ int bad;
+    const int s = blockIdx.x, t = threadIdx.x;
+    const float xv = x[(size_t)s * kD + t];
+    const double sq = block_sum((double)xv * (double)xv, red);
+    const double l1 = block_sum(fabs((double)xv), red);
+    const float xmax = block_max(fabsf(xv), redf);
+    const double sqrtG = sqrt((double)kHeadG), sqrtK = sqrt((double)kD);
+    const double gamma = 0x1p-10 + ((double)kD + 7.0 + 6.0) * 0x1p-24 + (kHeadGroups + 6) * 0x1p-24;
+    const double xh = sqrtG * sqrt(sq);
+    const float c1 = (float)(1.25 * (gamma * xh + 0x1p-37 * kHeadG * (double)xmax * sqrtK));
+    const float c2 = (float)(1.25 * 0.5 * sqrtG / 8191.0 * (double)cb_max * l1);
+    const float c3 = (float)(1.25 * 0x1p-37 * (double)wmax * sqrtK * xh);
+    if (t == 0) {
+        count = 0;
+        bad = !(isfinite(sq) && isfinite(l1));
+    }
+    const float *yr = y + (size_t)s * vocab;
+    float m = -INFINITY;
+    int nonfinite = 0;
+    for (int r = t; r < vocab; r += kThreads) {
+        const float v = yr[r];
+        if (!isfinite(v)) nonfinite = 1;
+        m = fmaxf(m, v - (c1 * wn[r] + c2 * nmax[r] + c3));
+    }
+    if (nonfinite) bad = 1;
+    // Block max of m (−inf allowed).
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((t & 31) == 0) redf[t >> 5] = m;
+    __syncthreads();
+    if (t == 0) {
+        float mm = -INFINITY;
+        for (int w = 0; w < kThreads / 32; w++) mm = fmaxf(mm, redf[w]);
+        redf[32] = mm;
+    }
+    __syncthreads();
+    m = redf[32];
+    for (int r = t; r < vocab; r += kThreads) {
+        if (yr[r] + (c1 * wn[r] + c2 * nmax[r] + c3) >= m) {
+            const int k = atomicAdd(&count, 1);
+            if (k < kMaxCand) cand[(size_t)s * kMaxCand + k] = r;
+        }
+    }
+    __syncthreads();
+    if (t == 0) cnt[s] = (bad || count > kMaxCand || count == 0) ? -1 : count;
+}
+
+// The lut kernel's exact value of head row r for the activation whose
+// tables are tab (nibble tables [2·256][16]) and steps, computed by one
+// warp: lane l sums the 16 nibbles of its 8 index bytes, eight lanes make
+// a group's exact integer sum, and the group terms are added in order.
+__device__ float head_row_exact(const CqView &v, int r, const int16_t *tab, const float *steps, int lane) {
+    const int g = lane >> 3, off = (lane & 7) * 8;
+    const size_t lrow = (size_t)g * v.ld + (size_t)(v.row0 + r);
+    const uint2 w = __ldg(reinterpret_cast<const uint2 *>(v.idx + lrow * kHeadGB + off));
+    int32_t sum = 0;
+    const uint32_t ws[2] = {w.x, w.y};
+#pragma unroll
+    for (int b = 0; b < 8; b++) {
+        const uint32_t byte = (ws[b >> 2] >> (8 * (b & 3))) & 0xffu;
+        const int pos = g * kHeadGB + off + b;
+        sum += tab[(2 * pos) * 16 + (byte & 15u)];
+        sum += tab[(2 * pos + 1) * 16 + (byte >> 4)];
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    const float coef = __half2float(v.nrm[lrow]) * steps[g];
+    const float term = (float)sum * coef;
+    float acc = 0.0f;
+#pragma unroll
+    for (int gg = 0; gg < kHeadGroups; gg++) acc = acc + __shfl_sync(0xffffffffu, term, gg * 8);
+    return acc;
+}
+
+// head_argmax's key (decode_head.cu): the largest key is the largest value
+// at its first index; NaN keys are 0.
+__device__ __forceinline__ unsigned long long pick_key(float v, int i) {
+    if (v != v) return 0ull;
+    const uint32_t b = __float_as_uint(v == 0.0f ? 0.0f : v);
+    const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)ord << 32) | (uint32_t)(0xffffffffu - (uint32_t)i);
+}
+
+// Exact rescoring and the choice, one CTA per stream. mode 0: the
+// screen's candidates (or, for cnt = −1, every row, its exact logits
+// written to y); mode 1: the fixed list (the language tokens: the largest
+// at its first position in the list, greedy.go:81).
+__global__ void __launch_bounds__(kThreads)
+    head_pick_kernel(const __grid_constant__ CqShape sh, const CqView v, const float *__restrict__ x,
+                     const int32_t *__restrict__ cand, const int32_t *__restrict__ cnt, const int32_t *__restrict__ list,
+                     int nlist, int mode, float *__restrict__ y, int32_t *__restrict__ tok, int32_t *__restrict__ lang) {
+    __shared__ float xs[kD];
+    __shared__ float steps[kHeadGroups], invs[kHeadGroups];
+    __shared__ __align__(16) int16_t tab[2 * kHeadGB * kHeadGroups * 16];
+    __shared__ unsigned long long bestw[kThreads / 32];
+    __shared__ int nan0;
+    const int s = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    // Rotation (kernel.go:384 fwht per group, stage by stage), bounds and
+    // tables exactly as cq_lut.cu builds them.
+    xs[t] = x[(size_t)s * kD + t];
+    if (t == 0) nan0 = 0;
+    __syncthreads();
+    for (int h = 1; h < kHeadG; h <<= 1) {
+        if (t < kD / 2) {
+            const int g = t / (kHeadG / 2), q = t % (kHeadG / 2);
+            const int j = g * kHeadG + (q / h) * 2 * h + (q % h);
+            const float a = xs[j], c = xs[j + h];
+            xs[j] = __fadd_rn(a, c);
+            xs[j + h] = __fsub_rn(a, c);
+        }
+        __syncthreads();
+    }
+    if (warp < kHeadGroups) {
+        float mx = 0.0f;
+        for (int q = lane; q < kHeadG; q += 32) mx = fmaxf(mx, fabsf(xs[warp * kHeadG + q]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) {
+            const float m = __fmul_rn(sh.cb_max, mx);
+            invs[warp] = m > 0.0f ? __fdiv_rn((float)kLutQ, m) : 0.0f;
+            steps[warp] = __fmul_rn(m, sh.lut_step);
+        }
+    }
+    __syncthreads();
+    for (int e = t; e < kD * 16; e += kThreads) {  // 4-bit: one nibble position per column
+        const int pos = e >> 4, c = e & 15;
+        const float a = __fmul_rn(xs[pos], invs[pos / kHeadG]);
+        tab[e] = (int16_t)__float2int_rn(__fmul_rn(sh.cb[c], a));
+    }
+    __syncthreads();
+    unsigned long long best = 0ull;
+    const int n = cnt ? cnt[s] : 0;
+    if (mode == 1) {
+        for (int k = warp; k < nlist; k += kThreads / 32) {
+            const float val = head_row_exact(v, list[k], tab, steps, lane);
+            const unsigned long long key = pick_key(val, k);
+            best = key > best ? key : best;
+        }
+    } else if (n >= 0) {
+        for (int k = warp; k < n; k += kThreads / 32) {
+            const int r = cand[(size_t)s * kMaxCand + k];
+            const float val = head_row_exact(v, r, tab, steps, lane);
+            const unsigned long long key = pick_key(val, r);
+            best = key > best ? key : best;
+        }
+    } else {
+        for (int r = warp; r < v.out; r += kThreads / 32) {
+            const float val = head_row_exact(v, r, tab, steps, lane);
+            if (lane == 0) y[(size_t)s * v.out + r] = val;
+            if (r == 0 && val != val) nan0 = 1;
+            const unsigned long long key = pick_key(val, r);
+            best = key > best ? key : best;
+        }
+    }
+    if (lane == 0) bestw[warp] = best;
+    __syncthreads();
+    if (t == 0) {
+        unsigned long long b = 0ull;
+        for (int w = 0; w < kThreads / 32; w++) b = bestw[w] > b ? bestw[w] : b;
+        const int i = (int)(0xffffffffu - (uint32_t)(b & 0xffffffffull));
+        int chosen = b == 0ull || nan0 ? 0 : i;  // all NaN, or a NaN at index 0: index 0, as the reference
+        if (mode == 1) {
+            chosen = list[b == 0ull ? 0 : i];
+            lang[s] = chosen;
+        }
+        tok[s] = chosen;
+    }
 }
 
 }  // namespace
@@ -720,6 +944,11 @@ struct wc_decoder {
     float *mk = nullptr, *mv = nullptr;  // memory projection outputs [streams·frames][x_heads·x_qk | x_vd]
     void *tcbuf = nullptr;
     size_t tcbytes = 0;
+    // The head's screen (tensor cores, then exact rescoring of candidates).
+    bool screen = false;
+    float *wn = nullptr, *nmax = nullptr;  // [vocab] ‖ŵ_r‖, max_g |n_rg|
+    float wmax = 0.0f;                     // max |ŵ| of the head
+    int32_t *cand = nullptr, *ncand = nullptr;
     cudaGraphExec_t graph = nullptr;
     cudaStream_t graph_stream = nullptr;
     int graph_streams = 0;
@@ -807,8 +1036,9 @@ wc_status gemms(wc_decoder *d, std::initializer_list<const wc_cq *> ms, const fl
     } while (0)
 
 // One decoder step for every stream (decoder.go:252 Extend with one token
-// each, the token in d->tok): up to the logits in d->logits, the position
-// advanced.
+// each, the token in d->tok): up to the head's input in d->fin (the lane
+// mean after the final norm), the position advanced. The head runs after
+// it (run_head).
 wc_status step_body(wc_decoder *d, cudaStream_t st) {
     const int S = d->streams;
     const wc_decoder_desc &D = d->d;
@@ -841,8 +1071,9 @@ wc_status step_body(wc_decoder *d, cudaStream_t st) {
         DEC_ST(gemms(d, {L.ppre, L.ppost, L.pres}, d->xq, {d->phi_pre, d->phi_post, d->phi_res}, S, st));
         const float *ek = site >= 0 ? d->ek + (size_t)site * S * kD : nullptr;
         const float *ev = site >= 0 ? d->ev + (size_t)site * S * kD : nullptr;
+        DEC_LAUNCH(sinkhorn_kernel<<<(S + 63) / 64, 64, 0, st>>>(L.k, d->phi_res, d->hr, S));
         DEC_LAUNCH(mhc_block_in_kernel<<<S, kThreads, 0, st>>>(L.k, d->stream, d->phi_pre, d->phi_post, d->phi_res, ek,
-                                                               ev, d->u, d->h, d->n, d->hp, d->hr));
+                                                               ev, d->u, d->h, d->n, d->hp));
         DEC_ST(gemms(d, {L.q, L.kk, L.v, L.g}, d->n, {d->q, d->k, d->v, d->g}, S, st));
         const size_t cap = (size_t)d->cap;
         int8_t *k8 = d->k8 + (size_t)l * d->max_streams * cap * kw;
@@ -870,7 +1101,6 @@ wc_status step_body(wc_decoder *d, cudaStream_t st) {
                                                             d->stream));
     }
     DEC_LAUNCH(final_kernel<<<S, kThreads, 0, st>>>(d->stream, d->g_final, d->fin));
-    DEC_ST(gemms(d, {d->emb}, d->fin, {d->logits}, S, st));
     DEC_LAUNCH(advance_kernel<<<(S + 127) / 128, 128, 0, st>>>(d->tok, d->tokhist, d->ring_t, d->pos, S));
     return WC_OK;
 }
@@ -915,6 +1145,40 @@ wc_status run_step(wc_decoder *d, cudaStream_t st) {
     WB_CUDA(cudaGraphLaunch(d->graph, st));
     count_launch();
     d->len++;
+    return WC_OK;
+}
+
+enum HeadMode { kHeadLogits = 0, kHeadGreedy = 1, kHeadLang = 2 };
+
+// The tied head on d->fin (decoder.go:508 logits, greedy.go:182 argmax,
+// greedy.go:81 language): kHeadLogits, the exact logits into d->logits;
+// kHeadGreedy, the argmax into d->tok (screened on the tensor cores and
+// rescored exactly where the head's shape allows, else exact logits and
+// their argmax); kHeadLang, the language token among d->langs into d->tok
+// and lang.
+wc_status run_head(wc_decoder *d, int mode, int nlangs, int32_t *lang, cudaStream_t st) {
+    const int S = d->streams;
+    CqShape sh{};
+    CqView v{};
+    cq_internal(d->emb, &sh, &v);
+    if (mode == kHeadLang) {
+        DEC_LAUNCH(head_pick_kernel<<<S, kThreads, 0, st>>>(sh, v, d->fin, nullptr, nullptr, d->langs, nlangs, 1,
+                                                            d->logits, d->tok, lang));
+        return WC_OK;
+    }
+    if (mode == kHeadLogits || !d->screen) {
+        DEC_ST(gemms_device(&d->emb, 1, d->fin, &d->logits, S, false, nullptr, 0, st));
+        if (mode == kHeadGreedy) {
+            cudaError_t e = launch_head_argmax(d->logits, S, d->d.vocab, 1.0f, nullptr, d->tok, st);
+            if (e != cudaSuccess) return cuda_error(e, "decoder argmax");
+        }
+        return WC_OK;
+    }
+    DEC_ST(gemms_device(&d->emb, 1, d->fin, &d->logits, S, true, d->tcbuf, d->tcbytes, st));
+    DEC_LAUNCH(head_screen_kernel<<<S, kThreads, 0, st>>>(d->logits, d->d.vocab, d->fin, d->wn, d->nmax, sh.cb_max,
+                                                          d->wmax, d->cand, d->ncand));
+    DEC_LAUNCH(head_pick_kernel<<<S, kThreads, 0, st>>>(sh, v, d->fin, d->cand, d->ncand, nullptr, 0, 0, d->logits,
+                                                        d->tok, nullptr));
     return WC_OK;
 }
 
@@ -1158,14 +1422,41 @@ extern "C" wc_status wc_decoder_create(const wc_decoder_desc *desc, int max_stre
     DEC_ST(d->alloc(&d->xvs, L * S * F * D.x_heads));
     DEC_ST(d->alloc(&d->mk, S * F * xqw));
     DEC_ST(d->alloc(&d->mv, S * F * xvw));
-    if (d->tc) {
-        // The largest rotated image any product needs: S·F rows at 512 in
-        // (the memory), S rows at 2048 in (φ).
-        const size_t a = tc_a_bytes((int)(S * F), (kD + 63) / 64), b = tc_a_bytes((int)S, (kLanes * kD + 63) / 64);
-        d->tcbytes = std::max(a, b);
+    {
+        // The rotated image of the tensor-core products: the head's (S rows
+        // at 512 in), and with WC_DECODER_TENSOR_CORES every product's (S·F
+        // rows at 512 in for the memory, S rows at 2048 in for φ).
+        size_t need = tc_a_bytes((int)S, (kD + 63) / 64);
+        if (d->tc)
+            need = std::max(need, std::max(tc_a_bytes((int)(S * F), (kD + 63) / 64),
+                                           tc_a_bytes((int)S, (kLanes * kD + 63) / 64)));
+        d->tcbytes = need;
         unsigned char *p = nullptr;
         DEC_ST(d->alloc(&p, d->tcbytes));
         d->tcbuf = p;
+    }
+    {
+        CqShape sh{};
+        CqView v{};
+        cq_internal(d->emb, &sh, &v);
+        d->screen = sh.group == kHeadG && sh.bits == kHeadBits && sh.in == kD && sh.groups == kHeadGroups;
+        if (d->screen) {
+            DEC_ST(wc_cq_prepare_tc(d->emb));
+            DEC_ST(d->alloc(&d->wn, D.vocab));
+            DEC_ST(d->alloc(&d->nmax, D.vocab));
+            DEC_ST(d->alloc(&d->cand, S * kMaxCand));
+            DEC_ST(d->alloc(&d->ncand, S));
+            head_rownorm_kernel<<<(D.vocab + 255) / 256, 256>>>(sh, v, d->wn, d->nmax);
+            count_launch();
+            WB_CUDA(cudaGetLastError());
+            std::vector<float> nm(D.vocab);
+            WB_CUDA(cudaMemcpy(nm.data(), d->nmax, D.vocab * sizeof(float), cudaMemcpyDeviceToHost));
+            float mx = 0.0f;
+            for (float x : nm) mx = std::max(mx, x);
+            d->wmax = sh.cb_max * mx * sh.inv_sqrt * 1.0001f;
+        }
+    }
+    if (d->tc) {
         for (auto &L2 : d->layers)
             for (wc_cq *m : {L2.q, L2.kk, L2.v, L2.g, L2.o, L2.xq, L2.xk, L2.xv, L2.xg, L2.xo, L2.ppre, L2.ppost,
                              L2.pres})
@@ -1250,6 +1541,7 @@ extern "C" wc_status wc_decoder_extend(wc_decoder *d, const int32_t *tokens, flo
     const int S = d->streams;
     WB_CUDA(cudaMemcpyAsync(d->tok, tokens, S * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
     DEC_ST(run_step(d, st));
+    if (logits || next) DEC_ST(run_head(d, kHeadLogits, 0, nullptr, st));
     if (logits)
         WB_CUDA(cudaMemcpyAsync(logits, d->logits, (size_t)S * d->d.vocab * sizeof(float), cudaMemcpyDeviceToDevice,
                                 st));
@@ -1287,12 +1579,12 @@ extern "C" wc_status wc_decoder_greedy(wc_decoder *d, int bos, const int32_t *la
     WB_CUDA(cudaMemcpyAsync(d->langs, d->langs_host, n_langs * sizeof(int32_t), cudaMemcpyHostToDevice, st));
     int32_t *dl = d->langs;
     DEC_LAUNCH(greedy_init_kernel<<<S, 128, 0, st>>>(d->tok, bos, tokens, out_w, counts, eos_hit, d->done, S));
+    (void)dl;
     DEC_ST(run_step(d, st));
-    DEC_LAUNCH(lang_kernel<<<(S + 127) / 128, 128, 0, st>>>(d->logits, D.vocab, dl, n_langs, d->tok, lang, S));
+    DEC_ST(run_head(d, kHeadLang, n_langs, lang, st));
     for (int step = 0; step < max_tokens - 1; step++) {
         DEC_ST(run_step(d, st));
-        cudaError_t e = launch_head_argmax(d->logits, S, D.vocab, 1.0f, nullptr, d->tok, st);
-        if (e != cudaSuccess) return cuda_error(e, "decoder argmax");
+        DEC_ST(run_head(d, kHeadGreedy, 0, nullptr, st));
         DEC_LAUNCH(record_kernel<<<(S + 127) / 128, 128, 0, st>>>(d->tok, eos, out_w, tokens, counts, eos_hit, d->done,
                                                                   S));
     }

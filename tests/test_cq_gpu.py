@@ -431,3 +431,32 @@ def test_stream_runs(wb, orc, cuda):
     got = y4.cpu().numpy().reshape(300, 160)
     for j, i in enumerate(order):
         assert bits_eq(got[place[j]], want[160 * i:160 * (i + 1)])
+
+
+# Many activations against small matrices (Whistle's decode GEMMs at
+# batched streams, its prefill and the cross-memory projection): the
+# streaming kernel over (activation, tile) items from 5 activations and 128
+# rows, the per-activation kernel (cq_lut_acts.cu) for fewer rows of group
+# 128 (the mHC φ).
+ACTS_CASES = [(8, (384, 96, 128, 512), 512, 2), (37, (512,), 512, 2), (256, (384, 512), 512, 2), (5, (96, 40), 512, 2),
+              (9, (4, 4, 16), 2048, 4), (300, (24,), 2048, 4), (12, (16384,), 512, 4), (200, (1000, 7), 512, 4),
+              (64, (1, 3, 130, 511), 1024, 2)]
+
+
+@pytest.mark.parametrize("case", ACTS_CASES, ids=[f"r{c[0]}_{'+'.join(map(str, c[1]))}x{c[2]}b{c[3]}"
+                                                  for c in ACTS_CASES])
+def test_acts_kernel_bit_exact(wb, orc, cuda, case):
+    rows, outs, in_, bits = case
+    rng = np.random.default_rng(rows + in_ + bits + len(outs))
+    ps = [wb.synth.random_packed(rng, o, in_, 128, bits, "lloyd") for o in outs]
+    for q in ps[1:]:
+        q.Codebook = ps[0].Codebook
+    ms = [wb.cq.New(p) for p in ps]
+    x = (rng.normal(size=rows * in_) * rng.choice([1e-3, 1.0, 30.0], size=rows * in_)).astype(np.float32)
+    x[:in_] = 0.0  # an all-zero activation: M = 0 in every group
+    xd = cuda.from_numpy(x).cuda()
+    yds = [cuda.full((rows * m.Out(),), float("nan"), dtype=cuda.float32, device="cuda") for m in ms]
+    wb.cq.GEMMs(ms, yds, xd, rows)
+    wants = orc.gemms_lut([orc.OracleMatrix.of(p) for p in ps], x, rows)
+    for k in range(len(ms)):
+        assert bits_eq(yds[k].cpu().numpy(), wants[k].reshape(-1)), k

@@ -116,7 +116,7 @@ def test_extend_logits_match_oracle(wb, orc, cuda, model, flags):
 
 def test_greedy_tokens_identical(wb, orc, cuda, model):
     w, od = model
-    S, F, max_tok = 16, 375, 24
+    S, F, max_tok = 32, 375, 32
     S_ = wb.synth
     enc, denc = _enc(wb, cuda, S, F, 13)
     dec = wb.decoder.Decoder(w, max_streams=S, max_frames=F, max_positions=max_tok + 1)
