@@ -25,7 +25,7 @@ namespace wb {
 
 namespace {
 
-constexpr int kActsThreads = 256;
+constexpr int kActsThreads = 512;
 
 template <int B>  // bytes a lane takes per chunk: 4 (gb 32) or 8 (gb 64)
 __global__ void __launch_bounds__(kActsThreads) cq_lut_acts_kernel(const __grid_constant__ ActsParams p) {
@@ -43,11 +43,15 @@ __global__ void __launch_bounds__(kActsThreads) cq_lut_acts_kernel(const __grid_
     const float *x = p.x + (size_t)act * s.in;
     for (int k = tid; k < pad; k += kActsThreads) xs[k] = k < s.in ? x[k] : 0.0f;
     __syncthreads();
+    // Group sizes and table widths are powers of two: shifts, not divisions.
+    const int lg2 = 31 - __clz(G);      // log2 G
+    const int lq = 31 - __clz(2 * s.row_bytes);  // log2 NQ (row_bytes a power of two here)
     const int half = G >> 1;
-    for (int h = 1; h < G; h <<= 1) {
+    for (int st = 0; (1 << st) < G; st++) {
+        const int h = 1 << st;
         for (int b = tid; b < pad / 2; b += kActsThreads) {
-            const int g = b / half, t = b % half;
-            const int j = g * G + (t / h) * 2 * h + (t % h);
+            const int g = b >> (lg2 - 1), t = b & (half - 1);
+            const int j = (g << lg2) + ((t >> st) << (st + 1)) + (t & (h - 1));
             const float a = xs[j], c = xs[j + h];
             xs[j] = __fadd_rn(a, c);
             xs[j + h] = __fsub_rn(a, c);
@@ -72,14 +76,14 @@ __global__ void __launch_bounds__(kActsThreads) cq_lut_acts_kernel(const __grid_
     }
     __syncthreads();
     for (int e = tid; e < NQ * 16; e += kActsThreads) {
-        const int nib = e / NQ, q = e - nib * NQ;
+        const int nib = e >> lq, q = e & (NQ - 1);
         float val;
         if (s.bits == 2) {
-            const float inv = invs[(2 * q) / G];
+            const float inv = invs[(2 * q) >> lg2];
             const float a = __fmul_rn(xs[2 * q], inv), b = __fmul_rn(xs[2 * q + 1], inv);
             val = __fadd_rn(__fmul_rn(s.cb[nib & 3], a), __fmul_rn(s.cb[nib >> 2], b));
         } else {
-            val = __fmul_rn(s.cb[nib], __fmul_rn(xs[q], invs[q / G]));
+            val = __fmul_rn(s.cb[nib], __fmul_rn(xs[q], invs[q >> lg2]));
         }
         tab[e] = (int16_t)__float2int_rn(val);
     }
@@ -143,7 +147,8 @@ __global__ void __launch_bounds__(kActsThreads) cq_lut_acts_kernel(const __grid_
 bool acts_eligible(const CqShape &s) {
     if (!(s.bits == 2 && s.gb == 32) && !(s.bits == 4 && s.gb == 64)) return false;  // group 128
     const int chunk = 32 * (s.gb / 8);
-    return s.row_bytes % chunk == 0 && s.pad == s.row_bytes * 8 / s.bits && acts_smem_bytes(s) <= 200 * 1024;
+    return s.row_bytes % chunk == 0 && (s.row_bytes & (s.row_bytes - 1)) == 0 && s.pad == s.row_bytes * 8 / s.bits &&
+           acts_smem_bytes(s) <= 200 * 1024;
 }
 
 size_t acts_smem_bytes(const CqShape &s) {

@@ -143,10 +143,12 @@ __device__ void rotate_and_bound(const CqShape &s, const float *x, float *xs, fl
     }
     for (int k = tid; k < pad; k += nt) xs[k] = k < s.in ? x[k] : 0.0f;
     __syncthreads();
-    for (int h = 1; h < G; h <<= 1) {
+    const int lg2 = 31 - __clz(G);  // G is a power of two: shifts, not divisions
+    for (int st = 0; (1 << st) < G; st++) {
+        const int h = 1 << st;
         for (int b = tid; b < pad / 2; b += nt) {
-            int g = b / half, t = b % half;
-            int j = g * G + (t / h) * 2 * h + (t % h);
+            const int g = b >> (lg2 - 1), t = b & (half - 1);
+            const int j = (g << lg2) + ((t >> st) << (st + 1)) + (t & (h - 1));
             float a = xs[j], c = xs[j + h];
             xs[j] = __fadd_rn(a, c);
             xs[j + h] = __fsub_rn(a, c);
@@ -177,20 +179,20 @@ __device__ void rotate_and_bound(const CqShape &s, const float *x, float *xs, fl
 __device__ void build_pass_tables(const CqShape &s, const float *xs, const float *invs, int j0, int npos,
                                   uint16_t *nib, uint16_t *tab) {
     const int tid = threadIdx.x;
-    const int G = s.group;
+    const int lg2 = 31 - __clz(s.group);  // the group is a power of two
     // Nibble tables, biased: nib[e][c][j] for the lo (e = 0) and hi (e = 1)
     // nibble of byte position j0 + j (lut.go:248-255, 272-279).
     for (int u = tid; u < 2 * npos; u += (int)blockDim.x) {
-        const int e = u / npos, j = u % npos;
+        const int e = u >= npos, j = u - e * npos;
         uint16_t *dst = nib + e * 16 * kPassPositions + j;
         const int np = 2 * (j0 + j) + e;  // nibble position in the row
         if (s.bits == 4) {
-            const float a = __fmul_rn(xs[np], invs[np / G]);
+            const float a = __fmul_rn(xs[np], invs[np >> lg2]);
 #pragma unroll
             for (int c = 0; c < 16; c++)
                 dst[c * kPassPositions] = (uint16_t)(__float2int_rn(__fmul_rn(s.cb[c], a)) + (int)kEntryBias);
         } else {
-            const float inv = invs[(2 * np) / G];
+            const float inv = invs[(2 * np) >> lg2];
             const float a = __fmul_rn(xs[2 * np], inv), b = __fmul_rn(xs[2 * np + 1], inv);
 #pragma unroll
             for (int c = 0; c < 16; c++) {
@@ -207,9 +209,11 @@ __device__ void build_pass_tables(const CqShape &s, const float *xs, const float
     // 2^15). A warp's loads and stores each cover one 128-byte row, so they
     // are conflict-free.
     const int npairs = npos / 2;
+    const bool p2 = (npairs & (npairs - 1)) == 0;  // a power of two: shifts (the usual widths)
+    const int lp = 31 - __clz(npairs);
     const uint32_t *nw = reinterpret_cast<const uint32_t *>(nib);
     for (int u = tid; u < 4 * npairs; u += (int)blockDim.x) {
-        const int jp = u % npairs, hq = u / npairs, j = 2 * jp;
+        const int jp = p2 ? (u & (npairs - 1)) : u % npairs, hq = p2 ? (u >> lp) : u / npairs, j = 2 * jp;
         uint32_t lo[16], hi[4];
 #pragma unroll
         for (int c = 0; c < 16; c++) lo[c] = nw[(c * kPassPositions + j) >> 1];

@@ -231,72 +231,63 @@ __global__ void __launch_bounds__(kThreads) mhc_in_kernel(const float *__restric
         xq[((size_t)s * kLanes + k) * kD + c] = (float)quant8(v[k], sc) * sc;
 }
 
-// mhc.go:316 sinkhornExp / :374 sinkhornLog, one stream per thread with the
-// 4×4 matrix in registers: h_res = sinkhorn(a_res·(nx @ φ_res) + b_res).
-// Only the mix at the layer's end reads it, so it runs beside the block.
+// mhc.go:316 sinkhornExp / :374 sinkhornLog: h_res = sinkhorn(a_res·(nx @
+// φ_res) + b_res), one stream per warp. Lane e (and its mirror e + 16)
+// holds entry (e / 4, e % 4); each row or column sum is formed by every
+// lane of that row or column from shuffled values in the reference's order
+// (index order from 0), then the lane divides its own entry. Only the mix at
+// the layer's end reads h_res, so it runs beside the block.
 __global__ void sinkhorn_kernel(const LayerK L, const float *__restrict__ phi_res, float *__restrict__ hr,
                                 int streams) {
-    const int s = blockIdx.x * blockDim.x + threadIdx.x;
-    if (s >= streams) return;
-    constexpr int n = kLanes, nn = kLanes * kLanes;
-    float k[nn];
+    const int lane = threadIdx.x & 31;
+    const int s = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (s >= streams) return;  // whole warps
+    constexpr int n = kLanes;
+    const int e = lane & 15, r = e >> 2, c = e & 3;
+    const unsigned full = 0xffffffffu;
+    const float t = L.a_res * phi_res[(size_t)s * n * n + e];
+    const float k = t + L.b_res[e];
+    float lo = k, hi = k;
 #pragma unroll
-    for (int i = 0; i < nn; i++) {
-        const float t = L.a_res * phi_res[(size_t)s * nn + i];
-        k[i] = t + L.b_res[i];
-    }
-    float lo = k[0], hi = k[0];
-#pragma unroll
-    for (int i = 1; i < nn; i++) {
-        lo = fminf(lo, k[i]);
-        hi = fmaxf(hi, k[i]);
+    for (int o = 8; o > 0; o >>= 1) {
+        lo = fminf(lo, __shfl_xor_sync(full, lo, o, 16));
+        hi = fmaxf(hi, __shfl_xor_sync(full, hi, o, 16));
     }
     const double spread = (double)hi - (double)lo;
+    float out;
     if (!(isinf(spread) || isnan(spread) || spread + 2.0 * 20.0 * log((double)n) > 700.0)) {
-        double e[nn];
-#pragma unroll
-        for (int i = 0; i < nn; i++) e[i] = exp((double)k[i] - (double)hi);
+        double v = exp((double)k - (double)hi);
         for (int it = 0; it < 20; it++) {
+            double sum = 0.0;
 #pragma unroll
-            for (int r = 0; r < n; r++) {
-                double sum = 0.0;
+            for (int j = 0; j < n; j++) sum += __shfl_sync(full, v, r * n + j, 16);
+            v = v / sum;
+            sum = 0.0;
 #pragma unroll
-                for (int c = 0; c < n; c++) sum += e[r * n + c];
-#pragma unroll
-                for (int c = 0; c < n; c++) e[r * n + c] /= sum;
-            }
-#pragma unroll
-            for (int c = 0; c < n; c++) {
-                double sum = 0.0;
-#pragma unroll
-                for (int r = 0; r < n; r++) sum += e[r * n + c];
-#pragma unroll
-                for (int r = 0; r < n; r++) e[r * n + c] /= sum;
-            }
+            for (int j = 0; j < n; j++) sum += __shfl_sync(full, v, j * n + c, 16);
+            v = v / sum;
         }
+        out = (float)v;
+    } else {
+        float x = k;
+        for (int it = 0; it < 20; it++) {
+            for (int phase = 0; phase < 2; phase++) {
+                float vals[n];
 #pragma unroll
-        for (int i = 0; i < nn; i++) hr[(size_t)s * nn + i] = (float)e[i];
-        return;
-    }
-    for (int it = 0; it < 20; it++) {
-        for (int phase = 0; phase < 2; phase++) {
-#pragma unroll
-            for (int a = 0; a < n; a++) {
+                for (int j = 0; j < n; j++) vals[j] = __shfl_sync(full, x, phase == 0 ? r * n + j : j * n + c, 16);
                 float m = -INFINITY;
 #pragma unroll
-                for (int j = 0; j < n; j++) m = fmaxf(m, k[phase == 0 ? a * n + j : j * n + a]);
+                for (int j = 0; j < n; j++) m = fmaxf(m, vals[j]);
                 if (isinf(m)) m = 0.0f;
                 float sum = 0.0f;
 #pragma unroll
-                for (int j = 0; j < n; j++) sum += (float)exp((double)(k[phase == 0 ? a * n + j : j * n + a] - m));
-                const float l = m + (float)log((double)sum);
-#pragma unroll
-                for (int j = 0; j < n; j++) k[phase == 0 ? a * n + j : j * n + a] -= l;
+                for (int j = 0; j < n; j++) sum += (float)exp((double)(vals[j] - m));
+                x = x - (m + (float)log((double)sum));
             }
         }
+        out = (float)exp((double)x);
     }
-#pragma unroll
-    for (int i = 0; i < nn; i++) hr[(size_t)s * nn + i] = (float)exp((double)k[i]);
+    if (lane < 16) hr[(size_t)s * n * n + e] = out;
 }
 
 // mhc.go:241 logits and :205-221 (sigmoids, u), then block.go:148
@@ -468,21 +459,24 @@ __global__ void __launch_bounds__(kThreads) cross_q_kernel(const LayerK L, const
 
 // hadamard.go:300 kronApply (+ :281 mix's permutation for stages 0 and 1)
 // of z (shared, n = 512) into dst (shared): Yᵀ = bᵀ·Zᵀ, then out = aᵀ·Y,
-// each output a sequential sum as tensor.MatMulTransB forms it.
+// each output a sequential sum as tensor.MatMulTransB forms it. Y is kept
+// as Y[j][i] = Yᵀ[i][j] (na × nb), and the lanes of a warp take consecutive
+// i (first product) and l2 (second), so every shared load is a broadcast
+// or 32 consecutive words: no bank conflicts.
 __device__ void kron_mix(const float *__restrict__ wa, const float *__restrict__ wb, const int *__restrict__ perm,
-                         const float *z, float *yT, float *kb, float *dst) {
+                         const float *z, float *Y, float *kb, float *dst) {
     const int t = threadIdx.x;
     {
-        const int i = t / kNA, j = t % kNA;  // yT[i][j], i < nb, j < na
+        const int j = t / kNB, i = t % kNB;  // Yᵀ[i][j], i < nb, j < na
         float acc = 0.0f;
         for (int l = 0; l < kNB; l++) acc = acc + wb[l * kNB + i] * z[j * kNB + l];
-        yT[i * kNA + j] = acc;
+        Y[j * kNB + i] = acc;
     }
     __syncthreads();
     {
         const int kk = t / kNB, l2 = t % kNB;  // out[kk][l2], kk < na, l2 < nb
         float acc = 0.0f;
-        for (int l = 0; l < kNA; l++) acc = acc + wa[l * kNA + kk] * yT[l2 * kNA + l];
+        for (int l = 0; l < kNA; l++) acc = acc + wa[l * kNA + kk] * Y[l * kNB + l2];
         (perm ? kb : dst)[t] = acc;
     }
     __syncthreads();
@@ -1071,7 +1065,7 @@ wc_status step_body(wc_decoder *d, cudaStream_t st) {
         DEC_ST(gemms(d, {L.ppre, L.ppost, L.pres}, d->xq, {d->phi_pre, d->phi_post, d->phi_res}, S, st));
         const float *ek = site >= 0 ? d->ek + (size_t)site * S * kD : nullptr;
         const float *ev = site >= 0 ? d->ev + (size_t)site * S * kD : nullptr;
-        DEC_LAUNCH(sinkhorn_kernel<<<(S + 63) / 64, 64, 0, st>>>(L.k, d->phi_res, d->hr, S));
+        DEC_LAUNCH(sinkhorn_kernel<<<(S + 3) / 4, 128, 0, st>>>(L.k, d->phi_res, d->hr, S));
         DEC_LAUNCH(mhc_block_in_kernel<<<S, kThreads, 0, st>>>(L.k, d->stream, d->phi_pre, d->phi_post, d->phi_res, ek,
                                                                ev, d->u, d->h, d->n, d->hp));
         DEC_ST(gemms(d, {L.q, L.kk, L.v, L.g}, d->n, {d->q, d->k, d->v, d->g}, S, st));
