@@ -131,16 +131,9 @@ def run_reference(args, world, rank):
         om = oracle.OracleMatrix.of(p)
         preps.append((oracle.PreparedLUT(om), om, rng.normal(size=in_).astype(np.float32),
                       np.zeros(out, np.float32), gemv_bytes(out, in_, bits)))
-    # calls per shape so that one step is about 1.5 s of CPU work
-    reps = []
-    for prep, om, x, y, b in preps:
-        t0 = time.perf_counter()
-        n = 0
-        while time.perf_counter() - t0 < 0.05:
-            prep.gemm(x, 1, y, threads)
-            n += 1
-        per = (time.perf_counter() - t0) / n
-        reps.append(max(1, int(0.19 / per)))
+    # The GPU line's weighting: the same number of calls of every shape
+    # (args.calls, 1000), so the two arms time the same mix of bytes.
+    reps = [args.calls] * len(preps)
 
     def step():
         for (prep, om, x, y, b), r in zip(preps, reps):
@@ -155,51 +148,70 @@ def run_reference(args, world, rank):
     dt = time.perf_counter() - t0
     total = sum(b * r for (_, _, _, _, b), r in zip(preps, reps)) * args.steps
     value = total / dt / 1e9
+    # Per shape, for ratios against the GPU line's per_shape figures.
+    per_shape = {}
+    for (prep, om, x, y, b), (out, in_, bits) in zip(preps, SWEEP):
+        t0 = time.perf_counter()
+        for _ in range(args.calls // 4):
+            prep.gemm(x, 1, y, threads)
+        per_shape[f"{out}x{in_}/{bits}b"] = round(b * (args.calls // 4) / (time.perf_counter() - t0) / 1e9, 3)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8 index, int32 sums, f32",
-        "data": "synthetic", "config": {"workload": WORKLOAD, "calls_per_shape_per_step": reps},
+        "data": "synthetic", "config": {"workload": WORKLOAD, "calls_per_shape": args.calls, "group": GROUP,
+                                        "per_shape_gbs": per_shape},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{sum(reps)} GEMV calls per step over the 8 sweep shapes, one matrix each "
-                                   f"(cache-warm, as the reference's own benchmarks run), the reference's amd64 lut "
-                                   f"path restated in C (oracle/: AVX2 lookup, tables and FWHT of lut_amd64.s) with "
-                                   f"its work split on a persistent thread pool"},
+                         "cpu_model": cpu_model(),
+                         "sample": f"{args.calls} GEMV calls of each of the 8 sweep shapes per step (the GPU line's "
+                                   f"mix), one matrix per shape (cache-warm, as the reference's own benchmarks run), "
+                                   f"the reference's amd64 lut path restated in C (oracle/: AVX2 lookup, tables and "
+                                   f"FWHT of lut_amd64.s) with its work split on a persistent thread pool"},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_decode:
+        line["decode"] = decode_cpu_baseline(pkg)
     print(json.dumps(line), flush=True)
 
 
-def cpu_baseline(seconds_per_shape=1.2):
-    """Bounded CPU sample: the oracle's lut path (reference split), all cores."""
+def cpu_baseline(seconds_per_shape=0.6, one_core_seconds=0.25):
+    """Bounded CPU sample: the oracle's lut path (reference split) on all
+    cores, and on one core, with the GPU line's weighting (equal calls of
+    every shape: each shape's time per call measured, the sweep's GB/s
+    formed from them)."""
     import oracle
 
     pkg = __import__("importlib").import_module("go-whistle_b200")
     oracle.build()
     threads = os.cpu_count() or 1
     rng = np.random.default_rng(1002)
-    total_b, total_t, calls = 0, 0.0, 0
-    for out, in_, bits in SWEEP:
-        p = pkg.synth.random_packed(rng, out, in_, GROUP, bits)
-        prep = oracle.PreparedLUT(oracle.OracleMatrix.of(p))
-        x = rng.normal(size=in_).astype(np.float32)
-        y = np.zeros(out, np.float32)
-        prep.gemm(x, 1, y, threads)
-        t0 = time.perf_counter()
-        n = 0
-        while True:
-            prep.gemm(x, 1, y, threads)
-            n += 1
-            dt = time.perf_counter() - t0
-            if dt >= seconds_per_shape and n >= 3:
-                break
-        total_b += n * gemv_bytes(out, in_, bits)
-        total_t += dt
-        calls += n
-    return {"value": round(total_b / total_t / 1e9, 3), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{calls} GEMV calls over the 8 sweep shapes (~{seconds_per_shape}s each), one matrix per "
-                      f"shape (cache-warm), the reference's amd64 lut path restated in C (AVX2 lookup, tables and "
-                      f"FWHT of lut_amd64.s) with its work split on a persistent thread pool"}
+    res = {}
+    for nthr, secs in ((threads, seconds_per_shape), (1, one_core_seconds)):
+        total_b, total_t, calls = 0, 0.0, 0
+        for out, in_, bits in SWEEP:
+            p = pkg.synth.random_packed(rng, out, in_, GROUP, bits)
+            prep = oracle.PreparedLUT(oracle.OracleMatrix.of(p))
+            x = rng.normal(size=in_).astype(np.float32)
+            y = np.zeros(out, np.float32)
+            prep.gemm(x, 1, y, nthr)
+            t0 = time.perf_counter()
+            n = 0
+            while True:
+                prep.gemm(x, 1, y, nthr)
+                n += 1
+                dt = time.perf_counter() - t0
+                if dt >= secs and n >= 3:
+                    break
+            total_b += gemv_bytes(out, in_, bits)  # one call of each shape
+            total_t += dt / n
+            calls += n
+        res[nthr] = (total_b / total_t / 1e9, calls)
+    return {"value": round(res[threads][0], 3), "unit": UNIT, "cores": threads, "kind": "port",
+            "one_core": round(res[1][0], 3), "cpu_model": cpu_model(),
+            "sample": f"{res[threads][1]} GEMV calls over the 8 sweep shapes (~{seconds_per_shape}s each; "
+                      f"{res[1][1]} more on one core), one matrix per shape (cache-warm), weighted as the GPU line "
+                      f"(equal calls of every shape); the reference's amd64 lut path restated in C (AVX2 lookup, "
+                      f"tables and FWHT of lut_amd64.s) with its work split on a persistent thread pool"}
 
 
 # ------------------------------------------------------------------ b200 ----
@@ -638,9 +650,13 @@ def run_b200(args, world, rank, local):
                 ev1.synchronize()
                 res[hot] = s.bytes * reps / (ev0.elapsed_time(ev1) / 1e3) / 1e9
                 del g
-            per_shape[f"{s.out}x{s.in_}/{s.bits}b"] = {"cold_hbm_gbs": round(res[False], 1),
-                                                        "hot_l2_gbs": round(res[True], 1),
-                                                        "weight_copies": s.copies}
+            per_shape[f"{s.out}x{s.in_}/{s.bits}b"] = {
+                "cold_hbm_gbs": round(res[False], 1), "hot_l2_gbs": round(res[True], 1),
+                "weight_copies": s.copies,
+                # Distinct weight bytes the calls cycle through, in L2 sizes:
+                # below 4 the copies are capped by the 1000 calls and part of
+                # the "cold" figure is L2-resident.
+                "l2_multiple": round(s.copies * weight_bytes(s.out, s.in_, s.bits) / l2, 2)}
 
     # Capture one step in a CUDA graph.
     graph = torch.cuda.CUDAGraph()
@@ -725,7 +741,8 @@ def run_b200(args, world, rank, local):
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u8 index, int32 table sums, f32 epilogue", "data": "synthetic",
         "config": {"workload": WORKLOAD, "calls_per_shape": args.calls, "group": GROUP,
-                   "cache": "inputs larger than L2: weights cycle through >= 4x L2 of distinct copies per shape",
+                   "cache": "inputs larger than L2: each shape's weights cycle through distinct copies, >= 4x L2 "
+                            "where the 1000 calls allow it (per_shape.l2_multiple); the step's 9.6 GB is 76x L2",
                    "launch": "cq.GEMMs over the calls of a shape (shared x), CUDA graph of one step",
                    "bytes_per_step": bytes_per_step, "parallelism": f"replicas x{world} (no collectives)",
                    "per_shape": per_shape},
