@@ -320,6 +320,33 @@ def attention_component(pkg, torch, lib, stream, streams=256, layers=8, reps=5, 
             "launches": 2 * layers}
 
 
+def exact_rows(m) -> np.ndarray:
+    """The matrix's exact float32 rows (matrix.go:161 Row), as float64."""
+    w = np.empty((m.Out(), m.In()), np.float32)
+    for r in range(m.Out()):
+        m.Row(w[r], r)
+    return w.astype(np.float64)
+
+
+def check_sample(torch, x, pairs, rows=8, seed=0):
+    """A sample of a product's output rows against the float64 product with
+    the exact weights: the reference's accept, cosine >= 0.99999 per row
+    (internal/cq/cq_test.go:196-254). pairs: (exact weights, output tensor).
+    Raises if a sampled row falls short; returns the smallest cosine."""
+    n = x.shape[0]
+    pick = np.random.default_rng(seed).choice(n, size=min(rows, n), replace=False)
+    xs = x[torch.from_numpy(pick).to(x.device)].double().cpu().numpy()
+    worst = 1.0
+    for w, y in pairs:
+        want = xs @ w.T
+        got = y[torch.from_numpy(pick).to(y.device)].double().cpu().numpy()
+        cos = np.sum(got * want, axis=1) / (np.linalg.norm(got, axis=1) * np.linalg.norm(want, axis=1))
+        worst = min(worst, float(cos.min()))
+    if not worst >= 0.99999:
+        raise RuntimeError(f"sampled output rows fall short of cosine 0.99999: {worst}")
+    return worst
+
+
 def prefill_component(pkg, torch, lib, frames=24000, reps=5):
     """encoder prefill GEMMs, X = 64 streams x 375 frames = 24,000
     rows x 512 fp32 ~N(0,1) times 4-bit G32 CQ weights 512->2048 (up),
@@ -345,6 +372,7 @@ def prefill_component(pkg, torch, lib, frames=24000, reps=5):
         with torch.cuda.stream(st):
             pkg._lib.check(lib.wc_cq_gemm_ex(*args))
             st.synchronize()
+            cos = check_sample(torch, x, [(exact_rows(m), y)])
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=st, capture_error_mode="relaxed"):
                 pkg._lib.check(lib.wc_cq_gemm_ex(*args))
@@ -364,7 +392,7 @@ def prefill_component(pkg, torch, lib, frames=24000, reps=5):
         t_roof = max(algo / (peaks_gbs * 1e9), flops / (tflops_peak * 1e12))
         res[name] = {"us": round(ms * 1e3, 2), "gbs": round(algo / (ms / 1e3) / 1e9, 1),
                      "tflops": round(flops / (ms / 1e3) / 1e12, 1), "roofline_frac": round(t_roof / (ms / 1e3), 3),
-                     "algorithmic_bytes": algo}
+                     "algorithmic_bytes": algo, "sample_min_cosine": round(cos, 8)}
     return {"workload": f"configs[2]: {frames} x in fp32 ~N(0,1) prefill rows, tensor cores (fp16 operands in the "
                         f"rotated domain, fp32 accumulate)", "per_matrix": res,
             "roofline": "max(algorithmic bytes / measured HBM, flops / measured bf16 peak)"}
@@ -456,6 +484,7 @@ def decode_gemm_component(pkg, torch, lib, streams=256, reps=20):
             call()
             st.synchronize()
             launches = lib.wc_launch_count() - n0
+            cos = check_sample(torch, x, [(exact_rows(m), y) for m, y in zip(ms, ys)])
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=st, capture_error_mode="relaxed"):
                 call()
@@ -475,11 +504,67 @@ def decode_gemm_component(pkg, torch, lib, streams=256, reps=20):
         res[name] = {"us": round(ms_call * 1e3, 2), "gbs": round(algo / (ms_call / 1e3) / 1e9, 1),
                      "tflops": round(flops / (ms_call / 1e3) / 1e12, 1),
                      "roofline_frac": round(t_roof / (ms_call / 1e3), 3), "algorithmic_bytes": algo,
-                     "launches": launches}
+                     "launches": launches, "sample_min_cosine": round(cos, 8)}
     return {"workload": f"{streams} decode streams: one activation row each, WC_GEMM_AUTO (tensor cores, fp16 "
                         f"operands, fp32 accumulate)", "per_set": res,
             "roofline": "max(algorithmic bytes / measured HBM, flops / measured bf16 peak); launch-bound at "
                         "this size"}
+
+
+def rows_sweep_component(pkg, torch, lib, reps=20, rows_list=(1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 256)):
+    """The lut kernels against the tensor cores by activation rows: each
+    row count through wc_cq_gemms_ex with flags 0 (the bit-exact lut path
+    run_lut picks) and WC_GEMM_TENSOR_CORES, `reps` calls in a CUDA graph on
+    the same weights (L2-warm, as a decode loop's are), µs per call. The
+    crossover this shows is WC_GEMM_AUTO's row threshold."""
+    rng = np.random.default_rng(4100)
+    sets = [("qkvg 384+96+128+512 x512 CQ2 G128", [384, 96, 128, 512], 512, 128, 2),
+            ("2048x512 CQ4 G32", [2048], 512, 32, 4),
+            ("head 16384x512 CQ4 G32", [16384], 512, 32, 4)]
+    st = torch.cuda.Stream()
+    sptr = ctypes.c_void_p(st.cuda_stream)
+    out = {}
+    for name, outs, in_, group, bits in sets:
+        ps, ms = [], []
+        for o in outs:
+            p = pkg.synth.random_packed(rng, o, in_, group, bits)
+            if ps:
+                p.Codebook = ps[0].Codebook
+            ps.append(p)
+            ms.append(pkg.cq.New(p))
+            pkg._lib.check(lib.wc_cq_prepare_tc(ms[-1].handle))
+        hs = (ctypes.c_void_p * len(ms))(*[m.handle.value for m in ms])
+        rows_res = {}
+        for rows in rows_list:
+            x = torch.randn(rows, in_, device="cuda", dtype=torch.float32)
+            ys = [torch.empty(rows, o, device="cuda", dtype=torch.float32) for o in outs]
+            yp = (ctypes.c_void_p * len(ms))(*[y.data_ptr() for y in ys])
+            point = {}
+            for label, flags in (("lut", 0), ("tc", 1)):
+                def call():
+                    pkg._lib.check(lib.wc_cq_gemms_ex(hs, len(ms), ctypes.c_void_p(x.data_ptr()), yp, rows,
+                                                      flags, sptr))
+
+                with torch.cuda.stream(st):
+                    call()
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=st, capture_error_mode="relaxed"):
+                        for _ in range(reps):
+                            call()
+                    g.replay()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(st)
+                    g.replay()
+                    g.replay()
+                    e1.record(st)
+                torch.cuda.synchronize()
+                point[label + "_us"] = round(e0.elapsed_time(e1) * 1e3 / (2 * reps), 2)
+                del g
+            point["faster"] = "lut" if point["lut_us"] <= point["tc_us"] else "tc"
+            rows_res[rows] = point
+        out[name] = rows_res
+    return {"workload": "rows sweep: lut (bit-exact) against tensor cores per call, L2-warm weights, CUDA graph of "
+                        f"{reps} calls", "per_set": out}
 
 
 DECODE_STREAMS = 1024   # configs[4]: streams sharded over the GPUs (stream s -> rank s mod N)
@@ -792,6 +877,7 @@ def main():
     ap.add_argument("--decode-gemm-only", action="store_true", help="only the multi-stream decode GEMM component")
     ap.add_argument("--no-decode", action="store_true", help="skip the greedy decoder component")
     ap.add_argument("--decode-only", action="store_true", help="only the greedy decoder component")
+    ap.add_argument("--rows-sweep", action="store_true", help="only the lut / tensor-core rows sweep")
     ap.add_argument("--decode-streams", type=int, default=DECODE_STREAMS, help="--decode-only: total streams")
     ap.add_argument("--decode-tokens", type=int, default=DECODE_TOKENS, help="--decode-only: tokens per stream")
     ap.add_argument("--decode-eager", action="store_true", help="--decode-only: steps as eager launches (profiling)")
@@ -813,6 +899,13 @@ def main():
         pkg = __import__("importlib").import_module("go-whistle_b200")
         torch.cuda.set_device(local)
         print(json.dumps(decode_gemm_component(pkg, torch, pkg._lib.lib())), flush=True)
+        return
+    if args.rows_sweep:
+        import torch
+
+        pkg = __import__("importlib").import_module("go-whistle_b200")
+        torch.cuda.set_device(local)
+        print(json.dumps(rows_sweep_component(pkg, torch, pkg._lib.lib())), flush=True)
         return
     if args.decode_only:
         import torch

@@ -61,6 +61,7 @@ _SIGS = {
     "wc_cq_prepare_tc": (_c_int, [_c_void_p]),
     "wc_cq_gemm_tc_noalloc": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p]),
     "wc_device_status": (_c_int, [ctypes.POINTER(_c_int)]),
+    "wc_testing_gemm_tc_stall": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p]),
     "wc_cq_gemms": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_void_p]),
     "wc_cq_gemms_host": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_size, _c_void_p, _c_void_p, _c_int]),
     "wc_cq_row": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p]),
@@ -125,8 +126,9 @@ def check(status: int) -> None:
 
 
 def exported_symbols() -> list[str]:
-    """The entry points include/whistle_b200.h declares."""
+    """The entry points the headers under include/ declare (the boundary,
+    whistle_b200.h, and the test-only whistle_b200_testing.h)."""
     import re
 
-    text = HEADER.read_text()
+    text = "\n".join(h.read_text() for h in sorted(HEADER.parent.glob("*.h")))
     return sorted(set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(wc_\w+)\s*\(", text, re.M)))

@@ -448,8 +448,11 @@ static bool try_stream(const wc_cq *const *ms, int n, const float *x, float *con
 // Activations from which a product of matrices with the stream layout runs
 // on the streaming kernel over all of them (each CTA tabulates the
 // activations its share of (activation, tile) items touches) instead of
-// the per-activation or per-tile kernels.
-static const int kStreamActsMinRows = 5;
+// the cluster, per-activation or per-tile kernels. From 2 activations it is
+// the fastest lut kernel on every measured shape (the 16384 x 512 head at
+// 2 and 4 activations: 7.9 and 9.4 µs, against 38 and 73 µs on the
+// cluster kernel, which tabulates per tile).
+static const int kStreamActsMinRows = 2;
 
 // Rows (all matrices together) from which the streaming kernel's byte
 // tables (256 entries per index byte, rebuilt per activation) pay off
@@ -496,7 +499,16 @@ static bool try_stream_acts(const wc_cq *const *ms, int n, const float *x, float
         if (p->nruns == 0) continue;
         p->total_tiles = (int)tiles;
         const long long work = tiles * (long long)rows;
-        const int ctas = work < sms ? (int)work : sms;
+        int ctas = work < sms ? (int)work : sms;
+        // A CTA's share of the (activation, tile) items is the range
+        // [W·b/ctas, W·(b+1)/ctas) of W = tiles·rows: with ctas a multiple
+        // k·rows no range crosses an activation, so each CTA tabulates one
+        // activation. Taken while it keeps three quarters of the SMs busy.
+        if (rows <= sms) {
+            long long k = sms / rows;
+            if (k > tiles) k = tiles;
+            if (4 * k * rows >= 3LL * sms) ctas = (int)(k * rows);
+        }
         cudaError_t e = launch_stream(*p, ctas, st);
         if (e != cudaSuccess) {
             *status = cuda_error(e, "cq stream kernel (activations)");
@@ -597,8 +609,8 @@ static wc_status run_lut(const wc_cq *const *ms, int n, const float *x, float *c
                          cudaStream_t st) {
     wc_status sst;
     if (try_stream(ms, n, x, ys, rows, st, &sst)) return sst;
-    if (try_split(ms, n, x, ys, rows, st, &sst)) return sst;
     if (try_stream_acts(ms, n, x, ys, rows, st, &sst)) return sst;
+    if (try_split(ms, n, x, ys, rows, st, &sst)) return sst;
     if (try_acts(ms, n, x, ys, rows, st, &sst)) return sst;
     for (int base = 0; base < n; base += kMaxLaunchMats) {
         int cnt = n - base < kMaxLaunchMats ? n - base : kMaxLaunchMats;
@@ -1047,10 +1059,17 @@ extern "C" wc_status wc_cq_prepare_tc(const wc_cq *h) {
     return WC_OK;
 }
 
-// Batch size from which WC_GEMM_AUTO takes the tensor cores: below it the
-// exact lut kernel's table work per activation is cheaper than the
-// rotation, operand images and tiles of the tensor-core path.
-static const int kTcAutoRows = 32;
+// Where WC_GEMM_AUTO takes the tensor cores. The tensor-core call costs a
+// near-constant 8-11 µs up to 256 rows (rotation, then one tile wave); the
+// lut path's time grows with activations x output rows. Measured on B200,
+// L2-warm weights, µs per call (lut / tensor cores):
+//   qkvg 1120 x 512 CQ2 G128   64 rows 8.4 / 9.4    96 rows 12.6 / 9.9
+//   2048 x 512 CQ4 G32         24 rows 8.4 / 8.5    32 rows 9.2 / 8.7
+//   16384 x 512 CQ4 G32         2 rows 7.9 / 8.6     4 rows 9.4 / 8.6
+// so the tensor cores once activations x output rows (all matrices of the
+// call) reach 65,536, from 2 activations.
+static const int kTcAutoMinRows = 2;
+static const long long kTcAutoWork = 65536;
 // Rows from which the tensor-core path uses the persistent kernel.
 static const int kTcPersistRows = 1024;
 
@@ -1060,7 +1079,7 @@ static const int kTcPersistRows = 1024;
 // scratch, so one thread's calls must not overlap on the GPU (one stream
 // per thread, as the header states).
 static wc_status run_tc(const wc_cq *const *ms, int n, const float *x, float *const *ys, int rows, cudaStream_t s,
-                        void *ext = nullptr, size_t ext_bytes = 0) {
+                        void *ext = nullptr, size_t ext_bytes = 0, bool stall = false) {
     for (int k = 0; k < n; k++) {
         wc_status st = wc_cq_prepare_tc(ms[k]);
         if (st != WC_OK) return st;
@@ -1086,6 +1105,10 @@ static wc_status run_tc(const wc_cq *const *ms, int n, const float *x, float *co
         p.m = rows;
         p.kchunks = kchunks;
         p.err = err;
+        if (stall) {
+            p.stall = 1;
+            p.spin = 1u << 14;
+        }
         // Many rows: the persistent kernel (256-row weight tiles, two TMEM
         // accumulators); few: one 128 x 128 tile per CTA.
         const bool persistent = rows >= kTcPersistRows;
@@ -1124,12 +1147,14 @@ static wc_status run_tc(const wc_cq *const *ms, int n, const float *x, float *co
     return WC_OK;
 }
 
-static bool use_tc(int rows, int flags) {
-    return (flags & WC_GEMM_TENSOR_CORES) || ((flags & WC_GEMM_AUTO) && rows >= kTcAutoRows);
+static bool use_tc(int rows, int flags, long long outs) {
+    if (flags & WC_GEMM_TENSOR_CORES) return true;
+    if (!(flags & WC_GEMM_AUTO)) return false;
+    return rows >= kTcAutoMinRows && (long long)rows * outs >= kTcAutoWork;
 }
 
 extern "C" wc_status wc_cq_gemm_ex(const wc_cq *h, const float *x, float *y, int rows, int flags, wc_stream stream) {
-    if (!use_tc(rows, flags)) return wc_cq_gemm(h, x, y, rows, stream);
+    if (!use_tc(rows, flags, h ? h->out : 0)) return wc_cq_gemm(h, x, y, rows, stream);
     if (!h) return set_error(WC_ERR_INVALID, "cq: nil matrix");
     if (rows < 0) return set_error(WC_ERR_INVALID, fmt("cq: GEMM of %d rows on [%d, %d]", rows, h->out, h->shape.in));
     if (rows == 0 || h->out == 0) return WC_OK;
@@ -1138,9 +1163,23 @@ extern "C" wc_status wc_cq_gemm_ex(const wc_cq *h, const float *x, float *y, int
     return run_tc(&h, 1, x, &y, rows, (cudaStream_t)stream);
 }
 
+// Test entry point: one tensor-core GEMM whose producer issues no copies,
+// so that the kernel's bounded waits run out with nothing in flight (the
+// kernel records its error code, frees its TMEM and returns; y is left
+// undefined). The code is read by wc_device_status.
+extern "C" wc_status wc_testing_gemm_tc_stall(const wc_cq *h, const float *x, float *y, int rows, wc_stream stream) {
+    if (!h) return set_error(WC_ERR_INVALID, "cq: nil matrix");
+    if (rows <= 0 || h->out == 0) return set_error(WC_ERR_INVALID, "cq: stall test of an empty product");
+    wc_status st = check_device(h);
+    if (st != WC_OK) return st;
+    return run_tc(&h, 1, x, &y, rows, (cudaStream_t)stream, nullptr, 0, true);
+}
+
 extern "C" wc_status wc_cq_gemms_ex(const wc_cq *const *hs, int n, const float *x, float *const *ys, int rows,
                                     int flags, wc_stream stream) {
-    if (!use_tc(rows, flags)) return wc_cq_gemms(hs, n, x, ys, rows, stream);
+    long long outs = 0;
+    for (int k = 0; hs && k < n; k++) outs += hs[k] ? hs[k]->out : 0;
+    if (!use_tc(rows, flags, outs)) return wc_cq_gemms(hs, n, x, ys, rows, stream);
     if (n < 0 || (n > 0 && (!hs || !ys))) return set_error(WC_ERR_INVALID, "cq: GEMMs of a nil list");
     if (rows < 0) return set_error(WC_ERR_INVALID, fmt("cq: GEMMs of %d rows", rows));
     for (int k = 0; k < n; k++) {

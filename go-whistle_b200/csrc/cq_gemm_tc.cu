@@ -13,7 +13,7 @@
 // arithmetic, so it is not bit-exact: every element is within the fp16
 // bound stated in include/whistle_b200.h (WC_GEMM_TENSOR_CORES) of the
 // float64 product. It is only used when asked for (wc_cq_gemm_ex with
-// WC_GEMM_TENSOR_CORES, or WC_GEMM_AUTO from 32 rows).
+// WC_GEMM_TENSOR_CORES, or WC_GEMM_AUTO past the lut kernels' crossover).
 //
 // Operand images in global memory are pre-swizzled 128 x 64 fp16 tiles
 // (K-major, 128-byte swizzle: 16-byte chunk c of row r at chunk c ^ (r & 7)),
@@ -54,9 +54,9 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
 }
 
 // Bounded wait for the phase with the given parity; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = kSpinLimit) {
     const uint32_t a = smem_u32(bar);
-    for (uint32_t it = 0; it < kSpinLimit; it++) {
+    for (uint32_t it = 0; it < limit; it++) {
         uint32_t done;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
@@ -164,6 +164,7 @@ __global__ void __launch_bounds__(kTcThreads, kStages <= 2 ? 3 : kStages <= 3 ? 
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
+    const uint32_t spin = p.spin ? p.spin : kSpinLimit;  // the waits on the other roles
 
     const unsigned char *ga = p.a + (size_t)mt * kchunks * kChunkBytes;
     const unsigned char *gb = mat.b + (size_t)nt * kchunks * kChunkBytes;
@@ -174,9 +175,9 @@ __global__ void __launch_bounds__(kTcThreads, kStages <= 2 ? 3 : kStages <= 3 ? 
         // set-up above already overlapped its tail.
         if (p.pdl) asm volatile("griddepcontrol.wait;" ::: "memory");
         int issued = 0;
-        for (int kc = 0; kc < kchunks; kc++) {
+        for (int kc = 0; kc < kchunks && !p.stall; kc++) {
             const int s = kc % kStages, round = kc / kStages;
-            if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
+            if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, spin)) {
                 atomicExch(p.err, 1);
                 atomicExch(bail, 1);
                 break;
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(kTcThreads, kStages <= 2 ? 3 : kStages <= 3 ? 
         bool ok = true;
         for (int kc = 0; kc < kchunks && ok; kc++) {
             const int s = kc % kStages, round = kc / kStages;
-            if (!mbar_wait(&full[s], round & 1)) {
+            if (!mbar_wait(&full[s], round & 1, spin)) {
                 atomicExch(p.err, 2);
                 atomicExch(bail, 1);
                 ok = false;
@@ -209,10 +210,13 @@ __global__ void __launch_bounds__(kTcThreads, kStages <= 2 ? 3 : kStages <= 3 ? 
             umma_commit(&empty[s]);
         }
         umma_commit(done);
+        // After a failed wait the epilogue may have given up on `done`
+        // already: its arrival must still land before the CTA exits.
+        if (!ok && !mbar_wait(done, 0)) atomicExch(p.err, 5);
     } else if (warp >= 2) {
         // Epilogue: warp w reads TMEM lanes 32·(w mod 4) .. +31.
         const int part = warp & 3;
-        bool ok = mbar_wait(done, 0);
+        bool ok = mbar_wait(done, 0, spin);
         if (!ok) {
             atomicExch(p.err, 3);
             atomicExch(bail, 1);
@@ -354,18 +358,19 @@ __global__ void __launch_bounds__(kPThreads, 1) cq_gemm_tc_persistent_kernel(con
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
     volatile int *vbail = bail;
+    const uint32_t spin = p.spin ? p.spin : kSpinLimit;  // the waits on the other roles
 
     if (warp == 0 && lane == 0) {
         if (p.pdl) asm volatile("griddepcontrol.wait;" ::: "memory");
         int c = 0;
-        for (int t = blockIdx.x; t < total && !*vbail; t += gridDim.x) {
+        for (int t = blockIdx.x; t < total && !*vbail && !p.stall; t += gridDim.x) {
             const int nt = t % ntg, mt = t / ntg;
             const TcMat &mat = p.mats[p_matrix(p, nt)];
             const unsigned char *ga = p.a + (size_t)mt * kchunks * kChunkBytes;
             const unsigned char *gb = mat.b + (size_t)(2 * (nt - mat.tile0)) * kchunks * kChunkBytes;
             for (int kc = 0; kc < kchunks; kc++, c++) {
                 const int s = c % kPStages, round = c / kPStages;
-                if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
+                if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, spin)) {
                     atomicExch(p.err, 11);
                     atomicExch(bail, 1);
                     break;
@@ -384,7 +389,7 @@ __global__ void __launch_bounds__(kPThreads, 1) cq_gemm_tc_persistent_kernel(con
         int c = 0, i = 0;
         for (int t = blockIdx.x; t < total && !*vbail; t += gridDim.x, i++) {
             const int b = i & 1, u = i >> 1;
-            if (u > 0 && !mbar_wait(&acce[b], (u - 1) & 1)) {
+            if (u > 0 && !mbar_wait(&acce[b], (u - 1) & 1, spin)) {
                 atomicExch(p.err, 13);
                 atomicExch(bail, 1);
                 break;
@@ -394,7 +399,7 @@ __global__ void __launch_bounds__(kPThreads, 1) cq_gemm_tc_persistent_kernel(con
             bool ok = true;
             for (int kc = 0; kc < kchunks; kc++, c++) {
                 const int s = c % kPStages, round = c / kPStages;
-                if (!mbar_wait(&full[s], round & 1)) {
+                if (!mbar_wait(&full[s], round & 1, spin)) {
                     atomicExch(p.err, 14);
                     atomicExch(bail, 1);
                     ok = false;
@@ -408,7 +413,14 @@ __global__ void __launch_bounds__(kPThreads, 1) cq_gemm_tc_persistent_kernel(con
                     umma_f16_n256(d, umma_desc(a0 + 32 * k), umma_desc(b0 + 32 * k), (kc > 0 || k > 0) ? 1u : 0u);
                 umma_commit(&empty[s]);
             }
-            if (!ok) break;
+            if (!ok) {
+                // MMAs of this tile may still be running: let them finish
+                // (bounded) before the teardown frees their TMEM. An
+                // epilogue warp that sees accf[b] now also sees the bail.
+                umma_commit(&accf[b]);
+                if (!mbar_wait(&accf[b], u & 1)) atomicExch(p.err, 16);
+                break;
+            }
             umma_commit(&accf[b]);
         }
     } else if (warp >= 2) {
@@ -418,7 +430,7 @@ __global__ void __launch_bounds__(kPThreads, 1) cq_gemm_tc_persistent_kernel(con
         int i = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x, i++) {
             const int b = i & 1, u = i >> 1;
-            bool ok = mbar_wait(&accf[b], u & 1);
+            bool ok = mbar_wait(&accf[b], u & 1, spin);
             ok = __all_sync(0xffffffffu, ok && *vbail == 0);
             if (!ok) {
                 if (lane == 0) {

@@ -92,6 +92,11 @@ struct TcParams {
     int *err;                // device error word (bounded waits)
     int nmats;               // matrices in this launch (1 .. kMaxTcMats)
     int pdl;                 // launched as a programmatic dependent of the rotation
+    // Test hook (wc_testing_gemm_tc_stall): the producer issues no copies,
+    // so the MMA and epilogue waits run out with nothing in flight; spin
+    // bounds those waits (0: the default limit). Zero in every other call.
+    int stall;
+    uint32_t spin;
     TcMat mats[kMaxTcMats];
 };
 int tc_kchunks(const CqShape &s);

@@ -122,8 +122,10 @@ enum {
      * product on the reference's test distributions, its lut kernel's
      * accept (internal/cq/cq_test.go:196-254). In <= 4096. */
     WC_GEMM_TENSOR_CORES = 1,
-    /* The tensor cores from 32 rows on, the bit-exact lut kernel below:
-     * the choice a batched caller (multi-stream decode, prefill) makes. */
+    /* The tensor cores once rows x output rows (all matrices of a GEMMs
+     * call) reach 65,536, from 2 rows; the bit-exact lut kernels below:
+     * the faster of the two on B200 at each size, the choice a batched
+     * caller (multi-stream decode, prefill) makes. */
     WC_GEMM_AUTO = 2,
 };
 

@@ -1,5 +1,5 @@
 """The C ABI without a GPU: the library loads, exports every entry point
-include/whistle_b200.h declares, and rejects bad tensors with the
+include/*.h declare, and rejects bad tensors with the
 reference's error texts before it touches a device."""
 
 from __future__ import annotations

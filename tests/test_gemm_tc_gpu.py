@@ -118,17 +118,23 @@ def test_tc_gemms_grouped(wb, cuda, rows):
         assert np.all(np.abs(got[k] - want) <= bound), k
 
 
+def auto_takes_tc(rows, outs):
+    """WC_GEMM_AUTO's rule (include/whistle_b200.h): the tensor cores once
+    rows x output rows reach 65,536, from 2 rows."""
+    return rows >= 2 and rows * outs >= 65536
+
+
 def test_auto_dispatch(wb, orc, cuda):
-    """WC_GEMM_AUTO: below 32 rows the bit-exact lut kernel (the oracle's
-    bits), from 32 rows the tensor cores (WC_GEMM_TENSOR_CORES's bits)."""
+    """WC_GEMM_AUTO: the bit-exact lut kernels (the oracle's bits) below the
+    crossover, the tensor cores (WC_GEMM_TENSOR_CORES's bits) past it."""
     rng = np.random.default_rng(77)
     ps = [wb.synth.random_packed(rng, o, 512, 128, 2, "lloyd") for o in (384, 96)]
     ps[1].Codebook = ps[0].Codebook
     ms = [wb.cq.New(p) for p in ps]
-    for rows in (8, 31, 32, 64):
+    for rows in (2, 8, 136, 137, 160):
         x = rng.normal(size=(rows, 512)).astype(np.float32)
         got = tc_gemms(wb, cuda, ms, x, WC_GEMM_AUTO)
-        if rows < 32:
+        if not auto_takes_tc(rows, 384 + 96):
             for p, g in zip(ps, got):
                 want = orc.gemm_lut(orc.OracleMatrix.of(p), x, rows)
                 assert np.array_equal(g.view(np.uint32), want.view(np.uint32))
