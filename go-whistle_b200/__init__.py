@@ -8,8 +8,12 @@ mirroring the reference's Go API for the path:
   ``GEMMs`` — internal/cq;
 - ``needle``: ``QuantizeRow``, ``QuantizeRows``, ``Int8Rows``, ``AttendInt8``,
   ``AttendInt8Spans`` — internal/needle's int8 numerics;
-- ``decoder``: ``HeadArgmax``, the head scale and greedy argmax of
-  internal/decoder on device logits;
+- ``decoder``: ``Decoder`` (the device decode step and greedy loop) and
+  ``HeadArgmax`` — internal/decoder;
+- ``cact``: the .cact container (``Parse``, ``Open``, ``File``, the writer,
+  ``whistle_names``) — internal/cact;
+- ``weights``: tensors by name over a .cact file and the decoder's weight
+  set loaded from one, a synthetic whistle.cact writer — internal/weights;
 - ``synth``: seeded synthetic tensors in the reference's formats;
 - ``dp``: data parallelism over independent streams (shards, gathering,
   missing-shard detection).
@@ -17,7 +21,7 @@ mirroring the reference's Go API for the path:
 Import it by its directory name: ``importlib.import_module("go-whistle_b200")``.
 """
 
-from . import _lib, cq, decoder, dp, needle, synth  # noqa: F401
+from . import _lib, cact, cq, decoder, dp, needle, synth, weights  # noqa: F401
 from ._lib import CQError, CudaError, Panic, WhistleError  # noqa: F401
 
 LIB_PATH = _lib.LIB_PATH

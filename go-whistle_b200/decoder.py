@@ -152,6 +152,15 @@ class Decoder:
         self.handle = h
         self.streams = 0
 
+    @classmethod
+    def Load(cls, path_or_data, max_streams: int, max_frames: int = 375, max_positions: int = 80, flags: int = 0):
+        """decoder.LoadInt8 over a .cact file (a path or its bytes): the
+        decoder's tensors by name (weights.decoder_weights), CQ records
+        uploaded as stored."""
+        from . import weights
+
+        return cls(weights.load_decoder(path_or_data), max_streams, max_frames, max_positions, flags)
+
     def __del__(self):
         if getattr(self, "handle", None) and self.handle.value:
             lib().wc_decoder_destroy(self.handle)
