@@ -87,6 +87,10 @@ _SIGS = {
     "wc_decoder_len": (_c_int, [_c_void_p]),
     "wc_decoder_memory_of": (_c_int, [_c_void_p, _c_int, ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p),
                                       ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p)]),
+    "wc_decoder_memory_beams": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_void_p]),
+    "wc_beam_default": (None, [_c_void_p]),
+    "wc_decoder_beam": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p,
+                                 _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
 }
 
 _lib = None

@@ -37,15 +37,6 @@ wc_status cuda_error(cudaError_t e, const char *what) {
     return set_error(e == cudaErrorMemoryAllocation ? WC_ERR_NOMEM : WC_ERR_CUDA, m);
 }
 
-static std::string fmt(const char *f, ...) {
-    char buf[512];
-    va_list ap;
-    va_start(ap, f);
-    vsnprintf(buf, sizeof buf, f, ap);
-    va_end(ap);
-    return buf;
-}
-
 }  // namespace wb
 
 using namespace wb;
@@ -1498,10 +1489,31 @@ extern "C" wc_status wc_attend_int8_host(const float *q, size_t q_len, int t, in
     return WC_OK;
 }
 
+static wc_status attend_streams(int streams, const float *q, int heads, const int8_t *k8, const float *ks,
+                                const int8_t *v8, const float *vs, int cap, const int32_t *nkeys, int kv_heads, int qk,
+                                int vd, float scale, int flags, float *out, int kv_group, wc_stream stream);
+
 extern "C" wc_status wc_attend_int8_streams(int streams, const float *q, int heads, const int8_t *k8, const float *ks,
                                             const int8_t *v8, const float *vs, int cap, const int32_t *nkeys,
                                             int kv_heads, int qk, int vd, float scale, int flags, float *out,
                                             wc_stream stream) {
+    return attend_streams(streams, q, heads, k8, ks, v8, vs, cap, nkeys, kv_heads, qk, vd, scale, flags, out, 1,
+                          stream);
+}
+
+namespace wb {
+wc_status attend_streams_grouped(int streams, const float *q, int heads, const int8_t *k8, const float *ks,
+                                 const int8_t *v8, const float *vs, int cap, const int32_t *nkeys, int kv_heads,
+                                 int qk, int vd, float scale, int flags, float *out, int kv_group, cudaStream_t st) {
+    if (kv_group < 1) return set_error(WC_ERR_INVALID, fmt("needle: %d streams per K/V block", kv_group));
+    return attend_streams(streams, q, heads, k8, ks, v8, vs, cap, nkeys, kv_heads, qk, vd, scale, flags, out,
+                          kv_group, (wc_stream)st);
+}
+}  // namespace wb
+
+static wc_status attend_streams(int streams, const float *q, int heads, const int8_t *k8, const float *ks,
+                                const int8_t *v8, const float *vs, int cap, const int32_t *nkeys, int kv_heads, int qk,
+                                int vd, float scale, int flags, float *out, int kv_group, wc_stream stream) {
     wc_status st = check_attend(heads, kv_heads, qk, vd, cap);
     if (st != WC_OK) return st;
     if (streams < 0) return set_error(WC_ERR_INVALID, fmt("needle: %d streams", streams));
@@ -1528,5 +1540,6 @@ extern "C" wc_status wc_attend_int8_streams(int streams, const float *q, int hea
     p.scale = scale;
     p.quant_q = (flags & WC_ATTEND_QUANT_Q) ? 1 : 0;
     p.k_aligned4 = (qk % 4 == 0) && ((kv_heads * qk) % 4 == 0) && aligned4(k8);
+    p.kv_group = kv_group;
     return run_attend(p, streams, (cudaStream_t)stream, (flags & WC_ATTEND_ANY_ORDER) != 0);
 }

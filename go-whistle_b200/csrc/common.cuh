@@ -7,6 +7,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <cstdarg>
+#include <cstdio>
 
 #include <string>
 
@@ -65,6 +67,21 @@ wc_status gemms_device(const wc_cq *const *ms, int n, const float *x, float *con
                        void *tc_buf, size_t tc_bytes, cudaStream_t st);
 // A matrix's shape and device view, for the library's own kernels.
 bool cq_internal(const wc_cq *h, CqShape *s, CqView *v);
+// printf-style formatting of an error message.
+inline std::string fmt(const char *f, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, f);
+    vsnprintf(buf, sizeof buf, f, ap);
+    va_end(ap);
+    return buf;
+}
+// wc_attend_int8_streams with kv_group streams reading each K/V block
+// (stream b reads block b / kv_group): the beams of one clip share its
+// cross-attention memory.
+wc_status attend_streams_grouped(int streams, const float *q, int heads, const int8_t *k8, const float *ks,
+                                 const int8_t *v8, const float *vs, int cap, const int32_t *nkeys, int kv_heads,
+                                 int qk, int vd, float scale, int flags, float *out, int kv_group, cudaStream_t st);
 }  // namespace wb
 
 #define WB_CUDA(call)                                            \

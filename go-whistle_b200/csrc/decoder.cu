@@ -37,6 +37,7 @@
 // Positions live in device memory, so a step can be captured once as a
 // CUDA graph and replayed.
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstdarg>
 #include <cstring>
@@ -47,6 +48,7 @@
 #include "common.cuh"
 #include "cq_kernels.cuh"
 #include "needle_kernels.cuh"
+#include "decoder_beam.cuh"
 
 namespace wb {
 
@@ -682,6 +684,7 @@ __global__ void fill_kernel(int32_t *p, int32_t v, int n) {
 // bit for bit. More than kMaxCand candidates, or a non-finite value, and
 // the stream's whole row is computed exactly instead.
 constexpr int kMaxCand = 64;
+constexpr int kBeamMaxCand = 64;  // candidates a beam step asks per row
 constexpr int kHeadG = 128, kHeadBits = 4, kHeadGroups = kD / kHeadG, kHeadGB = kHeadG * kHeadBits / 8;
 
 // ‖ŵ_r‖₂ (rounded up) and max_g |n_rg| of every head row.
@@ -885,6 +888,123 @@ __global__ void __launch_bounds__(kThreads)
     }
 }
 
+// ------------------------------------------------ beam search (search/)
+//
+// A fork (decoder.go:223 State.Fork) copies one stream's state into
+// another: per layer the int8 self-attention rows of the positions so far
+// and their scales, and the tap history; the engram value ring and token
+// history, the position and key count. Block (pair, part): parts
+// 0 .. layers-1 are the layers, part `layers` the rest. 4-byte words (every
+// row length is a multiple of 4 bytes).
+struct ForkParams {
+    int8_t *k8, *v8;
+    float *ks, *vs, *hist, *evring;
+    int32_t *tokhist, *pos, *nk_self;
+    int layers, max_streams, streams, cap, len, kw, vw, kvh, th_w, sites, ring_kd, ring;
+};
+
+__device__ __forceinline__ void copy_words(void *dst, const void *src, size_t bytes) {
+    const uint32_t *s = static_cast<const uint32_t *>(src);
+    uint32_t *d = static_cast<uint32_t *>(dst);
+    for (size_t i = threadIdx.x; i < bytes / 4; i += blockDim.x) d[i] = s[i];
+}
+
+__global__ void fork_kernel(const int32_t *__restrict__ pairs, ForkParams f) {
+    const int src = pairs[2 * blockIdx.x], dst = pairs[2 * blockIdx.x + 1];
+    const int part = blockIdx.y;
+    if (part < f.layers) {
+        const size_t l = (size_t)part, ms = (size_t)f.max_streams, cap = (size_t)f.cap, n = (size_t)f.len;
+        copy_words(f.k8 + ((l * ms + dst) * cap) * f.kw, f.k8 + ((l * ms + src) * cap) * f.kw, n * f.kw);
+        copy_words(f.v8 + ((l * ms + dst) * cap) * f.vw, f.v8 + ((l * ms + src) * cap) * f.vw, n * f.vw);
+        copy_words(f.ks + ((l * ms + dst) * cap) * f.kvh, f.ks + ((l * ms + src) * cap) * f.kvh, n * f.kvh * 4);
+        copy_words(f.vs + ((l * ms + dst) * cap) * f.kvh, f.vs + ((l * ms + src) * cap) * f.kvh, n * f.kvh * 4);
+        copy_words(f.hist + (l * ms + dst) * f.th_w, f.hist + (l * ms + src) * f.th_w, (size_t)f.th_w * 4);
+        return;
+    }
+    for (int i = 0; i < f.sites; i++) {
+        float *base = f.evring + (size_t)i * f.streams * f.ring_kd;
+        copy_words(base + (size_t)dst * f.ring_kd, base + (size_t)src * f.ring_kd, (size_t)f.ring_kd * 4);
+    }
+    if (f.ring > 0)
+        copy_words(f.tokhist + (size_t)dst * f.ring, f.tokhist + (size_t)src * f.ring, (size_t)f.ring * 4);
+    if (threadIdx.x == 0) {
+        f.pos[dst] = f.pos[src];
+        f.nk_self[dst] = f.nk_self[src];
+    }
+}
+
+// The n best next tokens of each listed row of logits (beam.go:559
+// candidates, adjust off), best first, ties to the lower id; with an
+// allowed list, the n best of its tokens, ties to the earlier entry. And
+// the row's log-sum-exp in float64 (beam.go:605 logSoftmax: m + log Σ
+// exp(x − m)), so that log p = float64(x) − lse on the host.
+constexpr int kTopThreads = 256;
+
+__device__ __forceinline__ bool top_better(float a, int ia, float b, int ib) {
+    return a > b || (a == b && ia < ib);
+}
+
+__global__ void __launch_bounds__(kTopThreads) beam_topk_kernel(const float *__restrict__ logits, int vocab,
+                                                                 const int32_t *__restrict__ rows, int n,
+                                                                 const int32_t *__restrict__ allowed, int nallowed,
+                                                                 int32_t *__restrict__ otok, float *__restrict__ ologit,
+                                                                 double *__restrict__ olse) {
+    __shared__ float sv[kTopThreads / 32];
+    __shared__ int si[kTopThreads / 32];
+    __shared__ double sd[kTopThreads / 32];
+    __shared__ int picked[kBeamMaxCand];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float *x = logits + (size_t)rows[blockIdx.x] * vocab;
+    float m = -INFINITY;
+    for (int i = tid; i < vocab; i += kTopThreads) m = fmaxf(m, x[i]);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) sv[warp] = m;
+    __syncthreads();
+    m = sv[0];
+    for (int w = 1; w < kTopThreads / 32; w++) m = fmaxf(m, sv[w]);
+    double sum = 0.0;
+    for (int i = tid; i < vocab; i += kTopThreads) sum += exp((double)x[i] - (double)m);
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) sd[warp] = sum;
+    __syncthreads();
+    if (tid == 0) {
+        double t = 0.0;
+        for (int w = 0; w < kTopThreads / 32; w++) t += sd[w];
+        olse[blockIdx.x] = (double)m + log(t);
+    }
+    const int span = allowed ? nallowed : vocab;
+    for (int r = 0; r < n; r++) {
+        float bv = -INFINITY;
+        int bi = INT_MAX;
+        for (int j = tid; j < span; j += kTopThreads) {
+            bool taken = false;
+            for (int q = 0; q < r; q++) taken |= picked[q] == j;
+            if (taken) continue;
+            const float v = x[allowed ? allowed[j] : j];
+            if (bi == INT_MAX || top_better(v, j, bv, bi)) bv = v, bi = j;
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi != INT_MAX && (bi == INT_MAX || top_better(ov, oi, bv, bi))) bv = ov, bi = oi;
+        }
+        __syncthreads();  // the previous round's readers of sv/si are done
+        if (lane == 0) sv[warp] = bv, si[warp] = bi;
+        __syncthreads();
+        if (tid == 0) {
+            float v = sv[0];
+            int i = si[0];
+            for (int w = 1; w < kTopThreads / 32; w++)
+                if (si[w] != INT_MAX && (i == INT_MAX || top_better(sv[w], si[w], v, i))) v = sv[w], i = si[w];
+            picked[r] = i;
+            const size_t o = (size_t)blockIdx.x * n + r;
+            otok[o] = i == INT_MAX ? -1 : (allowed ? allowed[i] : i);
+            ologit[o] = v;
+        }
+        __syncthreads();
+    }
+}
+
 }  // namespace
 
 }  // namespace wb
@@ -946,6 +1066,12 @@ struct wc_decoder {
     cudaGraphExec_t graph = nullptr;
     cudaStream_t graph_stream = nullptr;
     int graph_streams = 0;
+    // Streams per cross-attention memory (the beams of a clip share one).
+    int mem_group = 1;
+    // Beam steps: candidate buffers and the fork list.
+    int32_t *btok = nullptr, *brows = nullptr, *bpairs = nullptr, *ballowed = nullptr;
+    float *blogit = nullptr;
+    double *blse = nullptr;
 
     ~wc_decoder() {
         int cur = 0;
@@ -987,15 +1113,6 @@ struct wc_decoder {
 };
 
 namespace {
-
-std::string fmt(const char *f, ...) {
-    char buf[512];
-    va_list ap;
-    va_start(ap, f);
-    vsnprintf(buf, sizeof buf, f, ap);
-    va_end(ap);
-    return buf;
-}
 
 float sigmoid_host(float x) { return (float)(1.0 / (1.0 + std::exp(-(double)x))); }
 
@@ -1086,9 +1203,10 @@ wc_status step_body(wc_decoder *d, cudaStream_t st) {
         DEC_LAUNCH(cross_q_kernel<<<S, kThreads, 0, st>>>(L.k, d->cq, D.x_heads, d->cqn));
         const size_t F = (size_t)d->frames;
         const size_t xoff = (size_t)l * d->max_streams * d->max_frames;
-        DEC_ST(wc_attend_int8_streams(S, d->cqn, D.x_heads, d->xk8 + xoff * D.x_heads * kQK, d->xks + xoff * D.x_heads,
-                                      d->xv8 + xoff * D.x_heads * kVD, d->xvs + xoff * D.x_heads, (int)F, d->nk_x,
-                                      D.x_heads, kQK, kVD, d->xatt_scale, WC_ATTEND_QUANT_Q, d->catt, st));
+        DEC_ST(attend_streams_grouped(S, d->cqn, D.x_heads, d->xk8 + xoff * D.x_heads * kQK,
+                                      d->xks + xoff * D.x_heads, d->xv8 + xoff * D.x_heads * kVD,
+                                      d->xvs + xoff * D.x_heads, (int)F, d->nk_x, D.x_heads, kQK, kVD,
+                                      d->xatt_scale, WC_ATTEND_QUANT_Q, d->catt, d->mem_group, st));
         DEC_LAUNCH(gate_kernel<<<S, kThreads, 0, st>>>(d->catt, d->cg, D.x_heads * kVD));
         DEC_ST(gemms(d, {L.xo}, d->catt, {d->cy}, S, st));
         DEC_LAUNCH(block_out_kernel<<<S, kThreads, 0, st>>>(L.k, d->p1, d->p2, d->cy, d->h, d->u, d->hp, d->hr,
@@ -1177,6 +1295,91 @@ wc_status run_head(wc_decoder *d, int mode, int nlangs, int32_t *lang, cudaStrea
 }
 
 }  // namespace
+
+static wc_status dec_check(const wc_decoder *d);
+
+namespace wb {
+
+wc_status dec_beam_info(const wc_decoder *d, DecBeamInfo *out) {
+    DEC_ST(dec_check(d));
+    if (d->streams == 0) return set_error(WC_ERR_INVALID, "decoder: no memory (call wc_decoder_memory_beams first)");
+    out->streams = d->streams;
+    out->group = d->mem_group;
+    out->len = d->len;
+    out->positions = std::min(d->cap, d->d.rope_len);
+    out->vocab = d->d.vocab;
+    return WC_OK;
+}
+
+static wc_status beam_buffers(wc_decoder *d) {
+    if (d->btok) return WC_OK;
+    const size_t S = (size_t)d->max_streams;
+    DEC_ST(d->alloc(&d->btok, S * kBeamMaxCand));
+    DEC_ST(d->alloc(&d->blogit, S * kBeamMaxCand));
+    DEC_ST(d->alloc(&d->blse, S));
+    DEC_ST(d->alloc(&d->brows, S));
+    DEC_ST(d->alloc(&d->bpairs, 2 * S));
+    DEC_ST(d->alloc(&d->ballowed, (size_t)kBeamMaxCand));
+    return WC_OK;
+}
+
+wc_status dec_beam_feed(wc_decoder *d, const int32_t *tokens, cudaStream_t st) {
+    WB_CUDA(cudaMemcpyAsync(d->tok, tokens, (size_t)d->streams * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    DEC_ST(run_step(d, st));
+    return run_head(d, kHeadLogits, 0, nullptr, st);
+}
+
+wc_status dec_beam_top(wc_decoder *d, const int32_t *rows, int nrows, int n, const int32_t *allowed, int nallowed,
+                       int32_t *tok, float *logit, double *lse, cudaStream_t st) {
+    if (nrows <= 0) return WC_OK;
+    const int span = allowed ? nallowed : d->d.vocab;
+    if (n < 1 || n > kBeamMaxCand || n > span || nrows > d->streams || (allowed && nallowed > kBeamMaxCand))
+        return set_error(WC_ERR_INVALID, fmt("decoder: %d candidates of %d rows among %d tokens", n, nrows, span));
+    for (int i = 0; i < nrows; i++)
+        if (rows[i] < 0 || rows[i] >= d->streams)
+            return set_error(WC_ERR_INVALID, fmt("decoder: candidates of stream %d (%d streams)", rows[i], d->streams));
+    for (int i = 0; allowed && i < nallowed; i++)
+        if (allowed[i] < 0 || allowed[i] >= d->d.vocab)
+            return set_error(WC_ERR_INVALID, fmt("decoder: token %d out of range [0, %d)", allowed[i], d->d.vocab));
+    DEC_ST(beam_buffers(d));
+    WB_CUDA(cudaMemcpyAsync(d->brows, rows, (size_t)nrows * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    if (allowed)
+        WB_CUDA(cudaMemcpyAsync(d->ballowed, allowed, (size_t)nallowed * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    DEC_LAUNCH(beam_topk_kernel<<<nrows, kTopThreads, 0, st>>>(d->logits, d->d.vocab, d->brows, n,
+                                                                 allowed ? d->ballowed : nullptr, nallowed, d->btok,
+                                                                 d->blogit, d->blse));
+    WB_CUDA(cudaMemcpyAsync(tok, d->btok, (size_t)nrows * n * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    WB_CUDA(cudaMemcpyAsync(logit, d->blogit, (size_t)nrows * n * sizeof(float), cudaMemcpyDeviceToHost, st));
+    WB_CUDA(cudaMemcpyAsync(lse, d->blse, (size_t)nrows * sizeof(double), cudaMemcpyDeviceToHost, st));
+    WB_CUDA(cudaStreamSynchronize(st));
+    return WC_OK;
+}
+
+wc_status dec_beam_fork(wc_decoder *d, const int32_t *pairs, int npairs, cudaStream_t st) {
+    if (npairs <= 0) return WC_OK;
+    if (npairs > d->streams) return set_error(WC_ERR_INVALID, fmt("decoder: %d forks of %d streams", npairs, d->streams));
+    for (int i = 0; i < 2 * npairs; i++)
+        if (pairs[i] < 0 || pairs[i] >= d->streams)
+            return set_error(WC_ERR_INVALID, fmt("decoder: fork of stream %d (%d streams)", pairs[i], d->streams));
+    DEC_ST(beam_buffers(d));
+    const wc_decoder_desc &D = d->d;
+    WB_CUDA(cudaMemcpyAsync(d->bpairs, pairs, (size_t)npairs * 2 * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    ForkParams f{};
+    f.k8 = d->k8, f.v8 = d->v8, f.ks = d->ks, f.vs = d->vs, f.hist = d->hist, f.evring = d->evring;
+    f.tokhist = d->tokhist, f.pos = d->pos, f.nk_self = d->nk_self;
+    f.layers = D.layers, f.max_streams = d->max_streams, f.streams = d->streams, f.cap = d->cap, f.len = d->len;
+    f.kw = D.kv_heads * kQK, f.vw = D.kv_heads * kVD, f.kvh = D.kv_heads;
+    const int th = D.taps - 1 > 0 ? D.taps - 1 : 1;
+    f.th_w = th * (D.heads * kQK + D.kv_heads * kQK + D.kv_heads * kVD);
+    f.sites = (int)d->sites.size();
+    const int R = (D.etaps - 1) * (D.n_tables > 0 ? d->ring_t + 1 : 1);
+    f.ring_kd = (R > 0 ? R : 1) * kD;
+    f.ring = d->ring_t;
+    DEC_LAUNCH(fork_kernel<<<dim3((unsigned)npairs, (unsigned)(D.layers + 1)), 256, 0, st>>>(d->bpairs, f));
+    return WC_OK;
+}
+
+}  // namespace wb
 
 extern "C" wc_status wc_decoder_create(const wc_decoder_desc *desc, int max_streams, int max_frames, int max_positions,
                                        int flags, wc_decoder **out) {
@@ -1480,7 +1683,23 @@ static wc_status dec_check(const wc_decoder *d) {
     return WC_OK;
 }
 
+static wc_status memory_group(wc_decoder *d, const float *enc, int streams, int frames, int group, wc_stream stream);
+
 extern "C" wc_status wc_decoder_memory(wc_decoder *d, const float *enc, int streams, int frames, wc_stream stream) {
+    return memory_group(d, enc, streams, frames, 1, stream);
+}
+
+extern "C" wc_status wc_decoder_memory_beams(wc_decoder *d, const float *enc, int clips, int frames, int beams,
+                                             wc_stream stream) {
+    DEC_ST(dec_check(d));
+    if (beams < 1 || clips <= 0 || (long long)clips * beams > d->max_streams)
+        return set_error(WC_ERR_INVALID, fmt("decoder: %d clips x %d beams (room for %d streams)", clips, beams,
+                                             d->max_streams));
+    return memory_group(d, enc, clips, frames, beams, stream);
+}
+
+// Memory of `streams` clips, each read by `group` consecutive streams.
+static wc_status memory_group(wc_decoder *d, const float *enc, int streams, int frames, int group, wc_stream stream) {
     DEC_ST(dec_check(d));
     if (streams <= 0 || streams > d->max_streams || frames <= 0 || frames > d->max_frames || !enc)
         return set_error(WC_ERR_INVALID, fmt("decoder: encoder output of %d streams x %d frames (room for %d x %d)",
@@ -1500,15 +1719,17 @@ extern "C" wc_status wc_decoder_memory(wc_decoder *d, const float *enc, int stre
                                                                d->xv8 + xoff * D.x_heads * kVD,
                                                                d->xvs + xoff * D.x_heads));
     }
-    DEC_LAUNCH(fill_kernel<<<(streams + 255) / 256, 256, 0, st>>>(d->nk_x, frames, streams));
-    DEC_LAUNCH(fill_kernel<<<(streams + 255) / 256, 256, 0, st>>>(d->pos, 0, streams));
-    if (d->streams != streams || d->frames != frames) {
+    const int S = streams * group;
+    DEC_LAUNCH(fill_kernel<<<(S + 255) / 256, 256, 0, st>>>(d->nk_x, frames, S));
+    DEC_LAUNCH(fill_kernel<<<(S + 255) / 256, 256, 0, st>>>(d->pos, 0, S));
+    if (d->streams != S || d->frames != frames || d->mem_group != group) {
         if (d->graph) cudaGraphExecDestroy(d->graph);
         d->graph = nullptr;
         d->graph_streams = 0;
     }
-    d->streams = streams;
+    d->streams = S;
     d->frames = frames;
+    d->mem_group = group;
     d->len = 0;
     return WC_OK;
 }

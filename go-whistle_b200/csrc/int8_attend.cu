@@ -67,10 +67,11 @@ __global__ void __launch_bounds__(kAttThreads) attend_int8_kernel(const __grid_c
     // This stream's cache and key count.
     int nkeys = p.nkeys;
     if (p.nkeys_dev) nkeys = min(p.nkeys_dev[b], p.cap);
-    const int8_t *k8 = p.k8 + (size_t)b * p.cap * kcols;
-    const float *ks = p.ks + (size_t)b * p.cap * kvh;
-    const int8_t *v8 = p.v8 + (size_t)b * p.cap * vcols;
-    const float *vs = p.vs + (size_t)b * p.cap * kvh;
+    const size_t blk = kv_block(p, b);
+    const int8_t *k8 = p.k8 + blk * p.cap * kcols;
+    const float *ks = p.ks + blk * p.cap * kvh;
+    const int8_t *v8 = p.v8 + blk * p.cap * vcols;
+    const float *vs = p.vs + blk * p.cap * kvh;
 
     int lo0, hi0, lo1, hi1;
     if (p.spans) {
@@ -194,10 +195,11 @@ __global__ void __launch_bounds__(kAtt2Threads, 6) attend_int8_v2_kernel(const _
 
     int nkeys = p.nkeys;
     if (p.nkeys_dev) nkeys = min(p.nkeys_dev[b], p.cap);
-    const int8_t *k8 = p.k8 + (size_t)b * p.cap * kcols;
-    const float *ks = p.ks + (size_t)b * p.cap * kvh;
-    const int8_t *v8 = p.v8 + (size_t)b * p.cap * vcols;
-    const float *vs = p.vs + (size_t)b * p.cap * kvh;
+    const size_t blk = kv_block(p, b);
+    const int8_t *k8 = p.k8 + blk * p.cap * kcols;
+    const float *ks = p.ks + blk * p.cap * kvh;
+    const int8_t *v8 = p.v8 + blk * p.cap * vcols;
+    const float *vs = p.vs + blk * p.cap * kvh;
 
     int lo0, hi0, lo1, hi1;
     if (p.spans) {
@@ -383,10 +385,11 @@ __global__ void __launch_bounds__(kAttFThreads) attend_int8_any_kernel(const __g
 
     int nkeys = p.nkeys;
     if (p.nkeys_dev) nkeys = min(p.nkeys_dev[b], p.cap);
-    const int8_t *k8 = p.k8 + (size_t)b * p.cap * kcols;
-    const float *ks = p.ks + (size_t)b * p.cap * kvh;
-    const int8_t *v8 = p.v8 + (size_t)b * p.cap * vcols;
-    const float *vs = p.vs + (size_t)b * p.cap * kvh;
+    const size_t blk = kv_block(p, b);
+    const int8_t *k8 = p.k8 + blk * p.cap * kcols;
+    const float *ks = p.ks + blk * p.cap * kvh;
+    const int8_t *v8 = p.v8 + blk * p.cap * vcols;
+    const float *vs = p.vs + blk * p.cap * kvh;
 
     int lo0, hi0, lo1, hi1;
     if (p.spans) {

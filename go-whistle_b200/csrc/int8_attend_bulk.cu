@@ -191,10 +191,11 @@ __global__ void __launch_bounds__(kBulkThreads, (COLS >= 8 || QKV >= 6) ? 4 : 6)
 
     if (warp == 0) {
         // Producer: segment s < nch is K chunk s, else V chunk s - nch.
-        const int8_t *k8 = p.k8 + (size_t)b * p.cap * krow + (size_t)kv0 * qk;
-        const int8_t *v8 = p.v8 + (size_t)b * p.cap * vrow + (size_t)kv0 * vd;
-        const float *ks = p.ks + (size_t)b * p.cap * kvh + kv0;
-        const float *vs = p.vs + (size_t)b * p.cap * kvh + kv0;
+        const size_t blk = kv_block(p, b);
+        const int8_t *k8 = p.k8 + blk * p.cap * krow + (size_t)kv0 * qk;
+        const int8_t *v8 = p.v8 + blk * p.cap * vrow + (size_t)kv0 * vd;
+        const float *ks = p.ks + blk * p.cap * kvh + kv0;
+        const float *vs = p.vs + blk * p.cap * kvh + kv0;
         int issued = 0;
         for (int s = 0; s < 2 * nch; s++) {
             const int st = s % NS, round = s / NS;

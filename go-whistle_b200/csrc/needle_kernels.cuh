@@ -28,7 +28,13 @@ struct AttendParams {
     int *err;        // bulk kernel: device error word of its bounded waits
     int bulk_whole;  // bulk kernel: the CTA holds every KV head (contiguous chunks)
     int bulk_scales; // bulk kernel: scale chunks start 16-byte aligned (cap·kv_heads % 4 == 0)
+    int kv_group;    // streams per K/V block: stream b reads block b / kv_group (0 or 1: its own)
 };
+
+// The K/V block stream b reads.
+__host__ __device__ inline size_t kv_block(const AttendParams &p, int b) {
+    return (size_t)(p.kv_group > 1 ? b / p.kv_group : b);
+}
 
 // Shared-memory layout of the bulk kernel (int8_attend_bulk.cu), in bytes.
 struct BulkLayout {

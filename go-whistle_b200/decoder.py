@@ -80,6 +80,30 @@ WC_DECODER_TENSOR_CORES = 1
 WC_DECODER_NO_GRAPH = 2
 
 
+class BeamOptions(ctypes.Structure):
+    """search/options.go:105 Options as wc_beam_options (no Adjust hook)."""
+
+    _fields_ = [("beams", ctypes.c_int), ("max_tokens", ctypes.c_int), ("language", ctypes.c_int),
+                ("norm", ctypes.c_int), ("alpha", ctypes.c_double), ("length", ctypes.c_int), ("stop", ctypes.c_int),
+                ("admit", ctypes.c_int), ("lang_step", ctypes.c_int)]
+
+
+def DefaultBeam(**kw) -> BeamOptions:
+    """options.go:143 Default, with any field overridden by keyword."""
+    o = BeamOptions()
+    lib().wc_beam_default(ctypes.addressof(o))
+    for k, v in kw.items():
+        setattr(o, k, v)
+    return o
+
+
+WC_NORM_NONE, WC_NORM_LEN, WC_NORM_POW, WC_NORM_GNMT = 1, 2, 3, 4
+WC_LEN_TEXT, WC_LEN_TEXT_EOS, WC_LEN_SEQ = 1, 2, 3
+WC_STOP_ALL, WC_STOP_BEST, WC_STOP_K, WC_STOP_HF = 1, 2, 3, 4
+WC_ADMIT_TOPK, WC_ADMIT_ABOVE_LIVE = 1, 2
+WC_LANG_ARGMAX, WC_LANG_ARGMAX_SCORED, WC_LANG_BEAM = 1, 2, 3
+
+
 class Decoder:
     """Whistle's decoder (decoder.go:25) with int8 numerics on the GPU, for
     up to ``max_streams`` independent streams.
@@ -96,6 +120,7 @@ class Decoder:
         from . import cq
 
         self.w, self.flags = w, flags
+        self.max_positions = min(max_positions, int(w.rope_len))
         self._keep = []
 
         def f(a):
@@ -178,6 +203,39 @@ class Decoder:
         streams, frames = enc.shape[0], enc.shape[1]
         check(lib().wc_decoder_memory(self.handle, ctypes.c_void_p(enc.data_ptr()), streams, frames, self._stream()))
         self.streams = streams
+
+    def MemoryBeams(self, enc, beams: int):
+        """Memory for a beam search: enc is a CUDA float32 tensor [clips,
+        frames, dim]; the decoder then runs clips × beams streams whose
+        beams share their clip's cross memory."""
+        clips, frames = enc.shape[0], enc.shape[1]
+        check(lib().wc_decoder_memory_beams(self.handle, ctypes.c_void_p(enc.data_ptr()), clips, frames, beams,
+                                            self._stream()))
+        self.streams, self.beams = clips * beams, beams
+
+    def Beam(self, bos: int, langs, eos: int, opts: "BeamOptions" = None):
+        """search/beam.go:73 Beam for every clip of the last MemoryBeams:
+        host numpy arrays (tokens [clips, max_tokens − 1] padded with −1,
+        counts, lang, eos_hit, score, lang_logprob, logprobs [clips,
+        max_tokens])."""
+        import numpy as np
+
+        o = opts if opts is not None else DefaultBeam(beams=self.beams)
+        clips = self.streams // max(1, o.beams)
+        max_tok = o.max_tokens if o.max_tokens > 0 else self.positions_left()
+        out_w = max(1, max_tok - 1)
+        lg = np.ascontiguousarray(langs, np.int32)
+        tokens = np.zeros((clips, out_w), np.int32)
+        counts, lang, eos_hit = (np.zeros(clips, np.int32) for _ in range(3))
+        score, lang_lp = np.zeros(clips, np.float64), np.zeros(clips, np.float64)
+        logprobs = np.zeros((clips, max_tok), np.float64)
+        check(lib().wc_decoder_beam(self.handle, ctypes.addressof(o), int(bos), lg.ctypes.data, lg.size, int(eos),
+                                    tokens.ctypes.data, counts.ctypes.data, lang.ctypes.data, eos_hit.ctypes.data,
+                                    score.ctypes.data, lang_lp.ctypes.data, logprobs.ctypes.data, self._stream()))
+        return tokens, counts, lang, eos_hit.astype(bool), score, lang_lp, logprobs
+
+    def positions_left(self) -> int:
+        return self.max_positions - self.Len()
 
     def memory_of(self, l: int):
         """Layer l's device memory pointers (k8, ks, v8, vs)."""

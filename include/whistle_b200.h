@@ -438,6 +438,62 @@ wc_status wc_decoder_greedy(wc_decoder *d, int bos, const int32_t *langs, int n_
 /* Positions fed so far (every stream advances together). */
 int wc_decoder_len(const wc_decoder *d);
 
+/* ---------------------------------------------------------- beam search */
+
+/*
+ * decoder.go:157 Memory for a beam search: enc holds `clips` encoder
+ * outputs (DEVICE [clips][frames][512]); the decoder then runs
+ * clips × beams streams, stream c·beams + b being beam b of clip c, and the
+ * beams of a clip read one shared int8 cross memory (no copy per beam).
+ * Needs clips × beams <= max_streams.
+ */
+wc_status wc_decoder_memory_beams(wc_decoder *d, const float *enc, int clips, int frames, int beams,
+                                  wc_stream stream);
+
+/* search/options.go: Norm, Length, Stop, Admit, LangStep. */
+enum {
+    WC_NORM_NONE = 1, WC_NORM_LEN = 2, WC_NORM_POW = 3, WC_NORM_GNMT = 4,
+    WC_LEN_TEXT = 1, WC_LEN_TEXT_EOS = 2, WC_LEN_SEQ = 3,
+    WC_STOP_ALL = 1, WC_STOP_BEST = 2, WC_STOP_K = 3, WC_STOP_HF = 4,
+    WC_ADMIT_TOPK = 1, WC_ADMIT_ABOVE_LIVE = 2,
+    WC_LANG_ARGMAX = 1, WC_LANG_ARGMAX_SCORED = 2, WC_LANG_BEAM = 3,
+};
+
+/* search/options.go:105 Options (the Adjust hook and the probe-only
+ * finished-hypothesis variants are not offered: their zero values,
+ * Whisper's, apply). */
+typedef struct wc_beam_options {
+    int beams;      /* hypotheses kept per step, >= 1 (<= 63) */
+    int max_tokens; /* tokens after the prompt, the language token included; 0: the positions the decoder holds */
+    int language;   /* index into langs of a forced language, or −1 to detect it */
+    int norm;       /* WC_NORM_* */
+    double alpha;   /* exponent of WC_NORM_POW and WC_NORM_GNMT */
+    int length;     /* WC_LEN_*: what the normalisation's L counts */
+    int stop;       /* WC_STOP_* */
+    int admit;      /* WC_ADMIT_* (all rules but WC_STOP_ALL) */
+    int lang_step;  /* WC_LANG_* */
+} wc_beam_options;
+
+/* options.go:143 Default: 5 beams, NormLen, α 1, LenText, StopK,
+ * AdmitAboveLive, LangArgmax, max_tokens 0, language −1. */
+void wc_beam_default(wc_beam_options *o);
+
+/*
+ * search/beam.go:73 Beam for every clip of the last
+ * wc_decoder_memory_beams (whose beams must equal o->beams): the prompt
+ * [bos], the language step among langs (HOST, n_langs ids; the language's
+ * code is its index), then beam steps until the stopping rule or the token
+ * limit; beams share their prefix through forks of the decoder's stream
+ * states (decoder.go:223 State.Fork). HOST outputs per clip: tokens
+ * [clips][max_tokens − 1] (the best hypothesis' text tokens, then −1),
+ * counts, lang (its language token), eos_hit, score (its ranking score),
+ * and optionally lang_logprob [clips] and logprobs [clips][max_tokens] (the
+ * model's log p of each text token, then of EOS when eos_hit; NULL to skip).
+ */
+wc_status wc_decoder_beam(wc_decoder *d, const wc_beam_options *o, int bos, const int32_t *langs, int n_langs,
+                          int eos, int32_t *tokens, int32_t *counts, int32_t *lang, int32_t *eos_hit, double *score,
+                          double *lang_logprob, double *logprobs, wc_stream stream);
+
 /* Layer l's int8 cross-attention memory for the tests: device pointers to
  * k8 [streams][frames][x_heads·x_qk], ks [streams][frames][x_heads], v8, vs
  * (layouts as wc_attend_int8_streams reads them, cap = frames). */

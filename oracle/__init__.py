@@ -338,6 +338,8 @@ def _dec_lib():
         L.wo_sinkhorn.argtypes = [_f32p, _i32]
         L.wo_dec_new.restype = sp
         L.wo_dec_new.argtypes = [dp, _i32, _i32]
+        L.wo_dec_fork.restype = sp
+        L.wo_dec_fork.argtypes = [dp, sp]
         L.wo_dec_free.argtypes = [sp]
         L.wo_dec_memory.argtypes = [dp, sp, _f32p, _i32]
         L.wo_dec_memory_of.argtypes = [dp, sp, _i32, ctypes.POINTER(_i8p), ctypes.POINTER(_f32p),
@@ -540,6 +542,13 @@ class OracleState:
                 np.ctypeslib.as_array(ks, (F * w.x_heads,)).copy(),
                 np.ctypeslib.as_array(v8, (F * w.x_heads * w.x_vd,)).copy(),
                 np.ctypeslib.as_array(vs, (F * w.x_heads,)).copy())
+
+    def fork(self) -> "OracleState":
+        """decoder.go:223 State.Fork: an independent copy."""
+        f = OracleState.__new__(OracleState)
+        f.dec, f.frames = self.dec, self.frames
+        f.h = _dec_lib().wo_dec_fork(ctypes.byref(self.dec.d), self.h)
+        return f
 
     def extend(self, tok: int) -> np.ndarray:
         logits = np.zeros(self.dec.w.vocab, np.float32)

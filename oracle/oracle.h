@@ -206,6 +206,8 @@ typedef struct wo_dec_state wo_dec_state;
 wo_dec_state *wo_dec_new(const wo_decoder *d, int cap, int frames);
 void wo_dec_free(wo_dec_state *s);
 int wo_dec_len(const wo_dec_state *s);
+/* decoder.go:223 State.Fork: an independent copy of s. */
+wo_dec_state *wo_dec_fork(const wo_decoder *d, const wo_dec_state *s);
 
 /* decoder.go:157 Memory for enc [frames][dim] (cross.go:181 project per
  * layer); starts the sequence afresh (decoder.go:194 NewState). */

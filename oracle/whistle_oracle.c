@@ -269,6 +269,34 @@ void wo_dec_free(wo_dec_state *s) {
 
 int wo_dec_len(const wo_dec_state *s) { return s->n; }
 
+/* decoder.go:223 State.Fork: a state with s's positions that extends
+ * independently of s. The reference shares the rows so far and copies on
+ * the next append; here the copy is made at once. */
+wo_dec_state *wo_dec_fork(const wo_decoder *d, const wo_dec_state *s) {
+    wo_dec_state *f = wo_dec_new(d, s->cap, s->frames);
+    int L = d->layers, kw = d->kv_heads * d->qk, vw = d->kv_heads * d->vd;
+    size_t cap = (size_t)s->cap, fr = (size_t)s->frames;
+    memcpy(f->k8, s->k8, (size_t)L * cap * kw);
+    memcpy(f->v8, s->v8, (size_t)L * cap * vw);
+    memcpy(f->ks, s->ks, (size_t)L * cap * d->kv_heads * sizeof(float));
+    memcpy(f->vs, s->vs, (size_t)L * cap * d->kv_heads * sizeof(float));
+    int th = d->taps > 1 ? d->taps - 1 : 1;
+    memcpy(f->qh, s->qh, (size_t)L * th * d->heads * d->qk * sizeof(float));
+    memcpy(f->kh, s->kh, (size_t)L * th * kw * sizeof(float));
+    memcpy(f->vh, s->vh, (size_t)L * th * vw * sizeof(float));
+    int sites = d->n_sites > 0 ? d->n_sites : 1;
+    memcpy(f->etoks, s->etoks, (size_t)sites * (d->max_order > 1 ? d->max_order - 1 : 1) * sizeof(int));
+    int vr = (d->etaps > 1 ? d->etaps - 1 : 1) * d->max_order;
+    memcpy(f->evraw, s->evraw, (size_t)sites * vr * d->dim * sizeof(float));
+    int xkw = d->x_heads * d->x_qk, xvw = d->x_heads * d->x_vd;
+    memcpy(f->xk8, s->xk8, (size_t)L * fr * xkw);
+    memcpy(f->xv8, s->xv8, (size_t)L * fr * xvw);
+    memcpy(f->xks, s->xks, (size_t)L * fr * d->x_heads * sizeof(float));
+    memcpy(f->xvs, s->xvs, (size_t)L * fr * d->x_heads * sizeof(float));
+    f->n = s->n, f->nh = s->nh, f->ntoks = s->ntoks, f->nvraw = s->nvraw;
+    return f;
+}
+
 /* The int8 memory of layer l (for the tests): k8 [frames][x_heads·x_qk],
  * ks [frames][x_heads], v8, vs. */
 void wo_dec_memory_of(const wo_decoder *d, const wo_dec_state *s, int l, const int8_t **k8, const float **ks,
