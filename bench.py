@@ -649,6 +649,72 @@ def decode_component(pkg, torch, lib, world, rank, pg, dev, total=DECODE_STREAMS
             "parity": "token ids identical to the CPU restatement (tests/test_decoder_step_gpu.py)"}
 
 
+BEAM_CLIPS = 256  # clips searched at once, 5 beams each (1280 decoder streams)
+
+
+def beam_component(pkg, torch, lib, clips=BEAM_CLIPS, beams=5, frames=DECODE_FRAMES, max_tok=DECODE_TOKENS,
+                   cpu_clips=1):
+    """Beam search (search/beam.go with options.go Default: 5 beams, Whisper's
+    StopK rule) on the device decoder for `clips` clips of the synthetic
+    Whistle decoder: every live hypothesis is a decoder stream, the beams of
+    a clip share its cross memory, forks copy stream states on the device,
+    the search's bookkeeping runs on the host each step. The EOS id the
+    synthetic weights never reach keeps every search to the token limit
+    (the language token and 64 text steps), the longest case. Timed by CUDA
+    events on the stream around wc_decoder_beam (host gaps included); the
+    CPU figure is the oracle's restatement of the same search on the same
+    weights, one clip on one host thread."""
+    import time
+
+    S_ = pkg.synth
+    w = S_.DecoderWeights(seed=4000, vocab=DECODE_VOCAB)
+    enc = np.stack([S_.encoder_output(np.random.default_rng(7000 + c), 1, frames)[0] for c in range(clips)])
+    denc = torch.from_numpy(enc).cuda()
+    dec = pkg.decoder.Decoder(w, max_streams=clips * beams, max_frames=frames, max_positions=max_tok + 1)
+    opts = pkg.decoder.DefaultBeam(beams=beams, max_tokens=max_tok)
+    stream = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    dec.MemoryBeams(denc, beams)  # warm-up search: captures the step graph
+    dec.Beam(S_.WHISTLE_BOS, S_.WHISTLE_LANGS, S_.WHISTLE_EOS, pkg.decoder.DefaultBeam(beams=beams, max_tokens=4))
+    ev[0].record(stream)
+    dec.MemoryBeams(denc, beams)
+    ev[1].record(stream)
+    n0 = lib.wc_launch_count()
+    ev[2].record(stream)
+    tok, cnt, lang, eos_hit, score, _, _ = dec.Beam(S_.WHISTLE_BOS, S_.WHISTLE_LANGS, S_.WHISTLE_EOS, opts)
+    ev[3].record(stream)
+    torch.cuda.synchronize()
+    launches = lib.wc_launch_count() - n0
+    ms = ev[2].elapsed_time(ev[3])
+    steps = max_tok
+    hyp_tokens = clips * (1 + beams * (steps - 1))  # tokens fed to live hypotheses
+    # The CPU restatement on one clip (same weights, same options).
+    import oracle
+    from oracle import beam as bm
+
+    od = oracle.OracleDecoder(w)
+    t0 = time.perf_counter()
+    same = True
+    for c in range(cpu_clips):
+        st = od.state(max_tok + 1, frames)
+        st.memory(enc[c])
+        r = bm.search(st, S_.WHISTLE_BOS, S_.WHISTLE_LANGS, S_.WHISTLE_EOS, bm.Options(beams=beams), max_tok)
+        same &= r.tokens == tok[c, :cnt[c]].tolist() and r.lang == int(lang[c])
+    cpu_s = (time.perf_counter() - t0) / cpu_clips
+    return {"workload": f"beam search: {clips} clips x {beams} beams (options.go Default, StopK), synthetic Whistle "
+                        f"decoder (vocab {DECODE_VOCAB}, {frames} frames of cross memory shared by a clip's beams), "
+                        f"{steps} positions per clip (the language token and {steps - 1} text steps)",
+            "metric": "beam search clips/s", "value": round(clips / (ms / 1e3), 2), "unit": "clips/s",
+            "hypothesis_tokens_per_s": round(hyp_tokens / (ms / 1e3), 1), "ms_search": round(ms, 2),
+            "ms_per_step": round(ms / steps, 3), "ms_memory_prefill": round(ev[0].elapsed_time(ev[1]), 2),
+            "gpu_launches": launches,
+            "cpu_baseline": {"value": round(1.0 / cpu_s, 4), "unit": "clips/s", "cores": 1, "kind": "port",
+                             "sample": f"{cpu_clips} clip(s) through the oracle's restatement of beam.go over its "
+                                       f"decoder, one host thread"},
+            "parity": "the CPU restatement's best hypothesis for the sampled clip(s): " + ("identical" if same
+                                                                                          else "DIFFERENT")}
+
+
 def decode_cpu_baseline(pkg, streams=16, max_tok=DECODE_TOKENS, frames=DECODE_FRAMES):
     """The decoder's CPU baseline: the oracle's restatement of the
     reference's greedy decode (internal/decoder, int8 numerics, the lut
@@ -851,7 +917,8 @@ def run_b200(args, world, rank, local):
                               "int8_attention_exact_order": attention_component(pkg, torch, lib, None, flags=1),
                               "cq_gemm_prefill": prefill_component(pkg, torch, lib),
                               "cq_gemm_decode_streams": decode_gemm_component(pkg, torch, lib),
-                              "cq_gemv_single_call": single_call_component(pkg, torch, lib)}
+                              "cq_gemv_single_call": single_call_component(pkg, torch, lib),
+                              "beam_search": beam_component(pkg, torch, lib)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.only:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -878,6 +945,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the greedy decoder component")
     ap.add_argument("--decode-only", action="store_true", help="only the greedy decoder component")
     ap.add_argument("--rows-sweep", action="store_true", help="only the lut / tensor-core rows sweep")
+    ap.add_argument("--beam-only", action="store_true", help="only the beam search component")
     ap.add_argument("--decode-streams", type=int, default=DECODE_STREAMS, help="--decode-only: total streams")
     ap.add_argument("--decode-tokens", type=int, default=DECODE_TOKENS, help="--decode-only: tokens per stream")
     ap.add_argument("--decode-eager", action="store_true", help="--decode-only: steps as eager launches (profiling)")
@@ -899,6 +967,13 @@ def main():
         pkg = __import__("importlib").import_module("go-whistle_b200")
         torch.cuda.set_device(local)
         print(json.dumps(decode_gemm_component(pkg, torch, pkg._lib.lib())), flush=True)
+        return
+    if args.beam_only:
+        import torch
+
+        pkg = __import__("importlib").import_module("go-whistle_b200")
+        torch.cuda.set_device(local)
+        print(json.dumps(beam_component(pkg, torch, pkg._lib.lib())), flush=True)
         return
     if args.rows_sweep:
         import torch
