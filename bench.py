@@ -782,6 +782,7 @@ def run_b200(args, world, rank, local):
     # hot (one weight copy, L2-resident), each shape's calls in its own CUDA
     # graph so host work stays outside the timing.
     per_shape = {}
+    distinct_ms = 0.0
     with torch.cuda.stream(stream):
         for s in shapes:
             res = {}
@@ -801,8 +802,37 @@ def run_b200(args, world, rank, local):
                 ev1.synchronize()
                 res[hot] = s.bytes * reps / (ev0.elapsed_time(ev1) / 1e3) / 1e9
                 del g
+            # The calls as a decode step issues them: each GEMV its own
+            # launch on its own activation (wc_cq_gemm, batch 1), the
+            # weights cycling through the copies, in one CUDA graph.
+            xs = torch.randn(s.calls, s.in_, device="cuda", dtype=torch.float32)
+
+            def run_distinct(s=s, xs=xs):
+                for c in range(s.calls):
+                    st = lib.wc_cq_gemm(s.handles[c], ctypes.c_void_p(xs.data_ptr() + 4 * s.in_ * c),
+                                        ctypes.c_void_p(s.ys[c]), 1, sptr)
+                    if st != 0:
+                        raise RuntimeError(s._err())
+
+            run_distinct()
+            stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream, capture_error_mode="relaxed"):
+                run_distinct()
+            g.replay()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+            for _ in range(3):
+                g.replay()
+            ev1.record(stream)
+            ev1.synchronize()
+            d_ms = ev0.elapsed_time(ev1) / 3
+            distinct_ms += d_ms
+            del g, xs
             per_shape[f"{s.out}x{s.in_}/{s.bits}b"] = {
                 "cold_hbm_gbs": round(res[False], 1), "hot_l2_gbs": round(res[True], 1),
+                "distinct_x_gbs": round(s.bytes / (d_ms / 1e3) / 1e9, 1),
+                "distinct_x_us_per_call": round(d_ms * 1e3 / s.calls, 2),
                 "weight_copies": s.copies,
                 # Distinct weight bytes the calls cycle through, in L2 sizes:
                 # below 4 the copies are capped by the 1000 calls and part of
@@ -897,6 +927,12 @@ def run_b200(args, world, rank, local):
                    "launch": "cq.GEMMs over the calls of a shape (shared x), CUDA graph of one step",
                    "bytes_per_step": bytes_per_step, "parallelism": f"replicas x{world} (no collectives)",
                    "per_shape": per_shape},
+        # The same step with every GEMV on its own activation, one launch a
+        # call (as a decode step issues them, each waiting for the last):
+        # the batch-1 latency figure, beside the shared-x `value`.
+        "distinct_x": {"gbs": round(bytes_per_step / (distinct_ms / 1e3) / 1e9, 1),
+                       "ms_per_step": round(distinct_ms, 3),
+                       "launch": "wc_cq_gemm per call (batch 1, its own x), every call of a shape in one CUDA graph"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
                      "kernel": "cq_lut_stream_kernel", "bytes_per_launch": int(bytes_per_launch)},

@@ -688,12 +688,15 @@ extern "C" wc_status wc_cq_gemms(const wc_cq *const *hs, int n, const float *x, 
 // Device buffers for the host-slice entry points: grown on demand, one set
 // per calling thread, freed at thread exit.
 namespace {
+// Slots: 0 and 1 the inputs and outputs of host calls, 2 the quantiser's
+// scales, 3 the tensor cores' rotated image, 4 the host attention's arrays.
 struct HostScratch {
-    void *p[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
-    size_t n[5] = {0, 0, 0, 0, 0};
-    int device[5] = {-1, -1, -1, -1, -1};
+    static const int kSlots = 5;
+    void *p[kSlots] = {};
+    size_t n[kSlots] = {};
+    int device[kSlots] = {-1, -1, -1, -1, -1};
     ~HostScratch() {
-        for (int i = 0; i < 5; i++)
+        for (int i = 0; i < kSlots; i++)
             if (p[i]) cudaFree(p[i]);
     }
     cudaError_t get(int i, size_t bytes, void **out) {
@@ -1335,7 +1338,13 @@ static bool try_attend_bulk(AttendParams &p, int streams, cudaStream_t st, bool 
     }
     if (ok.empty()) return false;
     size_t pick = ok.size() - 1;
-    if (ok.back() != p.kv_heads || 2LL * streams < sms) {
+    // Any order: every KV head in one CTA whenever that fits (one contiguous
+    // copy a chunk). Cross attention of 1 to 128 streams x 375 keys then
+    // takes 19.5 us against 33 us with a head a CTA, self attention 13 us
+    // against 22.5; splitting a stream's keys over CTAs (their softmax sums
+    // merged by the last) gained nothing at any stream count.
+    const bool whole_any = any_order && ok.back() == p.kv_heads;
+    if (!whole_any && (ok.back() != p.kv_heads || 2LL * streams < sms)) {
         for (size_t i = 0; i < ok.size(); i++)
             if (ok[i] * gs * p.vd >= 512) {
                 pick = i;
