@@ -318,7 +318,11 @@ __device__ __forceinline__ void load_superchunk(const CqView &v, int sc, int R, 
 template <int GB, int NSC>
 __host__ __device__ constexpr int stream_threads() { return GB == 8 && NSC == 4 ? 384 : kStreamThreads; }
 
-template <int GB, int NR, int NSC>  // group bytes; run capacity; most superchunks a pass holds (1, 2 or 4)
+// MA: the launch has several activations. The one-activation instances
+// are compiled without the activation loop, which would otherwise keep its
+// bounds live across the tile loop (the 4-bit, four-superchunk instance
+// spilled with it).
+template <int GB, int NR, int NSC, bool MA>  // group bytes; run capacity; most superchunks a pass holds (1, 2 or 4)
 __global__ void __launch_bounds__(stream_threads<GB, NSC>(), 1)
     cq_lut_stream_kernel(const __grid_constant__ StreamParamsN<NR> p) {
     constexpr int NW = stream_threads<GB, NSC>() / 32;  // warps
@@ -358,14 +362,14 @@ __global__ void __launch_bounds__(stream_threads<GB, NSC>(), 1)
     float *wterms = terms + warp * NG * 32;
     const int npass = (s.row_bytes + kPassPositions - 1) / kPassPositions;
 
-  for (int act = (int)(w_begin / T); (long long)act * T < w_end; act++) {
-    const int t_begin = (int)(w_begin > (long long)act * T ? w_begin - (long long)act * T : 0);
-    const int t_end = (int)(w_end < (long long)(act + 1) * T ? w_end - (long long)act * T : T);
+  for (int act = MA ? (int)(w_begin / T) : 0; MA ? (long long)act * T < w_end : act < 1; act++) {
+    const int t_begin = MA ? (int)(w_begin > (long long)act * T ? w_begin - (long long)act * T : 0) : (int)w_begin;
+    const int t_end = MA ? (int)(w_end < (long long)(act + 1) * T ? w_end - (long long)act * T : T) : (int)w_end;
     if (t_begin >= t_end) continue;
-    const float *x = p.x + (size_t)act * s.in;
+    const float *x = MA ? p.x + (size_t)act * s.in : p.x;
     // The previous activation's tables and steps are read until every warp
     // has finished its tiles.
-    __syncthreads();
+    if (MA) __syncthreads();
 
     // Rolling prefetch: a warp's first tile of a pass is loaded into its
     // registers before the pass's tables are built (for pass 0 before the
@@ -522,12 +526,12 @@ size_t stream_smem_bytes(const CqShape &s) {
 }
 
 template <int NR, int NSC>
-static void (*stream_fn(int gb))(StreamParamsN<NR>) {
+static void (*stream_fn(int gb, bool ma))(StreamParamsN<NR>) {
     switch (gb) {
-        case 8: return cq_lut_stream_kernel<8, NR, NSC>;
-        case 16: return cq_lut_stream_kernel<16, NR, NSC>;
-        case 32: return cq_lut_stream_kernel<32, NR, NSC>;
-        default: return cq_lut_stream_kernel<64, NR, NSC>;
+        case 8: return ma ? cq_lut_stream_kernel<8, NR, NSC, true> : cq_lut_stream_kernel<8, NR, NSC, false>;
+        case 16: return ma ? cq_lut_stream_kernel<16, NR, NSC, true> : cq_lut_stream_kernel<16, NR, NSC, false>;
+        case 32: return ma ? cq_lut_stream_kernel<32, NR, NSC, true> : cq_lut_stream_kernel<32, NR, NSC, false>;
+        default: return ma ? cq_lut_stream_kernel<64, NR, NSC, true> : cq_lut_stream_kernel<64, NR, NSC, false>;
     }
 }
 
@@ -537,7 +541,9 @@ static cudaError_t launch_stream_n(const StreamParamsN<NR> &p, int ctas, cudaStr
     // Registers for as many superchunks as a pass holds.
     const int nsc = p.shape.row_bytes / 64;
     void (*fn)(StreamParamsN<NR>) =
-        nsc <= 1 ? stream_fn<NR, 1>(p.shape.gb) : nsc == 2 ? stream_fn<NR, 2>(p.shape.gb) : stream_fn<NR, 4>(p.shape.gb);
+        nsc <= 1   ? stream_fn<NR, 1>(p.shape.gb, p.acts > 1)
+        : nsc == 2 ? stream_fn<NR, 2>(p.shape.gb, p.acts > 1)
+                   : stream_fn<NR, 4>(p.shape.gb, p.acts > 1);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     const int threads = p.shape.gb == 8 && nsc >= 3 ? stream_threads<8, 4>() : kStreamThreads;
