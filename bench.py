@@ -579,7 +579,7 @@ def decode_streams_of(rank, world, total=DECODE_STREAMS):
 
 
 def decode_component(pkg, torch, lib, world, rank, pg, dev, total=DECODE_STREAMS, frames=DECODE_FRAMES,
-                     max_tok=DECODE_TOKENS, flags=0):
+                     max_tok=DECODE_TOKENS, flags=0, keep=None):
     """configs[4]'s decoder: greedy decoding of `total` independent streams
     of the synthetic Whistle decoder (8 layers, 4 mHC lanes, int8 self and
     cross attention over 375 frames, engram, vocab 16384), sharded over the
@@ -614,6 +614,8 @@ def decode_component(pkg, torch, lib, world, rank, pg, dev, total=DECODE_STREAMS
     ms = ev[2].elapsed_time(ev[3])
     mem_ms = ev[0].elapsed_time(ev[1])
     counts_h, eos_h = counts.cpu().numpy(), eos.cpu().numpy()
+    if keep is not None:
+        keep["tokens"], keep["counts"], keep["lang"] = tokens.cpu().numpy(), counts_h, lang.cpu().numpy()
     ntok = int(len(mine) + counts_h.sum() + eos_h.sum())
     if pg:
         t = torch.tensor([ms, float(ntok)], device=dev, dtype=torch.float64)
@@ -943,7 +945,24 @@ def run_b200(args, world, rank, local):
         "clocks": clocks,
     }
     if not args.only and not args.no_decode:
-        line["decode"] = decode_component(pkg, torch, lib, world, rank, pg, dev)
+        exact, tc = {}, {}
+        line["decode"] = decode_component(pkg, torch, lib, world, rank, pg, dev, keep=exact)
+        # The same decode with every CQ product on the tensor cores (fp16
+        # operands within the stated bound, not the reference's lut bits):
+        # its speed, and how many streams decode the same tokens.
+        r = decode_component(pkg, torch, lib, world, rank, pg, dev, flags=pkg.decoder.WC_DECODER_TENSOR_CORES,
+                             keep=tc)
+        same = np.all(exact["tokens"] == tc["tokens"], axis=1) & (exact["counts"] == tc["counts"]) & (
+            exact["lang"] == tc["lang"])
+        agree = [int(same.sum()), int(same.size)]
+        if pg:
+            t = torch.tensor(agree, device=dev, dtype=torch.int64)
+            pg.all_reduce(t, op=pg.ReduceOp.SUM)
+            agree = [int(v) for v in t.tolist()]
+        line["decode"]["tensor_cores"] = {
+            "value": r["value"], "unit": r["unit"], "ms_per_step": r["ms_per_step"],
+            "streams_with_the_exact_tokens": f"{agree[0]} of {agree[1]}",
+            "numerics": "WC_DECODER_TENSOR_CORES: fp16 operands, fp32 accumulate, within the header's bound"}
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             line["decode"]["cpu_baseline"] = decode_cpu_baseline(pkg)
     if args.only:
@@ -985,6 +1004,7 @@ def main():
     ap.add_argument("--decode-streams", type=int, default=DECODE_STREAMS, help="--decode-only: total streams")
     ap.add_argument("--decode-tokens", type=int, default=DECODE_TOKENS, help="--decode-only: tokens per stream")
     ap.add_argument("--decode-eager", action="store_true", help="--decode-only: steps as eager launches (profiling)")
+    ap.add_argument("--decode-tc", action="store_true", help="--decode-only: CQ products on the tensor cores")
     args = ap.parse_args()
     world, rank, local = dist_env()
     if args.impl == "reference":
@@ -1034,7 +1054,8 @@ def main():
             pg = dist
         res = decode_component(pkg, torch, pkg._lib.lib(), world, rank, pg, torch.device("cuda", local),
                                total=args.decode_streams, max_tok=args.decode_tokens,
-                               flags=pkg.decoder.WC_DECODER_NO_GRAPH if args.decode_eager else 0)
+                               flags=(pkg.decoder.WC_DECODER_NO_GRAPH if args.decode_eager else 0) |
+                               (pkg.decoder.WC_DECODER_TENSOR_CORES if args.decode_tc else 0))
         if rank == 0:
             print(json.dumps(res), flush=True)
         if pg:
