@@ -934,7 +934,8 @@ def run_b200(args, world, rank, local):
         # the batch-1 latency figure, beside the shared-x `value`.
         "distinct_x": {"gbs": round(bytes_per_step / (distinct_ms / 1e3) / 1e9, 1),
                        "ms_per_step": round(distinct_ms, 3),
-                       "launch": "wc_cq_gemm per call (batch 1, its own x), every call of a shape in one CUDA graph"},
+                       "launch": "wc_cq_gemm per call (batch 1, its own x), every call of a shape in one CUDA graph",
+                       "scope": "rank 0's own step (per GPU)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
                      "kernel": "cq_lut_stream_kernel", "bytes_per_launch": int(bytes_per_launch)},
