@@ -1201,8 +1201,8 @@ wc_status gemms_device(const wc_cq *const *ms, int n, const float *x, float *con
 int *err_word() { return device_err_word(); }
 bool cq_internal(const wc_cq *h, CqShape *s, CqView *v) {
     if (!h) return false;
-    *s = h->shape;
-    *v = h->view();
+    if (s) *s = h->shape;
+    if (v) *v = h->view();
     return true;
 }
 }  // namespace wb

@@ -233,6 +233,142 @@ __global__ void __launch_bounds__(kThreads) mhc_in_kernel(const float *__restric
         xq[((size_t)s * kLanes + k) * kD + c] = (float)quant8(v[k], sc) * sc;
 }
 
+// The layer's three φ products fused with their input (mhc.go:193-205:
+// nx = RMSUnit(stream), the Act int8 fake-quant of linear.go:104-114, then
+// nx @ φ_pre, φ_post, φ_res): 4 + 4 + 16 rows of 2048 inputs, 4-bit, group
+// 128, on the lut kernels' exact arithmetic (lut.go:213-313) without the
+// table. With 24 rows a stream, tabulating 32K entries to look up 49K is the
+// larger part of the work; each term is instead formed where the table
+// would be read, by the table's own expression rint(cb[nib]·(x̂_q·inv_g)),
+// so every integer sum, every group term float32(Σ)·(norm·step) and every
+// row's sum over the groups in group order is the lut kernel's.
+// One CTA per stream; a warp per (row, group): lane l takes the four
+// nibbles of bytes 2l, 2l + 1.
+struct PhiViews {
+    CqView v[3];   // φ_pre, φ_post, φ_res rows of this layer
+    float *y[3];   // [streams][rows]
+};
+constexpr int kPhiRows = 2 * kLanes + kLanes * kLanes;  // 24
+constexpr int kPhiIn = kLanes * kD;                     // 2048
+constexpr int kPhiGroups = kPhiIn / 128;                // 16
+
+__global__ void __launch_bounds__(kThreads) mhc_phi_kernel(const float *__restrict__ stream,
+                                                           const __grid_constant__ CqShape sh,
+                                                           const __grid_constant__ PhiViews pv) {
+    __shared__ double red[33];
+    __shared__ float redf[33];
+    __shared__ float xs[kPhiIn];
+    __shared__ float steps[kPhiGroups], invs[kPhiGroups];
+    __shared__ float terms[kPhiRows][kPhiGroups];
+    __shared__ float nrm[kPhiRows * kPhiGroups];
+    __shared__ float cbs[16];  // the levels in shared memory: each lane indexes its own nibble
+    const int s = blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
+    if (c < 16) cbs[c] = sh.cb[c];
+    constexpr int NW = kThreads / 32, PER = kPhiRows * kPhiGroups / NW;  // (row, group) pairs a warp takes
+    static_assert(kPhiRows * kPhiGroups % NW == 0, "pairs divide over the warps");
+    // The layout row of pair pr = row·16 + g.
+    auto pair_row = [&](int pr, int *kk) -> size_t {
+        const int row = pr / kPhiGroups, g = pr % kPhiGroups;
+        const int k = row < kLanes ? 0 : row < 2 * kLanes ? 1 : 2;
+        const int r = row - (k == 0 ? 0 : k == 1 ? kLanes : 2 * kLanes);
+        *kk = k;
+        return (size_t)g * pv.v[k].ld + (size_t)(pv.v[k].row0 + r);
+    };
+    // Every load of the products first, so their latency passes under the
+    // norm and the rotation: lane l's two index bytes of each of the
+    // warp's pairs, and the pairs' norms.
+    uint32_t wq[PER];
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        int k;
+        const size_t lrow = pair_row(warp + NW * i, &k);
+        wq[i] = __ldg(reinterpret_cast<const uint16_t *>(pv.v[k].idx + lrow * 64) + lane);
+    }
+    if (c < kPhiRows * kPhiGroups) {
+        int k;
+        const size_t lrow = pair_row(c, &k);
+        nrm[c] = __half2float(pv.v[k].nrm[lrow]);
+    }
+    // 1. RMSUnit over the lanes, the int8 fake-quant (as mhc_in_kernel).
+    float v[kLanes];
+    double sq = 0.0;
+#pragma unroll
+    for (int k = 0; k < kLanes; k++) {
+        v[k] = stream[((size_t)s * kLanes + k) * kD + c];
+        sq += (double)v[k] * (double)v[k];
+    }
+    const double tot = block_sum(sq, red);
+    const float ms = (float)(tot / (double)(kLanes * kD)) + kEps;
+    const float inv = (float)(1.0 / sqrt((double)ms));
+    float m = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kLanes; k++) {
+        v[k] = v[k] * inv;
+        m = fmaxf(m, fabsf(v[k]));
+    }
+    m = block_max(m, redf);
+    const float sc = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
+#pragma unroll
+    for (int k = 0; k < kLanes; k++) xs[k * kD + c] = (float)quant8(v[k], sc) * sc;
+    __syncthreads();
+    // 2. x̂ per group of 128 (kernel.go:384 fwht), stage by stage.
+    for (int st = 0; st < 7; st++) {
+        const int h = 1 << st;
+        for (int b = c; b < kPhiIn / 2; b += kThreads) {
+            const int g = b >> 6, t = b & 63;
+            const int j = (g << 7) + ((t >> st) << (st + 1)) + (t & (h - 1));
+            const float a = xs[j], e = xs[j + h];
+            xs[j] = __fadd_rn(a, e);
+            xs[j + h] = __fsub_rn(a, e);
+        }
+        __syncthreads();
+    }
+    // 3. The group bounds (4-bit: max |x̂|), 8191/M and the steps; a warp a group.
+    if (warp < kPhiGroups) {
+        const float *xg = xs + warp * 128;
+        float mx = 0.0f;
+        for (int q = lane; q < 128; q += 32) mx = fmaxf(mx, fabsf(xg[q]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) {
+            const float mm = __fmul_rn(sh.cb_max, mx);
+            invs[warp] = mm > 0.0f ? __fdiv_rn((float)kLutQ, mm) : 0.0f;
+            steps[warp] = __fmul_rn(mm, sh.lut_step);
+        }
+    }
+    __syncthreads();
+    // 4. The table's operand x̂_q·inv_g, in place.
+    for (int q = c; q < kPhiIn; q += kThreads) xs[q] = __fmul_rn(xs[q], invs[q >> 7]);
+    __syncthreads();
+    // 5. The integer sums and group terms, a warp per (row, group).
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const int pr = warp + NW * i, row = pr / kPhiGroups, g = pr % kPhiGroups;
+        const uint32_t w = wq[i];
+        const float *a = xs + g * 128 + 4 * lane;
+        int32_t sum = __float2int_rn(__fmul_rn(cbs[w & 15u], a[0])) +
+                      __float2int_rn(__fmul_rn(cbs[(w >> 4) & 15u], a[1])) +
+                      __float2int_rn(__fmul_rn(cbs[(w >> 8) & 15u], a[2])) +
+                      __float2int_rn(__fmul_rn(cbs[(w >> 12) & 15u], a[3]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) {
+            const float coef = __fmul_rn(nrm[pr], steps[g]);
+            terms[row][g] = __fmul_rn(__int2float_rn(sum), coef);
+        }
+    }
+    __syncthreads();
+    // 6. Each row's sum of its group terms in group order (lut.go:309).
+    if (c < kPhiRows) {
+        const int k = c < kLanes ? 0 : c < 2 * kLanes ? 1 : 2;
+        const int r = c - (k == 0 ? 0 : k == 1 ? kLanes : 2 * kLanes);
+        const int rows = k == 2 ? kLanes * kLanes : kLanes;
+        float acc = 0.0f;
+        for (int g = 0; g < kPhiGroups; g++) acc = __fadd_rn(acc, terms[c][g]);
+        pv.y[k][(size_t)s * rows + r] = acc;
+    }
+}
+
 // mhc.go:316 sinkhornExp / :374 sinkhornLog: h_res = sinkhorn(a_res·(nx @
 // φ_res) + b_res), one stream per warp. Lane e (and its mirror e + 16)
 // holds entry (e / 4, e % 4); each row or column sum is formed by every
@@ -1030,6 +1166,7 @@ struct wc_decoder {
     struct Layer {
         LayerK k;
         wc_cq *q, *kk, *v, *g, *o, *xq, *xk, *xv, *xg, *xo, *ppre, *ppost, *pres;
+        bool phi_fused = false;  // the φ products by mhc_phi_kernel
     };
     std::vector<Layer> layers;
     struct Site {
@@ -1178,8 +1315,18 @@ wc_status step_body(wc_decoder *d, cudaStream_t st) {
         int site = -1;
         for (size_t i = 0; i < d->sites.size(); i++)
             if (d->sites[i].layer == l) site = (int)i;
-        DEC_LAUNCH(mhc_in_kernel<<<S, kThreads, 0, st>>>(d->stream, d->xq));
-        DEC_ST(gemms(d, {L.ppre, L.ppost, L.pres}, d->xq, {d->phi_pre, d->phi_post, d->phi_res}, S, st));
+        if (L.phi_fused) {
+            PhiViews pv{};
+            CqShape sh{};
+            cq_internal(L.ppre, &sh, &pv.v[0]);
+            cq_internal(L.ppost, nullptr, &pv.v[1]);
+            cq_internal(L.pres, nullptr, &pv.v[2]);
+            pv.y[0] = d->phi_pre, pv.y[1] = d->phi_post, pv.y[2] = d->phi_res;
+            DEC_LAUNCH(mhc_phi_kernel<<<S, kThreads, 0, st>>>(d->stream, sh, pv));
+        } else {
+            DEC_LAUNCH(mhc_in_kernel<<<S, kThreads, 0, st>>>(d->stream, d->xq));
+            DEC_ST(gemms(d, {L.ppre, L.ppost, L.pres}, d->xq, {d->phi_pre, d->phi_post, d->phi_res}, S, st));
+        }
         const float *ek = site >= 0 ? d->ek + (size_t)site * S * kD : nullptr;
         const float *ev = site >= 0 ? d->ev + (size_t)site * S * kD : nullptr;
         DEC_LAUNCH(sinkhorn_kernel<<<(S + 3) / 4, 128, 0, st>>>(L.k, d->phi_res, d->hr, S));
@@ -1466,6 +1613,22 @@ extern "C" wc_status wc_decoder_create(const wc_decoder_desc *desc, int max_stre
         DEC_ST(d->view(S.phi_pre, &L.ppre));
         DEC_ST(d->view(S.phi_post, &L.ppost));
         DEC_ST(d->view(S.phi_res, &L.pres));
+        // The fused φ kernel (exact mode): 4-bit group-128 rows of 2048
+        // inputs on one codebook, 4 + 4 + 16 of them.
+        {
+            CqShape a{}, b{}, c{};
+            CqView va{}, vb{}, vc{};
+            cq_internal(L.ppre, &a, &va);
+            cq_internal(L.ppost, &b, &vb);
+            cq_internal(L.pres, &c, &vc);
+            auto same = [](const CqShape &x, const CqShape &y) {
+                return x.in == y.in && x.group == y.group && x.bits == y.bits && x.cb_max == y.cb_max &&
+                       x.lut_step == y.lut_step && std::memcmp(x.cb, y.cb, sizeof x.cb) == 0;
+            };
+            L.phi_fused = !d->tc && a.bits == 4 && a.group == 128 && a.in == kPhiIn && a.gb == 64 &&
+                          a.pad == kPhiIn && same(a, b) && same(a, c) && va.out == kLanes && vb.out == kLanes &&
+                          vc.out == kLanes * kLanes;
+        }
         LayerK &K = L.k;
         const int nn = kNA * kNB;
         DEC_ST(d->upload(&K.g_norm_in, S.norm_in, kD, true));
