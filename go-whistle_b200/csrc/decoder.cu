@@ -242,8 +242,9 @@ __global__ void __launch_bounds__(kThreads) mhc_in_kernel(const float *__restric
 // would be read, by the table's own expression rint(cb[nib]·(x̂_q·inv_g)),
 // so every integer sum, every group term float32(Σ)·(norm·step) and every
 // row's sum over the groups in group order is the lut kernel's.
-// One CTA per stream; a warp per (row, group): lane l takes the four
-// nibbles of bytes 2l, 2l + 1.
+// One CTA per stream, a warp per group of 128: lane l holds the positions
+// 4l .. 4l + 3 its row bytes 2l, 2l + 1 index, rotates them with its
+// warp by registers and shuffles and forms the 24 rows' terms.
 struct PhiViews {
     CqView v[3];   // φ_pre, φ_post, φ_res rows of this layer
     float *y[3];   // [streams][rows]
@@ -257,37 +258,24 @@ __global__ void __launch_bounds__(kThreads) mhc_phi_kernel(const float *__restri
                                                            const __grid_constant__ PhiViews pv) {
     __shared__ double red[33];
     __shared__ float redf[33];
-    __shared__ float xs[kPhiIn];
-    __shared__ float steps[kPhiGroups], invs[kPhiGroups];
+    __shared__ __align__(16) float xs[kPhiIn];
     __shared__ float terms[kPhiRows][kPhiGroups];
-    __shared__ float nrm[kPhiRows * kPhiGroups];
     __shared__ float cbs[16];  // the levels in shared memory: each lane indexes its own nibble
-    const int s = blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
+    const int s = blockIdx.x, c = threadIdx.x, lane = c & 31, g = c >> 5;  // warp g owns group g
+    static_assert(kThreads / 32 == kPhiGroups, "a warp per group");
     if (c < 16) cbs[c] = sh.cb[c];
-    constexpr int NW = kThreads / 32, PER = kPhiRows * kPhiGroups / NW;  // (row, group) pairs a warp takes
-    static_assert(kPhiRows * kPhiGroups % NW == 0, "pairs divide over the warps");
-    // The layout row of pair pr = row·16 + g.
-    auto pair_row = [&](int pr, int *kk) -> size_t {
-        const int row = pr / kPhiGroups, g = pr % kPhiGroups;
+    // Every load of the products first, so their latency passes under the
+    // norm: lane l's two index bytes (positions 4l .. 4l + 3 of group g) of
+    // each of the 24 rows, and lane r's norm of row r.
+    uint32_t wq[kPhiRows];
+    float nr = 0.0f;
+#pragma unroll
+    for (int row = 0; row < kPhiRows; row++) {
         const int k = row < kLanes ? 0 : row < 2 * kLanes ? 1 : 2;
         const int r = row - (k == 0 ? 0 : k == 1 ? kLanes : 2 * kLanes);
-        *kk = k;
-        return (size_t)g * pv.v[k].ld + (size_t)(pv.v[k].row0 + r);
-    };
-    // Every load of the products first, so their latency passes under the
-    // norm and the rotation: lane l's two index bytes of each of the
-    // warp's pairs, and the pairs' norms.
-    uint32_t wq[PER];
-#pragma unroll
-    for (int i = 0; i < PER; i++) {
-        int k;
-        const size_t lrow = pair_row(warp + NW * i, &k);
-        wq[i] = __ldg(reinterpret_cast<const uint16_t *>(pv.v[k].idx + lrow * 64) + lane);
-    }
-    if (c < kPhiRows * kPhiGroups) {
-        int k;
-        const size_t lrow = pair_row(c, &k);
-        nrm[c] = __half2float(pv.v[k].nrm[lrow]);
+        const size_t lrow = (size_t)g * pv.v[k].ld + (size_t)(pv.v[k].row0 + r);
+        wq[row] = __ldg(reinterpret_cast<const uint16_t *>(pv.v[k].idx + lrow * 64) + lane);
+        if (lane == row) nr = __half2float(pv.v[k].nrm[lrow]);
     }
     // 1. RMSUnit over the lanes, the int8 fake-quant (as mhc_in_kernel).
     float v[kLanes];
@@ -311,51 +299,46 @@ __global__ void __launch_bounds__(kThreads) mhc_phi_kernel(const float *__restri
 #pragma unroll
     for (int k = 0; k < kLanes; k++) xs[k * kD + c] = (float)quant8(v[k], sc) * sc;
     __syncthreads();
-    // 2. x̂ per group of 128 (kernel.go:384 fwht), stage by stage.
-    for (int st = 0; st < 7; st++) {
-        const int h = 1 << st;
-        for (int b = c; b < kPhiIn / 2; b += kThreads) {
-            const int g = b >> 6, t = b & 63;
-            const int j = (g << 7) + ((t >> st) << (st + 1)) + (t & (h - 1));
-            const float a = xs[j], e = xs[j + h];
-            xs[j] = __fadd_rn(a, e);
-            xs[j + h] = __fsub_rn(a, e);
-        }
-        __syncthreads();
+    // 2. x̂ of group g (kernel.go:384 fwht, stage by stage h = 1 .. 64):
+    //    lane l holds positions 4l .. 4l + 3; stages 1 and 2 in registers,
+    //    4 .. 64 with the lane l ^ (h / 4). Lower element a + b, upper a − b.
+    const float4 x4 = *reinterpret_cast<const float4 *>(xs + g * 128 + 4 * lane);
+    float x0 = x4.x, x1 = x4.y, x2 = x4.z, x3 = x4.w;
+    {
+        const float a0 = __fadd_rn(x0, x1), a1 = __fsub_rn(x0, x1), a2 = __fadd_rn(x2, x3), a3 = __fsub_rn(x2, x3);
+        x0 = __fadd_rn(a0, a2), x2 = __fsub_rn(a0, a2), x1 = __fadd_rn(a1, a3), x3 = __fsub_rn(a1, a3);
     }
-    // 3. The group bounds (4-bit: max |x̂|), 8191/M and the steps; a warp a group.
-    if (warp < kPhiGroups) {
-        const float *xg = xs + warp * 128;
-        float mx = 0.0f;
-        for (int q = lane; q < 128; q += 32) mx = fmaxf(mx, fabsf(xg[q]));
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (lane == 0) {
-            const float mm = __fmul_rn(sh.cb_max, mx);
-            invs[warp] = mm > 0.0f ? __fdiv_rn((float)kLutQ, mm) : 0.0f;
-            steps[warp] = __fmul_rn(mm, sh.lut_step);
+    for (int mk = 1; mk < 32; mk <<= 1) {
+        const float p0 = __shfl_xor_sync(0xffffffffu, x0, mk), p1 = __shfl_xor_sync(0xffffffffu, x1, mk);
+        const float p2 = __shfl_xor_sync(0xffffffffu, x2, mk), p3 = __shfl_xor_sync(0xffffffffu, x3, mk);
+        if (lane & mk) {
+            x0 = __fsub_rn(p0, x0), x1 = __fsub_rn(p1, x1), x2 = __fsub_rn(p2, x2), x3 = __fsub_rn(p3, x3);
+        } else {
+            x0 = __fadd_rn(x0, p0), x1 = __fadd_rn(x1, p1), x2 = __fadd_rn(x2, p2), x3 = __fadd_rn(x3, p3);
         }
     }
-    __syncthreads();
-    // 4. The table's operand x̂_q·inv_g, in place.
-    for (int q = c; q < kPhiIn; q += kThreads) xs[q] = __fmul_rn(xs[q], invs[q >> 7]);
-    __syncthreads();
-    // 5. The integer sums and group terms, a warp per (row, group).
+    // 3. The group bound (4-bit: max |x̂|), 8191/M and the step.
+    float mx = fmaxf(fmaxf(fabsf(x0), fabsf(x1)), fmaxf(fabsf(x2), fabsf(x3)));
 #pragma unroll
-    for (int i = 0; i < PER; i++) {
-        const int pr = warp + NW * i, row = pr / kPhiGroups, g = pr % kPhiGroups;
-        const uint32_t w = wq[i];
-        const float *a = xs + g * 128 + 4 * lane;
-        int32_t sum = __float2int_rn(__fmul_rn(cbs[w & 15u], a[0])) +
-                      __float2int_rn(__fmul_rn(cbs[(w >> 4) & 15u], a[1])) +
-                      __float2int_rn(__fmul_rn(cbs[(w >> 8) & 15u], a[2])) +
-                      __float2int_rn(__fmul_rn(cbs[(w >> 12) & 15u], a[3]));
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float mm = __fmul_rn(sh.cb_max, mx);
+    const float ginv = mm > 0.0f ? __fdiv_rn((float)kLutQ, mm) : 0.0f;
+    const float step = __fmul_rn(mm, sh.lut_step);
+    // 4. The table's operands x̂_q·inv_g.
+    const float a0 = __fmul_rn(x0, ginv), a1 = __fmul_rn(x1, ginv), a2 = __fmul_rn(x2, ginv),
+                a3 = __fmul_rn(x3, ginv);
+    // 5. Each row's integer sum over the group and its term.
+#pragma unroll
+    for (int row = 0; row < kPhiRows; row++) {
+        const uint32_t w = wq[row];
+        int32_t sum = __float2int_rn(__fmul_rn(cbs[w & 15u], a0)) + __float2int_rn(__fmul_rn(cbs[(w >> 4) & 15u], a1)) +
+                      __float2int_rn(__fmul_rn(cbs[(w >> 8) & 15u], a2)) +
+                      __float2int_rn(__fmul_rn(cbs[(w >> 12) & 15u], a3));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) {
-            const float coef = __fmul_rn(nrm[pr], steps[g]);
-            terms[row][g] = __fmul_rn(__int2float_rn(sum), coef);
-        }
+        const float nrow = __shfl_sync(0xffffffffu, nr, row);
+        if (lane == 0) terms[row][g] = __fmul_rn(__int2float_rn(sum), __fmul_rn(nrow, step));
     }
     __syncthreads();
     // 6. Each row's sum of its group terms in group order (lut.go:309).
@@ -364,7 +347,7 @@ __global__ void __launch_bounds__(kThreads) mhc_phi_kernel(const float *__restri
         const int r = c - (k == 0 ? 0 : k == 1 ? kLanes : 2 * kLanes);
         const int rows = k == 2 ? kLanes * kLanes : kLanes;
         float acc = 0.0f;
-        for (int g = 0; g < kPhiGroups; g++) acc = __fadd_rn(acc, terms[c][g]);
+        for (int q = 0; q < kPhiGroups; q++) acc = __fadd_rn(acc, terms[c][q]);
         pv.y[k][(size_t)s * rows + r] = acc;
     }
 }
