@@ -123,10 +123,30 @@ __device__ __forceinline__ uint32_t load_cols(const unsigned char *p) {
 template <int CPT, bool EXACT>
 __device__ __forceinline__ void accumulate(float *acc, float w, uint32_t v) {
     const uint32_t u = v ^ 0x80808080u;
+    if constexpr (!EXACT && CPT % 2 == 0) {
+        // Any order: two columns a packed f32x2 FMA (sm_100a). The exact
+        // order keeps the scalar operations: its packed multiply-then-add
+        // did not give the scalar path's bits (1-2 ulp apart).
+        uint64_t ww, bias;
+        asm("mov.b64 %0, {%1, %1};" : "=l"(ww) : "f"(w));
+        asm("mov.b64 %0, {%1, %1};" : "=l"(bias) : "f"(-8388736.0f));
 #pragma unroll
-    for (int i = 0; i < CPT; i++) {
-        const float c = __fadd_rn(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7540u + i)), -8388736.0f);
-        acc[i] = EXACT ? __fadd_rn(acc[i], __fmul_rn(w, c)) : fmaf(w, c, acc[i]);
+        for (int i = 0; i < CPT; i += 2) {
+            uint64_t c, a;
+            asm("mov.b64 %0, {%1, %2};"
+                : "=l"(c)
+                : "r"(__byte_perm(u, 0x4B000000u, 0x7540u + i)), "r"(__byte_perm(u, 0x4B000000u, 0x7540u + i + 1)));
+            asm("add.rn.f32x2 %0, %0, %1;" : "+l"(c) : "l"(bias));
+            asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(acc[i]), "f"(acc[i + 1]));
+            asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(a) : "l"(ww), "l"(c));
+            asm("mov.b64 {%0, %1}, %2;" : "=f"(acc[i]), "=f"(acc[i + 1]) : "l"(a));
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < CPT; i++) {
+            const float c = __fadd_rn(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7540u + i)), -8388736.0f);
+            acc[i] = EXACT ? __fadd_rn(acc[i], __fmul_rn(w, c)) : fmaf(w, c, acc[i]);
+        }
     }
 }
 
