@@ -807,6 +807,12 @@ def run_b200(args, world, rank, local):
             # The calls as a decode step issues them: each GEMV its own
             # launch on its own activation (wc_cq_gemm, batch 1), the
             # weights cycling through the copies, in one CUDA graph.
+            if args.no_distinct:
+                per_shape[f"{s.out}x{s.in_}/{s.bits}b"] = {
+                    "cold_hbm_gbs": round(res[False], 1), "hot_l2_gbs": round(res[True], 1),
+                    "weight_copies": s.copies,
+                    "l2_multiple": round(s.copies * weight_bytes(s.out, s.in_, s.bits) / l2, 2)}
+                continue
             xs = torch.randn(s.calls, s.in_, device="cuda", dtype=torch.float32)
 
             def run_distinct(s=s, xs=xs):
@@ -932,7 +938,7 @@ def run_b200(args, world, rank, local):
         # The same step with every GEMV on its own activation, one launch a
         # call (as a decode step issues them, each waiting for the last):
         # the batch-1 latency figure, beside the shared-x `value`.
-        "distinct_x": {"gbs": round(bytes_per_step / (distinct_ms / 1e3) / 1e9, 1),
+        "distinct_x": None if args.no_distinct else {"gbs": round(bytes_per_step / (distinct_ms / 1e3) / 1e9, 1),
                        "ms_per_step": round(distinct_ms, 3),
                        "launch": "wc_cq_gemm per call (batch 1, its own x), every call of a shape in one CUDA graph",
                        "scope": "rank 0's own step (per GPU)"},
@@ -1002,6 +1008,8 @@ def main():
     ap.add_argument("--decode-only", action="store_true", help="only the greedy decoder component")
     ap.add_argument("--rows-sweep", action="store_true", help="only the lut / tensor-core rows sweep")
     ap.add_argument("--beam-only", action="store_true", help="only the beam search component")
+    ap.add_argument("--no-distinct", action="store_true",
+                    help="skip the distinct-activation figure (its 8000 launches a step; profiling runs)")
     ap.add_argument("--decode-streams", type=int, default=DECODE_STREAMS, help="--decode-only: total streams")
     ap.add_argument("--decode-tokens", type=int, default=DECODE_TOKENS, help="--decode-only: tokens per stream")
     ap.add_argument("--decode-eager", action="store_true", help="--decode-only: steps as eager launches (profiling)")
