@@ -1329,7 +1329,12 @@ static bool try_attend_bulk(AttendParams &p, int streams, cudaStream_t st, bool 
         if (p.kv_heads % kvpc != 0 || !attend_bulk_shape_ok(p, kvpc)) continue;
         AttendParams q = p;
         q.kv_per_cta = kvpc;
-        const BulkLayout L = attend_bulk_pick_layout(q, (size_t)per_sm, (size_t)limit);
+        // A ring shallow enough for four CTAs an SM when the launch has
+        // more than two CTAs an SM (1024 decode streams: the step 4.01 ->
+        // 3.83 ms), else the deepest ring two CTAs an SM allow (256 streams
+        // all fit at two; four there cost 4 % of the configs[3] component).
+        const int share = (long long)streams * (p.kv_heads / kvpc) > 2LL * sms ? 4 : 2;
+        const BulkLayout L = attend_bulk_pick_layout(q, (size_t)per_sm, (size_t)limit, share);
         if (L.total > (size_t)limit) continue;
         int blocks = 0;
         if (attend_bulk_occupancy(q, L, !any_order, &blocks) != cudaSuccess || blocks < 1) continue;

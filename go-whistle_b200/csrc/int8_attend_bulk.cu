@@ -518,10 +518,11 @@ bool attend_bulk_shape_ok(const AttendParams &p, int kvpc) {
            p.kv_heads % kvpc == 0 && kBulkConsumers % hb == 0 && hb * p.vd <= 16 * kBulkConsumers;
 }
 
-// The deepest ring (up to 8 stages) that still lets two CTAs share an SM,
-// or, when even two stages do not, the deepest that fits one CTA.
-BulkLayout attend_bulk_pick_layout(const AttendParams &p, size_t smem_per_sm, size_t smem_per_block) {
-    const size_t two = smem_per_sm / 2 > 1024 ? smem_per_sm / 2 - 1024 : 0;  // 1 KB reserved per CTA
+// The deepest ring (up to 8 stages) that still lets `share` CTAs share an
+// SM, or, when even two stages do not, the deepest that fits one CTA.
+BulkLayout attend_bulk_pick_layout(const AttendParams &p, size_t smem_per_sm, size_t smem_per_block, int share) {
+    const size_t part = smem_per_sm / (size_t)(share > 0 ? share : 1);
+    const size_t two = part > 1024 ? part - 1024 : 0;  // 1 KB reserved per CTA
     for (int st = kBulkMaxStages; st >= 2; st--) {
         BulkLayout L = attend_bulk_layout(p, st);
         if (L.total <= two) return L;

@@ -56,7 +56,7 @@ cudaError_t launch_attend_any(const AttendParams &p, int streams, cudaStream_t s
 size_t attend_v2_smem_bytes(const AttendParams &p);
 cudaError_t launch_attend_v2(const AttendParams &p, int streams, cudaStream_t st);
 BulkLayout attend_bulk_layout(const AttendParams &p, int stages);
-BulkLayout attend_bulk_pick_layout(const AttendParams &p, size_t smem_per_sm, size_t smem_per_block);
+BulkLayout attend_bulk_pick_layout(const AttendParams &p, size_t smem_per_sm, size_t smem_per_block, int share);
 bool attend_bulk_shape_ok(const AttendParams &p, int kvpc);
 cudaError_t attend_bulk_occupancy(const AttendParams &p, const BulkLayout &L, bool exact, int *blocks_per_sm);
 cudaError_t launch_attend_bulk(const AttendParams &p, const BulkLayout &L, int streams, bool exact, cudaStream_t st);
