@@ -21,7 +21,7 @@ mirroring the reference's Go API for the path:
 Import it by its directory name: ``importlib.import_module("go-whistle_b200")``.
 """
 
-from . import _lib, cact, cq, decoder, dp, needle, synth, weights  # noqa: F401
+from . import _lib, cact, cq, decoder, dp, encoder, needle, synth, weights  # noqa: F401
 from ._lib import CQError, CudaError, Panic, WhistleError  # noqa: F401
 
 LIB_PATH = _lib.LIB_PATH

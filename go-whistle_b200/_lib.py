@@ -91,6 +91,9 @@ _SIGS = {
     "wc_beam_default": (None, [_c_void_p]),
     "wc_decoder_beam": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p,
                                  _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "wc_encoder_create": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, ctypes.POINTER(_c_void_p)]),
+    "wc_encoder_destroy": (None, [_c_void_p]),
+    "wc_encoder_stack": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
 }
 
 _lib = None

@@ -1136,15 +1136,102 @@ struct DevBuf {
     size_t bytes = 0;
 };
 
-struct wc_decoder {
-    wc_decoder_desc d{};  // sizes (pointers not kept)
-    int max_streams = 0, max_frames = 0, cap = 0, flags = 0, device = 0;
-    int streams = 0, frames = 0, len = 0;
-    int ring_t = 0;  // token history ring: max_order − 1
-    bool tc = false;
+// The device buffers and matrix views a model object owns, freed with it on
+// its own device.
+struct DevStore {
+    int device = 0;
     std::vector<DevBuf> bufs;
     // views of the caller's matrices (they keep the storage alive)
     std::vector<wc_cq *> views;
+
+    DevStore() = default;
+    DevStore(const DevStore &) = delete;
+    DevStore &operator=(const DevStore &) = delete;
+    ~DevStore() {
+        int cur = 0;
+        cudaGetDevice(&cur);
+        if (cur != device) cudaSetDevice(device);
+        for (auto &b : bufs) cudaFree(b.p);
+        for (auto *vw : views) wc_cq_destroy(vw);
+        if (cur != device) cudaSetDevice(cur);
+    }
+
+    template <typename T>
+    wc_status alloc(T **p, size_t count) {
+        void *q = nullptr;
+        const size_t bytes = (count > 0 ? count : 1) * sizeof(T);
+        cudaError_t e = cudaMalloc(&q, bytes);
+        if (e != cudaSuccess) return set_error(WC_ERR_NOMEM, std::string("device memory: ") + cudaGetErrorString(e));
+        bufs.push_back({q, bytes});
+        *p = static_cast<T *>(q);
+        return WC_OK;
+    }
+    // A host float array copied to the device (n values); with gain, the
+    // stored norm scales become gains 1 + scale (norm.go:22 NewZCRMSNorm).
+    wc_status upload(const float **dst, const float *src, size_t n, bool gain = false) {
+        float *p = nullptr;
+        wc_status st = alloc(&p, n);
+        if (st != WC_OK) return st;
+        std::vector<float> tmp(src, src + n);
+        if (gain)
+            for (auto &x : tmp) x = 1.0f + x;
+        WB_CUDA(cudaMemcpy(p, tmp.data(), n * sizeof(float), cudaMemcpyHostToDevice));
+        *dst = p;
+        return WC_OK;
+    }
+    wc_status view(const wc_cq *h, wc_cq **out) {
+        wc_status st = wc_cq_rows(h, 0, wc_cq_out(h), out);
+        if (st == WC_OK) views.push_back(*out);
+        return st;
+    }
+    // rope.go:20 NewRope's tables [len][qk/2] for heads of 48, in the same
+    // float32 steps (the host's libm).
+    wc_status rope_tables(double theta, int len, const float **cs, const float **sn) {
+        const int half = kQK / 2;
+        std::vector<float> freqs(half), c((size_t)len * half), s((size_t)len * half);
+        for (int i = 0; i < half; i++) {
+            const float e = (float)(2 * i) / (float)kQK;
+            freqs[i] = 1.0f / (float)std::pow(theta, (double)e);
+        }
+        for (int t = 0; t < len; t++)
+            for (int i = 0; i < half; i++) {
+                const double angle = (double)((float)t * freqs[i]);
+                c[(size_t)t * half + i] = (float)std::cos(angle);
+                s[(size_t)t * half + i] = (float)std::sin(angle);
+            }
+        wc_status st = upload(cs, c.data(), c.size());
+        return st != WC_OK ? st : upload(sn, s.data(), s.size());
+    }
+    // The HadamardMLP permutations hada_p1, hada_p2 (hadamard.go:281),
+    // checked and copied to the device.
+    wc_status hada_perms(const int32_t *h1, const int32_t *h2, const int **p1, const int **p2) {
+        std::vector<int> seen(kNA * kNB, 0);
+        for (const int32_t *pp : {h1, h2}) {
+            std::fill(seen.begin(), seen.end(), 0);
+            for (int i = 0; i < kNA * kNB; i++) {
+                if (pp[i] < 0 || pp[i] >= kNA * kNB || seen[pp[i]])
+                    return set_error(WC_ERR_INVALID, fmt("needle: hada_p is not a permutation of %d (entry %d = %d)",
+                                                         kNA * kNB, i, pp[i]));
+                seen[pp[i]] = 1;
+            }
+        }
+        int32_t *p = nullptr;
+        wc_status st = alloc(&p, 2 * kNA * kNB);
+        if (st != WC_OK) return st;
+        WB_CUDA(cudaMemcpy(p, h1, kNA * kNB * sizeof(int32_t), cudaMemcpyHostToDevice));
+        WB_CUDA(cudaMemcpy(p + kNA * kNB, h2, kNA * kNB * sizeof(int32_t), cudaMemcpyHostToDevice));
+        *p1 = p;
+        *p2 = p + kNA * kNB;
+        return WC_OK;
+    }
+};
+
+struct wc_decoder : DevStore {
+    wc_decoder_desc d{};  // sizes (pointers not kept)
+    int max_streams = 0, max_frames = 0, cap = 0, flags = 0;
+    int streams = 0, frames = 0, len = 0;
+    int ring_t = 0;  // token history ring: max_order − 1
+    bool tc = false;
     wc_cq *emb = nullptr;
     struct Layer {
         LayerK k;
@@ -1198,37 +1285,7 @@ struct wc_decoder {
         cudaGetDevice(&cur);
         if (cur != device) cudaSetDevice(device);
         if (graph) cudaGraphExecDestroy(graph);
-        for (auto &b : bufs) cudaFree(b.p);
-        for (auto *vw : views) wc_cq_destroy(vw);
         if (cur != device) cudaSetDevice(cur);
-    }
-
-    template <typename T>
-    wc_status alloc(T **p, size_t count) {
-        void *q = nullptr;
-        const size_t bytes = (count > 0 ? count : 1) * sizeof(T);
-        cudaError_t e = cudaMalloc(&q, bytes);
-        if (e != cudaSuccess) return set_error(WC_ERR_NOMEM, std::string("decoder: device memory: ") + cudaGetErrorString(e));
-        bufs.push_back({q, bytes});
-        *p = static_cast<T *>(q);
-        return WC_OK;
-    }
-    // A host float array copied to the device (n values).
-    wc_status upload(const float **dst, const float *src, size_t n, bool gain = false) {
-        float *p = nullptr;
-        wc_status st = alloc(&p, n);
-        if (st != WC_OK) return st;
-        std::vector<float> tmp(src, src + n);
-        if (gain)
-            for (auto &x : tmp) x = 1.0f + x;  // norm.go:22 NewZCRMSNorm
-        WB_CUDA(cudaMemcpy(p, tmp.data(), n * sizeof(float), cudaMemcpyHostToDevice));
-        *dst = p;
-        return WC_OK;
-    }
-    wc_status view(const wc_cq *h, wc_cq **out) {
-        wc_status st = wc_cq_rows(h, 0, wc_cq_out(h), out);
-        if (st == WC_OK) views.push_back(*out);
-        return st;
     }
 };
 
@@ -1680,42 +1737,9 @@ extern "C" wc_status wc_decoder_create(const wc_decoder_desc *desc, int max_stre
     }
     d->ring_t = max_order - 1;
     d->d.etaps = D.etaps;
-    {
-        std::vector<int> seen(kNA * kNB, 0);
-        for (const int32_t *pp : {D.hada_p1, D.hada_p2}) {
-            std::fill(seen.begin(), seen.end(), 0);
-            for (int i = 0; i < kNA * kNB; i++) {
-                if (pp[i] < 0 || pp[i] >= kNA * kNB || seen[pp[i]])
-                    return set_error(WC_ERR_INVALID, fmt("needle: hada_p is not a permutation of %d (entry %d = %d)",
-                                                         kNA * kNB, i, pp[i]));
-                seen[pp[i]] = 1;
-            }
-        }
-        int32_t *p = nullptr;
-        DEC_ST(d->alloc(&p, 2 * kNA * kNB));
-        WB_CUDA(cudaMemcpy(p, D.hada_p1, kNA * kNB * sizeof(int32_t), cudaMemcpyHostToDevice));
-        WB_CUDA(cudaMemcpy(p + kNA * kNB, D.hada_p2, kNA * kNB * sizeof(int32_t), cudaMemcpyHostToDevice));
-        d->p1 = p;
-        d->p2 = p + kNA * kNB;
-    }
+    DEC_ST(d->hada_perms(D.hada_p1, D.hada_p2, &d->p1, &d->p2));
     DEC_ST(d->upload(&d->g_final, D.final_norm, kD, true));
-    // rope.go:20 NewRope, in the same float32 steps (the host's libm).
-    {
-        const int half = kQK / 2;
-        std::vector<float> freqs(half), c((size_t)D.rope_len * half), s((size_t)D.rope_len * half);
-        for (int i = 0; i < half; i++) {
-            const float e = (float)(2 * i) / (float)kQK;
-            freqs[i] = 1.0f / (float)std::pow(D.rope_theta, (double)e);
-        }
-        for (int t = 0; t < D.rope_len; t++)
-            for (int i = 0; i < half; i++) {
-                const double angle = (double)((float)t * freqs[i]);
-                c[(size_t)t * half + i] = (float)std::cos(angle);
-                s[(size_t)t * half + i] = (float)std::sin(angle);
-            }
-        DEC_ST(d->upload(&d->rcos, c.data(), c.size()));
-        DEC_ST(d->upload(&d->rsin, s.data(), s.size()));
-    }
+    DEC_ST(d->rope_tables(D.rope_theta, D.rope_len, &d->rcos, &d->rsin));
     d->in_scale = (float)std::sqrt((double)kD);    // decoder.go:313 ScaleSqrtDim
     d->att_scale = (float)std::sqrt((double)kQK);  // attention.go:407 attendScale
     d->xatt_scale = (float)std::sqrt((double)kQK); // cross.go:276
@@ -1949,5 +1973,525 @@ extern "C" wc_status wc_decoder_greedy(wc_decoder *d, int bos, const int32_t *la
         DEC_LAUNCH(record_kernel<<<(S + 127) / 128, 128, 0, st>>>(d->tok, eos, out_w, tokens, counts, eos_hit, d->done,
                                                                   S));
     }
+    return WC_OK;
+}
+
+// =========================================================================
+// The encoder stack (wc_encoder_*): internal/encoder's Stack (encoder.go:167)
+// with the Best() hypothesis and the engine's int8 numerics, for many clips
+// at once. The stack's rows are frames (clip-major), and every row-wise
+// phase is the decoder's kernel or one written the same way: a 512-thread
+// CTA per frame, one thread per model column, every float32 operation a
+// separate rounding in the reference's order. Per layer l:
+//   mhc_phi / mhc_in + GEMMs, sinkhorn, mhc_block_in (u, pre_hada_0 norm)
+//   enc_ffn      FFN1: x += 1/2 · HadamardMLP, then norm_in
+//   GEMMs        q, k, v, gate (one shared input)
+//   enc_qkv      per-head q/k norm, RoPE at the frame's position, the int8
+//                codes and scales of k and v (QuantizeRows per head)
+//   attention    the int8 kernel: every frame of a clip reads that clip's
+//                keys and values (kv_group = frames), no mask
+//   gate, GEMM   σ(gate) ⊙, out_proj
+//   post_attn    post_attn_norm, gated residual, conv_norm
+//   GEMM, enc_glu, enc_dw, GEMM   pw1, GLU, depthwise + conv_out_norm +
+//                SiLU, pw2
+//   enc_out      conv residual, FFN2, mHC mix back into the lanes
+// then the lane mean and the final norm (final_kernel).
+namespace wb {
+namespace {
+
+// One HadamardMLP's device tensors.
+struct HadaK {
+    const float *d1, *d2, *b2, *d3, *d4;
+    const float *wa[3], *wb[3];
+    const float *cond_v, *cond_u;
+};
+
+// The encoder layer's tensors beside its LayerK (whose g_norm_in is
+// pre_hada_0's gain, g_post post_norm's, g_xn conv_norm's).
+struct EncK {
+    const float *g_attn_in, *g_qn, *g_kn, *g_conv_out, *g_pre_hada;
+    const float *dw;  // [dw_k][kD]
+    int dw_k;
+};
+
+// The shared memory of one HadamardMLP per CTA.
+struct HadaSmem {
+    float pv[kD], z[kD], o[kD], yT[kD], kb[kD];
+    float lg[kRank];
+    float cv[kD * kRank];
+    float wa[3][kNA * kNA], wb[3][kNB * kNB];
+};
+
+__device__ void hada_load(const HadaK &H, HadaSmem &S) {
+    const int c = threadIdx.x;
+    for (int i = c; i < kD * kRank; i += kThreads) S.cv[i] = H.cond_v[i];
+    for (int st = 0; st < 3; st++) {
+        for (int i = c; i < kNA * kNA; i += kThreads) S.wa[st][i] = H.wa[st][i];
+        for (int i = c; i < kNB * kNB; i += kThreads) S.wb[st][i] = H.wb[st][i];
+    }
+}
+
+// hadamard.go:211 rows for the CTA's row, p its normed input (column c):
+// returns column c of mlp(p), the same operations as block_out_kernel's.
+__device__ float hada_col(const HadaK &H, const int *__restrict__ p1, const int *__restrict__ p2, float p,
+                          HadaSmem &S) {
+    const int c = threadIdx.x;
+    S.pv[c] = p;
+    __syncthreads();
+    if (c < kRank) {
+        float acc = 0.0f;
+        for (int i = 0; i < kD; i++) acc = acc + S.pv[i] * S.cv[i * kRank + c];
+        S.lg[c] = acc;
+    }
+    __syncthreads();
+    if (c == 0) {  // load.go:127 softmaxInPlace with exp.go:238 expSubSumGeneric
+        float m = -INFINITY;
+        for (int r = 0; r < kRank; r++) m = fmaxf(m, S.lg[r]);
+        float sum = 0.0f;
+        for (int r = 0; r < kRank; r++) {
+            const float e = (float)exp((double)(S.lg[r] - m));
+            S.lg[r] = e;
+            sum = sum + e;
+        }
+        for (int r = 0; r < kRank; r++) S.lg[r] = __fdiv_rn(S.lg[r], sum);
+    }
+    __syncthreads();
+    float cond = 0.0f;
+    for (int r = 0; r < kRank; r++) cond = cond + S.lg[r] * H.cond_u[r * kD + c];
+    cond = cond + 1.0f;
+    S.z[c] = H.d1[c] * p;
+    __syncthreads();
+    kron_mix(S.wa[0], S.wb[0], p1, S.z, S.yT, S.kb, S.o);
+    {
+        const float a2 = H.d2[c] * cond * S.o[c] + H.b2[c];
+        S.z[c] = a2 * sigm(a2);
+    }
+    __syncthreads();
+    kron_mix(S.wa[1], S.wb[1], p2, S.z, S.yT, S.kb, S.o);
+    S.z[c] = H.d3[c] * S.o[c];
+    __syncthreads();
+    kron_mix(S.wa[2], S.wb[2], nullptr, S.z, S.yT, S.kb, S.o);
+    return S.o[c] * H.d4[c];
+}
+
+// mhc.go:131 ExpandLanes: every frame row into every lane.
+__global__ void __launch_bounds__(kThreads) enc_expand_kernel(const float *__restrict__ x, float *__restrict__ stream) {
+    const int r = blockIdx.x, c = threadIdx.x;
+    const float v = x[(size_t)r * kD + c];
+#pragma unroll
+    for (int k = 0; k < kLanes; k++) stream[((size_t)r * kLanes + k) * kD + c] = v;
+}
+
+// block.go:172 ffn (FFN1): x += 1/2 · mlp(n) with n the pre_hada_0 norm of
+// x; then block.go:193's norm_in of the result (the attention's input).
+__global__ void __launch_bounds__(kThreads)
+    enc_ffn_kernel(const __grid_constant__ HadaK H, const int *__restrict__ p1, const int *__restrict__ p2,
+                   const float *__restrict__ n, float *__restrict__ h, const float *__restrict__ g_next,
+                   float *__restrict__ n_out) {
+    __shared__ double red[33];
+    __shared__ HadaSmem S;
+    const int r = blockIdx.x, c = threadIdx.x;
+    hada_load(H, S);
+    const float m = hada_col(H, p1, p2, n[(size_t)r * kD + c], S);
+    const float hv = h[(size_t)r * kD + c] + 0.5f * m;
+    h[(size_t)r * kD + c] = hv;
+    n_out[(size_t)r * kD + c] = zc_norm_row(hv, g_next[c], red);
+}
+
+// attention.go:300 normRotate at the frame's position (RoPE from 0 in each
+// clip) and :342 quantQKV's keys and values as int8 codes per head
+// (int8.go:115 QuantizeRows: the codes fakeQuant's values stand for); the
+// queries stay float (the attention quantises them per head).
+__global__ void __launch_bounds__(kThreads)
+    enc_qkv_kernel(const __grid_constant__ EncK K, const float *__restrict__ q, const float *__restrict__ k,
+                   const float *__restrict__ v, int heads, int kv_heads, int frames, const float *__restrict__ rcos,
+                   const float *__restrict__ rsin, float *__restrict__ qo, int8_t *__restrict__ k8,
+                   float *__restrict__ ks, int8_t *__restrict__ v8, float *__restrict__ vs) {
+    const int r = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int f = r % frames, half = kQK / 2;
+    const int qw = heads * kQK, kw = kv_heads * kQK, vw = kv_heads * kVD;
+    for (int hd = warp; hd < heads + 2 * kv_heads; hd += nw) {
+        if (hd < heads + kv_heads) {
+            const bool isq = hd < heads;
+            const int h2 = isq ? hd : hd - heads;
+            const float *src = isq ? q + (size_t)r * qw + h2 * kQK : k + (size_t)r * kw + h2 * kQK;
+            const float *g = isq ? K.g_qn : K.g_kn;
+            float a = 0.0f, b = 0.0f;
+            if (lane < half) {
+                a = src[lane];
+                b = src[lane + half];
+            }
+            const float rms = (float)sqrt((double)head_ms48(a, b, lane));
+            float ra = 0.0f, rb = 0.0f;
+            if (lane < half) {
+                a = __fdiv_rn(g[lane] * a, rms);
+                b = __fdiv_rn(g[lane + half] * b, rms);
+                const float cs = rcos[(size_t)f * half + lane], sn = rsin[(size_t)f * half + lane];
+                const float ac = a * cs, bs = b * sn, bc = b * cs, as = a * sn;
+                ra = ac - bs;
+                rb = bc + as;
+            }
+            if (isq) {
+                if (lane < half) {
+                    qo[(size_t)r * qw + h2 * kQK + lane] = ra;
+                    qo[(size_t)r * qw + h2 * kQK + lane + half] = rb;
+                }
+            } else {
+                float m = fmaxf(fabsf(ra), fabsf(rb));
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                const float sc = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
+                if (lane < half) {
+                    k8[(size_t)r * kw + h2 * kQK + lane] = quant8(ra, sc);
+                    k8[(size_t)r * kw + h2 * kQK + lane + half] = quant8(rb, sc);
+                }
+                if (lane == 0) ks[(size_t)r * kv_heads + h2] = sc;
+            }
+        } else {
+            const int h2 = hd - heads - kv_heads;
+            const float a = v[(size_t)r * vw + h2 * kVD + lane], b = v[(size_t)r * vw + h2 * kVD + lane + 32];
+            float m = fmaxf(fabsf(a), fabsf(b));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const float sc = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
+            v8[(size_t)r * vw + h2 * kVD + lane] = quant8(a, sc);
+            v8[(size_t)r * vw + h2 * kVD + lane + 32] = quant8(b, sc);
+            if (lane == 0) vs[(size_t)r * kv_heads + h2] = sc;
+        }
+    }
+}
+
+// block.go:257 gated, GLUValueGate: value · σ(gate) of pw1's two halves.
+__global__ void __launch_bounds__(kThreads) enc_glu_kernel(const float *__restrict__ p, float *__restrict__ out) {
+    const int r = blockIdx.x, c = threadIdx.x;
+    const float a = p[(size_t)r * 2 * kD + c], g = p[(size_t)r * 2 * kD + kD + c];
+    out[(size_t)r * kD + c] = a * sigm(g);
+}
+
+// block.go:290 depthwise (DWCentred: frames i − pad … i + pad of the same
+// clip, zeros outside it, taps in order from 0), then block.go:236
+// NormBeforeAct: conv_out_norm and SiLU (stem.go:367 applyAct).
+__global__ void __launch_bounds__(kThreads)
+    enc_dw_kernel(const __grid_constant__ EncK K, const float *__restrict__ g, int frames, float *__restrict__ out) {
+    __shared__ double red[33];
+    const int r = blockIdx.x, c = threadIdx.x;
+    const int f = r % frames, r0 = r - f, pad = (K.dw_k - 1) / 2;
+    float acc = 0.0f;
+    for (int j = 0; j < K.dw_k; j++) {
+        const int src = f - pad + j;
+        if (src < 0 || src >= frames) continue;
+        acc = acc + K.dw[(size_t)j * kD + c] * g[(size_t)(r0 + src) * kD + c];
+    }
+    const float nv = zc_norm_row(acc, K.g_conv_out[c], red);
+    out[(size_t)r * kD + c] = nv * sigm(nv);
+}
+
+// block.go:246 the conv residual; block.go:172 ffn (FFN2); mhc.go:229
+// y = block(u) − u and :270 mix into the lanes.
+__global__ void __launch_bounds__(kThreads)
+    enc_out_kernel(const __grid_constant__ HadaK H, const __grid_constant__ EncK K, const int *__restrict__ p1,
+                   const int *__restrict__ p2, const float *__restrict__ conv, const float *__restrict__ h,
+                   const float *__restrict__ u, const float *__restrict__ hp, const float *__restrict__ hr,
+                   float *__restrict__ stream) {
+    __shared__ double red[33];
+    __shared__ HadaSmem S;
+    const int r = blockIdx.x, c = threadIdx.x;
+    hada_load(H, S);
+    const float h2 = h[(size_t)r * kD + c] + conv[(size_t)r * kD + c];
+    const float p = zc_norm_row(h2, K.g_pre_hada[c], red);
+    const float m = hada_col(H, p1, p2, p, S);
+    const float hf = h2 + 0.5f * m;
+    const float Y = hf - u[(size_t)r * kD + c];
+    float st[kLanes], out[kLanes];
+#pragma unroll
+    for (int b = 0; b < kLanes; b++) st[b] = stream[((size_t)r * kLanes + b) * kD + c];
+#pragma unroll
+    for (int a = 0; a < kLanes; a++) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int b = 0; b < kLanes; b++) acc = acc + hr[(size_t)r * kLanes * kLanes + a * kLanes + b] * st[b];
+        out[a] = acc + hp[(size_t)r * kLanes + a] * Y;
+    }
+#pragma unroll
+    for (int a = 0; a < kLanes; a++) stream[((size_t)r * kLanes + a) * kD + c] = out[a];
+}
+
+}  // namespace
+}  // namespace wb
+
+struct wc_encoder : DevStore {
+    wc_encoder_desc d{};  // sizes (pointers not kept)
+    int max_clips = 0, max_frames = 0, flags = 0, dw_k = 0;
+    bool tc = false, any = false, xq_needed = false;
+    struct Layer {
+        LayerK k;
+        EncK e;
+        HadaK h0, h1;
+        wc_cq *q, *kk, *v, *g, *o, *pw1, *pw2, *ppre, *ppost, *pres;
+        bool phi_fused = false;
+    };
+    std::vector<Layer> layers;
+    const float *g_final = nullptr, *rcos = nullptr, *rsin = nullptr;
+    const int *p1 = nullptr, *p2 = nullptr;
+    float att_scale = 1.0f;
+    // [rows][…] buffers, rows = clips · frames
+    float *stream = nullptr, *xq = nullptr, *phi_pre = nullptr, *phi_post = nullptr, *phi_res = nullptr;
+    float *hr = nullptr, *hp = nullptr, *u = nullptr, *h = nullptr, *n = nullptr;
+    float *q = nullptr, *k = nullptr, *v = nullptr, *g = nullptr, *qo = nullptr, *att = nullptr, *a = nullptr;
+    float *p = nullptr, *glu = nullptr, *cv = nullptr;
+    int8_t *k8 = nullptr, *v8 = nullptr;
+    float *ks = nullptr, *vs = nullptr;
+    int32_t *nk = nullptr;
+    void *tcbuf = nullptr;
+    size_t tcbytes = 0;
+};
+
+namespace {
+
+wc_status enc_matrix(const wc_cq *m, const char *what, int layer, int out, int in) {
+    if (!m) return set_error(WC_ERR_INVALID, fmt("encoder: layer %d %s: nil matrix", layer, what));
+    if (wc_cq_out(m) != out || wc_cq_in(m) != in)
+        return set_error(WC_ERR_INVALID, fmt("encoder: layer %d %s has shape (%d, %d), want (%d, %d)", layer, what,
+                                             wc_cq_out(m), wc_cq_in(m), out, in));
+    return WC_OK;
+}
+
+wc_status enc_gemms(wc_encoder *e, std::initializer_list<const wc_cq *> ms, const float *x,
+                    std::initializer_list<float *> ys, int rows, cudaStream_t st) {
+    std::vector<const wc_cq *> m(ms);
+    std::vector<float *> y(ys);
+    return gemms_device(m.data(), (int)m.size(), x, y.data(), rows, e->tc, e->tcbuf, e->tcbytes, st);
+}
+
+wc_status enc_hada(wc_encoder *e, const wc_hadamard_mlp &S, HadaK *H) {
+    const int nn = kNA * kNB;
+    if (!S.d1 || !S.d2 || !S.b2 || !S.d3 || !S.d4 || !S.w1a || !S.w1b || !S.w2a || !S.w2b || !S.w3a || !S.w3b ||
+        !S.cond_v || !S.cond_u)
+        return set_error(WC_ERR_INVALID, "encoder: nil HadamardMLP tensor");
+    DEC_ST(e->upload(&H->d1, S.d1, nn));
+    DEC_ST(e->upload(&H->d2, S.d2, nn));
+    DEC_ST(e->upload(&H->b2, S.b2, nn));
+    DEC_ST(e->upload(&H->d3, S.d3, nn));
+    DEC_ST(e->upload(&H->d4, S.d4, nn));
+    const float *wa[3] = {S.w1a, S.w2a, S.w3a}, *wbb[3] = {S.w1b, S.w2b, S.w3b};
+    for (int i = 0; i < 3; i++) {
+        DEC_ST(e->upload(&H->wa[i], wa[i], kNA * kNA));
+        DEC_ST(e->upload(&H->wb[i], wbb[i], kNB * kNB));
+    }
+    DEC_ST(e->upload(&H->cond_v, S.cond_v, (size_t)kD * kRank));
+    DEC_ST(e->upload(&H->cond_u, S.cond_u, (size_t)kRank * nn));
+    return WC_OK;
+}
+
+// One encoder layer on R rows of `frames` frames per clip.
+wc_status enc_layer(wc_encoder *e, int l, int R, int frames, cudaStream_t st) {
+    auto &L = e->layers[l];
+    const wc_encoder_desc &D = e->d;
+    if (L.phi_fused) {
+        PhiViews pv{};
+        CqShape sh{};
+        cq_internal(L.ppre, &sh, &pv.v[0]);
+        cq_internal(L.ppost, nullptr, &pv.v[1]);
+        cq_internal(L.pres, nullptr, &pv.v[2]);
+        pv.y[0] = e->phi_pre, pv.y[1] = e->phi_post, pv.y[2] = e->phi_res;
+        DEC_LAUNCH(mhc_phi_kernel<<<R, kThreads, 0, st>>>(e->stream, sh, pv));
+    } else {
+        DEC_LAUNCH(mhc_in_kernel<<<R, kThreads, 0, st>>>(e->stream, e->xq));
+        DEC_ST(enc_gemms(e, {L.ppre, L.ppost, L.pres}, e->xq, {e->phi_pre, e->phi_post, e->phi_res}, R, st));
+    }
+    DEC_LAUNCH(sinkhorn_kernel<<<(R + 3) / 4, 128, 0, st>>>(L.k, e->phi_res, e->hr, R));
+    // u, and FFN1's input: the pre_hada_0 norm of u (LayerK's g_norm_in).
+    DEC_LAUNCH(mhc_block_in_kernel<<<R, kThreads, 0, st>>>(L.k, e->stream, e->phi_pre, e->phi_post, e->phi_res,
+                                                           nullptr, nullptr, e->u, e->h, e->n, e->hp));
+    DEC_LAUNCH(enc_ffn_kernel<<<R, kThreads, 0, st>>>(L.h0, e->p1, e->p2, e->n, e->h, L.e.g_attn_in, e->a));
+    DEC_ST(enc_gemms(e, {L.q, L.kk, L.v, L.g}, e->a, {e->q, e->k, e->v, e->g}, R, st));
+    DEC_LAUNCH(enc_qkv_kernel<<<R, kThreads, 0, st>>>(L.e, e->q, e->k, e->v, D.heads, D.kv_heads, frames, e->rcos,
+                                                      e->rsin, e->qo, e->k8, e->ks, e->v8, e->vs));
+    DEC_ST(attend_streams_grouped(R, e->qo, D.heads, e->k8, e->ks, e->v8, e->vs, frames, e->nk, D.kv_heads, kQK,
+                                  kVD, e->att_scale, WC_ATTEND_QUANT_Q | (e->any ? WC_ATTEND_ANY_ORDER : 0), e->att,
+                                  frames, st));
+    DEC_LAUNCH(gate_kernel<<<R, kThreads, 0, st>>>(e->att, e->g, D.heads * kVD));
+    DEC_ST(enc_gemms(e, {L.o}, e->att, {e->a}, R, st));
+    // post_attn_norm, the σ(attn_gate) residual, then conv_norm (g_xn).
+    DEC_LAUNCH(post_attn_kernel<<<R, kThreads, 0, st>>>(L.k, e->a, e->h, e->n));
+    DEC_ST(enc_gemms(e, {L.pw1}, e->n, {e->p}, R, st));
+    DEC_LAUNCH(enc_glu_kernel<<<R, kThreads, 0, st>>>(e->p, e->glu));
+    DEC_LAUNCH(enc_dw_kernel<<<R, kThreads, 0, st>>>(L.e, e->glu, frames, e->cv));
+    DEC_ST(enc_gemms(e, {L.pw2}, e->cv, {e->a}, R, st));
+    DEC_LAUNCH(enc_out_kernel<<<R, kThreads, 0, st>>>(L.h1, L.e, e->p1, e->p2, e->a, e->h, e->u, e->hp, e->hr,
+                                                      e->stream));
+    return WC_OK;
+}
+
+}  // namespace
+
+extern "C" wc_status wc_encoder_create(const wc_encoder_desc *desc, int max_clips, int max_frames, int flags,
+                                       wc_encoder **out) {
+    if (!out) return set_error(WC_ERR_INVALID, "encoder: nil handle pointer");
+    *out = nullptr;
+    if (!desc) return set_error(WC_ERR_INVALID, "encoder: nil description");
+    const wc_encoder_desc &D = *desc;
+    if (D.dim != kD || D.lanes != kLanes || D.qk != kQK || D.vd != kVD || D.na != kNA || D.nb != kNB ||
+        D.rank != kRank)
+        return set_error(WC_ERR_UNSUPPORTED,
+                         fmt("encoder: this build's kernels take width 512 in 4 lanes, heads of 48/64 and a 16 x 32 "
+                             "HadamardMLP of rank 8 (got width %d, %d lanes, heads %d/%d, %d x %d rank %d)",
+                             D.dim, D.lanes, D.qk, D.vd, D.na, D.nb, D.rank));
+    if (D.layers <= 0 || D.heads <= 0 || D.kv_heads <= 0 || D.heads % D.kv_heads != 0)
+        return set_error(WC_ERR_INVALID,
+                         fmt("encoder: %d layers, %d query heads over %d KV heads", D.layers, D.heads, D.kv_heads));
+    if (D.heads * kVD != kD)
+        return set_error(WC_ERR_UNSUPPORTED, "encoder: the attention output must be as wide as the model (heads·64 = 512)");
+    if (D.dw_kernel < 1 || D.dw_kernel > 31 || D.dw_kernel % 2 == 0)
+        return set_error(WC_ERR_INVALID, fmt("encoder: depthwise kernel of %d taps (odd, at most 31)", D.dw_kernel));
+    if (max_clips <= 0 || max_frames <= 0 || (long long)max_clips * max_frames > 65535)
+        return set_error(WC_ERR_INVALID, fmt("encoder: room for %d clips of %d frames (at most 65535 rows)", max_clips,
+                                             max_frames));
+    if (!D.layer || !D.final_norm || !D.hada_p1 || !D.hada_p2 || D.rope_len <= 0)
+        return set_error(WC_ERR_INVALID, "encoder: nil tensor");
+
+    std::unique_ptr<wc_encoder> e(new (std::nothrow) wc_encoder);
+    if (!e) return set_error(WC_ERR_NOMEM, "encoder: out of host memory");
+    WB_CUDA(cudaGetDevice(&e->device));
+    e->d = D;
+    e->d.layer = nullptr;
+    e->d.hada_p1 = e->d.hada_p2 = nullptr;
+    e->d.final_norm = nullptr;
+    e->max_clips = max_clips;
+    e->max_frames = max_frames;
+    e->flags = flags;
+    e->tc = (flags & WC_ENCODER_TENSOR_CORES) != 0;
+    e->any = (flags & WC_ENCODER_ANY_ORDER) != 0;
+    e->dw_k = D.dw_kernel;
+    const int qw = D.heads * kQK, kw = D.kv_heads * kQK, vw = D.kv_heads * kVD;
+    for (int l = 0; l < D.layers; l++) {
+        const wc_encoder_layer &S = D.layer[l];
+        DEC_ST(enc_matrix(S.q_proj, "q_proj", l, qw, kD));
+        DEC_ST(enc_matrix(S.k_proj, "k_proj", l, kw, kD));
+        DEC_ST(enc_matrix(S.v_proj, "v_proj", l, vw, kD));
+        DEC_ST(enc_matrix(S.gate_proj, "gate_proj", l, D.heads * kVD, kD));
+        DEC_ST(enc_matrix(S.out_proj, "out_proj", l, kD, D.heads * kVD));
+        DEC_ST(enc_matrix(S.pw1, "pw1", l, 2 * kD, kD));
+        DEC_ST(enc_matrix(S.pw2, "pw2", l, kD, kD));
+        DEC_ST(enc_matrix(S.phi_pre, "mhc_phi_pre", l, kLanes, kLanes * kD));
+        DEC_ST(enc_matrix(S.phi_post, "mhc_phi_post", l, kLanes, kLanes * kD));
+        DEC_ST(enc_matrix(S.phi_res, "mhc_phi_res", l, kLanes * kLanes, kLanes * kD));
+        if (!S.pre_hada_0 || !S.norm_in || !S.post_norm || !S.conv_norm || !S.conv_out_norm || !S.pre_hada ||
+            !S.q_norm || !S.k_norm || !S.dw || !S.b_pre || !S.b_post || !S.b_res)
+            return set_error(WC_ERR_INVALID, fmt("encoder: layer %d: nil tensor", l));
+        wc_encoder::Layer L{};
+        DEC_ST(e->view(S.q_proj, &L.q));
+        DEC_ST(e->view(S.k_proj, &L.kk));
+        DEC_ST(e->view(S.v_proj, &L.v));
+        DEC_ST(e->view(S.gate_proj, &L.g));
+        DEC_ST(e->view(S.out_proj, &L.o));
+        DEC_ST(e->view(S.pw1, &L.pw1));
+        DEC_ST(e->view(S.pw2, &L.pw2));
+        DEC_ST(e->view(S.phi_pre, &L.ppre));
+        DEC_ST(e->view(S.phi_post, &L.ppost));
+        DEC_ST(e->view(S.phi_res, &L.pres));
+        {
+            CqShape a{}, b{}, c{};
+            CqView va{}, vb{}, vc{};
+            cq_internal(L.ppre, &a, &va);
+            cq_internal(L.ppost, &b, &vb);
+            cq_internal(L.pres, &c, &vc);
+            auto same = [](const CqShape &x, const CqShape &y) {
+                return x.in == y.in && x.group == y.group && x.bits == y.bits && x.cb_max == y.cb_max &&
+                       x.lut_step == y.lut_step && std::memcmp(x.cb, y.cb, sizeof x.cb) == 0;
+            };
+            L.phi_fused = !e->tc && a.bits == 4 && a.group == 128 && a.in == kPhiIn && a.gb == 64 &&
+                          a.pad == kPhiIn && same(a, b) && same(a, c);
+            if (!L.phi_fused) e->xq_needed = true;
+        }
+        LayerK &K = L.k;
+        DEC_ST(e->upload(&K.g_norm_in, S.pre_hada_0, kD, true));
+        DEC_ST(e->upload(&K.g_post, S.post_norm, kD, true));
+        DEC_ST(e->upload(&K.g_xn, S.conv_norm, kD, true));
+        DEC_ST(e->upload(&K.b_pre, S.b_pre, kLanes));
+        DEC_ST(e->upload(&K.b_post, S.b_post, kLanes));
+        DEC_ST(e->upload(&K.b_res, S.b_res, kLanes * kLanes));
+        K.gate = sigmoid_host(S.attn_gate);
+        K.a_pre = S.a_pre;
+        K.a_post = S.a_post;
+        K.a_res = S.a_res;
+        K.lane = l % kLanes;
+        EncK &E = L.e;
+        DEC_ST(e->upload(&E.g_attn_in, S.norm_in, kD, true));
+        DEC_ST(e->upload(&E.g_qn, S.q_norm, kQK, true));
+        DEC_ST(e->upload(&E.g_kn, S.k_norm, kQK, true));
+        DEC_ST(e->upload(&E.g_conv_out, S.conv_out_norm, kD, true));
+        DEC_ST(e->upload(&E.g_pre_hada, S.pre_hada, kD, true));
+        DEC_ST(e->upload(&E.dw, S.dw, (size_t)D.dw_kernel * kD));
+        E.dw_k = D.dw_kernel;
+        DEC_ST(enc_hada(e.get(), S.hada_0, &L.h0));
+        DEC_ST(enc_hada(e.get(), S.hada, &L.h1));
+        e->layers.push_back(L);
+    }
+    DEC_ST(e->hada_perms(D.hada_p1, D.hada_p2, &e->p1, &e->p2));
+    DEC_ST(e->upload(&e->g_final, D.final_norm, kD, true));
+    DEC_ST(e->rope_tables(D.rope_theta, D.rope_len, &e->rcos, &e->rsin));
+    e->att_scale = (float)std::sqrt((double)kQK);  // attention.go:407 attendScale
+
+    const size_t R = (size_t)max_clips * max_frames;
+    DEC_ST(e->alloc(&e->stream, R * kLanes * kD));
+    if (e->xq_needed) DEC_ST(e->alloc(&e->xq, R * kLanes * kD));
+    DEC_ST(e->alloc(&e->phi_pre, R * kLanes));
+    DEC_ST(e->alloc(&e->phi_post, R * kLanes));
+    DEC_ST(e->alloc(&e->phi_res, R * kLanes * kLanes));
+    DEC_ST(e->alloc(&e->hr, R * kLanes * kLanes));
+    DEC_ST(e->alloc(&e->hp, R * kLanes));
+    DEC_ST(e->alloc(&e->u, R * kD));
+    DEC_ST(e->alloc(&e->h, R * kD));
+    DEC_ST(e->alloc(&e->n, R * kD));
+    DEC_ST(e->alloc(&e->q, R * qw));
+    DEC_ST(e->alloc(&e->k, R * kw));
+    DEC_ST(e->alloc(&e->v, R * vw));
+    DEC_ST(e->alloc(&e->g, R * D.heads * kVD));
+    DEC_ST(e->alloc(&e->qo, R * qw));
+    DEC_ST(e->alloc(&e->att, R * D.heads * kVD));
+    DEC_ST(e->alloc(&e->a, R * kD));
+    DEC_ST(e->alloc(&e->p, R * 2 * kD));
+    DEC_ST(e->alloc(&e->glu, R * kD));
+    DEC_ST(e->alloc(&e->cv, R * kD));
+    DEC_ST(e->alloc(&e->k8, R * kw));
+    DEC_ST(e->alloc(&e->v8, R * vw));
+    DEC_ST(e->alloc(&e->ks, R * D.kv_heads));
+    DEC_ST(e->alloc(&e->vs, R * D.kv_heads));
+    DEC_ST(e->alloc(&e->nk, R));
+    if (e->tc) {
+        // The rotated image of the tensor-core products: R rows at 512 in,
+        // and at 2048 in for the φ products.
+        e->tcbytes = std::max(tc_a_bytes((int)R, (kD + 63) / 64), tc_a_bytes((int)R, (kLanes * kD + 63) / 64));
+        unsigned char *pb = nullptr;
+        DEC_ST(e->alloc(&pb, e->tcbytes));
+        e->tcbuf = pb;
+    }
+    *out = e.release();
+    return WC_OK;
+}
+
+extern "C" void wc_encoder_destroy(wc_encoder *e) { delete e; }
+
+extern "C" wc_status wc_encoder_stack(wc_encoder *e, const float *x, int clips, int frames, float *out,
+                                      wc_stream stream) {
+    if (!e) return set_error(WC_ERR_INVALID, "encoder: nil encoder");
+    int cur = 0;
+    WB_CUDA(cudaGetDevice(&cur));
+    if (cur != e->device)
+        return set_error(WC_ERR_INVALID, fmt("encoder: built on device %d, called on device %d", e->device, cur));
+    if (clips < 0 || frames < 0 || clips > e->max_clips || frames > e->max_frames)
+        return set_error(WC_ERR_INVALID, fmt("encoder: %d clips of %d frames exceed the room for %d of %d", clips,
+                                             frames, e->max_clips, e->max_frames));
+    if (frames > e->d.rope_len)
+        return set_error(WC_ERR_INVALID, fmt("encoder: RoPE tables for %d positions, want %d", e->d.rope_len, frames));
+    if (clips == 0 || frames == 0) return WC_OK;
+    if (!x || !out) return set_error(WC_ERR_INVALID, "encoder: nil input or output");
+    cudaStream_t st = (cudaStream_t)stream;
+    const int R = clips * frames;
+    DEC_LAUNCH(fill_kernel<<<(R + 255) / 256, 256, 0, st>>>(e->nk, frames, R));
+    DEC_LAUNCH(enc_expand_kernel<<<R, kThreads, 0, st>>>(x, e->stream));
+    for (int l = 0; l < e->d.layers; l++) DEC_ST(enc_layer(e, l, R, frames, st));
+    DEC_LAUNCH(final_kernel<<<R, kThreads, 0, st>>>(e->stream, e->g_final, out));
     return WC_OK;
 }

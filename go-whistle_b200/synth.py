@@ -194,6 +194,83 @@ class DecoderWeights:
         return l * per, (l + 1) * per
 
 
+class EncoderWeights:
+    """A synthetic Whistle encoder stack (encNN.*, enc.mhc_*, enc.final_norm;
+    the shapes of the exported file's map): sizes as attributes, CQ tensors
+    as Packed (2-bit projections, pw1 and pw2; 4-bit φ), float tensors as
+    float32 arrays; per-layer tensors in ``layers[l]`` keyed by the .cact
+    names without the prefix, the FFN1 HadamardMLP under ``hada_0.*`` and
+    the FFN2 one under ``hada.*``."""
+
+    def __init__(self, seed: int = 5000, layers: int = 8):
+        rng = np.random.default_rng(seed)
+        self.seed = seed
+        self.dim, self.lanes, self.n_layers = 512, 4, layers
+        self.heads, self.kv_heads, self.qk, self.vd = 8, 2, 48, 64
+        self.na, self.nb, self.rank = 16, 32, 8
+        self.dw_k = 9
+        self.rope_theta, self.rope_len = 1e5, 1536
+        G = 128
+        self.cb2, self.cb4 = lloyd_max_codebook(2, G), lloyd_max_codebook(4, G)
+        D, n = self.dim, self.lanes
+
+        def vec(k, mean=0.0, sd=0.02):
+            return (mean + rng.normal(0.0, sd, size=k)).astype(np.float32)
+
+        def mlp(L, pre):
+            nn_ = self.na * self.nb
+            for k in ("d1", "d2", "d3", "d4"):
+                L[pre + k] = vec(nn_, 1.0)
+            L[pre + "b2"] = vec(nn_)
+            for s in range(3):
+                L[f"{pre}w{s + 1}a"] = rng.normal(0.0, 1.0 / np.sqrt(self.na), size=(self.na, self.na)).astype(
+                    np.float32)
+                L[f"{pre}w{s + 1}b"] = rng.normal(0.0, 1.0 / np.sqrt(self.nb), size=(self.nb, self.nb)).astype(
+                    np.float32)
+            L[pre + "cond_v"] = rng.normal(0.0, 0.02, size=(D, self.rank)).astype(np.float32)
+            L[pre + "cond_u"] = rng.normal(0.0, 0.02, size=(self.rank, nn_)).astype(np.float32)
+
+        self.final_norm = vec(D)
+        self.hada_p1 = rng.permutation(self.na * self.nb).astype(np.int32)
+        self.hada_p2 = rng.permutation(self.na * self.nb).astype(np.int32)
+        self.phi_pre = _cq_tensor(rng, layers * n, n * D, 4, G, self.cb4)
+        self.phi_post = _cq_tensor(rng, layers * n, n * D, 4, G, self.cb4)
+        self.phi_res = _cq_tensor(rng, layers * n * n, n * D, 4, G, self.cb4)
+        self.layers = []
+        qw, kw, vw, ow = self.heads * self.qk, self.kv_heads * self.qk, self.kv_heads * self.vd, self.heads * self.vd
+        for _ in range(layers):
+            L = {}
+            for k in ("pre_hada_0", "norm_in", "post_norm", "conv_norm", "conv_out_norm", "pre_hada"):
+                L[k] = vec(D)
+            for k in ("q_norm", "k_norm"):
+                L[k] = vec(self.qk)
+            L["attn_gate"] = float(rng.normal(0.0, 0.5))
+            for k, o, i in (("q_proj", qw, D), ("k_proj", kw, D), ("v_proj", vw, D), ("gate_proj", ow, D),
+                            ("out_proj", D, ow), ("pw1", 2 * D, D), ("pw2", D, D)):
+                L[k] = _cq_tensor(rng, o, i, 2, G, self.cb2)
+            dw = rng.normal(0.0, 0.1, size=(self.dw_k, D)).astype(np.float32)
+            dw[self.dw_k // 2] += 1.0
+            L["dw"] = dw
+            mlp(L, "hada_0.")
+            mlp(L, "hada.")
+            L["a_pre"], L["a_post"], L["a_res"] = (float(v) for v in 0.1 + rng.normal(0.0, 0.02, size=3))
+            L["b_pre"], L["b_post"] = vec(n, 0.0, 0.1), vec(n, 0.0, 0.1)
+            L["b_res"] = (2.0 * np.eye(n) + rng.normal(0.0, 0.1, size=(n, n))).astype(np.float32).reshape(-1)
+            self.layers.append(L)
+
+    def phi_rows(self, name: str, l: int):
+        """Layer l's row range of a stacked φ (mhc.go:94-96)."""
+        n = self.lanes
+        per = n * n if name == "phi_res" else n
+        return l * per, (l + 1) * per
+
+
+def stem_output(rng: np.random.Generator, clips: int, frames: int = 375, dim: int = 512) -> np.ndarray:
+    """Synthetic stem outputs [clips][frames][dim] (the encoder stack's
+    input), ~N(0, 1)."""
+    return rng.normal(0.0, 1.0, size=(clips, frames, dim)).astype(np.float32)
+
+
 def encoder_output(rng: np.random.Generator, streams: int, frames: int = 375, dim: int = 512) -> np.ndarray:
     """Synthetic encoder outputs [streams][frames][dim] (the final-normed
     memory the decoder reads), ~N(0, 1)."""

@@ -500,6 +500,81 @@ wc_status wc_decoder_beam(wc_decoder *d, const wc_beam_options *o, int bos, cons
 wc_status wc_decoder_memory_of(const wc_decoder *d, int l, const int8_t **k8, const float **ks, const int8_t **v8,
                                const float **vs);
 
+/* ------------------------------------------------------------------
+ * Whistle's encoder stack on the device: internal/encoder's Stack
+ * (encoder.go:167) with the Best() hypothesis (hypothesis.go:284) and the
+ * engine's int8 numerics (whistle/model.go:85 WithInt8 -> encoder.go:50
+ * LoadInt8): per layer, mHC (needle/mhc.go:182) around the macaron block
+ * (block.go:148: FFN1 at scale 1/2, attention with no mask and RoPE
+ * θ = 1e5, the conv module pw1 -> GLU value·σ(gate) -> centred depthwise
+ * conv -> conv_out_norm -> SiLU -> pw2, FFN2 at scale 1/2), then the lane
+ * mean and the final norm. Its input is the stem's output (encoder.go:132
+ * Stem: the log-mel front end and the conv stem run before it).
+ */
+
+/* One HadamardMLP's tensors (needle/hadamard.go:28). */
+typedef struct wc_hadamard_mlp {
+    const float *d1, *d2, *b2, *d3, *d4;            /* [na·nb] */
+    const float *w1a, *w1b, *w2a, *w2b, *w3a, *w3b; /* [na][na], [nb][nb] */
+    const float *cond_v;                            /* [dim][rank] */
+    const float *cond_u;                            /* [rank][na·nb] */
+} wc_hadamard_mlp;
+
+/* One encoder layer, encNN.* (block.go:17 block) and its mHC rows. Norm
+ * vectors are the stored scales (gain = 1 + scale); attn_gate is raw. */
+typedef struct wc_encoder_layer {
+    const float *pre_hada_0, *norm_in, *post_norm, *conv_norm, *conv_out_norm, *pre_hada; /* [dim] */
+    float attn_gate;
+    const wc_cq *q_proj, *k_proj, *v_proj, *gate_proj, *out_proj; /* self-attention */
+    const wc_cq *pw1, *pw2;                                       /* [2·dim][dim], [dim][dim] */
+    const float *q_norm, *k_norm;                                 /* [qk] */
+    const float *dw;                                              /* [dw_kernel][dim] */
+    wc_hadamard_mlp hada_0, hada;                                 /* FFN1, FFN2 */
+    float a_pre, a_post, a_res;
+    const float *b_pre, *b_post; /* [lanes] */
+    const float *b_res;          /* [lanes][lanes] */
+    const wc_cq *phi_pre, *phi_post, *phi_res;
+} wc_encoder_layer;
+
+typedef struct wc_encoder_desc {
+    int dim, lanes, layers, heads, kv_heads, qk, vd, dw_kernel, na, nb, rank;
+    const int32_t *hada_p1, *hada_p2; /* [na·nb] */
+    double rope_theta;
+    int rope_len;
+    const float *final_norm;        /* [dim] */
+    const wc_encoder_layer *layer;  /* [layers] */
+} wc_encoder_desc;
+
+typedef struct wc_encoder wc_encoder;
+
+/* Flags of wc_encoder_create. */
+enum {
+    /* Every CQ product on the tensor cores (WC_GEMM_TENSOR_CORES' fp16
+     * bound) instead of the bit-exact lut kernels. */
+    WC_ENCODER_TENSOR_CORES = 1,
+    /* The attention in any order (WC_ATTEND_ANY_ORDER's 1e-5 bound) instead
+     * of int8.go's exact order. */
+    WC_ENCODER_ANY_ORDER = 2,
+};
+
+/*
+ * Builds an encoder stack (encoder.go:50 LoadInt8's stack part) with device
+ * room for up to max_clips clips of up to max_frames frames. This build's
+ * kernels take Whistle's widths: dim 512 in 4 lanes, heads of 48/64 with
+ * 8·64 = 512, a 16 × 32 HadamardMLP of rank 8, an odd depthwise kernel of
+ * up to 31 taps. max_clips · max_frames is at most 65,535 rows.
+ */
+wc_status wc_encoder_create(const wc_encoder_desc *desc, int max_clips, int max_frames, int flags, wc_encoder **out);
+void wc_encoder_destroy(wc_encoder *e);
+
+/*
+ * encoder.go:167 Stack for `clips` clips of `frames` frames each: x DEVICE
+ * [clips][frames][dim] (the stem's output; not written), out DEVICE
+ * [clips][frames][dim]. Each clip's frames attend to that clip's frames
+ * only; RoPE positions count from 0 in every clip.
+ */
+wc_status wc_encoder_stack(wc_encoder *e, const float *x, int clips, int frames, float *out, wc_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

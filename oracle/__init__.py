@@ -571,3 +571,139 @@ class OracleState:
         if getattr(self, "h", None):
             _dec_lib().wo_dec_free(self.h)
             self.h = None
+
+
+# ---------------------------------------------------------------- encoder
+# internal/encoder's Stack (Best() hypothesis, needle.Int8{Act, KV}) over a
+# synthetic weight set (go-whistle_b200's synth.EncoderWeights).
+
+ENC_ATTEND_FLOAT, ENC_ATTEND_INT8 = 0, 1
+
+
+class _EncLayer(ctypes.Structure):
+    _fields_ = [("b", _DecLayer), ("hada0", _DecLayer), ("conv_norm", _f32p), ("conv_out_norm", _f32p),
+                ("pw1", Packed), ("pw2", Packed), ("dw", _f32p)]
+
+
+class _Encoder(ctypes.Structure):
+    _fields_ = [("d", _Decoder), ("dw_k", _i32), ("layer", ctypes.POINTER(_EncLayer))]
+
+
+def _enc_lib():
+    L = lib()
+    if not getattr(L, "_enc_ready", False):
+        ep = ctypes.POINTER(_Encoder)
+        L.wo_enc_stack.restype = _i32
+        L.wo_enc_stack.argtypes = [ep, _f32p, _i32, _i32, _i32, _f32p]
+        L.wo_enc_stack_mt.restype = _i32
+        L.wo_enc_stack_mt.argtypes = [ep, _f32p, _i32, _i32, _i32, _f32p, _i32]
+        L.wo_enc_glu.argtypes = [_f32p, _i32, _i32, _f32p]
+        L.wo_enc_depthwise.argtypes = [_f32p, _i32, _i32, _f32p, _i32, _f32p]
+        L.wo_silu.argtypes = [_f32p, _i32]
+        L._enc_ready = True
+    return L
+
+
+def enc_glu(p: np.ndarray, t: int, half: int) -> np.ndarray:
+    p = _c(p, np.float32)
+    out = np.zeros(t * half, np.float32)
+    _enc_lib().wo_enc_glu(_ptr(p, _f32p), t, half, _ptr(out, _f32p))
+    return out
+
+
+def enc_depthwise(x: np.ndarray, t: int, h: int, dw: np.ndarray) -> np.ndarray:
+    x, dw = _c(x, np.float32), _c(dw, np.float32)
+    out = np.zeros(t * h, np.float32)
+    _enc_lib().wo_enc_depthwise(_ptr(x, _f32p), t, h, _ptr(dw, _f32p), dw.size // h, _ptr(out, _f32p))
+    return out
+
+
+def silu(x: np.ndarray) -> np.ndarray:
+    x = _c(x, np.float32).copy()
+    _enc_lib().wo_silu(_ptr(x, _f32p), x.size)
+    return x
+
+
+class OracleEncoder:
+    """The CPU restatement of Whistle's encoder stack over weights ``w``."""
+
+    def __init__(self, w):
+        self._keep = []
+
+        def arr(a, dt=np.float32):
+            a = _c(a, dt).reshape(-1)
+            self._keep.append(a)
+            return a
+
+        def f(a):
+            return _ptr(arr(a), _f32p)
+
+        def pk(p, lo=None, hi=None):
+            m = OracleMatrix.of(p)
+            self._keep.append(m)
+            if lo is None:
+                return m.s
+            groups = (m.in_ + m.group - 1) // m.group
+            rb = groups * m.group * m.bits // 8
+            return Packed(hi - lo, m.in_, m.group, m.bits, _ptr(m.index[lo * rb:], _u8p),
+                          _ptr(m.norms16[lo * groups:], _u16p), _ptr(m.cb, _f32p))
+
+        def mlp(d, L, pre, norm):
+            for k in ("d1", "d2", "b2", "d3", "d4", "cond_v", "cond_u"):
+                setattr(d, k, f(L[pre + k]))
+            for s in range(3):
+                d.hada_w[s][0] = f(L[f"{pre}w{s + 1}a"])
+                d.hada_w[s][1] = f(L[f"{pre}w{s + 1}b"])
+            d.pre_hada = f(L[norm])
+
+        self.w = w
+        n = len(w.layers)
+        layers = (_EncLayer * n)()
+        for l, L in enumerate(w.layers):
+            e = layers[l]
+            b = e.b
+            b.norm_in, b.post_norm = f(L["norm_in"]), f(L["post_norm"])
+            b.q_norm, b.k_norm = f(L["q_norm"]), f(L["k_norm"])
+            b.attn_gate = float(L["attn_gate"])
+            for k in ("q_proj", "k_proj", "v_proj", "gate_proj", "out_proj"):
+                setattr(b, k, pk(L[k]))
+            mlp(b, L, "hada.", "pre_hada")
+            mlp(e.hada0, L, "hada_0.", "pre_hada_0")
+            for k in ("a_pre", "a_post", "a_res"):
+                setattr(b, k, float(L[k]))
+            for k in ("b_pre", "b_post", "b_res"):
+                setattr(b, k, f(L[k]))
+            for k in ("phi_pre", "phi_post", "phi_res"):
+                lo, hi = w.phi_rows(k, l)
+                setattr(b, k, pk(getattr(w, k), lo, hi))
+            e.conv_norm, e.conv_out_norm = f(L["conv_norm"]), f(L["conv_out_norm"])
+            e.pw1, e.pw2 = pk(L["pw1"]), pk(L["pw2"])
+            e.dw = f(L["dw"])
+        self._layers = layers
+        self.rope_cos, self.rope_sin = rope_tables(w.qk, w.rope_len, w.rope_theta)
+        D = _Decoder()
+        D.dim, D.lanes, D.layers, D.heads, D.kv_heads, D.qk, D.vd = (w.dim, w.lanes, n, w.heads, w.kv_heads, w.qk,
+                                                                      w.vd)
+        D.na, D.nb, D.rank = w.na, w.nb, w.rank
+        D.hada_p1 = _ptr(arr(w.hada_p1, np.int32), _i32p)
+        D.hada_p2 = _ptr(arr(w.hada_p2, np.int32), _i32p)
+        D.rope_cos, D.rope_sin = _ptr(self.rope_cos, _f32p), _ptr(self.rope_sin, _f32p)
+        D.rope_len = w.rope_len
+        D.final_norm = f(w.final_norm)
+        self.e = _Encoder(D, w.dw_k, layers)
+
+    def stack(self, x: np.ndarray, form: int = ENC_ATTEND_INT8, threads: int = 1) -> np.ndarray:
+        """encoder.go:167 Stack on x [clips][t][dim] (or [t][dim])."""
+        x = _c(x, np.float32)
+        shape = x.shape
+        x3 = x.reshape(-1, shape[-2], shape[-1])
+        clips, t = x3.shape[0], x3.shape[1]
+        out = np.zeros_like(x3)
+        L = _enc_lib()
+        if threads > 1:
+            rc = L.wo_enc_stack_mt(ctypes.byref(self.e), _ptr(x3, _f32p), clips, t, form, _ptr(out, _f32p), threads)
+        else:
+            rc = L.wo_enc_stack(ctypes.byref(self.e), _ptr(x3, _f32p), clips, t, form, _ptr(out, _f32p))
+        if rc != 0:
+            raise ValueError(f"oracle: {t} frames exceed the RoPE tables ({self.w.rope_len})")
+        return out.reshape(shape)

@@ -240,6 +240,55 @@ void wo_dec_greedy_states_mt(const wo_decoder *d, wo_dec_state **st, int streams
                              int nlangs, int eos, int max_tok, int *tokens, int *counts, int *lang, int *eos_hit,
                              int threads);
 
+/* ------------------------------------------------------------------
+ * Whistle's encoder stack (whistle_oracle.c): internal/encoder's Stack
+ * (encoder.go:167) with the Best() hypothesis (hypothesis.go:284: macaron
+ * blocks, FFN scale 1/2, GLU value·σ(gate), SiLU after conv_out_norm,
+ * centred depthwise conv, mHC lanes, RoPE θ = 1e5, final norm) and
+ * needle.Int8{Act, KV} (whistle/model.go:85).
+ *
+ * One encoder layer (block.go:17). `b` holds the fields a decoder layer
+ * shares with it: norm_in, post_norm, pre_hada (FFN2's norm), attn_gate,
+ * q/k/v/gate/out_proj, q_norm, k_norm, the FFN2 HadamardMLP (hada.*: d1 …
+ * cond_u), the mHC scalars, biases and φ rows; its taps and cross fields
+ * are unused. hada0 holds the FFN1 HadamardMLP (hada_0.*) in the same
+ * fields, with pre_hada_0 as its pre_hada. */
+typedef struct {
+    wo_dec_layer b, hada0;
+    const float *conv_norm, *conv_out_norm; /* [dim] */
+    wo_packed pw1, pw2;                     /* [2·dim][dim], [dim][dim] */
+    const float *dw;                        /* [dw_k][dim] */
+} wo_enc_layer;
+
+/* `d` holds the sizes (dim, lanes, heads, kv_heads, qk, vd, na, nb, rank),
+ * hada_p1/2, the RoPE tables (θ = 1e5) and final_norm; the rest unused. */
+typedef struct {
+    wo_decoder d;
+    int dw_k;
+    const wo_enc_layer *layer; /* [d.layers] */
+} wo_encoder;
+
+/* Attention forms of wo_enc_stack. */
+enum {
+    WO_ENC_ATTEND_FLOAT = 0, /* attention.go:480 attendGEMM on the fake-quantised q, k, v (the reference) */
+    WO_ENC_ATTEND_INT8 = 1,  /* int8.go:208 AttendInt8Spans on their int8 codes (the device's exact order) */
+};
+
+/* encoder.go:167 Stack on `clips` clips of t rows of dim values each
+ * (the stem's output, [clips][t][dim]): out [clips][t][dim]. Returns -1 if
+ * t exceeds the RoPE tables, else 0. */
+int wo_enc_stack(const wo_encoder *e, const float *x, int clips, int t, int form, float *out);
+/* The same with one clip per task on `threads` OS threads. Same bits. */
+int wo_enc_stack_mt(const wo_encoder *e, const float *x, int clips, int t, int form, float *out, int threads);
+
+/* The block's row-wise pieces alone (the known-answer pins): block.go:257
+ * gated (GLUValueGate) on t rows of 2·half values; block.go:290 depthwise
+ * (DWCentred) on t rows of h channels with taps dw [k][h]; stem.go:367
+ * applyAct (ActSiLU) on n values in place. */
+void wo_enc_glu(const float *p, int t, int half, float *out);
+void wo_enc_depthwise(const float *x, int t, int h, const float *dw, int k, float *out);
+void wo_silu(float *x, int n);
+
 #ifdef __cplusplus
 }
 #endif

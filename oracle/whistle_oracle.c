@@ -837,3 +837,257 @@ void wo_dec_greedy_states_mt(const wo_decoder *d, wo_dec_state **st, int streams
     greedy_states_job job = {d, st, bos, nlangs, eos, max_tok, langs, tokens, counts, lang, eos_hit};
     wo_parallel_for(streams, threads < 1 ? 1 : threads, greedy_states_task, &job);
 }
+
+/* ------------------------------------------------------------------ encoder */
+
+/* internal/encoder/stem.go:367 applyAct, ActSiLU: v·σ(v) (stem.go:393
+ * sigmoid in float64). */
+void wo_silu(float *x, int n) {
+    for (int i = 0; i < n; i++) x[i] = x[i] * sigmoid(x[i]);
+}
+
+/* block.go:257 gated, GLUValueGate: o[k] = a[k]·σ(g[k]) with a, g the two
+ * halves of a row of pw1's output. */
+void wo_enc_glu(const float *p, int t, int half, float *out) {
+    for (int i = 0; i < t; i++) {
+        const float *a = p + (size_t)i * 2 * half, *g = a + half;
+        for (int k = 0; k < half; k++) out[(size_t)i * half + k] = a[k] * sigmoid(g[k]);
+    }
+}
+
+/* block.go:290 depthwise, DWCentred: out[i][c] = Σ_j dw[j][c]·x[i − pad + j][c]
+ * over the frames inside the clip, j ascending, from 0, pad = (k − 1)/2. */
+void wo_enc_depthwise(const float *x, int t, int h, const float *dw, int k, float *out) {
+    int pad = (k - 1) / 2;
+    memset(out, 0, (size_t)t * h * sizeof(float));
+    for (int i = 0; i < t; i++)
+        for (int j = 0; j < k; j++) {
+            int src = i - pad + j;
+            if (src < 0 || src >= t) continue;
+            for (int c = 0; c < h; c++) {
+                float tt = dw[(size_t)j * h + c] * x[(size_t)src * h + c];
+                out[(size_t)i * h + c] += tt;
+            }
+        }
+}
+
+/* block.go:172 ffn: x += 1/2 · mlp(norm(x)) per row (FFNHalf; the product
+ * is exact). */
+static void enc_ffn(const wo_decoder *d, const wo_dec_layer *H, const float *norm, float *x, int t) {
+    int c = d->dim;
+    float *n = malloc((size_t)c * sizeof(float)), *m = malloc((size_t)c * sizeof(float));
+    for (int i = 0; i < t; i++) {
+        float *row = x + (size_t)i * c;
+        zc_norm(n, row, 1, c, norm);
+        hadamard_mlp(d, H, n, m);
+        for (int k = 0; k < c; k++) {
+            float tt = 0.5f * m[k];
+            row[k] += tt;
+        }
+    }
+    free(n), free(m);
+}
+
+/* attention.go:226 forward with MaskNone and RoPE at positions 0 … t − 1
+ * over the t rows x of one clip, with Int8{Act, KV}: the projections
+ * (:262, one shared input), the per-head q/k norms and RoPE (:300
+ * normRotate), quantQKV (:342), attend (:360) and output (:242). form
+ * WO_ENC_ATTEND_FLOAT restates attendGEMM (:480): logits Σ q̃·k̃ over the
+ * fake-quantised values in index order, ÷ √qk, softmaxInPlace, then
+ * Σ_j p_j·ṽ_j in key order; WO_ENC_ATTEND_INT8 runs AttendInt8Spans on the
+ * same int8 codes (integer logits, the device kernel's exact order). */
+static void enc_attention(const wo_encoder *e, const wo_dec_layer *L, const float *x, int t, int form, float *y) {
+    const wo_decoder *d = &e->d;
+    int H = d->heads, KV = d->kv_heads, qk = d->qk, vd = d->vd;
+    int qw = H * qk, kw = KV * qk, vw = KV * vd, ow = H * vd, half = qk / 2;
+    float *q = malloc((size_t)t * qw * sizeof(float)), *k = malloc((size_t)t * kw * sizeof(float));
+    float *v = malloc((size_t)t * vw * sizeof(float)), *gate = malloc((size_t)t * ow * sizeof(float));
+    float *att = calloc((size_t)t * ow, sizeof(float));
+    wo_packed ms[4] = {L->q_proj, L->k_proj, L->v_proj, L->gate_proj};
+    float *ys[4] = {q, k, v, gate};
+    wo_cq_gemms_lut(ms, 4, x, t, ys);
+    zc_norm(q, q, t * H, qk, L->q_norm);
+    zc_norm(k, k, t * KV, qk, L->k_norm);
+    for (int i = 0; i < t; i++) {
+        const float *cs = d->rope_cos + (size_t)i * half, *sn = d->rope_sin + (size_t)i * half;
+        for (int h = 0; h < H; h++) rope_apply(q + ((size_t)i * H + h) * qk, half, cs, sn);
+        for (int h = 0; h < KV; h++) rope_apply(k + ((size_t)i * KV + h) * qk, half, cs, sn);
+    }
+    float scale = (float)sqrt((double)qk); /* attention.go:407 attendScale */
+    if (form == WO_ENC_ATTEND_FLOAT) {
+        fake_quant(q, q, t * qw, qk);
+        fake_quant(k, k, t * kw, qk);
+        fake_quant(v, v, t * vw, vd);
+        float *row = malloc((size_t)t * sizeof(float));
+        for (int h = 0; h < H; h++) {
+            int kv = h / (H / KV); /* attention.go:191 kvHead */
+            for (int i = 0; i < t; i++) {
+                const float *qi = q + (size_t)i * qw + (size_t)h * qk;
+                for (int j = 0; j < t; j++) row[j] = dot(qi, k + (size_t)j * kw + (size_t)kv * qk, qk);
+                for (int j = 0; j < t; j++) row[j] /= scale; /* attention.go:587 softmaxSpans */
+                wo_softmax(row, t);
+                float *o = att + (size_t)i * ow + (size_t)h * vd;
+                for (int dd = 0; dd < vd; dd++) {
+                    float s = 0.0f;
+                    for (int j = 0; j < t; j++) {
+                        float tt = row[j] * v[(size_t)j * vw + (size_t)kv * vd + dd];
+                        s += tt;
+                    }
+                    o[dd] = s;
+                }
+            }
+        }
+        free(row);
+    } else {
+        int8_t *k8 = malloc((size_t)t * kw), *v8 = malloc((size_t)t * vw);
+        float *ks = malloc((size_t)t * KV * sizeof(float)), *vs = malloc((size_t)t * KV * sizeof(float));
+        int32_t *sp = malloc((size_t)t * 4 * sizeof(int32_t));
+        wo_quantize_rows(k, t, kw, qk, k8, ks);
+        wo_quantize_rows(v, t, vw, vd, v8, vs);
+        for (int i = 0; i < t; i++) sp[4 * i] = sp[4 * i + 1] = sp[4 * i + 2] = 0, sp[4 * i + 3] = t;
+        wo_attend_int8_spans(q, t, H, k8, ks, v8, vs, t, KV, qk, vd, sp, scale, 1, NULL, att);
+        free(k8), free(v8), free(ks), free(vs), free(sp);
+    }
+    for (size_t i = 0; i < (size_t)t * ow; i++) {
+        gate[i] = sigmoid(gate[i]);
+        att[i] *= gate[i];
+    }
+    wo_cq_gemm_lut(&L->out_proj, att, t, y);
+    free(q), free(k), free(v), free(gate), free(att);
+}
+
+/* block.go:224 conv: x += pw2(SiLU(conv_out_norm(depthwise(glu(pw1(
+ * conv_norm(x))))))) (NormBeforeAct). */
+static void enc_conv(const wo_encoder *e, const wo_enc_layer *EL, float *x, int t) {
+    int c = e->d.dim;
+    float *n = malloc((size_t)t * c * sizeof(float)), *p = malloc((size_t)t * 2 * c * sizeof(float));
+    float *g = malloc((size_t)t * c * sizeof(float)), *dw = malloc((size_t)t * c * sizeof(float));
+    zc_norm(n, x, t, c, EL->conv_norm);
+    wo_cq_gemm_lut(&EL->pw1, n, t, p);
+    wo_enc_glu(p, t, c, g);
+    wo_enc_depthwise(g, t, c, EL->dw, e->dw_k, dw);
+    zc_norm(dw, dw, t, c, EL->conv_out_norm);
+    wo_silu(dw, t * c);
+    wo_cq_gemm_lut(&EL->pw2, dw, t, n);
+    for (size_t i = 0; i < (size_t)t * c; i++) x[i] += n[i];
+    free(n), free(p), free(g), free(dw);
+}
+
+/* mhc.go:182 MHC.forward of encoder layer l around block.go:148 forward
+ * (FFN1, attention, conv module, FFN2: OrderMacaron) on t rows. */
+static void enc_layer(const wo_encoder *e, int l, float *stream, int t, int form) {
+    const wo_decoder *d = &e->d;
+    const wo_enc_layer *EL = &e->layer[l];
+    const wo_dec_layer *L = &EL->b;
+    int n = d->lanes, c = d->dim, nC = n * c;
+    float *nx = malloc((size_t)t * nC * sizeof(float));
+    rms_unit(nx, stream, t, nC);
+    fake_quant(nx, nx, t * nC, nC); /* linear.go:108 ApplyShared's quantised copy */
+    float *pre = malloc((size_t)t * n * sizeof(float)), *post = malloc((size_t)t * n * sizeof(float));
+    float *res = malloc((size_t)t * n * n * sizeof(float));
+    wo_packed ms[3] = {L->phi_pre, L->phi_post, L->phi_res};
+    float *ys[3] = {pre, post, res};
+    wo_cq_gemms_lut(ms, 3, nx, t, ys);
+    float *u = calloc((size_t)t * c, sizeof(float));
+    for (int i = 0; i < t; i++) { /* mhc.go:241 logits, :205-221 */
+        float *pr = pre + (size_t)i * n, *po = post + (size_t)i * n, *rs = res + (size_t)i * n * n;
+        for (int k = 0; k < n; k++) {
+            float tt = L->a_pre * pr[k];
+            pr[k] = tt + L->b_pre[k] + (k == l % n ? 4.0f : -4.0f);
+            float t2 = L->a_post * po[k];
+            po[k] = t2 + L->b_post[k] + (k == l % n ? 0.0f : -4.0f);
+        }
+        for (int k = 0; k < n * n; k++) {
+            float tt = L->a_res * rs[k];
+            rs[k] = tt + L->b_res[k];
+        }
+        for (int k = 0; k < n; k++) {
+            pr[k] = sigmoid(pr[k]);
+            axpy(u + (size_t)i * c, pr[k], stream + ((size_t)i * n + k) * c, c);
+            po[k] = 2.0f * sigmoid(po[k]);
+        }
+        sinkhorn(rs, n);
+    }
+    /* block.go:148 forward */
+    float *xb = malloc((size_t)t * c * sizeof(float)), *nrm = malloc((size_t)t * c * sizeof(float));
+    float *a = malloc((size_t)t * c * sizeof(float));
+    memcpy(xb, u, (size_t)t * c * sizeof(float));
+    enc_ffn(d, &EL->hada0, EL->hada0.pre_hada, xb, t);
+    zc_norm(nrm, xb, t, c, L->norm_in); /* block.go:193 attend */
+    enc_attention(e, L, nrm, t, form, a);
+    zc_norm(a, a, t, c, L->post_norm);
+    float g = sigmoid(L->attn_gate); /* block.go:91 */
+    for (size_t i = 0; i < (size_t)t * c; i++) {
+        float tt = g * a[i];
+        xb[i] += tt;
+    }
+    enc_conv(e, EL, xb, t);
+    enc_ffn(d, L, L->pre_hada, xb, t);
+    /* mhc.go:229 y = block(u) − u; :270 mix */
+    float *out = calloc((size_t)t * nC, sizeof(float));
+    for (int i = 0; i < t; i++) {
+        float *y = xb + (size_t)i * c;
+        const float *ui = u + (size_t)i * c, *st = stream + (size_t)i * nC, *rs = res + (size_t)i * n * n;
+        for (int k = 0; k < c; k++) y[k] = y[k] - ui[k];
+        for (int aa = 0; aa < n; aa++) {
+            float *o = out + (size_t)i * nC + (size_t)aa * c;
+            for (int b = 0; b < n; b++) axpy(o, rs[aa * n + b], st + (size_t)b * c, c);
+            float hp = post[(size_t)i * n + aa];
+            for (int k = 0; k < c; k++) {
+                float tt = hp * y[k];
+                o[k] += tt;
+            }
+        }
+    }
+    memcpy(stream, out, (size_t)t * nC * sizeof(float));
+    free(nx), free(pre), free(post), free(res), free(u), free(xb), free(nrm), free(a), free(out);
+}
+
+/* encoder.go:167 Stack for one clip: mhc.go:131 ExpandLanes, the layers,
+ * mhc.go:140 CollapseLanes (Σ over the lanes, then ÷ lanes) and the final
+ * norm (OutFinalNorm). */
+static int enc_stack_clip(const wo_encoder *e, const float *x, int t, int form, float *out) {
+    const wo_decoder *d = &e->d;
+    if (t > d->rope_len) return -1;
+    int n = d->lanes, c = d->dim, nC = n * c;
+    float *stream = malloc((size_t)t * nC * sizeof(float)), *m = calloc((size_t)t * c, sizeof(float));
+    for (int i = 0; i < t; i++)
+        for (int k = 0; k < n; k++) memcpy(stream + (size_t)i * nC + (size_t)k * c, x + (size_t)i * c, c * sizeof(float));
+    for (int l = 0; l < d->layers; l++) enc_layer(e, l, stream, t, form);
+    for (int i = 0; i < t; i++) {
+        float *o = m + (size_t)i * c;
+        for (int k = 0; k < n; k++)
+            for (int j = 0; j < c; j++) o[j] += stream[(size_t)i * nC + (size_t)k * c + j];
+        for (int j = 0; j < c; j++) o[j] /= (float)n;
+    }
+    zc_norm(out, m, t, c, d->final_norm);
+    free(stream), free(m);
+    return 0;
+}
+
+int wo_enc_stack(const wo_encoder *e, const float *x, int clips, int t, int form, float *out) {
+    size_t per = (size_t)t * e->d.dim;
+    for (int b = 0; b < clips; b++)
+        if (enc_stack_clip(e, x + b * per, t, form, out + b * per) != 0) return -1;
+    return 0;
+}
+
+typedef struct {
+    const wo_encoder *e;
+    const float *x;
+    float *out;
+    int t, form;
+    atomic_int bad;
+} enc_job;
+
+static void enc_task(int b, void *arg) {
+    enc_job *j = arg;
+    size_t per = (size_t)j->t * j->e->d.dim;
+    if (enc_stack_clip(j->e, j->x + b * per, j->t, j->form, j->out + b * per) != 0) atomic_store(&j->bad, 1);
+}
+
+int wo_enc_stack_mt(const wo_encoder *e, const float *x, int clips, int t, int form, float *out, int threads) {
+    enc_job job = {e, x, out, t, form, 0};
+    wo_parallel_for(clips, threads < 1 ? 1 : threads, enc_task, &job);
+    return atomic_load(&job.bad) ? -1 : 0;
+}
