@@ -94,6 +94,10 @@ _SIGS = {
     "wc_encoder_create": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, ctypes.POINTER(_c_void_p)]),
     "wc_encoder_destroy": (None, [_c_void_p]),
     "wc_encoder_stack": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
+    "wc_encoder_logmel": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
+    "wc_encoder_stem_frames": (_c_int, [_c_int]),
+    "wc_encoder_stem": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
+    "wc_encoder_embed": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p]),
 }
 
 _lib = None

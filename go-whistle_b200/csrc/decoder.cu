@@ -2216,6 +2216,144 @@ __global__ void __launch_bounds__(kThreads)
     for (int a = 0; a < kLanes; a++) stream[((size_t)r * kLanes + a) * kD + c] = out[a];
 }
 
+
+// ---- the log-mel front end (frontend/stft.go, mel.go) and the conv stem
+// (encoder/stem.go), Best() hypothesis.
+constexpr int kNFFT = 512, kHop = 160, kBins = kNFFT / 2 + 1, kMels = 80;
+constexpr int kWinLo = (kNFFT - 400) / 2, kWinHi = kWinLo + 400;  // the 400-sample window's place in the frame
+
+// stft.go:113 spectrum for one frame: the frame centred on sample f·160
+// (zeros outside the clip), times the window, then |X_k|² for the 257
+// bins as a float64 DFT of the float32 products, rounded to float32.
+__global__ void __launch_bounds__(288)
+    logmel_spec_kernel(const float *__restrict__ samples, int n, int frames, const float *__restrict__ win,
+                       const double *__restrict__ twc, const double *__restrict__ tws, float *__restrict__ spec) {
+    __shared__ float xw[kNFFT];
+    __shared__ double cs[kNFFT], sn[kNFFT];
+    const int f = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
+    for (int j = t; j < kNFFT; j += blockDim.x) {
+        const long long smp = (long long)f * kHop - kNFFT / 2 + j;
+        const float v = smp >= 0 && smp < n ? samples[(size_t)b * n + smp] : 0.0f;
+        xw[j] = v * win[j];
+        cs[j] = twc[j];
+        sn[j] = tws[j];
+    }
+    __syncthreads();
+    if (t < kBins) {
+        double re = 0.0, im = 0.0;
+        for (int j = kWinLo; j < kWinHi; j++) {
+            const int m = (t * j) & (kNFFT - 1);
+            const double x = (double)xw[j];
+            re = re + x * cs[m];
+            im = im - x * sn[m];
+        }
+        spec[((size_t)b * frames + f) * kBins + t] = (float)(re * re + im * im);
+    }
+}
+
+// mel.go:78 MelBank.apply: channel m's float64 sum over its non-zero bins.
+__global__ void logmel_mel_kernel(const float *__restrict__ spec, int frames, const float *__restrict__ bank,
+                                  const int *__restrict__ lo, const int *__restrict__ hi, double *__restrict__ mel) {
+    const int f = blockIdx.x, b = blockIdx.y, m = threadIdx.x;
+    if (m >= kMels) return;
+    const float *row = spec + ((size_t)b * frames + f) * kBins;
+    double sum = 0.0;
+    for (int k = lo[m]; k < hi[m]; k++) sum = sum + (double)row[k] * (double)bank[k * kMels + m];
+    mel[((size_t)b * frames + f) * kMels + m] = sum;
+}
+
+// mel.go:302 softLog (ε = knee·max over the clip, log10 as Go's math.Log10:
+// ln(x)·(1/ln 10)) and :320 normalise, NormChannel (mean and n − 1
+// deviation per channel over time, sums in frame order): one CTA per clip,
+// a thread per channel.
+__global__ void __launch_bounds__(128) logmel_norm_kernel(double *__restrict__ mel, int frames, double knee,
+                                                          float *__restrict__ out) {
+    __shared__ double red[128];
+    const int b = blockIdx.x, m = threadIdx.x;
+    double *base = mel + (size_t)b * frames * kMels;
+    double mx = -INFINITY;
+    if (m < kMels)
+        for (int f = 0; f < frames; f++) mx = fmax(mx, base[(size_t)f * kMels + m]);
+    red[m] = mx;
+    __syncthreads();
+    if (m == 0) {
+        double t = -INFINITY;
+        for (int i = 0; i < kMels; i++) t = fmax(t, red[i]);
+        red[0] = t;
+    }
+    __syncthreads();
+    double eps = knee * red[0];
+    if (eps == 0.0) eps = 1e-10;
+    if (m >= kMels) return;
+    const double inv_ln10 = 1.0 / 2.30258509299404568401799145468436421;
+    double sum = 0.0;
+    for (int f = 0; f < frames; f++) {
+        const double v = log(base[(size_t)f * kMels + m] + eps) * inv_ln10;
+        base[(size_t)f * kMels + m] = v;
+        sum = sum + v;
+    }
+    const double mean = sum / (double)frames;
+    double dev = 0.0;
+    for (int f = 0; f < frames; f++) {
+        const double d = base[(size_t)f * kMels + m] - mean;
+        dev = dev + d * d;
+    }
+    const double sd = frames > 1 ? sqrt(dev / (double)(frames - 1)) : 0.0;
+    for (int f = 0; f < frames; f++)
+        out[((size_t)b * frames + f) * kMels + m] = (float)((base[(size_t)f * kMels + m] - mean) / (sd + 1e-5));
+}
+
+// stem.go:176 conv on one stage: a 3×3 stride-2 conv with one padding row
+// and column on each side (PadSymmetric), the taps in (time, mel) order
+// from 0, each product rounded before its add. Stage 0 reads one input
+// channel (stem.w, then SiLU, stem.go:367); the depthwise stages read
+// channel c for output channel c (groups = channels, no activation).
+// x [clips][h][w][cin], out [clips][h'][w'][channels]; a thread per
+// output value.
+__global__ void __launch_bounds__(256)
+    stem_conv_kernel(const float *__restrict__ x, int h, int w, int cin, const float *__restrict__ k, int channels,
+                     int ho, int wo, long long total, int silu, float *__restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const int c = (int)(i % channels);
+    const long long pix = i / channels;
+    const int ow = (int)(pix % wo);
+    const long long r = pix / wo;
+    const int oh = (int)(r % ho);
+    const long long b = r / ho;
+    const int ci = cin == 1 ? 0 : c;
+    float acc = 0.0f;
+    for (int kh = 0; kh < 3; kh++) {
+        const int ih = 2 * oh - 1 + kh;
+        if (ih < 0 || ih >= h) continue;
+        for (int kw = 0; kw < 3; kw++) {
+            const int iw = 2 * ow - 1 + kw;
+            if (iw < 0 || iw >= w) continue;
+            acc = acc + x[((b * h + ih) * w + iw) * cin + ci] * k[(kh * 3 + kw) * channels + c];
+        }
+    }
+    out[i] = silu ? acc * sigm(acc) : acc;
+}
+
+// stem.go:253 pointwise's activation (SiLU) in place, or with flatten set,
+// into stem.go:262 output's channel-major flatten: out[r][c·w + f] for
+// pixel (r, f) of w mel positions.
+__global__ void __launch_bounds__(256) stem_act_kernel(const float *__restrict__ y, long long total, int channels,
+                                                       int w, int flatten, float *__restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const float v = y[i];
+    const float a = v * sigm(v);
+    if (!flatten) {
+        out[i] = a;
+        return;
+    }
+    const int c = (int)(i % channels);
+    const long long pix = i / channels;
+    const int f = (int)(pix % w);
+    const long long r = pix / w;
+    out[r * (long long)(channels * w) + (long long)c * w + f] = a;
+}
 }  // namespace
 }  // namespace wb
 
@@ -2244,6 +2382,17 @@ struct wc_encoder : DevStore {
     int32_t *nk = nullptr;
     void *tcbuf = nullptr;
     size_t tcbytes = 0;
+    // The stem and the front end (when the desc has them).
+    bool has_stem = false;
+    int channels = 0;
+    const float *sw = nullptr, *sdw[2] = {nullptr, nullptr}, *win = nullptr, *bank = nullptr;
+    const double *twc = nullptr, *tws = nullptr;
+    const int *mlo = nullptr, *mhi = nullptr;
+    double knee = 0.0;
+    wc_cq *spw[2] = {nullptr, nullptr}, *sout = nullptr;
+    float *spec = nullptr, *melf = nullptr, *s0 = nullptr, *s1 = nullptr, *s2 = nullptr, *s3 = nullptr;
+    float *s4 = nullptr, *flat = nullptr, *xin = nullptr;
+    double *mel64 = nullptr;
 };
 
 namespace {
@@ -2432,6 +2581,85 @@ extern "C" wc_status wc_encoder_create(const wc_encoder_desc *desc, int max_clip
     DEC_ST(e->upload(&e->g_final, D.final_norm, kD, true));
     DEC_ST(e->rope_tables(D.rope_theta, D.rope_len, &e->rcos, &e->rsin));
     e->att_scale = (float)std::sqrt((double)kQK);  // attention.go:407 attendScale
+    const int Tm = max_frames;
+    const bool any_stem = D.stem_w || D.stem_dw_1 || D.stem_dw_2 || D.stem_pw_1 || D.stem_pw_2 || D.stem_out ||
+                          D.mel_filters;
+    if (any_stem) {
+        const int C = D.stem_channels;
+        if (!D.stem_w || !D.stem_dw_1 || !D.stem_dw_2 || !D.stem_pw_1 || !D.stem_pw_2 || !D.stem_out ||
+            !D.mel_filters || C <= 0 || C > 1024)
+            return set_error(WC_ERR_INVALID, fmt("encoder: stem of %d channels with a nil tensor", C));
+        const int wout = wc_encoder_stem_frames(kMels);  // 10 mel positions after three stages
+        auto stem_mat = [&](const wc_cq *m, const char *what, int out, int in) -> wc_status {
+            if (wc_cq_out(m) != out || wc_cq_in(m) != in)
+                return set_error(WC_ERR_INVALID, fmt("encoder: %s has shape (%d, %d), want (%d, %d)", what,
+                                                     wc_cq_out(m), wc_cq_in(m), out, in));
+            return WC_OK;
+        };
+        DEC_ST(stem_mat(D.stem_pw_1, "stem.pw_1", C, C));
+        DEC_ST(stem_mat(D.stem_pw_2, "stem.pw_2", C, C));
+        DEC_ST(stem_mat(D.stem_out, "stem.out", kD, wout * C));
+        e->has_stem = true;
+        e->channels = C;
+        DEC_ST(e->upload(&e->sw, D.stem_w, (size_t)9 * C));
+        DEC_ST(e->upload(&e->sdw[0], D.stem_dw_1, (size_t)9 * C));
+        DEC_ST(e->upload(&e->sdw[1], D.stem_dw_2, (size_t)9 * C));
+        DEC_ST(e->view(D.stem_pw_1, &e->spw[0]));
+        DEC_ST(e->view(D.stem_pw_2, &e->spw[1]));
+        DEC_ST(e->view(D.stem_out, &e->sout));
+        DEC_ST(e->upload(&e->bank, D.mel_filters, (size_t)kBins * kMels));
+        {
+            // mel.go:30 MelBank's non-zero bin range of every channel.
+            std::vector<int32_t> lh(2 * kMels, 0);
+            for (int m = 0; m < kMels; m++) {
+                int lo = -1, hi = -1;
+                for (int k = 0; k < kBins; k++)
+                    if (D.mel_filters[k * kMels + m] != 0.0f) {
+                        if (lo < 0) lo = k;
+                        hi = k + 1;
+                    }
+                lh[m] = lo < 0 ? 0 : lo;
+                lh[kMels + m] = lo < 0 ? 0 : hi;
+            }
+            int32_t *d = nullptr;
+            DEC_ST(e->alloc(&d, lh.size()));
+            WB_CUDA(cudaMemcpy(d, lh.data(), lh.size() * sizeof(int32_t), cudaMemcpyHostToDevice));
+            e->mlo = d;
+            e->mhi = d + kMels;
+        }
+        {
+            // stft.go:60: the 400-sample symmetric Hann window at offset 56
+            // of the 512-point frame, and the DFT's twiddles.
+            const double pi = 3.14159265358979323846;
+            std::vector<float> w(kNFFT, 0.0f);
+            for (int k = 0; k < 400; k++) w[kWinLo + k] = (float)(0.5 - 0.5 * std::cos(2.0 * pi * k / 399.0));
+            DEC_ST(e->upload(&e->win, w.data(), w.size()));
+            std::vector<double> c(kNFFT), sn(kNFFT);
+            for (int m = 0; m < kNFFT; m++) {
+                c[m] = std::cos(2.0 * pi * m / kNFFT);
+                sn[m] = std::sin(2.0 * pi * m / kNFFT);
+            }
+            double *dc = nullptr, *ds = nullptr;
+            DEC_ST(e->alloc(&dc, kNFFT));
+            DEC_ST(e->alloc(&ds, kNFFT));
+            WB_CUDA(cudaMemcpy(dc, c.data(), kNFFT * sizeof(double), cudaMemcpyHostToDevice));
+            WB_CUDA(cudaMemcpy(ds, sn.data(), kNFFT * sizeof(double), cudaMemcpyHostToDevice));
+            e->twc = dc;
+            e->tws = ds;
+        }
+        e->knee = std::pow(10.0, -7.6);  // mel.go:24 soft76
+        const size_t B = (size_t)max_clips, F = (size_t)8 * Tm;
+        DEC_ST(e->alloc(&e->spec, B * F * kBins));
+        DEC_ST(e->alloc(&e->mel64, B * F * kMels));
+        DEC_ST(e->alloc(&e->melf, B * F * kMels));
+        DEC_ST(e->alloc(&e->s0, B * 4 * Tm * 40 * C));
+        DEC_ST(e->alloc(&e->s1, B * 2 * Tm * 20 * C));
+        DEC_ST(e->alloc(&e->s2, B * 2 * Tm * 20 * C));
+        DEC_ST(e->alloc(&e->s3, B * Tm * wout * C));
+        DEC_ST(e->alloc(&e->s4, B * Tm * wout * C));
+        DEC_ST(e->alloc(&e->flat, B * Tm * wout * C));
+        DEC_ST(e->alloc(&e->xin, B * Tm * kD));
+    }
 
     const size_t R = (size_t)max_clips * max_frames;
     DEC_ST(e->alloc(&e->stream, R * kLanes * kD));
@@ -2461,8 +2689,14 @@ extern "C" wc_status wc_encoder_create(const wc_encoder_desc *desc, int max_clip
     DEC_ST(e->alloc(&e->nk, R));
     if (e->tc) {
         // The rotated image of the tensor-core products: R rows at 512 in,
-        // and at 2048 in for the φ products.
+        // and at 2048 in for the φ products; the stem's pointwise rows at
+        // its channel count and stem.out's rows at 10 · channels.
         e->tcbytes = std::max(tc_a_bytes((int)R, (kD + 63) / 64), tc_a_bytes((int)R, (kLanes * kD + 63) / 64));
+        if (e->has_stem) {
+            const int C = e->channels;
+            e->tcbytes = std::max(e->tcbytes, tc_a_bytes((int)(max_clips * 2LL * Tm * 20), (C + 63) / 64));
+            e->tcbytes = std::max(e->tcbytes, tc_a_bytes((int)R, (10 * C + 63) / 64));
+        }
         unsigned char *pb = nullptr;
         DEC_ST(e->alloc(&pb, e->tcbytes));
         e->tcbuf = pb;
@@ -2494,4 +2728,81 @@ extern "C" wc_status wc_encoder_stack(wc_encoder *e, const float *x, int clips, 
     for (int l = 0; l < e->d.layers; l++) DEC_ST(enc_layer(e, l, R, frames, st));
     DEC_LAUNCH(final_kernel<<<R, kThreads, 0, st>>>(e->stream, e->g_final, out));
     return WC_OK;
+}
+
+extern "C" int wc_encoder_stem_frames(int frames) {
+    int n = frames;
+    for (int st = 0; st < 3; st++) {
+        if (n + 2 < 3) return 0;
+        n = (n + 2 - 3) / 2 + 1;  // stem.go:166 length: 3 taps, stride 2, one padding position each side
+    }
+    return n;
+}
+
+static wc_status enc_stem_ready(wc_encoder *e) {
+    if (!e) return set_error(WC_ERR_INVALID, "encoder: nil encoder");
+    int cur = 0;
+    WB_CUDA(cudaGetDevice(&cur));
+    if (cur != e->device)
+        return set_error(WC_ERR_INVALID, fmt("encoder: built on device %d, called on device %d", e->device, cur));
+    if (!e->has_stem) return set_error(WC_ERR_INVALID, "encoder: built without the stem and the mel bank");
+    return WC_OK;
+}
+
+static int blocks_of(long long total, int threads) { return (int)((total + threads - 1) / threads); }
+
+extern "C" wc_status wc_encoder_logmel(wc_encoder *e, const float *samples, int clips, int n, float *mel,
+                                       wc_stream stream) {
+    DEC_ST(enc_stem_ready(e));
+    if (clips < 0 || n < 0 || clips > e->max_clips || n / kHop > 8 * e->max_frames)
+        return set_error(WC_ERR_INVALID, fmt("encoder: %d clips of %d samples exceed the room for %d of %d", clips, n,
+                                             e->max_clips, 8 * e->max_frames * kHop + kHop - 1));
+    const int F = n / kHop;  // stft.go:35 FrameCount, centred framing
+    if (clips == 0 || F == 0) return WC_OK;
+    if (!samples || !mel) return set_error(WC_ERR_INVALID, "encoder: nil samples or mel");
+    cudaStream_t st = (cudaStream_t)stream;
+    DEC_LAUNCH(logmel_spec_kernel<<<dim3(F, clips), 288, 0, st>>>(samples, n, F, e->win, e->twc, e->tws, e->spec));
+    DEC_LAUNCH(logmel_mel_kernel<<<dim3(F, clips), 96, 0, st>>>(e->spec, F, e->bank, e->mlo, e->mhi, e->mel64));
+    DEC_LAUNCH(logmel_norm_kernel<<<clips, 128, 0, st>>>(e->mel64, F, e->knee, mel));
+    return WC_OK;
+}
+
+extern "C" wc_status wc_encoder_stem(wc_encoder *e, const float *mel, int clips, int frames, float *x,
+                                     wc_stream stream) {
+    DEC_ST(enc_stem_ready(e));
+    const int T = wc_encoder_stem_frames(frames);
+    if (clips < 0 || frames < 0 || clips > e->max_clips || T > e->max_frames)
+        return set_error(WC_ERR_INVALID, fmt("encoder: %d clips of %d mel frames (%d stem frames) exceed the room for "
+                                             "%d of %d", clips, frames, T, e->max_clips, e->max_frames));
+    if (clips == 0 || T == 0) return WC_OK;
+    if (!mel || !x) return set_error(WC_ERR_INVALID, "encoder: nil mel or output");
+    cudaStream_t st = (cudaStream_t)stream;
+    const int C = e->channels;
+    const int h1 = (frames - 1) / 2 + 1, w1 = (kMels - 1) / 2 + 1;
+    const int h2 = (h1 - 1) / 2 + 1, w2 = (w1 - 1) / 2 + 1;
+    const int w3 = (w2 - 1) / 2 + 1;
+    long long tot = (long long)clips * h1 * w1 * C;
+    DEC_LAUNCH(stem_conv_kernel<<<blocks_of(tot, 256), 256, 0, st>>>(mel, frames, kMels, 1, e->sw, C, h1, w1, tot, 1,
+                                                                     e->s0));
+    tot = (long long)clips * h2 * w2 * C;
+    DEC_LAUNCH(stem_conv_kernel<<<blocks_of(tot, 256), 256, 0, st>>>(e->s0, h1, w1, C, e->sdw[0], C, h2, w2, tot, 0,
+                                                                     e->s1));
+    DEC_ST(enc_gemms(e, {e->spw[0]}, e->s1, {e->s2}, clips * h2 * w2, st));
+    DEC_LAUNCH(stem_act_kernel<<<blocks_of(tot, 256), 256, 0, st>>>(e->s2, tot, C, w2, 0, e->s2));
+    tot = (long long)clips * T * w3 * C;
+    DEC_LAUNCH(stem_conv_kernel<<<blocks_of(tot, 256), 256, 0, st>>>(e->s2, h2, w2, C, e->sdw[1], C, T, w3, tot, 0,
+                                                                     e->s3));
+    DEC_ST(enc_gemms(e, {e->spw[1]}, e->s3, {e->s4}, clips * T * w3, st));
+    DEC_LAUNCH(stem_act_kernel<<<blocks_of(tot, 256), 256, 0, st>>>(e->s4, tot, C, w3, 1, e->flat));
+    DEC_ST(enc_gemms(e, {e->sout}, e->flat, {x}, clips * T, st));
+    return WC_OK;
+}
+
+extern "C" wc_status wc_encoder_embed(wc_encoder *e, const float *samples, int clips, int n, float *out,
+                                      wc_stream stream) {
+    DEC_ST(enc_stem_ready(e));
+    const int F = n < 0 ? 0 : n / kHop, T = wc_encoder_stem_frames(F);
+    DEC_ST(wc_encoder_logmel(e, samples, clips, n, e->melf, stream));
+    DEC_ST(wc_encoder_stem(e, e->melf, clips, F, e->xin, stream));
+    return wc_encoder_stack(e, e->xin, clips, T, out, stream);
 }

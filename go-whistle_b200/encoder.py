@@ -42,7 +42,9 @@ class _Desc(ctypes.Structure):
     _fields_ = ([(k, ctypes.c_int) for k in ("dim", "lanes", "layers", "heads", "kv_heads", "qk", "vd", "dw_kernel",
                                              "na", "nb", "rank")]
                 + [("hada_p1", _p), ("hada_p2", _p), ("rope_theta", ctypes.c_double), ("rope_len", ctypes.c_int),
-                   ("final_norm", _p), ("layer", ctypes.POINTER(_Layer))])
+                   ("final_norm", _p), ("layer", ctypes.POINTER(_Layer))]
+                + [(k, _p) for k in ("stem_w", "stem_dw_1", "stem_dw_2", "stem_pw_1", "stem_pw_2", "stem_out")]
+                + [("stem_channels", ctypes.c_int), ("mel_filters", _p)])
 
 
 class Encoder:
@@ -110,6 +112,11 @@ class Encoder:
         desc.rope_theta, desc.rope_len = float(w.rope_theta), int(w.rope_len)
         desc.final_norm = f(w.final_norm)
         desc.layer = L
+        if getattr(w, "stem_w", None) is not None:
+            desc.stem_w, desc.stem_dw_1, desc.stem_dw_2 = f(w.stem_w), f(w.stem_dw_1), f(w.stem_dw_2)
+            desc.stem_pw_1, desc.stem_pw_2, desc.stem_out = m(w.stem_pw_1), m(w.stem_pw_2), m(w.stem_out)
+            desc.stem_channels = int(w.stem_channels)
+            desc.mel_filters = f(w.mel_filters)
         h = ctypes.c_void_p()
         check(lib().wc_encoder_create(ctypes.byref(desc), max_clips, max_frames, flags, ctypes.byref(h)))
         self.handle = h
@@ -132,5 +139,51 @@ class Encoder:
             out = torch.empty_like(x)
         st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
         check(lib().wc_encoder_stack(self.handle, ctypes.c_void_p(x3.data_ptr()), x3.shape[0], x3.shape[1],
+                                     ctypes.c_void_p(out.data_ptr()), st))
+        return out
+
+    @staticmethod
+    def stem_frames(frames: int) -> int:
+        """stem.go:166 length: the stem's output frames for `frames` mel frames."""
+        return lib().wc_encoder_stem_frames(int(frames))
+
+    def LogMel(self, samples, out=None):
+        """frontend/mel.go:226 LogMel on a CUDA tensor samples [clips][n] (16 kHz):
+        [clips][n // 160][80] float32."""
+        import torch
+
+        s2 = samples.contiguous().reshape(-1, samples.shape[-1])
+        F = s2.shape[1] // 160
+        if out is None:
+            out = torch.empty(s2.shape[0], F, 80, device=samples.device, dtype=torch.float32)
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        check(lib().wc_encoder_logmel(self.handle, ctypes.c_void_p(s2.data_ptr()), s2.shape[0], s2.shape[1],
+                                      ctypes.c_void_p(out.data_ptr()), st))
+        return out
+
+    def Stem(self, mel, out=None):
+        """encoder.go:132 Stem on a CUDA tensor mel [clips][frames][80]:
+        [clips][stem_frames(frames)][dim]."""
+        import torch
+
+        m3 = mel.contiguous().reshape(-1, mel.shape[-2], mel.shape[-1])
+        T = self.stem_frames(m3.shape[1])
+        if out is None:
+            out = torch.empty(m3.shape[0], T, self.w.dim, device=mel.device, dtype=torch.float32)
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        check(lib().wc_encoder_stem(self.handle, ctypes.c_void_p(m3.data_ptr()), m3.shape[0], m3.shape[1],
+                                    ctypes.c_void_p(out.data_ptr()), st))
+        return out
+
+    def Embed(self, samples, out=None):
+        """encoder.go:108 Embed: LogMel, Stem and Stack on samples [clips][n]."""
+        import torch
+
+        s2 = samples.contiguous().reshape(-1, samples.shape[-1])
+        T = self.stem_frames(s2.shape[1] // 160)
+        if out is None:
+            out = torch.empty(s2.shape[0], T, self.w.dim, device=samples.device, dtype=torch.float32)
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        check(lib().wc_encoder_embed(self.handle, ctypes.c_void_p(s2.data_ptr()), s2.shape[0], s2.shape[1],
                                      ctypes.c_void_p(out.data_ptr()), st))
         return out

@@ -257,12 +257,57 @@ class EncoderWeights:
             L["b_pre"], L["b_post"] = vec(n, 0.0, 0.1), vec(n, 0.0, 0.1)
             L["b_res"] = (2.0 * np.eye(n) + rng.normal(0.0, 0.1, size=(n, n))).astype(np.float32).reshape(-1)
             self.layers.append(L)
+        # The conv stem (stem.*: 3x3 kernels as (9, C), taps time-major;
+        # CQ2 pointwise and output products) and the front end's mel bank.
+        C = self.stem_channels = 128
+        self.stem_w = rng.normal(0.0, 0.4, size=(9, C)).astype(np.float32)
+        self.stem_dw_1 = rng.normal(0.0, 0.4, size=(9, C)).astype(np.float32)
+        self.stem_dw_2 = rng.normal(0.0, 0.4, size=(9, C)).astype(np.float32)
+        self.stem_pw_1 = _cq_tensor(rng, C, C, 2, G, self.cb2, rms=0.08)
+        self.stem_pw_2 = _cq_tensor(rng, C, C, 2, G, self.cb2, rms=0.08)
+        self.stem_out = _cq_tensor(rng, D, 10 * C, 2, G, self.cb2, rms=0.05)
+        self.mel_filters = triangular_mel_bank()
 
     def phi_rows(self, name: str, l: int):
         """Layer l's row range of a stacked φ (mhc.go:94-96)."""
         n = self.lanes
         per = n * n if name == "phi_res" else n
         return l * per, (l + 1) * per
+
+
+def triangular_mel_bank(bins: int = 257, mels: int = 80, rate: float = 16000.0) -> np.ndarray:
+    """A synthetic (bins, mels) filterbank standing in for the exported
+    audio.mel_filters: triangles evenly spaced on the HTK mel scale over
+    0 .. rate/2, each channel's non-zero bins contiguous."""
+    def mel(f):
+        return 2595.0 * np.log10(1.0 + f / 700.0)
+
+    def hz(m):
+        return 700.0 * (10.0 ** (m / 2595.0) - 1.0)
+
+    edges = hz(np.linspace(0.0, mel(rate / 2), mels + 2))
+    f = np.arange(bins) * rate / (2 * (bins - 1))
+    w = np.zeros((bins, mels), np.float32)
+    for m in range(mels):
+        lo, c, hi = edges[m], edges[m + 1], edges[m + 2]
+        up = (f - lo) / (c - lo)
+        down = (hi - f) / (hi - c)
+        w[:, m] = np.maximum(0.0, np.minimum(up, down)) * (2.0 / (hi - lo))
+    return w
+
+
+def audio(rng: np.random.Generator, clips: int, samples: int) -> np.ndarray:
+    """Synthetic 16 kHz clips [clips][samples]: a few tones with slow
+    amplitude changes over noise, peak about 0.5."""
+    t = np.arange(samples) / 16000.0
+    out = np.zeros((clips, samples), np.float32)
+    for c in range(clips):
+        x = 0.02 * rng.normal(size=samples)
+        for _ in range(4):
+            f0, a = rng.uniform(80, 4000), rng.uniform(0.05, 0.15)
+            x += a * np.sin(2 * np.pi * f0 * t + rng.uniform(0, 6.28)) * (1 + 0.5 * np.sin(2 * np.pi * 0.7 * t))
+        out[c] = x.astype(np.float32)
+    return out
 
 
 def stem_output(rng: np.random.Generator, clips: int, frames: int = 375, dim: int = 512) -> np.ndarray:

@@ -543,6 +543,15 @@ typedef struct wc_encoder_desc {
     int rope_len;
     const float *final_norm;        /* [dim] */
     const wc_encoder_layer *layer;  /* [layers] */
+    /* The conv stem (stem.go:20) and the front end's mel bank, or all NULL
+     * for the stack alone: 3×3 kernels as stored, (9, channels) with the
+     * taps time-major; pointwise products [channels][channels]; stem.out
+     * [dim][10·channels] over the channel-major flatten; mel_filters
+     * [257][80] (frontend/mel.go:30 MelBank). */
+    const float *stem_w, *stem_dw_1, *stem_dw_2;
+    const wc_cq *stem_pw_1, *stem_pw_2, *stem_out;
+    int stem_channels;
+    const float *mel_filters;
 } wc_encoder_desc;
 
 typedef struct wc_encoder wc_encoder;
@@ -574,6 +583,33 @@ void wc_encoder_destroy(wc_encoder *e);
  * only; RoPE positions count from 0 in every clip.
  */
 wc_status wc_encoder_stack(wc_encoder *e, const float *x, int clips, int frames, float *out, wc_stream stream);
+
+/*
+ * frontend/mel.go:226 LogMel with the Best() front end (hypothesis.go:288:
+ * a 400-sample symmetric Hann window centred in a 512-point frame every 160
+ * samples, zero padding, the power spectrum, the float64 mel sums, the soft
+ * log knee 76 dB below the clip's peak, each channel standardised over
+ * time): samples DEVICE [clips][n] at 16 kHz, mel DEVICE [clips][n/160][80].
+ * The spectrum is a float64 DFT of the float32 windowed frame (the
+ * reference's is algo-dsp's float32 FFT). Needs the desc's mel_filters.
+ */
+wc_status wc_encoder_logmel(wc_encoder *e, const float *samples, int clips, int n, float *mel, wc_stream stream);
+
+/* The stem's output length for `frames` mel frames (stem.go:166 length):
+ * three stride-2 stages of symmetric padding. */
+int wc_encoder_stem_frames(int frames);
+
+/*
+ * encoder.go:132 Stem with Best(): mel DEVICE [clips][frames][80] to x
+ * DEVICE [clips][wc_encoder_stem_frames(frames)][dim]. Each 3×3 tap sum
+ * runs in tap order (time, then mel); the products are the encoder's (lut
+ * or tensor cores). Needs the desc's stem tensors.
+ */
+wc_status wc_encoder_stem(wc_encoder *e, const float *mel, int clips, int frames, float *x, wc_stream stream);
+
+/* encoder.go:108 Embed: LogMel, Stem and Stack on samples DEVICE
+ * [clips][n]; out DEVICE [clips][wc_encoder_stem_frames(n/160)][dim]. */
+wc_status wc_encoder_embed(wc_encoder *e, const float *samples, int clips, int n, float *out, wc_stream stream);
 
 #ifdef __cplusplus
 }

@@ -118,3 +118,76 @@ def test_errors(wb, cuda, setup):
     w3.rope_len = 8
     with pytest.raises(wb.Panic, match="RoPE tables for 8 positions, want 16"):
         E(w3, max_clips=1, max_frames=16).Stack(dx[:1])
+
+
+# ------------------------------------------------------------ front end, stem
+# frontend/mel.go:226 LogMel and encoder/stem.go:198 against the CPU
+# restatement (oracle/frontend.py). LogMel: the device and the restatement
+# both take a float64 DFT and float64 mel sums, in different orders; the
+# float32 results agree to LOGMEL_ATOL (values are standardised, |x| < 10).
+# Stem: the same float32 operations in the same order and the lut products;
+# float64 exp in the SiLU may round the last bit differently.
+LOGMEL_ATOL = 1e-5
+
+
+def test_logmel_matches_oracle(wb, cuda, setup):
+    from oracle import frontend as fe
+
+    w, _ = setup
+    a = wb.synth.audio(np.random.default_rng(31), 2, 48000 + 77)
+    enc = wb.encoder.Encoder(w, max_clips=2, max_frames=40)
+    got = enc.LogMel(cuda.from_numpy(a).cuda()).cpu().numpy()
+    for c in range(2):
+        want = fe.logmel(a[c], w.mel_filters)
+        assert got[c].shape == want.shape == (300, 80)
+        assert np.abs(got[c] - want).max() <= LOGMEL_ATOL, np.abs(got[c] - want).max()
+
+
+@pytest.mark.parametrize("flags", [0, 1], ids=["lut", "tensor-cores"])
+def test_stem_matches_oracle(wb, orc, cuda, setup, flags):
+    from oracle import frontend as fe
+
+    w, _ = setup
+    a = wb.synth.audio(np.random.default_rng(32), 2, 40000)
+    mel = np.stack([fe.logmel(x, w.mel_filters) for x in a])  # 250 frames -> 32 stem frames
+    enc = wb.encoder.Encoder(w, max_clips=2, max_frames=32, flags=flags)
+    got = enc.Stem(cuda.from_numpy(mel).cuda()).cpu().numpy()
+    assert got.shape == (2, 32, 512)
+    for c in range(2):
+        want = fe.stem(mel[c], w, orc)
+        if flags == 0:
+            assert np.mean(got[c] == want) >= 0.99
+            assert np.abs(got[c] - want).max() <= 1e-5 * np.abs(want).max()
+        else:
+            cos = (got[c] * want).sum(-1) / np.linalg.norm(got[c], axis=-1) / np.linalg.norm(want, axis=-1)
+            assert cos.min() >= TC_COS, cos.min()
+
+
+@pytest.mark.parametrize("flags", [0, 3], ids=["exact", "tensor-cores"])
+def test_embed_matches_oracle(wb, orc, cuda, setup, flags):
+    """encoder.go:108 Embed: LogMel, Stem and Stack on the device against
+    the restatement's (the reference's float attention form)."""
+    from oracle import frontend as fe
+
+    w, oe = setup
+    a = wb.synth.audio(np.random.default_rng(33), 2, 64000)  # 400 mel frames -> 50 stem frames
+    enc = wb.encoder.Encoder(w, max_clips=2, max_frames=50, flags=flags)
+    got = enc.Embed(cuda.from_numpy(a).cuda()).cpu().numpy()
+    assert got.shape == (2, 50, 512)
+    want = np.stack([oe.stack(fe.stem(fe.logmel(x, w.mel_filters), w, orc), orc.ENC_ATTEND_FLOAT) for x in a])
+    cos, rel, _ = _cmp(got, want)
+    bound = (FORM_COS, FORM_ATOL) if flags == 0 else (TC_COS, TC_ATOL)
+    assert cos >= bound[0] and rel <= bound[1], (cos, rel)
+
+
+def test_stem_errors(wb, cuda, setup):
+    w0 = wb.synth.EncoderWeights(seed=5203, layers=1)
+    w0.stem_w = None
+    bare = wb.encoder.Encoder(w0, max_clips=1, max_frames=8)
+    x = cuda.zeros(1, 1600, device="cuda")
+    with pytest.raises(wb.Panic, match="built without the stem"):
+        bare.LogMel(x)
+    w, _ = setup
+    enc = wb.encoder.Encoder(w, max_clips=1, max_frames=8)
+    with pytest.raises(wb.Panic, match="exceed the room"):
+        enc.Embed(cuda.zeros(1, 160 * 65, device="cuda"))  # 65 mel frames -> 9 stem frames > 8

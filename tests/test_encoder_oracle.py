@@ -74,3 +74,56 @@ def test_rope_tables_bound_frames(wb, orc):
     oe = orc.OracleEncoder(w)
     with pytest.raises(ValueError, match="exceed the RoPE tables"):
         oe.stack(wb.synth.stem_output(np.random.default_rng(0), 1, 17))
+
+
+# ------------------------------------------------------------ front end, stem
+
+def test_stem_frames_known_answers(wb, orc):
+    """encoder_test.go:64 TestStemFrames (Best: stride 2 everywhere,
+    symmetric padding) and the engine's ceil(floor(n/160)/8) rule on its
+    measured lengths; the library's wc_encoder_stem_frames gives the same."""
+    from oracle import frontend as fe
+
+    assert fe.stem_frames(3000) == 375 and fe.stem_frames(80) == 10
+    for n, want in {1280: 1, 1281: 1, 2560: 2, 16000: 13, 53040: 42, 160000: 125, 480000: 375}.items():
+        assert fe.stem_frames(n // 160) == want, n
+        assert wb.encoder.Encoder.stem_frames(n // 160) == want, n
+    assert wb.encoder.Encoder.stem_frames(0) == 0
+
+
+def test_frame_count_known_answers():
+    """stft_test.go:54 TestFrameCount, centred framing: n // 160."""
+    from oracle import frontend as fe
+
+    for n, want in ((480000, 3000), (0, 0), (159, 0), (160, 1), (399, 2), (400, 2), (559, 3), (4321, 27),
+                    (16000, 100)):
+        assert fe.spectrum(np.zeros(n, np.float32)).shape[0] == want, n
+
+
+def test_spectrum_is_the_windowed_dft(wb):
+    """A tone at bin 32 puts its energy in bins 31-33 (the Hann main
+    lobe), and the power equals numpy's float64 rfft of the windowed frame."""
+    from oracle import frontend as fe
+
+    n = 16000
+    x = (0.5 * np.sin(2 * np.pi * 32 * np.arange(n) / 512)).astype(np.float32)
+    s = fe.spectrum(x)
+    mid = s[50]
+    assert set(np.argsort(mid)[-3:]) == {31, 32, 33}
+    pad = np.zeros(n + 512, np.float32)
+    pad[256:256 + n] = x
+    frame = (pad[50 * 160:50 * 160 + 512] * fe.window()).astype(np.float64)
+    ref = np.abs(np.fft.rfft(frame)) ** 2
+    assert np.allclose(mid, ref.astype(np.float32), rtol=1e-5, atol=1e-6 * ref.max())
+
+
+def test_logmel_standardises_each_channel(wb):
+    """mel.go:320 NormChannel: every channel has mean 0 and (n−1) deviation
+    1 over time (to the 1e-5 in the divisor)."""
+    from oracle import frontend as fe
+
+    w = wb.synth.EncoderWeights(seed=5103, layers=1)
+    m = fe.logmel(wb.synth.audio(np.random.default_rng(1), 1, 32000)[0], w.mel_filters).astype(np.float64)
+    assert m.shape == (200, 80)
+    assert np.abs(m.mean(0)).max() < 1e-5
+    assert np.abs(m.std(0, ddof=1) - 1).max() < 1e-4
