@@ -398,6 +398,101 @@ def prefill_component(pkg, torch, lib, frames=24000, reps=5):
             "roofline": "max(algorithmic bytes / measured HBM, flops / measured bf16 peak)"}
 
 
+ENCODER_CLIPS, ENCODER_FRAMES = 64, 375  # configs[2]: 64 streams x 375 frames = 24,000 rows
+
+
+def encoder_flops_per_frame(w) -> float:
+    """The stack's CQ product flops per frame (2 per multiply-add): per
+    layer the φ products (24 rows x 2048), q, k, v and gate (x 512),
+    out_proj, pw1 (1024 x 512) and pw2 (512 x 512)."""
+    D, n = w.dim, w.lanes
+    macs = (2 * n + n * n) * n * D
+    macs += D * (w.heads * w.qk + w.kv_heads * w.qk + w.kv_heads * w.vd + w.heads * w.vd)
+    macs += w.heads * w.vd * D + 2 * D * D + D * D
+    return 2.0 * macs * len(w.layers)
+
+
+def encoder_component(pkg, torch, lib, clips=ENCODER_CLIPS, frames=ENCODER_FRAMES, reps=3):
+    """f2: the encoder stack (wc_encoder_stack: encoder.go:167 Stack, 8
+    mHC-wrapped macaron blocks and the final norm) over configs[2]'s 64
+    clips x 375 frames of synthetic stem output ~N(0, 1), synthetic
+    Whistle-shaped weights. Two modes: the production one (products on the
+    tensor cores, attention in any order) and the exact one (lut products,
+    the attention's exact order). Each checks one clip against the CPU
+    restatement before timing."""
+    import oracle
+
+    w = pkg.synth.EncoderWeights(seed=5300, layers=8)
+    oe = oracle.OracleEncoder(w)
+    x = pkg.synth.stem_output(np.random.default_rng(5301), clips, frames)
+    dx = torch.from_numpy(x).cuda()
+    want_f = oe.stack(x[:1], oracle.ENC_ATTEND_FLOAT)[0]
+    pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    tflops_peak = float(pk.get("bf16_tflops", 1590.0))
+    flops = encoder_flops_per_frame(w) * clips * frames
+    res = {}
+    for name, flags in (("tensor cores, attention any order", 3), ("lut products, attention exact order", 0)):
+        enc = pkg.encoder.Encoder(w, max_clips=clips, max_frames=frames, flags=flags)
+        out = enc.Stack(dx)
+        torch.cuda.synchronize()
+        got = out[0].cpu().numpy()
+        cos = float(((got * want_f).sum(-1) / np.linalg.norm(got, axis=-1) / np.linalg.norm(want_f, axis=-1)).min())
+        if not cos >= 0.99999:
+            raise RuntimeError(f"encoder ({name}): clip 0 falls short of cosine 0.99999 against the oracle: {cos}")
+        n0 = lib.wc_launch_count()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            enc.Stack(dx, out)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        res[name] = {"ms_per_stack": round(ms, 3), "frames_per_s": round(clips * frames / (ms / 1e3)),
+                     "clips_per_s": round(clips / (ms / 1e3), 1), "launches_per_stack": (lib.wc_launch_count() - n0)
+                     // reps, "product_tflops": round(flops / (ms / 1e3) / 1e12, 1),
+                     "products_at_peak_ms": round(flops / (tflops_peak * 1e12) * 1e3, 3),
+                     "clip0_min_cosine_vs_reference_form": round(cos, 8)}
+        del enc
+    # The whole encoder (encoder.go:108 Embed): 30 s of 16 kHz audio per
+    # clip through the log-mel front end, the conv stem and the stack.
+    from oracle import frontend as fe
+
+    n = frames * 8 * 160
+    audio = pkg.synth.audio(np.random.default_rng(5302), clips, n)
+    daudio = torch.from_numpy(audio).cuda()
+    want_e = oe.stack(fe.stem(fe.logmel(audio[0], w.mel_filters), w, oracle), oracle.ENC_ATTEND_FLOAT)
+    enc = pkg.encoder.Encoder(w, max_clips=clips, max_frames=frames, flags=3)
+    out = enc.Embed(daudio)
+    torch.cuda.synchronize()
+    got = out[0].cpu().numpy()
+    cos = float(((got * want_e).sum(-1) / np.linalg.norm(got, axis=-1) / np.linalg.norm(want_e, axis=-1)).min())
+    if not cos >= 0.99999:
+        raise RuntimeError(f"encoder embed: clip 0 falls short of cosine 0.99999 against the oracle: {cos}")
+    parts = {}
+    mel = torch.empty(clips, n // 160, 80, device="cuda")
+    xs = torch.empty(clips, frames, w.dim, device="cuda")
+    for part, call in (("logmel", lambda: enc.LogMel(daudio, mel)), ("stem", lambda: enc.Stem(mel, xs)),
+                       ("embed", lambda: enc.Embed(daudio, out))):
+        call()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            call()
+        e1.record()
+        torch.cuda.synchronize()
+        parts[part] = round(e0.elapsed_time(e1) / reps, 3)
+    res["embed: front end + stem + stack, tensor cores, attention any order"] = {
+        "ms_per_embed": parts["embed"], "ms_logmel": parts["logmel"], "ms_stem": parts["stem"],
+        "audio_seconds_per_s": round(clips * n / 16000 / (parts["embed"] / 1e3)),
+        "clips_per_s": round(clips / (parts["embed"] / 1e3), 1), "clip0_min_cosine_vs_reference_form": round(cos, 8)}
+    del enc
+    return {"workload": f"configs[2]: encoder (8 layers, width 512, 4 mHC lanes, int8 attention over each clip's "
+                        f"frames) on {clips} clips x {frames} frames: the stack on synthetic stem output, and "
+                        f"Embed on {clips} clips of {n // 16000} s of synthetic 16 kHz audio",
+            "data": "synthetic weights (Whistle's shapes, a triangular mel bank) and inputs", "per_mode": res,
+            "product_flops": flops}
+
+
 def single_call_component(pkg, torch, lib, calls=20, reps=10):
     """Batch-1 latency: one GEMV call at a time (configs[0]'s 2048 x 512
     CQ4 G32, and the 16384 x 512 CQ4 vocabulary head), `calls` calls in a row
@@ -980,7 +1075,8 @@ def run_b200(args, world, rank, local):
                               "cq_gemm_prefill": prefill_component(pkg, torch, lib),
                               "cq_gemm_decode_streams": decode_gemm_component(pkg, torch, lib),
                               "cq_gemv_single_call": single_call_component(pkg, torch, lib),
-                              "beam_search": beam_component(pkg, torch, lib)}
+                              "beam_search": beam_component(pkg, torch, lib),
+                              "encoder_stack": encoder_component(pkg, torch, lib)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.only:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -1008,6 +1104,8 @@ def main():
     ap.add_argument("--decode-only", action="store_true", help="only the greedy decoder component")
     ap.add_argument("--rows-sweep", action="store_true", help="only the lut / tensor-core rows sweep")
     ap.add_argument("--beam-only", action="store_true", help="only the beam search component")
+    ap.add_argument("--encoder-only", action="store_true", help="only the encoder stack component")
+    ap.add_argument("--encoder-clips", type=int, default=ENCODER_CLIPS, help="--encoder-only: clips of 375 frames")
     ap.add_argument("--no-distinct", action="store_true",
                     help="skip the distinct-activation figure (its 8000 launches a step; profiling runs)")
     ap.add_argument("--decode-streams", type=int, default=DECODE_STREAMS, help="--decode-only: total streams")
@@ -1032,6 +1130,13 @@ def main():
         pkg = __import__("importlib").import_module("go-whistle_b200")
         torch.cuda.set_device(local)
         print(json.dumps(decode_gemm_component(pkg, torch, pkg._lib.lib())), flush=True)
+        return
+    if args.encoder_only:
+        import torch
+
+        pkg = __import__("importlib").import_module("go-whistle_b200")
+        torch.cuda.set_device(local)
+        print(json.dumps(encoder_component(pkg, torch, pkg._lib.lib(), clips=args.encoder_clips)), flush=True)
         return
     if args.beam_only:
         import torch

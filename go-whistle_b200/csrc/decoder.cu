@@ -2220,35 +2220,44 @@ __global__ void __launch_bounds__(kThreads)
 // ---- the log-mel front end (frontend/stft.go, mel.go) and the conv stem
 // (encoder/stem.go), Best() hypothesis.
 constexpr int kNFFT = 512, kHop = 160, kBins = kNFFT / 2 + 1, kMels = 80;
-constexpr int kWinLo = (kNFFT - 400) / 2, kWinHi = kWinLo + 400;  // the 400-sample window's place in the frame
+constexpr int kWinLo = (kNFFT - 400) / 2;  // the 400-sample window's offset in the frame
 
 // stft.go:113 spectrum for one frame: the frame centred on sample f·160
-// (zeros outside the clip), times the window, then |X_k|² for the 257
-// bins as a float64 DFT of the float32 products, rounded to float32.
-__global__ void __launch_bounds__(288)
+// (zeros outside the clip) times the window in float32, then |X_k|² of
+// bins 0 … 256 from a float64 radix-2 FFT (bit-reversed load, nine
+// butterfly stages; twiddles cos/sin(2πm/512) from the host's libm),
+// rounded to float32. One CTA of 256 threads per frame, one butterfly a
+// thread per stage.
+__device__ __forceinline__ int bitrev9(int j) { return (int)(__brev((unsigned)j) >> 23); }
+
+__global__ void __launch_bounds__(256)
     logmel_spec_kernel(const float *__restrict__ samples, int n, int frames, const float *__restrict__ win,
                        const double *__restrict__ twc, const double *__restrict__ tws, float *__restrict__ spec) {
-    __shared__ float xw[kNFFT];
-    __shared__ double cs[kNFFT], sn[kNFFT];
+    __shared__ double re[kNFFT], im[kNFFT];
     const int f = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
     for (int j = t; j < kNFFT; j += blockDim.x) {
         const long long smp = (long long)f * kHop - kNFFT / 2 + j;
         const float v = smp >= 0 && smp < n ? samples[(size_t)b * n + smp] : 0.0f;
-        xw[j] = v * win[j];
-        cs[j] = twc[j];
-        sn[j] = tws[j];
+        const int r = bitrev9(j);
+        re[r] = (double)(v * win[j]);
+        im[r] = 0.0;
     }
     __syncthreads();
-    if (t < kBins) {
-        double re = 0.0, im = 0.0;
-        for (int j = kWinLo; j < kWinHi; j++) {
-            const int m = (t * j) & (kNFFT - 1);
-            const double x = (double)xw[j];
-            re = re + x * cs[m];
-            im = im - x * sn[m];
-        }
-        spec[((size_t)b * frames + f) * kBins + t] = (float)(re * re + im * im);
+    for (int half = 1; half < kNFFT; half <<= 1) {
+        const int pos = t & (half - 1), i0 = ((t - pos) << 1) + pos, i1 = i0 + half;
+        const int m = pos * (kNFFT / (2 * half));
+        const double wr = twc[m], wi = -tws[m];
+        const double br = re[i1] * wr - im[i1] * wi, bi = re[i1] * wi + im[i1] * wr;
+        const double ar = re[i0], ai = im[i0];
+        __syncthreads();
+        re[i0] = ar + br;
+        im[i0] = ai + bi;
+        re[i1] = ar - br;
+        im[i1] = ai - bi;
+        __syncthreads();
     }
+    for (int k = t; k < kBins; k += blockDim.x)
+        spec[((size_t)b * frames + f) * kBins + k] = (float)(re[k] * re[k] + im[k] * im[k]);
 }
 
 // mel.go:78 MelBank.apply: channel m's float64 sum over its non-zero bins.
@@ -2264,42 +2273,58 @@ __global__ void logmel_mel_kernel(const float *__restrict__ spec, int frames, co
 
 // mel.go:302 softLog (ε = knee·max over the clip, log10 as Go's math.Log10:
 // ln(x)·(1/ln 10)) and :320 normalise, NormChannel (mean and n − 1
-// deviation per channel over time, sums in frame order): one CTA per clip,
-// a thread per channel.
-__global__ void __launch_bounds__(128) logmel_norm_kernel(double *__restrict__ mel, int frames, double knee,
-                                                          float *__restrict__ out) {
-    __shared__ double red[128];
-    const int b = blockIdx.x, m = threadIdx.x;
+// deviation per channel over time): one CTA per clip, 12 threads per
+// channel over interleaved frames; the float64 sums run in a fixed order
+// of partial sums (their rounding vanishes in the float32 output).
+constexpr int kNormGroups = 12;
+__global__ void __launch_bounds__(kMels * kNormGroups)
+    logmel_norm_kernel(double *__restrict__ mel, int frames, double knee, float *__restrict__ out) {
+    __shared__ double red[kMels * kNormGroups];
+    __shared__ double eps_s, mean_s[kMels], sd_s[kMels];
+    const int b = blockIdx.x, t = threadIdx.x, m = t % kMels, g = t / kMels;
     double *base = mel + (size_t)b * frames * kMels;
     double mx = -INFINITY;
-    if (m < kMels)
-        for (int f = 0; f < frames; f++) mx = fmax(mx, base[(size_t)f * kMels + m]);
-    red[m] = mx;
+    for (int f = g; f < frames; f += kNormGroups) mx = fmax(mx, base[(size_t)f * kMels + m]);
+    red[t] = mx;
     __syncthreads();
-    if (m == 0) {
-        double t = -INFINITY;
-        for (int i = 0; i < kMels; i++) t = fmax(t, red[i]);
-        red[0] = t;
+    if (t == 0) {
+        double v = -INFINITY;
+        for (int i = 0; i < kMels * kNormGroups; i++) v = fmax(v, red[i]);
+        v = knee * v;
+        eps_s = v == 0.0 ? 1e-10 : v;
     }
     __syncthreads();
-    double eps = knee * red[0];
-    if (eps == 0.0) eps = 1e-10;
-    if (m >= kMels) return;
-    const double inv_ln10 = 1.0 / 2.30258509299404568401799145468436421;
+    const double eps = eps_s, inv_ln10 = 1.0 / 2.30258509299404568401799145468436421;
     double sum = 0.0;
-    for (int f = 0; f < frames; f++) {
+    for (int f = g; f < frames; f += kNormGroups) {
         const double v = log(base[(size_t)f * kMels + m] + eps) * inv_ln10;
         base[(size_t)f * kMels + m] = v;
         sum = sum + v;
     }
-    const double mean = sum / (double)frames;
+    red[t] = sum;
+    __syncthreads();
+    if (g == 0) {
+        double s2 = 0.0;
+        for (int i = 0; i < kNormGroups; i++) s2 = s2 + red[i * kMels + m];
+        mean_s[m] = s2 / (double)frames;
+    }
+    __syncthreads();
+    const double mean = mean_s[m];
     double dev = 0.0;
-    for (int f = 0; f < frames; f++) {
+    for (int f = g; f < frames; f += kNormGroups) {
         const double d = base[(size_t)f * kMels + m] - mean;
         dev = dev + d * d;
     }
-    const double sd = frames > 1 ? sqrt(dev / (double)(frames - 1)) : 0.0;
-    for (int f = 0; f < frames; f++)
+    red[t] = dev;
+    __syncthreads();
+    if (g == 0) {
+        double s2 = 0.0;
+        for (int i = 0; i < kNormGroups; i++) s2 = s2 + red[i * kMels + m];
+        sd_s[m] = frames > 1 ? sqrt(s2 / (double)(frames - 1)) : 0.0;
+    }
+    __syncthreads();
+    const double sd = sd_s[m];
+    for (int f = g; f < frames; f += kNormGroups)
         out[((size_t)b * frames + f) * kMels + m] = (float)((base[(size_t)f * kMels + m] - mean) / (sd + 1e-5));
 }
 
@@ -2308,19 +2333,12 @@ __global__ void __launch_bounds__(128) logmel_norm_kernel(double *__restrict__ m
 // from 0, each product rounded before its add. Stage 0 reads one input
 // channel (stem.w, then SiLU, stem.go:367); the depthwise stages read
 // channel c for output channel c (groups = channels, no activation).
-// x [clips][h][w][cin], out [clips][h'][w'][channels]; a thread per
-// output value.
-__global__ void __launch_bounds__(256)
-    stem_conv_kernel(const float *__restrict__ x, int h, int w, int cin, const float *__restrict__ k, int channels,
-                     int ho, int wo, long long total, int silu, float *__restrict__ out) {
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= total) return;
-    const int c = (int)(i % channels);
-    const long long pix = i / channels;
-    const int ow = (int)(pix % wo);
-    const long long r = pix / wo;
-    const int oh = (int)(r % ho);
-    const long long b = r / ho;
+// x [clips][h][w][cin], out [clips][h'][w'][channels]; a CTA per output
+// pixel, a thread per channel.
+__global__ void stem_conv_kernel(const float *__restrict__ x, int h, int w, int cin, const float *__restrict__ k,
+                                 int ho, int wo, int silu, float *__restrict__ out) {
+    const int pix = blockIdx.x, c = threadIdx.x, channels = blockDim.x;
+    const int ow = pix % wo, r = pix / wo, oh = r % ho, b = r / ho;
     const int ci = cin == 1 ? 0 : c;
     float acc = 0.0f;
     for (int kh = 0; kh < 3; kh++) {
@@ -2329,30 +2347,25 @@ __global__ void __launch_bounds__(256)
         for (int kw = 0; kw < 3; kw++) {
             const int iw = 2 * ow - 1 + kw;
             if (iw < 0 || iw >= w) continue;
-            acc = acc + x[((b * h + ih) * w + iw) * cin + ci] * k[(kh * 3 + kw) * channels + c];
+            acc = acc + x[(((size_t)b * h + ih) * w + iw) * cin + ci] * k[(kh * 3 + kw) * channels + c];
         }
     }
-    out[i] = silu ? acc * sigm(acc) : acc;
+    out[(size_t)pix * channels + c] = silu ? acc * sigm(acc) : acc;
 }
 
 // stem.go:253 pointwise's activation (SiLU) in place, or with flatten set,
 // into stem.go:262 output's channel-major flatten: out[r][c·w + f] for
-// pixel (r, f) of w mel positions.
-__global__ void __launch_bounds__(256) stem_act_kernel(const float *__restrict__ y, long long total, int channels,
-                                                       int w, int flatten, float *__restrict__ out) {
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= total) return;
-    const float v = y[i];
+// pixel (r, f) of w mel positions. A CTA per pixel, a thread per channel.
+__global__ void stem_act_kernel(const float *__restrict__ y, int w, int flatten, float *__restrict__ out) {
+    const int pix = blockIdx.x, c = threadIdx.x, channels = blockDim.x;
+    const float v = y[(size_t)pix * channels + c];
     const float a = v * sigm(v);
     if (!flatten) {
-        out[i] = a;
+        out[(size_t)pix * channels + c] = a;
         return;
     }
-    const int c = (int)(i % channels);
-    const long long pix = i / channels;
-    const int f = (int)(pix % w);
-    const long long r = pix / w;
-    out[r * (long long)(channels * w) + (long long)c * w + f] = a;
+    const int f = pix % w, r = pix / w;
+    out[(size_t)r * channels * w + (size_t)c * w + f] = a;
 }
 }  // namespace
 }  // namespace wb
@@ -2749,8 +2762,6 @@ static wc_status enc_stem_ready(wc_encoder *e) {
     return WC_OK;
 }
 
-static int blocks_of(long long total, int threads) { return (int)((total + threads - 1) / threads); }
-
 extern "C" wc_status wc_encoder_logmel(wc_encoder *e, const float *samples, int clips, int n, float *mel,
                                        wc_stream stream) {
     DEC_ST(enc_stem_ready(e));
@@ -2761,9 +2772,9 @@ extern "C" wc_status wc_encoder_logmel(wc_encoder *e, const float *samples, int 
     if (clips == 0 || F == 0) return WC_OK;
     if (!samples || !mel) return set_error(WC_ERR_INVALID, "encoder: nil samples or mel");
     cudaStream_t st = (cudaStream_t)stream;
-    DEC_LAUNCH(logmel_spec_kernel<<<dim3(F, clips), 288, 0, st>>>(samples, n, F, e->win, e->twc, e->tws, e->spec));
+    DEC_LAUNCH(logmel_spec_kernel<<<dim3(F, clips), 256, 0, st>>>(samples, n, F, e->win, e->twc, e->tws, e->spec));
     DEC_LAUNCH(logmel_mel_kernel<<<dim3(F, clips), 96, 0, st>>>(e->spec, F, e->bank, e->mlo, e->mhi, e->mel64));
-    DEC_LAUNCH(logmel_norm_kernel<<<clips, 128, 0, st>>>(e->mel64, F, e->knee, mel));
+    DEC_LAUNCH(logmel_norm_kernel<<<clips, kMels * kNormGroups, 0, st>>>(e->mel64, F, e->knee, mel));
     return WC_OK;
 }
 
@@ -2781,19 +2792,14 @@ extern "C" wc_status wc_encoder_stem(wc_encoder *e, const float *mel, int clips,
     const int h1 = (frames - 1) / 2 + 1, w1 = (kMels - 1) / 2 + 1;
     const int h2 = (h1 - 1) / 2 + 1, w2 = (w1 - 1) / 2 + 1;
     const int w3 = (w2 - 1) / 2 + 1;
-    long long tot = (long long)clips * h1 * w1 * C;
-    DEC_LAUNCH(stem_conv_kernel<<<blocks_of(tot, 256), 256, 0, st>>>(mel, frames, kMels, 1, e->sw, C, h1, w1, tot, 1,
-                                                                     e->s0));
-    tot = (long long)clips * h2 * w2 * C;
-    DEC_LAUNCH(stem_conv_kernel<<<blocks_of(tot, 256), 256, 0, st>>>(e->s0, h1, w1, C, e->sdw[0], C, h2, w2, tot, 0,
-                                                                     e->s1));
-    DEC_ST(enc_gemms(e, {e->spw[0]}, e->s1, {e->s2}, clips * h2 * w2, st));
-    DEC_LAUNCH(stem_act_kernel<<<blocks_of(tot, 256), 256, 0, st>>>(e->s2, tot, C, w2, 0, e->s2));
-    tot = (long long)clips * T * w3 * C;
-    DEC_LAUNCH(stem_conv_kernel<<<blocks_of(tot, 256), 256, 0, st>>>(e->s2, h2, w2, C, e->sdw[1], C, T, w3, tot, 0,
-                                                                     e->s3));
-    DEC_ST(enc_gemms(e, {e->spw[1]}, e->s3, {e->s4}, clips * T * w3, st));
-    DEC_LAUNCH(stem_act_kernel<<<blocks_of(tot, 256), 256, 0, st>>>(e->s4, tot, C, w3, 1, e->flat));
+    const int p1 = clips * h1 * w1, p2 = clips * h2 * w2, p3 = clips * T * w3;
+    DEC_LAUNCH(stem_conv_kernel<<<p1, C, 0, st>>>(mel, frames, kMels, 1, e->sw, h1, w1, 1, e->s0));
+    DEC_LAUNCH(stem_conv_kernel<<<p2, C, 0, st>>>(e->s0, h1, w1, C, e->sdw[0], h2, w2, 0, e->s1));
+    DEC_ST(enc_gemms(e, {e->spw[0]}, e->s1, {e->s2}, p2, st));
+    DEC_LAUNCH(stem_act_kernel<<<p2, C, 0, st>>>(e->s2, w2, 0, e->s2));
+    DEC_LAUNCH(stem_conv_kernel<<<p3, C, 0, st>>>(e->s2, h2, w2, C, e->sdw[1], T, w3, 0, e->s3));
+    DEC_ST(enc_gemms(e, {e->spw[1]}, e->s3, {e->s4}, p3, st));
+    DEC_LAUNCH(stem_act_kernel<<<p3, C, 0, st>>>(e->s4, w3, 1, e->flat));
     DEC_ST(enc_gemms(e, {e->sout}, e->flat, {x}, clips * T, st));
     return WC_OK;
 }
