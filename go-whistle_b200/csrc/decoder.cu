@@ -2333,39 +2333,51 @@ __global__ void __launch_bounds__(kMels * kNormGroups)
 // from 0, each product rounded before its add. Stage 0 reads one input
 // channel (stem.w, then SiLU, stem.go:367); the depthwise stages read
 // channel c for output channel c (groups = channels, no activation).
-// x [clips][h][w][cin], out [clips][h'][w'][channels]; a CTA per output
-// pixel, a thread per channel.
+// x [clips][h][w][cin], out [clips][h'][w'][channels]; a CTA per
+// kStemPix output pixels, a thread per channel.
+constexpr int kStemPix = 16;
 __global__ void stem_conv_kernel(const float *__restrict__ x, int h, int w, int cin, const float *__restrict__ k,
-                                 int ho, int wo, int silu, float *__restrict__ out) {
-    const int pix = blockIdx.x, c = threadIdx.x, channels = blockDim.x;
-    const int ow = pix % wo, r = pix / wo, oh = r % ho, b = r / ho;
-    const int ci = cin == 1 ? 0 : c;
-    float acc = 0.0f;
-    for (int kh = 0; kh < 3; kh++) {
-        const int ih = 2 * oh - 1 + kh;
-        if (ih < 0 || ih >= h) continue;
-        for (int kw = 0; kw < 3; kw++) {
-            const int iw = 2 * ow - 1 + kw;
-            if (iw < 0 || iw >= w) continue;
-            acc = acc + x[(((size_t)b * h + ih) * w + iw) * cin + ci] * k[(kh * 3 + kw) * channels + c];
+                                 int ho, int wo, int npix, int silu, float *__restrict__ out) {
+    const int c = threadIdx.x, channels = blockDim.x, ci = cin == 1 ? 0 : c;
+    float kc[9];
+#pragma unroll
+    for (int t = 0; t < 9; t++) kc[t] = k[t * channels + c];
+    const int p1 = min(npix, (blockIdx.x + 1) * kStemPix);
+    for (int pix = blockIdx.x * kStemPix; pix < p1; pix++) {
+        const int ow = pix % wo, r = pix / wo, oh = r % ho, b = r / ho;
+        float acc = 0.0f;
+#pragma unroll
+        for (int kh = 0; kh < 3; kh++) {
+            const int ih = 2 * oh - 1 + kh;
+            if (ih < 0 || ih >= h) continue;
+#pragma unroll
+            for (int kw = 0; kw < 3; kw++) {
+                const int iw = 2 * ow - 1 + kw;
+                if (iw < 0 || iw >= w) continue;
+                acc = acc + x[(((size_t)b * h + ih) * w + iw) * cin + ci] * kc[kh * 3 + kw];
+            }
         }
+        out[(size_t)pix * channels + c] = silu ? acc * sigm(acc) : acc;
     }
-    out[(size_t)pix * channels + c] = silu ? acc * sigm(acc) : acc;
 }
 
 // stem.go:253 pointwise's activation (SiLU) in place, or with flatten set,
 // into stem.go:262 output's channel-major flatten: out[r][c·w + f] for
-// pixel (r, f) of w mel positions. A CTA per pixel, a thread per channel.
-__global__ void stem_act_kernel(const float *__restrict__ y, int w, int flatten, float *__restrict__ out) {
-    const int pix = blockIdx.x, c = threadIdx.x, channels = blockDim.x;
-    const float v = y[(size_t)pix * channels + c];
-    const float a = v * sigm(v);
-    if (!flatten) {
-        out[(size_t)pix * channels + c] = a;
-        return;
+// pixel (r, f) of w mel positions. A CTA per kStemPix pixels, a thread
+// per channel.
+__global__ void stem_act_kernel(const float *__restrict__ y, int w, int npix, int flatten, float *__restrict__ out) {
+    const int c = threadIdx.x, channels = blockDim.x;
+    const int p1 = min(npix, (blockIdx.x + 1) * kStemPix);
+    for (int pix = blockIdx.x * kStemPix; pix < p1; pix++) {
+        const float v = y[(size_t)pix * channels + c];
+        const float a = v * sigm(v);
+        if (!flatten) {
+            out[(size_t)pix * channels + c] = a;
+            continue;
+        }
+        const int f = pix % w, r = pix / w;
+        out[(size_t)r * channels * w + (size_t)c * w + f] = a;
     }
-    const int f = pix % w, r = pix / w;
-    out[(size_t)r * channels * w + (size_t)c * w + f] = a;
 }
 }  // namespace
 }  // namespace wb
@@ -2793,13 +2805,14 @@ extern "C" wc_status wc_encoder_stem(wc_encoder *e, const float *mel, int clips,
     const int h2 = (h1 - 1) / 2 + 1, w2 = (w1 - 1) / 2 + 1;
     const int w3 = (w2 - 1) / 2 + 1;
     const int p1 = clips * h1 * w1, p2 = clips * h2 * w2, p3 = clips * T * w3;
-    DEC_LAUNCH(stem_conv_kernel<<<p1, C, 0, st>>>(mel, frames, kMels, 1, e->sw, h1, w1, 1, e->s0));
-    DEC_LAUNCH(stem_conv_kernel<<<p2, C, 0, st>>>(e->s0, h1, w1, C, e->sdw[0], h2, w2, 0, e->s1));
+    auto ctas = [](int npix) { return (npix + kStemPix - 1) / kStemPix; };
+    DEC_LAUNCH(stem_conv_kernel<<<ctas(p1), C, 0, st>>>(mel, frames, kMels, 1, e->sw, h1, w1, p1, 1, e->s0));
+    DEC_LAUNCH(stem_conv_kernel<<<ctas(p2), C, 0, st>>>(e->s0, h1, w1, C, e->sdw[0], h2, w2, p2, 0, e->s1));
     DEC_ST(enc_gemms(e, {e->spw[0]}, e->s1, {e->s2}, p2, st));
-    DEC_LAUNCH(stem_act_kernel<<<p2, C, 0, st>>>(e->s2, w2, 0, e->s2));
-    DEC_LAUNCH(stem_conv_kernel<<<p3, C, 0, st>>>(e->s2, h2, w2, C, e->sdw[1], T, w3, 0, e->s3));
+    DEC_LAUNCH(stem_act_kernel<<<ctas(p2), C, 0, st>>>(e->s2, w2, p2, 0, e->s2));
+    DEC_LAUNCH(stem_conv_kernel<<<ctas(p3), C, 0, st>>>(e->s2, h2, w2, C, e->sdw[1], T, w3, p3, 0, e->s3));
     DEC_ST(enc_gemms(e, {e->spw[1]}, e->s3, {e->s4}, p3, st));
-    DEC_LAUNCH(stem_act_kernel<<<p3, C, 0, st>>>(e->s4, w3, 1, e->flat));
+    DEC_LAUNCH(stem_act_kernel<<<ctas(p3), C, 0, st>>>(e->s4, w3, p3, 1, e->flat));
     DEC_ST(enc_gemms(e, {e->sout}, e->flat, {x}, clips * T, st));
     return WC_OK;
 }
