@@ -121,6 +121,15 @@ class Encoder:
         check(lib().wc_encoder_create(ctypes.byref(desc), max_clips, max_frames, flags, ctypes.byref(h)))
         self.handle = h
 
+    @classmethod
+    def Load(cls, path_or_data, max_clips: int, max_frames: int = 375, flags: int = 0):
+        """encoder.LoadInt8 over a .cact file (a path or its bytes): the
+        encoder's, the stem's and the mel bank's tensors by name
+        (weights.encoder_weights), CQ records uploaded as stored."""
+        from . import weights
+
+        return cls(weights.load_encoder(path_or_data), max_clips, max_frames, flags)
+
     def __del__(self):
         if getattr(self, "handle", None) and self.handle.value:
             lib().wc_encoder_destroy(self.handle)

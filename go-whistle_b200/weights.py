@@ -229,6 +229,70 @@ def decoder_weights(src: Source) -> DecoderTensors:
     return w
 
 
+class EncoderTensors:
+    """The encoder's weight set as ``encoder.Encoder`` takes it (the
+    attributes of synth.EncoderWeights), loaded from a Source."""
+
+    def phi_rows(self, name: str, l: int):
+        """Layer l's row range of a stacked φ (mhc.go:94-96)."""
+        per = self.lanes * self.lanes if name == "phi_res" else self.lanes
+        return l * per, (l + 1) * per
+
+
+ENC_ROPE_LEN = 4096  # RoPE positions the device tables hold (encoder.go:276 rope builds them per call)
+_ENC_FLOATS = ("pre_hada_0", "norm_in", "post_norm", "conv_norm", "conv_out_norm", "pre_hada", "q_norm", "k_norm",
+               "dw")
+_ENC_MLP = ("d1", "d2", "b2", "d3", "d4", "w1a", "w1b", "w2a", "w2b", "w3a", "w3b", "cond_v", "cond_u")
+_ENC_CQ = ("q_proj", "k_proj", "v_proj", "gate_proj", "out_proj", "pw1", "pw2")
+
+
+def encoder_weights(src: Source) -> EncoderTensors:
+    """The encoder's tensors by the names internal/encoder loads
+    (encoder.go:50 LoadInt8, block.go:42 loadBlock, mhc.go LoadMHC with the
+    "enc." prefix, stem.go:43 loadStem, frontend/mel.go:67 LoadMelBank),
+    the layer and lane counts from the audio manifest, the widths from the
+    shapes (Best(): RoPE θ = 1e5, the shared Hadamard permutations)."""
+    cfg = src.Config()
+    w = EncoderTensors()
+    w.n_layers, w.lanes = cfg.EncLayers, cfg.EncLanes
+    w.final_norm = src.Tensor("enc.final_norm").astype(np.float32)
+    w.dim = int(w.final_norm.size)
+    w.hada_p1 = _perm(src, "hada_p1", cfg.HadaN)
+    w.hada_p2 = _perm(src, "hada_p2", cfg.HadaN)
+    a = {k: src.Tensor("enc.mhc_a_" + k) for k in ("pre", "post", "res")}
+    b = {k: src.Tensor("enc.mhc_b_" + k) for k in ("pre", "post", "res")}
+    w.phi_pre, w.phi_post, w.phi_res = (src.Matrix("enc.mhc_phi_" + k) for k in ("pre", "post", "res"))
+    w.layers = []
+    for l in range(cfg.EncLayers):
+        p = f"enc{l:02d}."
+        L = {k: src.Tensor(p + k).astype(np.float32) for k in _ENC_FLOATS}
+        for m in ("hada_0.", "hada."):
+            for k in _ENC_MLP:
+                L[m + k] = src.Tensor(p + m + k).astype(np.float32)
+        L["attn_gate"] = float(src.Tensor(p + "attn_gate").reshape(-1)[0])
+        for k in _ENC_CQ:
+            L[k] = src.Matrix(p + k)
+        L["a_pre"], L["a_post"], L["a_res"] = (float(a[k][l]) for k in ("pre", "post", "res"))
+        L["b_pre"], L["b_post"] = b["pre"][l].astype(np.float32), b["post"][l].astype(np.float32)
+        L["b_res"] = b["res"][l].astype(np.float32).reshape(-1)
+        w.layers.append(L)
+    L0 = w.layers[0]
+    w.qk = int(L0["q_norm"].size)
+    w.heads, w.kv_heads = L0["q_proj"].Out // w.qk, L0["k_proj"].Out // w.qk
+    w.vd = L0["v_proj"].Out // w.kv_heads
+    w.dw_k = int(L0["dw"].shape[0])
+    w.na, w.nb = int(L0["hada.w1a"].shape[0]), int(L0["hada.w1b"].shape[0])
+    w.rank = int(L0["hada.cond_v"].shape[1])
+    w.rope_theta, w.rope_len = 1e5, ENC_ROPE_LEN
+    w.stem_w, w.stem_dw_1, w.stem_dw_2 = (src.Tensor("stem." + k).astype(np.float32) for k in ("w", "dw_1", "dw_2"))
+    w.stem_pw_1, w.stem_pw_2, w.stem_out = (src.Matrix("stem." + k) for k in ("pw_1", "pw_2", "out"))
+    w.stem_channels = int(w.stem_w.shape[1])
+    w.mel_filters = src.Tensor("audio.mel_filters").astype(np.float32)
+    w.cb2 = np.asarray(L0["q_proj"].Codebook, np.float32)
+    w.cb4 = np.asarray(w.phi_pre.Codebook, np.float32)
+    return w
+
+
 # ---- a synthetic whistle.cact -------------------------------------------
 
 # The audio manifest of a Whistle export: magic, version, then text vocab,
@@ -276,13 +340,15 @@ def whistle_header(w, max_seq: int = 320) -> cact.Header:
                        RopeTheta=float(w.rope_theta))
 
 
-def write_whistle_cact(w, path: Optional[str] = None, seed: int = 0) -> bytes:
+def write_whistle_cact(w, path: Optional[str] = None, seed: int = 0, enc=None) -> bytes:
     """A whistle.cact holding decoder weights w (synth.DecoderWeights of
-    Whistle's shapes: vocab 8199, 8 layers, 18,432 engram slots) and seeded
-    random audio tensors; returns the bytes and writes them to path if
-    given. The file's CQ group is w's (one group for the whole file, as
-    _pack_cact writes), its codebook w's 2- and 4-bit levels and the 3-bit
-    Lloyd-Max levels over sqrt(group)."""
+    Whistle's shapes: vocab 8199, 8 layers, 18,432 engram slots) and, with
+    enc (synth.EncoderWeights of Whistle's shapes, the same hada_p1/hada_p2:
+    the file holds one pair), the encoder's, the stem's and the mel bank's;
+    without enc those audio tensors are seeded random. Returns the bytes and
+    writes them to path if given. The file's CQ group is w's (one group for
+    the whole file, as _pack_cact writes), its codebook w's 2- and 4-bit
+    levels and the 3-bit Lloyd-Max levels over sqrt(group)."""
     from .synth import _cq_tensor
 
     group = int(w.embedding.Group)
@@ -318,10 +384,38 @@ def write_whistle_cact(w, path: Optional[str] = None, seed: int = 0) -> bytes:
             return w.sites[s][k]
         return None
 
+    if enc is not None and not (np.array_equal(enc.hada_p1, w.hada_p1) and np.array_equal(enc.hada_p2, w.hada_p2)):
+        raise WeightsError("weights: the encoder's hada_p1/hada_p2 differ from the decoder's (a file holds one pair)")
+
+    def enc_value(name):
+        """enc's tensor for an encoder, stem or mel-bank record, else None."""
+        if enc is None:
+            return None
+        if name == "enc.final_norm":
+            return enc.final_norm
+        if name.startswith("enc.mhc_"):
+            k = name[8:]
+            if k.startswith("phi_"):
+                return getattr(enc, k)
+            if k.startswith("a_"):
+                return np.array([L[k] for L in enc.layers], np.float32)
+            vals = np.stack([np.asarray(L[k], np.float32) for L in enc.layers])
+            return vals.reshape(len(enc.layers), enc.lanes, enc.lanes) if k == "b_res" else vals
+        if name.startswith("enc") and name[3:5].isdigit():
+            v = enc.layers[int(name[3:5])][name.split(".", 1)[1]]
+            return np.array([v], np.float32) if np.isscalar(v) else v
+        if name.startswith("stem."):
+            return getattr(enc, "stem_" + name[5:])
+        if name == "audio.mel_filters":
+            return enc.mel_filters
+        return None
+
     tensors = []
     for e in entries:
         dtype, bits = cact.whistle_storage(e.Name)
         v = dec_value(e.Name)
+        if v is None:
+            v = enc_value(e.Name)
         if dtype == cact.RAW:
             tensors.append(cact.raw_tensor(np.uint32(w.vocab).tobytes() + b"synthetic tokenizer"))
             continue
@@ -358,3 +452,9 @@ def load_decoder(path_or_data: Union[str, bytes], names: Optional[Sequence[cact.
     """The decoder's weight set from a .cact file (a path or its bytes)."""
     src = Parse(path_or_data, names) if isinstance(path_or_data, (bytes, bytearray)) else Open(path_or_data, names)
     return decoder_weights(src)
+
+
+def load_encoder(path_or_data: Union[str, bytes], names: Optional[Sequence[cact.Entry]] = None) -> EncoderTensors:
+    """The encoder's weight set from a .cact file (a path or its bytes)."""
+    src = Parse(path_or_data, names) if isinstance(path_or_data, (bytes, bytearray)) else Open(path_or_data, names)
+    return encoder_weights(src)

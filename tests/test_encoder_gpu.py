@@ -191,3 +191,21 @@ def test_stem_errors(wb, cuda, setup):
     enc = wb.encoder.Encoder(w, max_clips=1, max_frames=8)
     with pytest.raises(wb.Panic, match="exceed the room"):
         enc.Embed(cuda.zeros(1, 160 * 65, device="cuda"))  # 65 mel frames -> 9 stem frames > 8
+
+
+def test_loaded_encoder_matches_oracle(wb, orc, cuda):
+    """An encoder loaded from a synthetic whistle.cact (encoder.Encoder.Load):
+    Embed against the CPU restatement on the same loaded weights."""
+    from oracle import frontend as fe
+
+    w = wb.synth.DecoderWeights(seed=4520, vocab=8199)
+    e = wb.synth.EncoderWeights(seed=5520)
+    e.hada_p1, e.hada_p2 = w.hada_p1, w.hada_p2
+    data = wb.weights.write_whistle_cact(w, seed=4, enc=e)
+    le = wb.weights.load_encoder(data)
+    a = wb.synth.audio(np.random.default_rng(34), 2, 48000)  # 300 mel frames -> 38 stem frames
+    got = wb.encoder.Encoder.Load(data, max_clips=2, max_frames=38).Embed(cuda.from_numpy(a).cuda()).cpu().numpy()
+    oe = orc.OracleEncoder(le)
+    want = np.stack([oe.stack(fe.stem(fe.logmel(x, le.mel_filters), le, orc), orc.ENC_ATTEND_FLOAT) for x in a])
+    cos, rel, _ = _cmp(got, want)
+    assert cos >= FORM_COS and rel <= FORM_ATOL, (cos, rel)
