@@ -2379,6 +2379,167 @@ __global__ void stem_act_kernel(const float *__restrict__ y, int w, int npix, in
         out[(size_t)r * channels * w + (size_t)c * w + f] = a;
     }
 }
+
+// The encoder's self-attention in any order (WC_ENCODER_ANY_ORDER): a CTA
+// stages one clip's int8 keys and values of one KV head and their scales
+// in shared memory once, then its 8 warps serve 32 query frames × the KV
+// head's query heads, a (frame, head) pair per warp at a time. Per pair:
+// the query quantised per head as int8.go:36 QuantizeRow does it (the int8
+// kernel's codes); lane l takes keys l, l + 32, …: logits (Σ q8·k8 exact
+// in int32)·(s_q·s_k)/√qk, the softmax weights with expf, and all 64
+// columns of Σ_j p_j·s_v,j·v8_j by packed f32x2 FMAs; a halving shuffle
+// reduction leaves each lane two finished columns, ÷ Σ p. The int8
+// kernel's any-order arithmetic in another order (WC_ATTEND_ANY_ORDER's
+// bound).
+constexpr int kEaFrames = 32, kEaThreads = 256, kEaWarps = kEaThreads / 32, kEaMaxKeys = 1024;
+constexpr int kEaVRow = kVD + 16;  // staged V row stride: 16-byte loads of 8 lanes hit distinct banks
+
+// Shared memory: K [nk][48] and V [nk][80] int8 (offsets multiples of 16),
+// the warps' query codes [8][64], the key and value scales [nk] and the
+// warps' logits [8][nk] (floats).
+__host__ __device__ inline size_t ea_smem(int nk) {
+    return (size_t)nk * (kQK + kEaVRow) + (size_t)kEaWarps * 64 + 2 * (size_t)nk * 4 + (size_t)kEaWarps * nk * 4;
+}
+
+__global__ void __launch_bounds__(kEaThreads, 2)
+    enc_attend_kernel(const float *__restrict__ q, const int8_t *__restrict__ k8, const float *__restrict__ ks,
+                      const int8_t *__restrict__ v8, const float *__restrict__ vs, int frames, int heads,
+                      int kv_heads, float scale, float *__restrict__ out) {
+    extern __shared__ __align__(16) unsigned char sm[];
+    const int nk = frames, b = blockIdx.z, g = blockIdx.y, f0 = blockIdx.x * kEaFrames;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int8_t *K = reinterpret_cast<int8_t *>(sm);
+    int8_t *V = K + (size_t)nk * kQK;
+    int8_t *q8 = V + (size_t)nk * kEaVRow + warp * 64;
+    float *kss = reinterpret_cast<float *>(V + (size_t)nk * kEaVRow + kEaWarps * 64);
+    float *vss = kss + nk;
+    float *pw = vss + nk + (size_t)warp * nk;  // this warp's logits: lane l owns keys l, l + 32, ...
+    const size_t row0 = (size_t)b * frames;
+    for (int i = tid; i < nk * (kQK / 16); i += kEaThreads) {
+        const int j = i / (kQK / 16), w = i % (kQK / 16);
+        reinterpret_cast<uint4 *>(K)[i] =
+            reinterpret_cast<const uint4 *>(k8 + ((row0 + j) * kv_heads + g) * kQK)[w];
+    }
+    for (int i = tid; i < nk * (kVD / 16); i += kEaThreads) {
+        const int j = i / (kVD / 16), w = i % (kVD / 16);
+        reinterpret_cast<uint4 *>(V + (size_t)j * kEaVRow)[w] =
+            reinterpret_cast<const uint4 *>(v8 + ((row0 + j) * kv_heads + g) * kVD)[w];
+    }
+    for (int j = tid; j < nk; j += kEaThreads) {
+        kss[j] = ks[(row0 + j) * kv_heads + g];
+        vss[j] = vs[(row0 + j) * kv_heads + g];
+    }
+    __syncthreads();
+    const int gs = heads / kv_heads, half = kQK / 2;
+    uint64_t bias;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(bias) : "f"(-8388736.0f));
+    for (int task = warp; task < kEaFrames * gs; task += kEaWarps) {
+        const int f = f0 + task / gs, h = g * gs + task % gs;
+        if (f >= frames) break;  // warp-uniform; later tasks are later frames
+        const size_t r = row0 + f;
+        const float *qh = q + (r * heads + h) * kQK;
+        const float x0 = lane < half ? qh[lane] : 0.0f, x1 = lane < half ? qh[lane + half] : 0.0f;
+        float m = fmaxf(fabsf(x0), fabsf(x1));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const float sq = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
+        if (lane < half) {
+            q8[lane] = quant8(x0, sq);
+            q8[lane + half] = quant8(x1, sq);
+        }
+        __syncwarp();
+        uint32_t qw[kQK / 4];
+#pragma unroll
+        for (int w = 0; w < kQK / 16; w++) {
+            const uint4 v = reinterpret_cast<const uint4 *>(q8)[w];
+            qw[4 * w] = v.x, qw[4 * w + 1] = v.y, qw[4 * w + 2] = v.z, qw[4 * w + 3] = v.w;
+        }
+        __syncwarp();  // q8 is rewritten by the next pair
+        // Logits of this lane's keys.
+        float mx = -INFINITY;
+        for (int j = lane; j < nk; j += 32) {
+            const uint4 *kr = reinterpret_cast<const uint4 *>(K + (size_t)j * kQK);
+            int32_t d0 = 0, d1 = 0;
+#pragma unroll
+            for (int w = 0; w < kQK / 16; w++) {
+                const uint4 kv = kr[w];
+                d0 = __dp4a((int)qw[4 * w], (int)kv.x, d0);
+                d1 = __dp4a((int)qw[4 * w + 1], (int)kv.y, d1);
+                d0 = __dp4a((int)qw[4 * w + 2], (int)kv.z, d0);
+                d1 = __dp4a((int)qw[4 * w + 3], (int)kv.w, d1);
+            }
+            const float l = (float)(d0 + d1) * (sq * kss[j]) / scale;
+            pw[j] = l;
+            mx = fmaxf(mx, l);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        // Σ_j p_j·s_v·v8_j over this lane's keys, all 64 columns, packed.
+        uint64_t acc[kVD / 2];
+#pragma unroll
+        for (int c = 0; c < kVD / 2; c++) acc[c] = 0;
+        float sum = 0.0f;
+        for (int j = lane; j < nk; j += 32) {
+            {
+                const float e = expf(pw[j] - mx);
+                sum += e;
+                uint64_t ww;
+                asm("mov.b64 %0, {%1, %1};" : "=l"(ww) : "f"(e * vss[j]));
+                const uint4 *vr = reinterpret_cast<const uint4 *>(V + (size_t)j * kEaVRow);
+#pragma unroll
+                for (int w = 0; w < kVD / 16; w++) {
+                    const uint4 v = vr[w];
+                    const uint32_t vw[4] = {v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u,
+                                            v.w ^ 0x80808080u};
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+#pragma unroll
+                        for (int bb = 0; bb < 4; bb += 2) {
+                            // Two codes as floats: 2^23 + (code + 128), less the bias.
+                            uint64_t cv;
+                            asm("mov.b64 %0, {%1, %2};"
+                                : "=l"(cv)
+                                : "r"(__byte_perm(vw[u], 0x4B000000u, 0x7540u + bb)),
+                                  "r"(__byte_perm(vw[u], 0x4B000000u, 0x7540u + bb + 1)));
+                            asm("add.rn.f32x2 %0, %0, %1;" : "+l"(cv) : "l"(bias));
+                            uint64_t &a = acc[(16 * w + 4 * u + bb) / 2];
+                            asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(a) : "l"(ww), "l"(cv));
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        // Halving reduction over the lanes: after the step of width s the lane
+        // keeps s of the column pairs; at the end lane l holds pair l.
+        float av[kVD];
+#pragma unroll
+        for (int c = 0; c < kVD / 2; c++) asm("mov.b64 {%0, %1}, %2;" : "=f"(av[2 * c]), "=f"(av[2 * c + 1]) : "l"(acc[c]));
+#pragma unroll
+        for (int s = 16; s >= 1; s >>= 1) {
+            const bool upper = (lane & s) != 0;
+#pragma unroll
+            for (int c = 0; c < s; c++) {
+                // pairs [0, 2s): the lower half stays with the lanes without bit s
+                const float k0 = upper ? av[2 * c] : av[2 * (c + s)];
+                const float k1 = upper ? av[2 * c + 1] : av[2 * (c + s) + 1];
+                const float g0 = __shfl_xor_sync(0xffffffffu, k0, s);
+                const float g1 = __shfl_xor_sync(0xffffffffu, k1, s);
+                const float m0 = upper ? av[2 * (c + s)] : av[2 * c];
+                const float m1 = upper ? av[2 * (c + s) + 1] : av[2 * c + 1];
+                av[2 * c] = m0 + g0;
+                av[2 * c + 1] = m1 + g1;
+            }
+        }
+        // The lanes with bit s set kept the upper half at every step, so lane
+        // l holds column pair l.
+        const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+        float *o = out + (r * heads + h) * kVD + 2 * lane;
+        o[0] = av[0] * inv;
+        o[1] = av[1] * inv;
+    }
+}
 }  // namespace
 }  // namespace wb
 
@@ -2481,9 +2642,15 @@ wc_status enc_layer(wc_encoder *e, int l, int R, int frames, cudaStream_t st) {
     DEC_ST(enc_gemms(e, {L.q, L.kk, L.v, L.g}, e->a, {e->q, e->k, e->v, e->g}, R, st));
     DEC_LAUNCH(enc_qkv_kernel<<<R, kThreads, 0, st>>>(L.e, e->q, e->k, e->v, D.heads, D.kv_heads, frames, e->rcos,
                                                       e->rsin, e->qo, e->k8, e->ks, e->v8, e->vs));
-    DEC_ST(attend_streams_grouped(R, e->qo, D.heads, e->k8, e->ks, e->v8, e->vs, frames, e->nk, D.kv_heads, kQK,
-                                  kVD, e->att_scale, WC_ATTEND_QUANT_Q | (e->any ? WC_ATTEND_ANY_ORDER : 0), e->att,
-                                  frames, st));
+    if (e->any && frames <= kEaMaxKeys) {
+        const dim3 grid((frames + kEaFrames - 1) / kEaFrames, D.kv_heads, R / frames);
+        DEC_LAUNCH(enc_attend_kernel<<<grid, kEaThreads, ea_smem(frames), st>>>(
+            e->qo, e->k8, e->ks, e->v8, e->vs, frames, D.heads, D.kv_heads, e->att_scale, e->att));
+    } else {
+        DEC_ST(attend_streams_grouped(R, e->qo, D.heads, e->k8, e->ks, e->v8, e->vs, frames, e->nk, D.kv_heads, kQK,
+                                      kVD, e->att_scale, WC_ATTEND_QUANT_Q | (e->any ? WC_ATTEND_ANY_ORDER : 0),
+                                      e->att, frames, st));
+    }
     DEC_LAUNCH(gate_kernel<<<R, kThreads, 0, st>>>(e->att, e->g, D.heads * kVD));
     DEC_ST(enc_gemms(e, {L.o}, e->att, {e->a}, R, st));
     // post_attn_norm, the σ(attn_gate) residual, then conv_norm (g_xn).
@@ -2536,6 +2703,9 @@ extern "C" wc_status wc_encoder_create(const wc_encoder_desc *desc, int max_clip
     e->flags = flags;
     e->tc = (flags & WC_ENCODER_TENSOR_CORES) != 0;
     e->any = (flags & WC_ENCODER_ANY_ORDER) != 0;
+    if (e->any)
+        WB_CUDA(cudaFuncSetAttribute(enc_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)ea_smem(std::min(max_frames, kEaMaxKeys))));
     e->dw_k = D.dw_kernel;
     const int qw = D.heads * kQK, kw = D.kv_heads * kQK, vw = D.kv_heads * kVD;
     for (int l = 0; l < D.layers; l++) {
