@@ -2342,22 +2342,33 @@ __global__ void stem_conv_kernel(const float *__restrict__ x, int h, int w, int 
     float kc[9];
 #pragma unroll
     for (int t = 0; t < 9; t++) kc[t] = k[t * channels + c];
-    const int p1 = min(npix, (blockIdx.x + 1) * kStemPix);
-    for (int pix = blockIdx.x * kStemPix; pix < p1; pix++) {
-        const int ow = pix % wo, r = pix / wo, oh = r % ho, b = r / ho;
+    const int p0 = blockIdx.x * kStemPix, p1 = min(npix, p0 + kStemPix);
+    // The first pixel's coordinates once; the next ones by stepping.
+    int ow = p0 % wo, oh = (p0 / wo) % ho, b = p0 / wo / ho;
+    for (int pix = p0; pix < p1; pix++) {
+        const float *xb = x + (size_t)b * h * w * cin + ci;
+        const int ih0 = 2 * oh - 1, iw0 = 2 * ow - 1;
         float acc = 0.0f;
 #pragma unroll
         for (int kh = 0; kh < 3; kh++) {
-            const int ih = 2 * oh - 1 + kh;
+            const int ih = ih0 + kh;
             if (ih < 0 || ih >= h) continue;
+            const float *xr = xb + (size_t)ih * w * cin;
 #pragma unroll
             for (int kw = 0; kw < 3; kw++) {
-                const int iw = 2 * ow - 1 + kw;
+                const int iw = iw0 + kw;
                 if (iw < 0 || iw >= w) continue;
-                acc = acc + x[(((size_t)b * h + ih) * w + iw) * cin + ci] * kc[kh * 3 + kw];
+                acc = acc + xr[iw * cin] * kc[kh * 3 + kw];
             }
         }
         out[(size_t)pix * channels + c] = silu ? acc * sigm(acc) : acc;
+        if (++ow == wo) {
+            ow = 0;
+            if (++oh == ho) {
+                oh = 0;
+                ++b;
+            }
+        }
     }
 }
 
