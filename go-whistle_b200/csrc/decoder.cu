@@ -1988,8 +1988,10 @@ extern "C" wc_status wc_decoder_greedy(wc_decoder *d, int bos, const int32_t *la
 //   GEMMs        q, k, v, gate (one shared input)
 //   enc_qkv      per-head q/k norm, RoPE at the frame's position, the int8
 //                codes and scales of k and v (QuantizeRows per head)
-//   attention    the int8 kernel: every frame of a clip reads that clip's
-//                keys and values (kv_group = frames), no mask
+//   attention    every frame against its clip's keys and values, no mask:
+//                enc_attend_kernel (any order: a clip's keys and values
+//                staged once per CTA of 32 frames) or the int8 decode
+//                kernel (exact order, kv_group = frames)
 //   gate, GEMM   σ(gate) ⊙, out_proj
 //   post_attn    post_attn_norm, gated residual, conv_norm
 //   GEMM, enc_glu, enc_dw, GEMM   pw1, GLU, depthwise + conv_out_norm +
