@@ -490,7 +490,7 @@ def encoder_component(pkg, torch, lib, clips=ENCODER_CLIPS, frames=ENCODER_FRAME
                         f"frames) on {clips} clips x {frames} frames: the stack on synthetic stem output, and "
                         f"Embed on {clips} clips of {n // 16000} s of synthetic 16 kHz audio",
             "data": "synthetic weights (Whistle's shapes, a triangular mel bank) and inputs", "per_mode": res,
-            "product_flops": flops}
+            "product_flops": flops, "cpu_baseline": encoder_cpu_baseline(pkg)}
 
 
 def single_call_component(pkg, torch, lib, calls=20, reps=10):
@@ -831,6 +831,28 @@ def decode_cpu_baseline(pkg, streams=16, max_tok=DECODE_TOKENS, frames=DECODE_FR
     return {"value": round(ntok / secs, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
             "sample": f"{streams} streams x {max_tok} greedy tokens of the same synthetic decoder, one stream per "
                       f"thread (memories untimed)", "cpu_model": cpu_model()}
+
+
+def encoder_cpu_baseline(pkg, clips=16, frames=ENCODER_FRAMES):
+    """The encoder stack's CPU baseline: the oracle's restatement of the
+    reference's Stack (encoder.go:167, int8 numerics, the lut products,
+    attendGEMM's float attention) on a sample of clips, one clip per host
+    thread, timed by the wall clock."""
+    import time
+
+    import oracle
+
+    oracle.build()
+    w = pkg.synth.EncoderWeights(seed=5300, layers=8)
+    oe = oracle.OracleEncoder(w)
+    x = pkg.synth.stem_output(np.random.default_rng(5303), clips, frames)
+    threads = min(clips, os.cpu_count() or 1)
+    t0 = time.perf_counter()
+    oe.stack(x, oracle.ENC_ATTEND_FLOAT, threads=threads)
+    secs = time.perf_counter() - t0
+    return {"value": round(clips * frames / secs), "unit": "frames/s", "cores": threads, "kind": "port",
+            "sample": f"{clips} clips x {frames} frames through the 8-layer stack, one clip per thread",
+            "cpu_model": cpu_model()}
 
 
 def cpu_model() -> str:
