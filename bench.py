@@ -493,6 +493,68 @@ def encoder_component(pkg, torch, lib, clips=ENCODER_CLIPS, frames=ENCODER_FRAME
             "product_flops": flops, "cpu_baseline": encoder_cpu_baseline(pkg)}
 
 
+def transcribe_component(pkg, torch, lib, clips=64, check_clips=4, max_tok=None):
+    """The full synthetic forward, whistle.Transcribe's greedy path: 30 s of
+    16 kHz audio per clip through the device encoder (encoder.go:108 Embed:
+    front end, stem, stack on the tensor cores with any-order attention)
+    and the device decoder (decoder.go:157 Memory, greedy.go:40
+    GreedyMemory on the bit-exact lut kernels), one stream per clip; timed
+    from the samples in HBM to the tokens in HBM. Before that, check_clips
+    clips run with every product on the lut kernels and the attention in
+    its exact order, and their tokens are compared with the CPU
+    restatement's whole chain (the reference's float attention in the
+    encoder)."""
+    import oracle
+    from oracle import frontend as fe
+
+    max_tok = max_tok or DECODE_TOKENS
+    S_ = pkg.synth
+    dw = S_.DecoderWeights(seed=4000, vocab=DECODE_VOCAB)
+    ew = S_.EncoderWeights(seed=5300)
+    n = ENCODER_FRAMES * 8 * 160
+    audio = S_.audio(np.random.default_rng(5304), clips, n)
+    da = torch.from_numpy(audio).cuda()
+    args = (S_.WHISTLE_BOS, S_.WHISTLE_LANGS, S_.WHISTLE_EOS, max_tok)
+
+    enc_x = pkg.encoder.Encoder(ew, max_clips=check_clips, max_frames=ENCODER_FRAMES)
+    dec_x = pkg.decoder.Decoder(dw, max_streams=check_clips, max_frames=ENCODER_FRAMES, max_positions=max_tok + 1)
+    dec_x.Memory(enc_x.Embed(da[:check_clips].contiguous()))
+    tok, cnt, lang, _ = (t.cpu().numpy() for t in dec_x.GreedyMemory(*args))
+    del enc_x, dec_x
+    oe, od = oracle.OracleEncoder(ew), oracle.OracleDecoder(dw)
+    xs = np.stack([fe.stem(fe.logmel(a, ew.mel_filters), ew, oracle) for a in audio[:check_clips]])
+    enc_o = oe.stack(xs, oracle.ENC_ATTEND_FLOAT, threads=check_clips)
+    otok, ocnt, olang, _ = od.greedy_streams(enc_o, *args, threads=check_clips)
+    same = sum(int(lang[b] == olang[b] and cnt[b] == ocnt[b] and np.array_equal(tok[b], otok[b, :max_tok - 1]))
+               for b in range(check_clips))
+
+    enc = pkg.encoder.Encoder(ew, max_clips=clips, max_frames=ENCODER_FRAMES,
+                              flags=pkg.encoder.WC_ENCODER_TENSOR_CORES | pkg.encoder.WC_ENCODER_ANY_ORDER)
+    dec = pkg.decoder.Decoder(dw, max_streams=clips, max_frames=ENCODER_FRAMES, max_positions=max_tok + 1)
+    out = torch.empty(clips, ENCODER_FRAMES, ew.dim, device="cuda")
+
+    def run():
+        enc.Embed(da, out)
+        dec.Memory(out)
+        return dec.GreedyMemory(*args)
+
+    run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    _, cnt, _, eh = run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    ntok = int(clips + cnt.sum().item() + eh.sum().item())
+    return {"workload": f"{clips} clips of {n // 16000} s of synthetic 16 kHz audio -> encoder (tensor cores, any-order "
+                        f"attention) -> decoder (lut kernels), greedy {max_tok} tokens per clip (language + text)",
+            "ms": round(ms, 2), "audio_seconds_per_s": round(clips * n / 16000 / (ms / 1e3)),
+            "tokens_per_s": round(ntok / (ms / 1e3)), "tokens": ntok,
+            "exact_chain_vs_cpu_restatement": f"{same} of {check_clips} clips with the CPU restatement's tokens "
+                                              f"(lut products, exact attention order on the device)"}
+
+
 def single_call_component(pkg, torch, lib, calls=20, reps=10):
     """Batch-1 latency: one GEMV call at a time (configs[0]'s 2048 x 512
     CQ4 G32, and the 16384 x 512 CQ4 vocabulary head), `calls` calls in a row
@@ -1127,6 +1189,7 @@ def main():
     ap.add_argument("--rows-sweep", action="store_true", help="only the lut / tensor-core rows sweep")
     ap.add_argument("--beam-only", action="store_true", help="only the beam search component")
     ap.add_argument("--encoder-only", action="store_true", help="only the encoder stack component")
+    ap.add_argument("--transcribe-only", action="store_true", help="only the audio-to-tokens forward (not in the default run)")
     ap.add_argument("--encoder-clips", type=int, default=ENCODER_CLIPS, help="--encoder-only: clips of 375 frames")
     ap.add_argument("--no-distinct", action="store_true",
                     help="skip the distinct-activation figure (its 8000 launches a step; profiling runs)")
@@ -1159,6 +1222,13 @@ def main():
         pkg = __import__("importlib").import_module("go-whistle_b200")
         torch.cuda.set_device(local)
         print(json.dumps(encoder_component(pkg, torch, pkg._lib.lib(), clips=args.encoder_clips)), flush=True)
+        return
+    if args.transcribe_only:
+        import torch
+
+        pkg = __import__("importlib").import_module("go-whistle_b200")
+        torch.cuda.set_device(local)
+        print(json.dumps(transcribe_component(pkg, torch, pkg._lib.lib())), flush=True)
         return
     if args.beam_only:
         import torch
