@@ -3,7 +3,13 @@ path: 16 kHz audio through encoder.Encoder.Embed (front end, stem, the
 8-layer stack; lut products, the attention's exact order) and
 decoder.Decoder (Memory, GreedyMemory), against the CPU restatement's
 whole chain (oracle/frontend.py, wo_enc_stack with the reference's float
-attention, the decoder restatement): the same language and text tokens."""
+attention, the decoder restatement): the same language and text tokens.
+
+On these synthetic weights the decoder, fed the synthetic encoder's output,
+emits one repeated token, so this test pins the chain's plumbing end to
+end more than its numerics; those are pinned piece by piece (the encoder's
+per-frame bounds in tests/test_encoder_gpu.py, the decoder's logits and
+diverse greedy tokens on random memories in tests/test_decoder_step_gpu.py)."""
 
 from __future__ import annotations
 
@@ -35,4 +41,3 @@ def test_audio_to_tokens_matches_oracle(wb, orc, cuda):
     assert np.array_equal(lang, olang)
     assert np.array_equal(cnt, ocnt) and np.array_equal(eos, oeos)
     assert np.array_equal(tok, otok[:, :MAX_TOK - 1])
-    assert len({tuple(t) for t in otok}) > 1  # the clips decode differently
